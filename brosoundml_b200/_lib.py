@@ -1,0 +1,135 @@
+"""ctypes binding of libbsml_b200.so (include/bsml_decoder.h).
+
+The product path has no fallback: if the CUDA library is missing this module
+raises, it never substitutes a CPU implementation.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libbsml_b200.so")
+
+
+class BsmlConfig(ctypes.Structure):
+    """Mirror of bsml_decoder_config."""
+
+    _fields_ = [
+        ("asr_dim", ctypes.c_int), ("style_dim", ctypes.c_int), ("asr_res_dim", ctypes.c_int),
+        ("enc_dim", ctypes.c_int), ("n_decode", ctypes.c_int), ("dec_out", ctypes.c_int * 8),
+        ("upsample_block", ctypes.c_int), ("n_ups", ctypes.c_int), ("init_ch", ctypes.c_int),
+        ("ups_rate", ctypes.c_int * 4), ("ups_kernel", ctypes.c_int * 4),
+        ("noise_kernel", ctypes.c_int * 4), ("noise_stride", ctypes.c_int * 4),
+        ("noise_pad", ctypes.c_int * 4), ("nr_kernel", ctypes.c_int * 4),
+        ("nr_dil", (ctypes.c_int * 3) * 4), ("n_kernels", ctypes.c_int),
+        ("rb_kernel", ctypes.c_int * 4), ("rb_dil", (ctypes.c_int * 3) * 4),
+        ("har_ch", ctypes.c_int), ("n_fft", ctypes.c_int), ("hop", ctypes.c_int),
+        ("post_kernel", ctypes.c_int), ("harmonic_num", ctypes.c_int),
+        ("sample_rate", ctypes.c_int), ("upsample_scale", ctypes.c_int),
+    ]
+
+
+class BsmlParamEntry(ctypes.Structure):
+    _fields_ = [("name", ctypes.c_char * 96), ("offset", ctypes.c_int64), ("numel", ctypes.c_int64),
+                ("ndim", ctypes.c_int), ("shape", ctypes.c_int * 3), ("trainable", ctypes.c_int)]
+
+
+def make_config(d: dict) -> BsmlConfig:
+    c = BsmlConfig()
+    for k, v in d.items():
+        f = getattr(c, k)
+        if isinstance(v, (list, tuple)):
+            if v and isinstance(v[0], (list, tuple)):
+                for i, row in enumerate(v):
+                    for j, x in enumerate(row):
+                        f[i][j] = int(x)
+            else:
+                for i, x in enumerate(v):
+                    f[i] = int(x)
+        else:
+            setattr(c, k, int(v))
+    return c
+
+
+# Every exported entry point with its argument types (restype int unless noted).
+_P, _I, _F, _L = ctypes.c_void_p, ctypes.c_int, ctypes.c_float, ctypes.c_int64
+_CFG = ctypes.POINTER(BsmlConfig)
+SIGNATURES = {
+    "bsml_last_error": ([], ctypes.c_char_p),
+    "bsml_version": ([], _I),
+    "bsml_decoder_create": ([_CFG, _I, ctypes.POINTER(_P)], _I),
+    "bsml_decoder_destroy": ([_P], None),
+    "bsml_decoder_param_count": ([_P, ctypes.POINTER(_L), ctypes.POINTER(_I), ctypes.POINTER(_I),
+                                  ctypes.POINTER(_L)], _I),
+    "bsml_decoder_param_table": ([_P, _P, _I, _P], _I),
+    "bsml_decoder_set_math": ([_P, _I], _I),
+    "bsml_config_param_count": ([_CFG, ctypes.POINTER(_L), ctypes.POINTER(_I), ctypes.POINTER(_I),
+                                 ctypes.POINTER(_L)], _I),
+    "bsml_config_param_table": ([_CFG, _P, _I, _P], _I),
+    "bsml_decoder_forward": ([_P, _I, _I, _P, _P, _P, _P, _P, _P, _I, _P, _P, _P, _P], _I),
+    "bsml_decoder_backward": ([_P, _P, _P, _P, _P, _P, _P], _I),
+    "bsml_decoder_workspace_bytes": ([_P], _L),
+    "bsml_decoder_set_profiling": ([_P, _I], _I),
+    "bsml_launch_count": ([], _L),
+    "bsml_decoder_read_profile": ([_P, _P], _I),
+    "bsml_loss_l1": ([_P, _P, _L, _P, _P, _P], _I),
+    "bsml_adam_step": ([_P, _P, _P, _P, _L, _F, _F, _F, _F, _I, _P], _I),
+    "bsml_conv1d_forward": ([_P, _I, _I, _I, _P, _P, _I, _I, _I, _I, _I, _P, _P], _I),
+    "bsml_conv1d_backward_input": ([_P, _I, _I, _I, _P, _I, _I, _I, _I, _I, _P, _P], _I),
+    "bsml_conv1d_backward_weight": ([_P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _P, _P, _P], _I),
+    "bsml_conv_transpose1d_forward": ([_P, _I, _I, _I, _P, _P, _I, _I, _I, _I, _P, _P], _I),
+    "bsml_conv_transpose1d_backward_input": ([_P, _I, _I, _I, _P, _I, _I, _I, _I, _P, _P], _I),
+    "bsml_conv_transpose1d_backward_weight": ([_P, _P, _I, _I, _I, _I, _I, _I, _I, _P, _P, _P], _I),
+    "bsml_adain_affine_forward": ([_P, _P, _I, _I, _I, _F, _P, _P], _I),
+    "bsml_adain_affine_backward": ([_P, _P, _P, _I, _I, _I, _F, _P, _P, _P], _I),
+    "bsml_snake_forward": ([_P, _P, _I, _I, _I, _P, _P], _I),
+    "bsml_snake_backward": ([_P, _P, _P, _I, _I, _I, _P, _P, _P], _I),
+    "bsml_istft_forward": ([_P, _P, _I, _I, _I, _I, _P, _P], _I),
+    "bsml_istft_backward": ([_P, _I, _I, _I, _I, _P, _P, _P], _I),
+    "bsml_harmonic_source": ([_CFG, _P, _I, _I, _P, _P, _P, _P], _I),
+}
+
+_lib = None
+
+
+class BsmlError(RuntimeError):
+    pass
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise BsmlError(f"brosoundml: CUDA library not built ({LIB_PATH}); run __graft_entry__.build()")
+        L = ctypes.CDLL(LIB_PATH)
+        for name, (args, res) in SIGNATURES.items():
+            fn = getattr(L, name)
+            fn.argtypes = args
+            fn.restype = res
+        _lib = L
+    return _lib
+
+
+def check(rc: int) -> None:
+    if rc != 0:
+        raise BsmlError(lib().bsml_last_error().decode())
+
+
+def layout(cfg: dict):
+    """Parameter table of a config without a device: (n_params, table, aff_C, aff_per_clip)."""
+    L = lib()
+    c = make_config(cfg)
+    n, ne, na, apc = ctypes.c_int64(), ctypes.c_int(), ctypes.c_int(), ctypes.c_int64()
+    check(L.bsml_config_param_count(ctypes.byref(c), ctypes.byref(n), ctypes.byref(ne), ctypes.byref(na),
+                                    ctypes.byref(apc)))
+    arr = (BsmlParamEntry * ne.value)()
+    affc = (ctypes.c_int * na.value)()
+    rc = L.bsml_config_param_table(ctypes.byref(c), ctypes.cast(arr, ctypes.c_void_p), ne.value,
+                                   ctypes.cast(affc, ctypes.c_void_p))
+    if rc < 0:
+        check(rc)
+    table = [dict(name=e.name.decode(), offset=e.offset, numel=e.numel, shape=tuple(e.shape[:e.ndim]),
+                  trainable=bool(e.trainable)) for e in arr]
+    return n.value, table, list(affc), apc.value

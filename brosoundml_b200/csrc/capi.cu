@@ -1,0 +1,414 @@
+// extern "C" boundary (include/bsml_decoder.h). Every entry point converts
+// exceptions into a negative status and a thread-local message.
+#include <cstring>
+#include <memory>
+#include <string>
+
+#include "bsml_decoder.h"
+#include "engine.h"
+#include "kernels.h"
+
+namespace {
+
+thread_local std::string g_err;
+
+template <class F>
+int guarded(F&& f) {
+    try {
+        f();
+        return 0;
+    } catch (const std::exception& e) {
+        g_err = e.what();
+        return -1;
+    } catch (...) {
+        g_err = "brosoundml: unknown error";
+        return -1;
+    }
+}
+
+cudaStream_t S(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+// Stream-ordered scratch for the atom entry points (which, like the reference's
+// detail:: atoms, own their temporaries).
+struct Scratch {
+    cudaStream_t st;
+    std::vector<void*> ptrs;
+    explicit Scratch(cudaStream_t s) : st(s) {}
+    float* f(int64_t n) {
+        void* p = nullptr;
+        bsml::check_cuda(cudaMallocAsync(&p, std::max<int64_t>(n, 1) * 4, st), "cudaMallocAsync");
+        ptrs.push_back(p);
+        return (float*)p;
+    }
+    double* d(int64_t n) {
+        void* p = nullptr;
+        bsml::check_cuda(cudaMallocAsync(&p, std::max<int64_t>(n, 1) * 8, st), "cudaMallocAsync");
+        ptrs.push_back(p);
+        return (double*)p;
+    }
+    bsml::Act act(int B, int L, int C) {
+        bsml::Act a;
+        a.B = B; a.L = L; a.C = C; a.ld = bsml::pitch(C);
+        a.bstride = (int64_t)L * a.ld;
+        a.p = f((int64_t)B * a.bstride);
+        return a;
+    }
+    ~Scratch() {
+        for (void* p : ptrs) cudaFreeAsync(p, st);
+    }
+};
+
+void need(bool ok, const char* where, const char* why) {
+    if (!ok) bsml::fail(where, why);
+}
+
+int conv_out(int L, int k, int s, int p, int d) { return (L + 2 * p - d * (k - 1) - 1) / s + 1; }
+
+}  // namespace
+
+struct bsml_decoder {
+    std::unique_ptr<bsml::Engine> eng;
+};
+
+extern "C" {
+
+const char* bsml_last_error(void) { return g_err.c_str(); }
+int bsml_version(void) { return 1; }
+
+int bsml_decoder_create(const bsml_decoder_config* cfg, int device, bsml_decoder** out) {
+    return guarded([&] {
+        need(cfg && out, "bsml_decoder_create", "null argument");
+        auto* d = new bsml_decoder;
+        try {
+            d->eng = std::make_unique<bsml::Engine>(*cfg, device);
+        } catch (...) {
+            delete d;
+            throw;
+        }
+        *out = d;
+    });
+}
+
+void bsml_decoder_destroy(bsml_decoder* d) { delete d; }
+
+int bsml_decoder_param_count(const bsml_decoder* d, int64_t* n_params, int* n_entries, int* n_affine,
+                             int64_t* aff_per_clip) {
+    return guarded([&] {
+        need(d != nullptr, "bsml_decoder_param_count", "null handle");
+        const auto& L = d->eng->layout();
+        if (n_params) *n_params = L.total;
+        if (n_entries) *n_entries = (int)L.table.size();
+        if (n_affine) *n_affine = (int)L.aff_C.size();
+        if (aff_per_clip) *aff_per_clip = L.aff_per_clip;
+    });
+}
+
+int bsml_decoder_param_table(const bsml_decoder* d, bsml_param_entry* out, int max_entries, int* aff_channels) {
+    int n = 0;
+    const int rc = guarded([&] {
+        need(d != nullptr, "bsml_decoder_param_table", "null handle");
+        const auto& L = d->eng->layout();
+        n = std::min<int>(max_entries, (int)L.table.size());
+        for (int i = 0; i < n; ++i) out[i] = L.table[i];
+        if (aff_channels)
+            for (size_t i = 0; i < L.aff_C.size(); ++i) aff_channels[i] = L.aff_C[i];
+    });
+    return rc ? rc : n;
+}
+
+int bsml_config_param_count(const bsml_decoder_config* cfg, int64_t* n_params, int* n_entries, int* n_affine,
+                            int64_t* aff_per_clip) {
+    return guarded([&] {
+        need(cfg != nullptr, "bsml_config_param_count", "null config");
+        const bsml::Layout L(*cfg);
+        if (n_params) *n_params = L.total;
+        if (n_entries) *n_entries = (int)L.table.size();
+        if (n_affine) *n_affine = (int)L.aff_C.size();
+        if (aff_per_clip) *aff_per_clip = L.aff_per_clip;
+    });
+}
+
+int bsml_config_param_table(const bsml_decoder_config* cfg, bsml_param_entry* out, int max_entries,
+                            int* aff_channels) {
+    int n = 0;
+    const int rc = guarded([&] {
+        need(cfg != nullptr && out != nullptr, "bsml_config_param_table", "null argument");
+        const bsml::Layout L(*cfg);
+        n = std::min<int>(max_entries, (int)L.table.size());
+        for (int i = 0; i < n; ++i) out[i] = L.table[i];
+        if (aff_channels)
+            for (size_t i = 0; i < L.aff_C.size(); ++i) aff_channels[i] = L.aff_C[i];
+    });
+    return rc ? rc : n;
+}
+
+int bsml_decoder_set_math(bsml_decoder* d, int math_mode) {
+    return guarded([&] {
+        need(d != nullptr, "bsml_decoder_set_math", "null handle");
+        d->eng->set_math(math_mode);
+    });
+}
+
+int bsml_decoder_forward(bsml_decoder* d, int B, int T, const float* params, const float* asr, const float* F0,
+                         const float* N, const float* style, const float* har, int frames, const float* aff_in,
+                         float* audio, float* aff_out, void* stream) {
+    return guarded([&] {
+        need(d != nullptr, "bsml_decoder_forward", "null handle");
+        d->eng->forward(B, T, params, asr, F0, N, style, har, frames, aff_in, audio, aff_out, S(stream));
+    });
+}
+
+int bsml_decoder_backward(bsml_decoder* d, const float* daudio, float* grads, float* d_asr, float* d_style,
+                          float* d_aff, void* stream) {
+    return guarded([&] {
+        need(d != nullptr, "bsml_decoder_backward", "null handle");
+        d->eng->backward(daudio, grads, d_asr, d_style, d_aff, S(stream));
+    });
+}
+
+int64_t bsml_decoder_workspace_bytes(const bsml_decoder* d) { return d ? d->eng->workspace_bytes() : 0; }
+
+int64_t bsml_launch_count(void) { return bsml::launch_count(); }
+
+int bsml_decoder_set_profiling(bsml_decoder* d, int on) {
+    return guarded([&] {
+        need(d != nullptr, "bsml_decoder_set_profiling", "null handle");
+        d->eng->set_profiling(on != 0);
+    });
+}
+
+int bsml_decoder_read_profile(bsml_decoder* d, double* out12) {
+    return guarded([&] {
+        need(d != nullptr && out12 != nullptr, "bsml_decoder_read_profile", "null argument");
+        d->eng->read_profile(out12);
+    });
+}
+
+int bsml_loss_l1(const float* audio, const float* target, int64_t n, float* loss, float* daudio, void* stream) {
+    return guarded([&] {
+        need(audio && target && loss && daudio && n > 0, "bsml_loss_l1", "bad argument");
+        Scratch sc(S(stream));
+        bsml::l1_loss(audio, target, n, loss, daudio, sc.d(1), S(stream));
+    });
+}
+
+int bsml_adam_step(float* param, const float* grad, float* m, float* v, int64_t n, float lr, float beta1,
+                   float beta2, float eps, int step, void* stream) {
+    return guarded([&] {
+        need(param && grad && m && v && step >= 1, "bsml_adam_step", "bad argument");
+        bsml::adam(param, grad, m, v, n, lr, beta1, beta2, eps, step, S(stream));
+    });
+}
+
+// ── atoms
+
+int bsml_conv1d_forward(const float* x, int B, int Ci, int L, const float* W, const float* bias, int Co, int k,
+                        int stride, int pad, int dil, float* y, void* stream) {
+    return guarded([&] {
+        const int Lo = conv_out(L, k, stride, pad, dil);
+        need(x && W && y && B > 0 && Ci > 0 && Co > 0 && Lo > 0, "bsml_conv1d_forward", "bad argument");
+        cudaStream_t st = S(stream);
+        Scratch sc(st);
+        bsml::Act xa = sc.act(B, L, Ci), ya = sc.act(B, Lo, Co);
+        float* wp = sc.f((int64_t)k * Ci * bsml::round_up(Co, 4));
+        bsml::ncl_to_cl(x, xa, st);
+        bsml::pack_conv_fwd(W, Co, Ci, k, wp, st);
+        bsml::ConvFwd a;
+        a.x = xa; a.y = ya; a.wp = wp; a.bias = bias; a.k = k; a.s = stride; a.p = pad; a.d = dil; a.No = Lo;
+        bsml::conv_fwd_simt(a, st);
+        bsml::cl_to_ncl(ya, y, st);
+    });
+}
+
+int bsml_conv1d_backward_input(const float* dy, int B, int Ci, int L, const float* W, int Co, int k, int stride,
+                               int pad, int dil, float* dx, void* stream) {
+    return guarded([&] {
+        need(stride == 1, "bsml_conv1d_backward_input", "only stride 1 is supported");
+        const int Lo = conv_out(L, k, stride, pad, dil);
+        need(dy && W && dx && B > 0 && Lo > 0, "bsml_conv1d_backward_input", "bad argument");
+        cudaStream_t st = S(stream);
+        Scratch sc(st);
+        bsml::Act ga = sc.act(B, Lo, Co), xa = sc.act(B, L, Ci);
+        float* wp = sc.f((int64_t)k * Co * bsml::round_up(Ci, 4));
+        bsml::ncl_to_cl(dy, ga, st);
+        bsml::pack_conv_dgrad(W, Co, Ci, k, wp, st);
+        bsml::ConvFwd a;
+        a.x = ga; a.y = xa; a.wp = wp; a.k = k; a.s = 1; a.p = dil * (k - 1) - pad; a.d = dil; a.No = L;
+        bsml::conv_fwd_simt(a, st);
+        bsml::cl_to_ncl(xa, dx, st);
+    });
+}
+
+int bsml_conv1d_backward_weight(const float* dy, const float* x, int B, int Ci, int L, int Co, int k, int stride,
+                                int pad, int dil, float* dW, float* db, void* stream) {
+    return guarded([&] {
+        const int Lo = conv_out(L, k, stride, pad, dil);
+        need(dy && x && dW && B > 0 && Lo > 0, "bsml_conv1d_backward_weight", "bad argument");
+        cudaStream_t st = S(stream);
+        Scratch sc(st);
+        bsml::Act ga = sc.act(B, Lo, Co), xa = sc.act(B, L, Ci);
+        bsml::ncl_to_cl(dy, ga, st);
+        bsml::ncl_to_cl(x, xa, st);
+        bsml::ConvWgrad a;
+        a.dy = ga; a.x = xa; a.k = k; a.s = stride; a.p = pad; a.d = dil; a.dW = dW; a.db = db;
+        float* part = sc.f(std::max(bsml::wgrad_partial_floats(a), bsml::colsum_partial_floats(ga)));
+        bsml::conv_wgrad_simt(a, part, st);
+    });
+}
+
+int bsml_conv_transpose1d_forward(const float* x, int B, int Ci, int L, const float* W, const float* bias, int Co,
+                                  int k, int stride, int pad, float* y, void* stream) {
+    return guarded([&] {
+        const int Lu = (L - 1) * stride - 2 * pad + k;
+        need(x && W && y && B > 0 && Lu > 0, "bsml_conv_transpose1d_forward", "bad argument");
+        cudaStream_t st = S(stream);
+        Scratch sc(st);
+        bsml::Act xa = sc.act(B, L, Ci), ya = sc.act(B, Lu, Co);
+        bsml::ncl_to_cl(x, xa, st);
+        for (int ph = 0; ph < stride; ++ph) {
+            const int kr = (k - ph + stride - 1) / stride;
+            if (kr <= 0) continue;
+            const int qmin = (int)bsml::ceil_div(std::max(pad - ph, 0), stride);
+            const int qmax = (Lu - 1 + pad - ph) >= 0 ? (Lu - 1 + pad - ph) / stride : -1;
+            if (qmax < qmin) continue;
+            float* wp = sc.f((int64_t)kr * Ci * bsml::round_up(Co, 4));
+            bsml::pack_convT_phase(W, Ci, Co, k, stride, ph, wp, st);
+            bsml::ConvFwd a;
+            a.x = xa; a.y = ya; a.wp = wp; a.bias = bias; a.k = kr; a.s = 1; a.p = kr - 1; a.d = 1;
+            a.No = qmax - qmin + 1; a.o_base = qmin; a.orow_mul = stride; a.orow_off = ph - pad;
+            bsml::conv_fwd_simt(a, st);
+        }
+        bsml::cl_to_ncl(ya, y, st);
+    });
+}
+
+int bsml_conv_transpose1d_backward_input(const float* dy, int B, int Ci, int L, const float* W, int Co, int k,
+                                         int stride, int pad, float* dx, void* stream) {
+    return guarded([&] {
+        const int Lu = (L - 1) * stride - 2 * pad + k;
+        need(dy && W && dx && B > 0 && Lu > 0, "bsml_conv_transpose1d_backward_input", "bad argument");
+        cudaStream_t st = S(stream);
+        Scratch sc(st);
+        bsml::Act ga = sc.act(B, Lu, Co), xa = sc.act(B, L, Ci);
+        float* wp = sc.f((int64_t)k * Co * bsml::round_up(Ci, 4));
+        bsml::ncl_to_cl(dy, ga, st);
+        bsml::pack_convT_dgrad(W, Ci, Co, k, wp, st);
+        bsml::ConvFwd a;
+        a.x = ga; a.y = xa; a.wp = wp; a.k = k; a.s = stride; a.p = pad; a.d = 1; a.No = L;
+        bsml::conv_fwd_simt(a, st);
+        bsml::cl_to_ncl(xa, dx, st);
+    });
+}
+
+int bsml_conv_transpose1d_backward_weight(const float* dy, const float* x, int B, int Ci, int L, int Co, int k,
+                                          int stride, int pad, float* dW, float* db, void* stream) {
+    return guarded([&] {
+        const int Lu = (L - 1) * stride - 2 * pad + k;
+        need(dy && x && dW && B > 0 && Lu > 0, "bsml_conv_transpose1d_backward_weight", "bad argument");
+        cudaStream_t st = S(stream);
+        Scratch sc(st);
+        bsml::Act ga = sc.act(B, Lu, Co), xa = sc.act(B, L, Ci);
+        bsml::ncl_to_cl(dy, ga, st);
+        bsml::ncl_to_cl(x, xa, st);
+        bsml::ConvWgrad a;
+        a.dy = xa; a.x = ga; a.k = k; a.s = stride; a.p = pad; a.d = 1; a.dW = dW;
+        float* part = sc.f(std::max(bsml::wgrad_partial_floats(a), bsml::colsum_partial_floats(ga)));
+        bsml::conv_wgrad_simt(a, part, st);
+        if (db) bsml::colsum(ga, db, false, part, st);
+    });
+}
+
+int bsml_adain_affine_forward(const float* x, const float* gb, int B, int C, int L, float eps, float* y,
+                              void* stream) {
+    return guarded([&] {
+        need(x && gb && y && B > 0 && C > 0 && L > 0, "bsml_adain_affine_forward", "bad argument");
+        cudaStream_t st = S(stream);
+        Scratch sc(st);
+        bsml::Act xa = sc.act(B, L, C), ya = sc.act(B, L, C);
+        float* mean = sc.f((int64_t)B * C);
+        float* rstd = sc.f((int64_t)B * C);
+        bsml::ncl_to_cl(x, xa, st);
+        bsml::in_stats(xa, eps, sc.d((int64_t)B * C * 2), mean, rstd, st);
+        bsml::adain_act_fwd(xa, mean, rstd, gb, bsml::ACT_NONE, 0.f, nullptr, ya, st);
+        bsml::cl_to_ncl(ya, y, st);
+    });
+}
+
+int bsml_adain_affine_backward(const float* x, const float* gb, const float* dy, int B, int C, int L, float eps,
+                               float* dx, float* dgb, void* stream) {
+    return guarded([&] {
+        need(x && gb && dy && dx && dgb && B > 0 && C > 0 && L > 0, "bsml_adain_affine_backward", "bad argument");
+        cudaStream_t st = S(stream);
+        Scratch sc(st);
+        bsml::Act xa = sc.act(B, L, C), ga = sc.act(B, L, C), da = sc.act(B, L, C);
+        float* mean = sc.f((int64_t)B * C);
+        float* rstd = sc.f((int64_t)B * C);
+        double* acc = sc.d((int64_t)B * C * 3);
+        bsml::ncl_to_cl(x, xa, st);
+        bsml::ncl_to_cl(dy, ga, st);
+        bsml::in_stats(xa, eps, acc, mean, rstd, st);
+        bsml::adain_act_bwd(xa, mean, rstd, gb, bsml::ACT_NONE, 0.f, nullptr, ga, da, nullptr, dgb, nullptr, acc, st);
+        bsml::cl_to_ncl(da, dx, st);
+    });
+}
+
+int bsml_snake_forward(const float* x, const float* alpha, int B, int C, int L, float* y, void* stream) {
+    return guarded([&] {
+        need(x && alpha && y && B > 0 && C > 0 && L > 0, "bsml_snake_forward", "bad argument");
+        cudaStream_t st = S(stream);
+        Scratch sc(st);
+        bsml::Act xa = sc.act(B, L, C), ya = sc.act(B, L, C);
+        bsml::ncl_to_cl(x, xa, st);
+        bsml::snake_fwd(xa, alpha, ya, st);
+        bsml::cl_to_ncl(ya, y, st);
+    });
+}
+
+int bsml_snake_backward(const float* x, const float* alpha, const float* dy, int B, int C, int L, float* dx,
+                        float* dalpha, void* stream) {
+    return guarded([&] {
+        need(x && alpha && dy && dx && dalpha && B > 0 && C > 0 && L > 0, "bsml_snake_backward", "bad argument");
+        cudaStream_t st = S(stream);
+        Scratch sc(st);
+        bsml::Act xa = sc.act(B, L, C), ga = sc.act(B, L, C), da = sc.act(B, L, C);
+        bsml::ncl_to_cl(x, xa, st);
+        bsml::ncl_to_cl(dy, ga, st);
+        bsml::snake_bwd(xa, alpha, ga, da, dalpha, sc.d((int64_t)B * C), st);
+        bsml::cl_to_ncl(da, dx, st);
+    });
+}
+
+int bsml_istft_forward(const float* re, const float* im, int B, int n_fft, int hop, int L, float* audio,
+                       void* stream) {
+    return guarded([&] {
+        need(re && im && audio && B > 0 && L > 1 && hop > 0, "bsml_istft_forward", "bad argument");
+        cudaStream_t st = S(stream);
+        Scratch sc(st);
+        bsml::istft_fwd_ncl(re, im, B, L, n_fft, hop, audio, sc.f((int64_t)B * L * (n_fft + 2)), st);
+    });
+}
+
+int bsml_istft_backward(const float* daudio, int B, int n_fft, int hop, int L, float* dre, float* dim, void* stream) {
+    return guarded([&] {
+        need(daudio && dre && dim && B > 0 && L > 1 && hop > 0, "bsml_istft_backward", "bad argument");
+        bsml::istft_bwd_ncl(daudio, B, L, n_fft, hop, dre, dim, S(stream));
+    });
+}
+
+int bsml_harmonic_source(const bsml_decoder_config* cfg, const float* F0, int B, int F, const float* l_weight,
+                         const float* l_bias, float* har, void* stream) {
+    return guarded([&] {
+        need(cfg && F0 && l_weight && l_bias && har && B > 0 && F > 0, "bsml_harmonic_source", "bad argument");
+        cudaStream_t st = S(stream);
+        Scratch sc(st);
+        const int S_len = F * cfg->upsample_scale;
+        const int frames = S_len / cfg->hop + 1;
+        bsml::Act ha = sc.act(B, frames, cfg->n_fft + 2);
+        bsml::harmonic_source(F0, B, F, cfg->upsample_scale, cfg->harmonic_num, cfg->sample_rate, cfg->n_fft, cfg->hop,
+                              l_weight, l_bias, sc.d((int64_t)B * (cfg->harmonic_num + 1) * F), sc.f((int64_t)B * S_len),
+                              ha, st);
+        bsml::cl_to_ncl(ha, har, st);
+    });
+}
+
+}  // extern "C"

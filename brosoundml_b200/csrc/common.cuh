@@ -1,0 +1,55 @@
+// Shared helpers for the sm_100a kernels and the host engine.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <stdexcept>
+#include <string>
+
+namespace bsml {
+
+// Errors cross the C ABI as a status code plus a thread-local message in the
+// reference's format: "brosoundml: <where>: <reason>".
+struct Error : std::runtime_error {
+    explicit Error(const std::string& m) : std::runtime_error(m) {}
+};
+
+[[noreturn]] inline void fail(const char* where, const std::string& why) {
+    throw Error(std::string("brosoundml: ") + where + ": " + why);
+}
+
+inline void check_cuda(cudaError_t e, const char* where) {
+    if (e != cudaSuccess) fail(where, cudaGetErrorString(e));
+}
+
+#define BSML_CUDA(call) ::bsml::check_cuda((call), #call)
+#define BSML_LAUNCH(where) ::bsml::check_cuda(cudaGetLastError(), where)
+
+// Kernel launches issued by this library (every launch site counts itself).
+void count_launch();
+int64_t launch_count();
+
+inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+inline int64_t round_up(int64_t a, int64_t b) { return ceil_div(a, b) * b; }
+
+// Channels-last activation view: element (b, l, c) at p[b*bstride + l*ld + c].
+struct Act {
+    float* p = nullptr;
+    int B = 0, L = 0, C = 0, ld = 0;
+    int64_t bstride = 0;
+    __host__ __device__ float* row(int b, int l) const { return p + (int64_t)b * bstride + (int64_t)l * ld; }
+    Act slice_c(int c0, int nc) const {
+        Act a = *this;
+        a.p = p + c0;
+        a.C = nc;
+        return a;
+    }
+    __host__ __device__ int64_t numel() const { return (int64_t)B * L * C; }
+};
+
+// Padded row pitch used for every channels-last buffer: 16-byte aligned rows
+// (a TMA requirement for the tensor-core path).
+inline int pitch(int C) { return (int)round_up(C, 4); }
+
+}  // namespace bsml

@@ -1,0 +1,710 @@
+// Decoder engine: the reference's decoder_backbone_forward_train / _backward and
+// generator_forward_train / _backward (src/kokoro_decoder_backward.cpp:482-737),
+// batched over clips, on channels-last device buffers, with the weight, bias,
+// Snake-alpha, fc and input gradients the reference drops.
+#include "engine.h"
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+
+
+namespace bsml {
+
+namespace {
+
+Act view(const Act& buf, int L, int C) {
+    Act a = buf;
+    a.L = L;
+    a.C = C;
+    a.ld = pitch(C);
+    a.bstride = (int64_t)L * a.ld;
+    return a;
+}
+
+// rows [r0, r0 + n) of an activation
+Act rows(const Act& a, int r0, int n) {
+    Act v = a;
+    v.p = a.p + (int64_t)r0 * a.ld;
+    v.L = n;
+    return v;
+}
+
+Act flat_input(const float* p, int B, int L) {   // (B, L) as channels-last with C = 1, ld = 1
+    Act a;
+    a.p = const_cast<float*>(p);
+    a.B = B; a.L = L; a.C = 1; a.ld = 1;
+    a.bstride = L;
+    return a;
+}
+
+int conv_out(int L, const ConvP& c) { return (L + 2 * c.p - c.d * (c.k - 1) - 1) / c.s + 1; }
+
+}  // namespace
+
+Engine::Engine(const bsml_decoder_config& cfg, int device) : lay_(cfg), device_(device) {
+    BSML_CUDA(cudaSetDevice(device));
+    // packed weights: forward + dgrad layouts for every conv, phases + dgrad for every convT
+    int64_t bytes = 0;
+    auto sz = [&](int64_t floats) { bytes = round_up(bytes, 256) + floats * 4; };
+    for (auto* c : lay_.convs) {
+        sz((int64_t)c->k * c->cin * round_up(c->cout, 4));
+        sz((int64_t)c->k * c->cout * round_up(c->cin, 4));
+    }
+    for (auto& u : lay_.ups) {
+        for (int r = 0; r < u.s; ++r) sz((int64_t)((u.k - r + u.s - 1) / u.s) * u.cin * round_up(u.cout, 4));
+        sz((int64_t)u.k * u.cout * round_up(u.cin, 4));
+    }
+    wp_bytes_ = round_up(bytes, 256);
+    BSML_CUDA(cudaMalloc(&wp_mem_, wp_bytes_));
+    int64_t off = 0;
+    auto take = [&](int64_t floats) {
+        off = round_up(off, 256);
+        float* p = (float*)(wp_mem_ + off);
+        off += floats * 4;
+        return p;
+    };
+    wp_fwd_.resize(lay_.convs.size());
+    wp_dgrad_.resize(lay_.convs.size());
+    for (auto* c : lay_.convs) {
+        wp_fwd_[c->id] = take((int64_t)c->k * c->cin * round_up(c->cout, 4));
+        wp_dgrad_[c->id] = take((int64_t)c->k * c->cout * round_up(c->cin, 4));
+    }
+    wp_up_.resize(lay_.ups.size());
+    wp_up_dgrad_.resize(lay_.ups.size());
+    for (auto& u : lay_.ups) {
+        for (int r = 0; r < u.s; ++r) wp_up_[u.id].push_back(take((int64_t)((u.k - r + u.s - 1) / u.s) * u.cin * round_up(u.cout, 4)));
+        wp_up_dgrad_[u.id] = take((int64_t)u.k * u.cout * round_up(u.cin, 4));
+    }
+    // fc row table (out offsets depend on B: rebuilt in ensure_plan)
+    fc_rows_ = 0;
+    for (int c : lay_.aff_C) fc_rows_ += 2 * c;
+    BSML_CUDA(cudaMalloc(&fc_tab_, sizeof(FcRow) * lay_.aff_C.size()));
+    BSML_CUDA(cudaMalloc(&fc_row_entry_, sizeof(int) * fc_rows_));
+    std::vector<int> re(fc_rows_);
+    int q = 0;
+    for (size_t a = 0; a < lay_.aff_C.size(); ++a)
+        for (int o = 0; o < 2 * lay_.aff_C[a]; ++o) re[q++] = (int)a;
+    BSML_CUDA(cudaMemcpy(fc_row_entry_, re.data(), sizeof(int) * fc_rows_, cudaMemcpyHostToDevice));
+}
+
+Engine::~Engine() {
+    cudaSetDevice(device_);
+    for (auto ev : ev_pool_) cudaEventDestroy(ev);
+    cudaFree(wp_mem_);
+    cudaFree(ws_);
+    cudaFree(fc_tab_);
+    cudaFree(fc_row_entry_);
+}
+
+void Engine::set_math(int m) {
+    if (m != BSML_MATH_FP32_SIMT && m != BSML_MATH_TF32X3 && m != BSML_MATH_BF16)
+        fail("bsml_decoder_set_math", "unknown math mode " + std::to_string(m));
+    math_ = m;
+}
+
+void Engine::set_profiling(bool on) { prof_on_ = on; }
+
+int Engine::prof_begin(int cls, double work, cudaStream_t st) {
+    if (!prof_on_) return -1;
+    while (ev_pool_.size() < ev_used_ + 2) {
+        cudaEvent_t e;
+        BSML_CUDA(cudaEventCreate(&e));
+        ev_pool_.push_back(e);
+    }
+    ProfRec r{cls, work, ev_pool_[ev_used_], ev_pool_[ev_used_ + 1]};
+    ev_used_ += 2;
+    BSML_CUDA(cudaEventRecord(r.a, st));
+    prof_.push_back(r);
+    return (int)prof_.size() - 1;
+}
+
+void Engine::prof_end(int id, cudaStream_t st) {
+    if (id >= 0) BSML_CUDA(cudaEventRecord(prof_[id].b, st));
+}
+
+void Engine::read_profile(double* out) {
+    for (int i = 0; i < PROF_N * 3; ++i) out[i] = 0;
+    BSML_CUDA(cudaDeviceSynchronize());
+    for (auto& r : prof_) {
+        float ms = 0;
+        BSML_CUDA(cudaEventElapsedTime(&ms, r.a, r.b));
+        out[r.cls * 3] += ms;
+        out[r.cls * 3 + 1] += r.work;
+        out[r.cls * 3 + 2] += 1;
+    }
+    prof_.clear();
+    ev_used_ = 0;
+}
+
+Engine::Stats Engine::stats(Planner& P, int B, int C) {
+    Stats s;
+    s.mean = P.f((int64_t)B * C);
+    s.rstd = P.f((int64_t)B * C);
+    return s;
+}
+
+Engine::BlkC Engine::plan_blk(Planner& P, const BlkP& w, int Lin, bool) {
+    BlkC c;
+    c.Lin = Lin;
+    c.Lout = w.up ? 2 * Lin : Lin;
+    c.s1 = stats(P, B_, w.cin);
+    c.s2 = stats(P, B_, w.cout);
+    c.r = P.act(B_, Lin, w.cin);
+    if (w.up) c.pooled = P.act(B_, c.Lout, w.cin);
+    c.c1 = P.act(B_, c.Lout, w.cout);
+    c.n2 = P.act(B_, c.Lout, w.cout);
+    if (w.sc) c.sc = P.act(B_, Lin, w.cout);
+    return c;
+}
+
+Engine::RB1C Engine::plan_rb1(Planner& P, int L, int C) {
+    RB1C c;
+    c.L = L;
+    for (int i = 0; i < 3; ++i) {
+        if (i > 0) c.x[i] = P.act(B_, L, C);
+        c.s1[i] = P.act(B_, L, C);
+        c.c1[i] = P.act(B_, L, C);
+        c.s2[i] = P.act(B_, L, C);
+        c.st1[i] = stats(P, B_, C);
+        c.st2[i] = stats(P, B_, C);
+    }
+    return c;
+}
+
+void Engine::plan(Planner& P) {
+    const auto& cf = lay_.cfg;
+    const int B = B_, T = T_;
+    int64_t max_elems = 0;
+    int max_c = 0;
+    auto note = [&](int L, int C) {
+        max_elems = std::max<int64_t>(max_elems, (int64_t)B * L * pitch(C));
+        max_c = std::max(max_c, C);
+    };
+    asr_ = P.act(B, T, cf.asr_dim);
+    F0_copy_ = P.f((int64_t)B * 2 * T);
+    N_copy_ = P.f((int64_t)B * 2 * T);
+    style_copy_ = P.f((int64_t)B * cf.style_dim);
+    F0dn_ = P.act(B, T, 1);
+    Ndn_ = P.act(B, T, 1);
+    asrres_ = P.act(B, T, cf.asr_res_dim);
+    enc_in_ = P.act(B, T, cf.asr_dim + 2);
+    aff_ = P.f((int64_t)B * lay_.aff_per_clip);
+    daff_ = P.f((int64_t)B * lay_.aff_per_clip);
+    encc_ = plan_blk(P, lay_.enc, T, true);
+    encc_.x = enc_in_;
+    note(T, lay_.enc.cin);
+    note(T, lay_.enc.cout);
+    const int nd = (int)lay_.dec.size();
+    dec_in_.resize(nd);
+    decc_.resize(nd);
+    res_applied_.assign(nd, 0);
+    x_ch_.assign(nd, 0);
+    int L = T, Cx = cf.enc_dim;
+    bool res = true;
+    for (int i = 0; i < nd; ++i) {
+        const BlkP& w = lay_.dec[i];
+        x_ch_[i] = Cx;
+        res_applied_[i] = res ? 1 : 0;
+        dec_in_[i] = P.act(B, L, w.cin);
+        decc_[i] = plan_blk(P, w, L, true);
+        decc_[i].x = dec_in_[i];
+        note(L, w.cin);
+        note(decc_[i].Lout, w.cin);
+        note(decc_[i].Lout, w.cout);
+        L = decc_[i].Lout;
+        Cx = w.cout;
+        if (w.up) res = false;
+    }
+    genin_ = P.act(B, L, cf.init_ch);
+    // harmonic source / har
+    const int Fr = 2 * T;
+    if (have_har_) {
+        har_ = P.act(B, frames_, cf.har_ch);
+    } else {
+        frames_ = (Fr * cf.upsample_scale) / cf.hop + 1;
+        har_ = P.act(B, frames_, cf.har_ch);
+        hs_phase_ = P.d((int64_t)B * (cf.harmonic_num + 1) * Fr);
+        hs_src_ = P.f((int64_t)B * Fr * cf.upsample_scale);
+    }
+    // generator stages
+    const int U = cf.n_ups, K = cf.n_kernels;
+    stc_.assign(U, StageC{});
+    for (int i = 0; i < U; ++i) {
+        StageC& s = stc_[i];
+        const UpP& u = lay_.ups[i];
+        s.Lin = L;
+        s.x_in = (i == 0) ? genin_ : stc_[i - 1].out;
+        s.a = P.act(B, L, u.cin);
+        s.Lu = (L - 1) * u.s - 2 * u.p + u.k;
+        s.Lx = s.Lu + (i == U - 1 ? 1 : 0);
+        const int Lsrc = conv_out(frames_, lay_.noise[i]);
+        if (Lsrc != s.Lx)
+            fail("bsml_decoder_forward", "noise source length " + std::to_string(Lsrc) + " != upsampled length " +
+                                             std::to_string(s.Lx) + " at stage " + std::to_string(i));
+        s.xsrc = P.act(B, s.Lx, u.cout);
+        s.src = P.act(B, s.Lx, u.cout);
+        s.m = P.act(B, s.Lx, u.cout);
+        s.out = P.act(B, s.Lx, u.cout);
+        s.noise = plan_rb1(P, s.Lx, u.cout);
+        s.noise.x[0] = s.xsrc;
+        s.res.resize(K);
+        for (int j = 0; j < K; ++j) {
+            s.res[j] = plan_rb1(P, s.Lx, u.cout);
+            s.res[j].x[0] = s.m;
+        }
+        note(L, u.cin);
+        note(s.Lx, u.cout);
+        L = s.Lx;
+    }
+    xl_ = P.act(B, L, lay_.post.cin);
+    post_ = P.act(B, L, lay_.post.cout);
+    spec_ = P.f((int64_t)B * L * (cf.n_fft + 2));
+    note(L, lay_.post.cout);
+    // backward-only buffers
+    dasr_cl_ = P.act(B, T, cf.asr_dim);
+    dasrres_ = P.act(B, T, cf.asr_res_dim);
+    dF0dn_ = P.act(B, T, 1);
+    dNdn_ = P.act(B, T, 1);
+    dacc_ = P.d((int64_t)B * std::max(max_c, 1) * 3);
+    part_floats_ = 48ll << 20;
+    part_ = P.f(part_floats_);
+    fc_part_ = P.f(ceil_div(fc_rows_, 256) * (int64_t)B * cf.style_dim + 64);
+    for (Act& s : S_) {
+        s = Act{};
+        s.B = B;
+        s.p = P.f(max_elems);
+    }
+}
+
+void Engine::ensure_plan(int B, int T, int frames, bool have_har) {
+    if (planned_ && B == B_ && T == T_ && have_har == have_har_ && (!have_har || frames == frames_)) return;
+    B_ = B; T_ = T; frames_ = frames; have_har_ = have_har;
+    Planner p0;
+    plan(p0);
+    const int64_t need = round_up(p0.off, 1 << 20);
+    if (need > ws_bytes_) {
+        if (ws_) BSML_CUDA(cudaFree(ws_));
+        ws_ = nullptr;
+        ws_bytes_ = 0;
+        BSML_CUDA(cudaMalloc(&ws_, need));
+        ws_bytes_ = need;
+    }
+    Planner p1;
+    p1.base = ws_;
+    plan(p1);
+    // fc table for this B
+    std::vector<FcRow> tab(lay_.aff_C.size());
+    int row0 = 0;
+    auto fill_tab = [&](const AdaP& a) {
+        FcRow& f = tab[a.idx];
+        f.w_off = a.fw;
+        f.b_off = a.fb;
+        f.out_off = (int64_t)B * lay_.aff_base[a.idx];
+        f.n_out = 2 * a.C;
+    };
+    fill_tab(lay_.enc.n1); fill_tab(lay_.enc.n2);
+    for (auto& d : lay_.dec) { fill_tab(d.n1); fill_tab(d.n2); }
+    for (auto& r : lay_.nres) for (int i = 0; i < 3; ++i) { fill_tab(r.a1[i]); fill_tab(r.a2[i]); }
+    for (auto& r : lay_.rbs) for (int i = 0; i < 3; ++i) { fill_tab(r.a1[i]); fill_tab(r.a2[i]); }
+    for (auto& f : tab) { f.row0 = row0; row0 += f.n_out; }
+    BSML_CUDA(cudaMemcpy(fc_tab_, tab.data(), sizeof(FcRow) * tab.size(), cudaMemcpyHostToDevice));
+    planned_ = true;
+}
+
+// ── weight packing (every step: the parameters may have changed)
+void Engine::pack_weights(cudaStream_t st) {
+    for (auto* c : lay_.convs) pack_conv_fwd(params_ + c->w, c->cout, c->cin, c->k, wp_fwd_[c->id], st);
+    for (auto& u : lay_.ups)
+        for (int r = 0; r < u.s; ++r) pack_convT_phase(params_ + u.w, u.cin, u.cout, u.k, u.s, r, wp_up_[u.id][r], st);
+}
+void Engine::pack_dgrad_weights(cudaStream_t st) {
+    for (auto* c : lay_.convs)
+        if (c->s == 1) pack_conv_dgrad(params_ + c->w, c->cout, c->cin, c->k, wp_dgrad_[c->id], st);
+    for (auto& u : lay_.ups) pack_convT_dgrad(params_ + u.w, u.cin, u.cout, u.k, wp_up_dgrad_[u.id], st);
+}
+
+// ── conv wrappers
+void Engine::conv(const ConvP& c, const Act& x, const Act& y, const Act* r, int r_shift, float alpha, bool accum,
+                  cudaStream_t st) {
+    ConvFwd a;
+    a.x = x; a.y = y; a.wp = wp_fwd_[c.id]; a.bias = P(c.b); a.r = r; a.r_shift = r_shift;
+    a.k = c.k; a.s = c.s; a.p = c.p; a.d = c.d;
+    a.No = conv_out(x.L, c);
+    a.alpha = alpha; a.accum = accum;
+    if (a.No != y.L) fail("conv", "output length mismatch");
+    const int id = prof_begin(PROF_CONV, 2.0 * c.cin * c.cout * c.k * (double)a.No * x.B, st);
+    conv_fwd_simt(a, st);
+    prof_end(id, st);
+}
+
+// dx[j] = sum_{t,co} W[co,ci,t] dy[j + p - t*d]: a forward conv over dy with the
+// flipped, transposed weight and padding d*(k-1) - p (stride 1 only).
+void Engine::conv_dgrad(const ConvP& c, const Act& dy, const Act& dx, bool accum, cudaStream_t st) {
+    if (c.s != 1) fail("conv_dgrad", "strided conv input gradients are not needed on this path");
+    ConvFwd a;
+    a.x = dy; a.y = dx; a.wp = wp_dgrad_[c.id];
+    a.k = c.k; a.s = 1; a.p = c.d * (c.k - 1) - c.p; a.d = c.d;
+    a.No = dx.L;
+    a.accum = accum;
+    const int id = prof_begin(PROF_CONV, 2.0 * c.cin * c.cout * c.k * (double)dy.L * dy.B, st);
+    conv_fwd_simt(a, st);
+    prof_end(id, st);
+}
+
+void Engine::conv_wgrad(const ConvP& c, const Act& dy, const Act& x, cudaStream_t st) {
+    if (!grads_) return;
+    ConvWgrad a;
+    a.dy = dy; a.x = x; a.k = c.k; a.s = c.s; a.p = c.p; a.d = c.d;
+    a.dW = grads_ + c.w;
+    a.db = G(c.b);
+    if (wgrad_partial_floats(a) > part_floats_) fail("conv_wgrad", "split-K partial buffer too small");
+    const int id = prof_begin(PROF_WGRAD, 2.0 * c.cin * c.cout * c.k * (double)dy.L * dy.B, st);
+    conv_wgrad_simt(a, part_, st);
+    prof_end(id, st);
+}
+
+// ConvTranspose1d forward as one forward conv per stride phase r:
+//   y[q*s + r - p] = sum_m sum_ci W[ci, co, r + m*s] x[q - m, ci]
+void Engine::convT(const UpP& u, const Act& x, const Act& y, int row_off, const Act* r, cudaStream_t st) {
+    const int Lu = (x.L - 1) * u.s - 2 * u.p + u.k;
+    for (int ph = 0; ph < u.s; ++ph) {
+        const int kr = (u.k - ph + u.s - 1) / u.s;
+        if (kr <= 0) continue;
+        // q with 0 <= q*s + ph - p < Lu
+        const int qmin = (int)ceil_div(std::max(u.p - ph, 0), u.s);
+        const int qmax = (Lu - 1 + u.p - ph) >= 0 ? (Lu - 1 + u.p - ph) / u.s : -1;
+        if (qmax < qmin) continue;
+        ConvFwd a;
+        a.x = x; a.y = y; a.wp = wp_up_[u.id][ph]; a.bias = P(u.b); a.r = r;
+        a.k = kr; a.s = 1; a.p = kr - 1; a.d = 1;
+        a.No = qmax - qmin + 1; a.o_base = qmin;
+        a.orow_mul = u.s; a.orow_off = ph - u.p + row_off;
+        const int id = prof_begin(PROF_CONV, 2.0 * u.cin * u.cout * kr * (double)a.No * x.B, st);
+        conv_fwd_simt(a, st);
+        prof_end(id, st);
+    }
+}
+
+// dx[l, ci] = sum_{t, co} W[ci, co, t] dy[l*s - p + t, co]: a strided forward conv over dy
+void Engine::convT_dgrad(const UpP& u, const Act& dy, const Act& dx, cudaStream_t st) {
+    ConvFwd a;
+    a.x = dy; a.y = dx; a.wp = wp_up_dgrad_[u.id];
+    a.k = u.k; a.s = u.s; a.p = u.p; a.d = 1;
+    a.No = dx.L;
+    const int id = prof_begin(PROF_CONV, 2.0 * u.cin * u.cout * u.k * (double)dx.L * dx.B, st);
+    conv_fwd_simt(a, st);
+    prof_end(id, st);
+}
+
+// dW[ci, co, t] = sum x[l, ci] dy[l*s - p + t, co]  (conv wgrad with roles swapped), db = colsum(dy)
+void Engine::convT_wgrad(const UpP& u, const Act& dy, const Act& x, cudaStream_t st) {
+    if (!grads_) return;
+    ConvWgrad a;
+    a.dy = x; a.x = dy; a.k = u.k; a.s = u.s; a.p = u.p; a.d = 1;
+    a.dW = grads_ + u.w;
+    a.db = nullptr;
+    if (wgrad_partial_floats(a) > part_floats_) fail("convT_wgrad", "split-K partial buffer too small");
+    const int id = prof_begin(PROF_WGRAD, 2.0 * u.cin * u.cout * u.k * (double)x.L * x.B, st);
+    conv_wgrad_simt(a, part_, st);
+    colsum(dy, grads_ + u.b, false, part_, st);
+    prof_end(id, st);
+}
+
+void Engine::stats_of(const Act& x, const Stats& s, cudaStream_t st) { in_stats(x, 1e-5f, dacc_, s.mean, s.rstd, st); }
+
+// ── AdainResBlk1d (kokoro_decoder_backward.cpp:152-285)
+void Engine::blk_fwd(const BlkP& w, BlkC& c, const Act& y, cudaStream_t st) {
+    stats_of(c.x, c.s1, st);
+    adain_act_fwd(c.x, c.s1.mean, c.s1.rstd, aff(w.n1), ACT_LEAKY, 0.2f, nullptr, c.r, st);
+    Act pooled = c.r;
+    if (w.up) {
+        dwconvT_fwd(c.r, P(w.pool_w), P(w.pool_b), 3, 2, 1, c.pooled, st);
+        pooled = c.pooled;
+    }
+    conv(w.c1, pooled, c.c1, nullptr, 0, 1.f, false, st);
+    stats_of(c.c1, c.s2, st);
+    adain_act_fwd(c.c1, c.s2.mean, c.s2.rstd, aff(w.n2), ACT_LEAKY, 0.2f, nullptr, c.n2, st);
+    // shortcut: a 1x1 conv commutes with nearest-2x, so it runs at L_in and the
+    // conv2 epilogue reads it at row >> 1
+    const Act* sc = &c.x;
+    if (w.sc) {
+        conv(w.c1x1, c.x, c.sc, nullptr, 0, 1.f, false, st);
+        sc = &c.sc;
+    }
+    conv(w.c2, c.n2, y, sc, w.up ? 1 : 0, 1.f / std::sqrt(2.f), false, st);
+}
+
+void Engine::blk_bwd(const BlkP& w, BlkC& c, const Act& dY, const Act& dX, cudaStream_t st) {
+    const int Lin = c.Lin, Lout = c.Lout;
+    // d_branch = dY / sqrt(2)  (S_[0])
+    Act db = view(S_[0], Lout, w.cout);
+    copy_act(dY, db, st);
+    scale_act(db, 1.f / std::sqrt(2.f), st);
+    Act t1 = view(S_[1], Lout, w.cout);
+    conv_dgrad(w.c2, db, t1, false, st);
+    conv_wgrad(w.c2, db, c.n2, st);
+    Act dc1 = view(S_[2], Lout, w.cout);
+    adain_act_bwd(c.c1, c.s2.mean, c.s2.rstd, aff(w.n2), ACT_LEAKY, 0.2f, nullptr, t1, dc1, nullptr, daff(w.n2),
+                  nullptr, dacc_, st);
+    Act dpooled = view(S_[1], Lout, w.cin);
+    conv_dgrad(w.c1, dc1, dpooled, false, st);
+    conv_wgrad(w.c1, dc1, w.up ? c.pooled : c.r, st);
+    Act dr = dpooled;
+    if (w.up) {
+        dr = view(S_[2], Lin, w.cin);
+        dwconvT_dgrad(dpooled, P(w.pool_w), 3, 2, 1, dr, st);
+        if (grads_) dwconvT_wgrad(dpooled, c.r, 3, 2, 1, G(w.pool_w), G(w.pool_b), st);
+    }
+    adain_act_bwd(c.x, c.s1.mean, c.s1.rstd, aff(w.n1), ACT_LEAKY, 0.2f, nullptr, dr, dX, nullptr, daff(w.n1),
+                  nullptr, dacc_, st);
+    // shortcut branch
+    Act dbs = db;
+    if (w.up) {
+        dbs = view(S_[3], Lin, w.cout);
+        pair_sum_rows(db, dbs, st);
+    }
+    if (w.sc) {
+        conv_dgrad(w.c1x1, dbs, dX, true, st);
+        conv_wgrad(w.c1x1, dbs, c.x, st);
+    } else {
+        add_act(dbs, dX, 1.f, st);
+    }
+}
+
+// ── AdaINResBlock1 (kokoro_decoder_backward.cpp:287-376)
+void Engine::rb1_fwd(const RB1P& w, RB1C& c, const Act& x0, const Act& out, float out_alpha, bool out_accum,
+                     cudaStream_t st) {
+    c.x[0] = x0;
+    // algorithmic bytes of one fused AdaIN+Snake forward: read x, write y
+    const double nb = 8.0 * (double)x0.numel();
+    for (int i = 0; i < 3; ++i) {
+        int id = prof_begin(PROF_NORM_FWD, nb, st);
+        stats_of(c.x[i], c.st1[i], st);
+        adain_act_fwd(c.x[i], c.st1[i].mean, c.st1[i].rstd, aff(w.a1[i]), ACT_SNAKE, 0.f, P(w.al1[i]), c.s1[i], st);
+        prof_end(id, st);
+        conv(w.c1[i], c.s1[i], c.c1[i], nullptr, 0, 1.f, false, st);
+        id = prof_begin(PROF_NORM_FWD, nb, st);
+        stats_of(c.c1[i], c.st2[i], st);
+        adain_act_fwd(c.c1[i], c.st2[i].mean, c.st2[i].rstd, aff(w.a2[i]), ACT_SNAKE, 0.f, P(w.al2[i]), c.s2[i], st);
+        prof_end(id, st);
+        if (i < 2)
+            conv(w.c2[i], c.s2[i], c.x[i + 1], &c.x[i], 0, 1.f, false, st);
+        else
+            conv(w.c2[i], c.s2[i], out, &c.x[i], 0, out_alpha, out_accum, st);
+    }
+}
+
+void Engine::rb1_bwd(const RB1P& w, RB1C& c, const Act& dOut, float scale, const Act& D, cudaStream_t st) {
+    const int L = c.L, C = w.C;
+    copy_act(dOut, D, st);
+    if (scale != 1.f) scale_act(D, scale, st);
+    Act t = view(S_[4], L, C), u = view(S_[5], L, C);
+    // algorithmic bytes of one fused AdaIN+Snake backward: read x and dy, write dx
+    const double nb = 12.0 * (double)D.numel();
+    for (int i = 2; i >= 0; --i) {
+        conv_dgrad(w.c2[i], D, t, false, st);
+        conv_wgrad(w.c2[i], D, c.s2[i], st);
+        int id = prof_begin(PROF_NORM_BWD, nb, st);
+        adain_act_bwd(c.c1[i], c.st2[i].mean, c.st2[i].rstd, aff(w.a2[i]), ACT_SNAKE, 0.f, P(w.al2[i]), t, u, nullptr,
+                      daff(w.a2[i]), G(w.al2[i]), dacc_, st);
+        prof_end(id, st);
+        conv_dgrad(w.c1[i], u, t, false, st);
+        conv_wgrad(w.c1[i], u, c.s1[i], st);
+        id = prof_begin(PROF_NORM_BWD, nb, st);
+        adain_act_bwd(c.x[i], c.st1[i].mean, c.st1[i].rstd, aff(w.a1[i]), ACT_SNAKE, 0.f, P(w.al1[i]), t, D, &D,
+                      daff(w.a1[i]), G(w.al1[i]), dacc_, st);
+        prof_end(id, st);
+    }
+}
+
+// ── forward
+void Engine::forward(int B, int T, const float* params, const float* asr, const float* F0, const float* N,
+                     const float* style, const float* har, int frames, const float* aff_in, float* audio,
+                     float* aff_out, cudaStream_t st) {
+    if (B < 1 || T < 1) fail("bsml_decoder_forward", "B and T must be positive");
+    if (!params || !asr || !F0 || !N || !audio) fail("bsml_decoder_forward", "null input");
+    if (!aff_in && !style) fail("bsml_decoder_forward", "style is required unless aff_in is given");
+    BSML_CUDA(cudaSetDevice(device_));
+    ensure_plan(B, T, frames, har != nullptr);
+    const auto& cf = lay_.cfg;
+    params_ = params;
+    // the backward needs F0, N (conv weight grads) and style (fc grads): keep copies
+    BSML_CUDA(cudaMemcpyAsync(F0_copy_, F0, sizeof(float) * B * 2 * T, cudaMemcpyDeviceToDevice, st));
+    BSML_CUDA(cudaMemcpyAsync(N_copy_, N, sizeof(float) * B * 2 * T, cudaMemcpyDeviceToDevice, st));
+    if (style)
+        BSML_CUDA(cudaMemcpyAsync(style_copy_, style, sizeof(float) * B * cf.style_dim, cudaMemcpyDeviceToDevice, st));
+    F0_ = F0_copy_;
+    N_ = N_copy_;
+    style_ = style ? style_copy_ : nullptr;
+    ref_mode_ = aff_in != nullptr;
+    fwd_done_ = false;
+    pack_weights(st);
+    // affines: fc(style) (compute_style_affine, kokoro_modules.cpp:563-572) or caller-supplied
+    if (ref_mode_)
+        BSML_CUDA(cudaMemcpyAsync(aff_, aff_in, sizeof(float) * B * lay_.aff_per_clip, cudaMemcpyDeviceToDevice, st));
+    else
+        affine_fc_fwd(fc_tab_, (int)lay_.aff_C.size(), fc_rows_, fc_row_entry_, params_, style_, B, cf.style_dim,
+                      aff_, st);
+    if (aff_out)
+        BSML_CUDA(cudaMemcpyAsync(aff_out, aff_, sizeof(float) * B * lay_.aff_per_clip, cudaMemcpyDeviceToDevice, st));
+    // backbone (kokoro_decoder_backward.cpp:482-537)
+    ncl_to_cl(asr, asr_, st);
+    conv(lay_.F0c, flat_input(F0, B, 2 * T), F0dn_, nullptr, 0, 1.f, false, st);
+    conv(lay_.Nc, flat_input(N, B, 2 * T), Ndn_, nullptr, 0, 1.f, false, st);
+    conv(lay_.asr_res, asr_, asrres_, nullptr, 0, 1.f, false, st);
+    copy_act(asr_, enc_in_.slice_c(0, cf.asr_dim), st);
+    copy_act(F0dn_, enc_in_.slice_c(cf.asr_dim, 1), st);
+    copy_act(Ndn_, enc_in_.slice_c(cf.asr_dim + 1, 1), st);
+    const int nd = (int)lay_.dec.size();
+    for (int i = -1; i < nd; ++i) {
+        BlkC& c = i < 0 ? encc_ : decc_[i];
+        const BlkP& w = i < 0 ? lay_.enc : lay_.dec[i];
+        Act y;
+        if (i + 1 < nd) {
+            y = dec_in_[i + 1].slice_c(0, w.cout);
+        } else {
+            y = genin_;
+        }
+        blk_fwd(w, c, y, st);
+        if (i + 1 < nd && res_applied_[i + 1]) {
+            Act& din = dec_in_[i + 1];
+            const int Cx = x_ch_[i + 1];
+            copy_act(asrres_, din.slice_c(Cx, cf.asr_res_dim), st);
+            copy_act(F0dn_, din.slice_c(Cx + cf.asr_res_dim, 1), st);
+            copy_act(Ndn_, din.slice_c(Cx + cf.asr_res_dim + 1, 1), st);
+        }
+    }
+    // har
+    if (have_har_) {
+        ncl_to_cl(har, har_, st);
+    } else {
+        harmonic_source(F0, B, 2 * T, cf.upsample_scale, cf.harmonic_num, cf.sample_rate, cf.n_fft, cf.hop,
+                        params_ + lay_.llin_w, params_ + lay_.llin_b, hs_phase_, hs_src_, har_, st);
+    }
+    // generator (kokoro_decoder_backward.cpp:592-667)
+    const int U = cf.n_ups, K = cf.n_kernels;
+    for (int i = 0; i < U; ++i) {
+        StageC& s = stc_[i];
+        const UpP& u = lay_.ups[i];
+        leaky_fwd(s.x_in, 0.1f, s.a, st);
+        conv(lay_.noise[i], har_, s.xsrc, nullptr, 0, 1.f, false, st);
+        rb1_fwd(lay_.nres[i], s.noise, s.xsrc, s.src, 1.f, false, st);
+        if (i == U - 1) {
+            // u written to rows 1..Lu, row 0 = reflection of row 1 (pad1d mode 1), then m = u + src
+            convT(u, s.a, s.m, 1, nullptr, st);
+            reflect_left1_fwd(s.m, st);
+            add_act(s.src, s.m, 1.f, st);
+        } else {
+            convT(u, s.a, s.m, 0, &s.src, st);
+        }
+        for (int j = 0; j < K; ++j)
+            rb1_fwd(lay_.rbs[i * K + j], s.res[j], s.m, s.out, 1.f / (float)K, j > 0, st);
+    }
+    // spectral head (kokoro_decoder_backward.cpp:378-410)
+    const Act& xlast = stc_[U - 1].out;
+    leaky_fwd(xlast, 0.01f, xl_, st);
+    conv(lay_.post, xl_, post_, nullptr, 0, 1.f, false, st);
+    const int nf = cf.n_fft / 2 + 1;
+    polar_fwd(post_, nf, spec_, st);
+    istft_fwd(spec_, B, post_.L, cf.n_fft, cf.hop, audio, st);
+    fwd_done_ = true;
+}
+
+// ── backward
+void Engine::backward(const float* daudio, float* grads, float* d_asr, float* d_style, float* d_aff,
+                      cudaStream_t st) {
+    if (!fwd_done_) fail("bsml_decoder_backward", "no matching forward");
+    if (!daudio) fail("bsml_decoder_backward", "null daudio");
+    BSML_CUDA(cudaSetDevice(device_));
+    const auto& cf = lay_.cfg;
+    const int B = B_, T = T_;
+    grads_ = grads;
+    if (grads_) fill(grads_, lay_.total, 0.f, st);
+    pack_dgrad_weights(st);
+    const int U = cf.n_ups, K = cf.n_kernels;
+    // spectral head
+    const int L1 = post_.L;
+    const Act& xlast = stc_[U - 1].out;
+    Act dpost = view(S_[0], L1, lay_.post.cout);
+    istft_polar_bwd(daudio, post_, cf.n_fft, cf.hop, dpost, st);
+    Act dxl = view(S_[1], L1, lay_.post.cin);
+    conv_dgrad(lay_.post, dpost, dxl, false, st);
+    conv_wgrad(lay_.post, dpost, xl_, st);
+    // dX lives in S_[2]/S_[3] alternately; dm in S_[1]
+    Act dX = view(S_[2], L1, lay_.post.cin);
+    leaky_bwd(xlast, 0.01f, dxl, dX, st);
+    int xbuf = 2;
+    for (int i = U - 1; i >= 0; --i) {
+        StageC& s = stc_[i];
+        const UpP& u = lay_.ups[i];
+        // dm = sum_j rb_j^T (dX / K)   (D in S_[xbuf^1], dm in S_[1])
+        Act D = view(S_[xbuf ^ 1], s.Lx, u.cout);
+        Act dm = view(S_[1], s.Lx, u.cout);
+        for (int j = 0; j < K; ++j) {
+            rb1_bwd(lay_.rbs[i * K + j], s.res[j], dX, 1.f / (float)K, D, st);
+            if (j == 0) copy_act(D, dm, st);
+            else add_act(D, dm, 1.f, st);
+        }
+        // noise branch: affine / alpha / conv grads; its input grad only feeds noise_convs' wgrad
+        rb1_bwd(lay_.nres[i], s.noise, dm, 1.f, D, st);
+        conv_wgrad(lay_.noise[i], D, har_, st);
+        Act du = dm;
+        if (i == U - 1) {
+            reflect_left1_bwd(dm, st);
+            du = rows(dm, 1, s.Lu);
+        }
+        Act da = view(S_[xbuf ^ 1], s.Lin, u.cin);
+        convT_dgrad(u, du, da, st);
+        convT_wgrad(u, du, s.a, st);
+        Act dprev = view(S_[xbuf], s.Lin, u.cin);
+        leaky_bwd(s.x_in, 0.1f, da, dprev, st);
+        dX = dprev;
+    }
+    // backbone (kokoro_decoder_backward.cpp:539-574) + the cat-channel grads
+    fill(dasrres_.p, (int64_t)B * dasrres_.bstride, 0.f, st);
+    fill(dF0dn_.p, (int64_t)B * dF0dn_.bstride, 0.f, st);
+    fill(dNdn_.p, (int64_t)B * dNdn_.bstride, 0.f, st);
+    // the block backward uses S_[0..3]; the running dX alternates between S_[4] and S_[5]
+    Act dY = view(S_[4], dX.L, dX.C);
+    copy_act(dX, dY, st);
+    int ybuf = 4;
+    const int nd = (int)lay_.dec.size();
+    for (int i = nd - 1; i >= -1; --i) {
+        BlkC& c = i < 0 ? encc_ : decc_[i];
+        const BlkP& w = i < 0 ? lay_.enc : lay_.dec[i];
+        Act bdx = view(S_[ybuf ^ 1], c.Lin, w.cin);
+        blk_bwd(w, c, dY, bdx, st);
+        if (i >= 0 && res_applied_[i]) {
+            const int Cx = x_ch_[i];
+            add_act(bdx.slice_c(Cx, cf.asr_res_dim), dasrres_, 1.f, st);
+            add_act(bdx.slice_c(Cx + cf.asr_res_dim, 1), dF0dn_, 1.f, st);
+            add_act(bdx.slice_c(Cx + cf.asr_res_dim + 1, 1), dNdn_, 1.f, st);
+            dY = bdx.slice_c(0, Cx);
+        } else if (i >= 0) {
+            dY = bdx;
+        } else {
+            // encode: input = [asr, F0_dn, N_dn]
+            add_act(bdx.slice_c(cf.asr_dim, 1), dF0dn_, 1.f, st);
+            add_act(bdx.slice_c(cf.asr_dim + 1, 1), dNdn_, 1.f, st);
+            copy_act(bdx.slice_c(0, cf.asr_dim), dasr_cl_, st);
+        }
+        ybuf ^= 1;
+    }
+    conv_wgrad(lay_.F0c, dF0dn_, flat_input(F0_, B, 2 * T), st);
+    conv_wgrad(lay_.Nc, dNdn_, flat_input(N_, B, 2 * T), st);
+    conv_dgrad(lay_.asr_res, dasrres_, dasr_cl_, true, st);
+    conv_wgrad(lay_.asr_res, dasrres_, asr_, st);
+    if (d_asr) cl_to_ncl(dasr_cl_, d_asr, st);
+    if (d_aff)
+        BSML_CUDA(cudaMemcpyAsync(d_aff, daff_, sizeof(float) * B * lay_.aff_per_clip, cudaMemcpyDeviceToDevice, st));
+    if (ref_mode_) {
+        if (d_style) fill(d_style, (int64_t)B * cf.style_dim, 0.f, st);
+    } else {
+        affine_fc_bwd(fc_tab_, (int)lay_.aff_C.size(), fc_rows_, fc_row_entry_, params_, style_, daff_, B,
+                      cf.style_dim, grads_, d_style, fc_part_, st);
+    }
+    grads_ = nullptr;
+}
+
+}  // namespace bsml

@@ -1,0 +1,159 @@
+// The batched decoder engine: forward with caches, backward, workspace planning.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <memory>
+#include <vector>
+
+#include "common.cuh"
+#include "kernels.h"
+#include "layout.h"
+
+namespace bsml {
+
+class Engine {
+   public:
+    Engine(const bsml_decoder_config& cfg, int device);
+    ~Engine();
+    Engine(const Engine&) = delete;
+    Engine& operator=(const Engine&) = delete;
+
+    const Layout& layout() const { return lay_; }
+    void set_math(int m);
+    int math() const { return math_; }
+
+    void forward(int B, int T, const float* params, const float* asr, const float* F0, const float* N,
+                 const float* style, const float* har, int frames, const float* aff_in, float* audio,
+                 float* aff_out, cudaStream_t st);
+    void backward(const float* daudio, float* grads, float* d_asr, float* d_style, float* d_aff, cudaStream_t st);
+    int64_t workspace_bytes() const { return ws_bytes_ + wp_bytes_; }
+
+    // Per-kernel-class timing with CUDA events (off by default). Classes:
+    // 0 conv fwd-like (fwd, dgrad, convT), 1 conv wgrad, 2 AdaIN/Snake forward,
+    // 3 AdaIN/Snake backward. Per class: ms, algorithmic work (FLOPs for 0-1,
+    // bytes for 2-3), launches. Reading the profile synchronises the device.
+    enum { PROF_CONV = 0, PROF_WGRAD = 1, PROF_NORM_FWD = 2, PROF_NORM_BWD = 3, PROF_N = 4 };
+    void set_profiling(bool on);
+    void read_profile(double* out);   // PROF_N * 3 doubles, then clears
+
+   private:
+    // ── planning
+    struct Planner {
+        char* base = nullptr;
+        int64_t off = 0;
+        void* take(int64_t bytes) {
+            off = round_up(off, 256);
+            void* p = base ? base + off : nullptr;
+            off += bytes;
+            return p;
+        }
+        Act act(int B, int L, int C) {
+            Act a;
+            a.B = B; a.L = L; a.C = C; a.ld = pitch(C);
+            a.bstride = (int64_t)L * a.ld;
+            a.p = (float*)take((int64_t)B * a.bstride * 4);
+            return a;
+        }
+        float* f(int64_t n) { return (float*)take(n * 4); }
+        double* d(int64_t n) { return (double*)take(n * 8); }
+    };
+    struct Stats { float* mean = nullptr; float* rstd = nullptr; };
+    struct BlkC { Act x, r, pooled, c1, n2, sc; Stats s1, s2; int Lin = 0, Lout = 0; };
+    struct RB1C { Act x[3], s1[3], c1[3], s2[3]; Stats st1[3], st2[3]; int L = 0; };
+    struct StageC { Act x_in, a, xsrc, src, m, out; RB1C noise; std::vector<RB1C> res; int Lin = 0, Lu = 0, Lx = 0; };
+
+    void plan(Planner& P);
+    void ensure_plan(int B, int T, int frames, bool have_har);
+    Stats stats(Planner& P, int B, int C);
+    BlkC plan_blk(Planner& P, const BlkP& w, int Lin, bool input_owned);
+    RB1C plan_rb1(Planner& P, int L, int C);
+
+    // ── execution helpers
+    void pack_weights(cudaStream_t st);
+    void pack_dgrad_weights(cudaStream_t st);
+    const float* aff(const AdaP& a) const { return aff_ + (int64_t)B_ * lay_.aff_base[a.idx]; }
+    float* daff(const AdaP& a) const { return daff_ + (int64_t)B_ * lay_.aff_base[a.idx]; }
+    const float* P(int64_t off) const { return off >= 0 ? params_ + off : nullptr; }
+    float* G(int64_t off) const { return (grads_ && off >= 0) ? grads_ + off : nullptr; }
+
+    void conv(const ConvP& c, const Act& x, const Act& y, const Act* r, int r_shift, float alpha, bool accum,
+              cudaStream_t st);
+    void conv_dgrad(const ConvP& c, const Act& dy, const Act& dx, bool accum, cudaStream_t st);
+    void conv_wgrad(const ConvP& c, const Act& dy, const Act& x, cudaStream_t st);
+    void convT(const UpP& u, const Act& x, const Act& y, int row_off, const Act* r, cudaStream_t st);
+    void convT_dgrad(const UpP& u, const Act& dy, const Act& dx, cudaStream_t st);
+    void convT_wgrad(const UpP& u, const Act& dy, const Act& x, cudaStream_t st);
+    void stats_of(const Act& x, const Stats& s, cudaStream_t st);
+
+    void blk_fwd(const BlkP& w, BlkC& c, const Act& y, cudaStream_t st);
+    void blk_bwd(const BlkP& w, BlkC& c, const Act& dY, const Act& dX, cudaStream_t st);
+    void rb1_fwd(const RB1P& w, RB1C& c, const Act& x0, const Act& out, float out_alpha, bool out_accum,
+                 cudaStream_t st);
+    // returns the gradient w.r.t. the block input in `D` (scratch, may alias nothing else)
+    void rb1_bwd(const RB1P& w, RB1C& c, const Act& dOut, float scale, const Act& D, cudaStream_t st);
+
+    struct ProfRec { int cls; double work; cudaEvent_t a, b; };
+    int prof_begin(int cls, double work, cudaStream_t st);
+    void prof_end(int id, cudaStream_t st);
+    bool prof_on_ = false;
+    std::vector<ProfRec> prof_;
+    std::vector<cudaEvent_t> ev_pool_;
+    size_t ev_used_ = 0;
+
+    Layout lay_;
+    int device_ = 0;
+    int math_ = BSML_MATH_FP32_SIMT;
+
+    // packed weights (persistent, independent of B/T)
+    char* wp_mem_ = nullptr;
+    int64_t wp_bytes_ = 0;
+    std::vector<float*> wp_fwd_, wp_dgrad_;       // per conv id
+    std::vector<std::vector<float*>> wp_up_;      // per ups: phases
+    std::vector<float*> wp_up_dgrad_;
+    FcRow* fc_tab_ = nullptr;                     // device
+    int* fc_row_entry_ = nullptr;                 // device
+    int fc_rows_ = 0;
+    int fc_tab_B_ = -1;
+
+    // workspace (depends on B, T, frames)
+    char* ws_ = nullptr;
+    int64_t ws_bytes_ = 0;
+    int B_ = 0, T_ = 0, frames_ = 0;
+    bool have_har_ = false;
+    bool planned_ = false;
+
+    // per-call pointers
+    const float* params_ = nullptr;
+    float* grads_ = nullptr;
+    const float* F0_ = nullptr;
+    const float* N_ = nullptr;
+    const float* style_ = nullptr;
+    bool ref_mode_ = false;
+    bool fwd_done_ = false;
+
+    // planned buffers
+    Act asr_, F0dn_, Ndn_, asrres_, enc_in_, har_, xl_, post_, genin_;
+    std::vector<Act> dec_in_;
+    BlkC encc_;
+    std::vector<BlkC> decc_;
+    std::vector<char> res_applied_;
+    std::vector<int> x_ch_;
+    std::vector<StageC> stc_;
+    float* aff_ = nullptr;
+    float* daff_ = nullptr;
+    float* spec_ = nullptr;
+    float* hs_src_ = nullptr;
+    double* hs_phase_ = nullptr;
+    double* dacc_ = nullptr;          // reduction scratch (B * max C * 3)
+    float* part_ = nullptr;           // split-K partials
+    int64_t part_floats_ = 0;
+    float* fc_part_ = nullptr;
+    Act S_[6];                        // backward scratch at the largest shape
+    Act dasr_cl_, dasrres_, dF0dn_, dNdn_;
+    float* F0_copy_ = nullptr;        // the forward's inputs, kept for the backward
+    float* N_copy_ = nullptr;
+    float* style_copy_ = nullptr;
+};
+
+}  // namespace bsml

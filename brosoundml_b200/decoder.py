@@ -1,0 +1,136 @@
+"""Python host mirror of the reference's decoder training interface, over the C ABI.
+
+``Decoder`` wraps one ``bsml_decoder`` engine (forward with caches, backward),
+``DecoderLora``-style training loops are built from it in ``train.py``.
+Tensors are torch CUDA tensors (torch is the device-memory and stream
+plumbing here; every computation runs in libbsml_b200.so).
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+
+MATH = {"fp32": 0, "tf32x3": 1, "bf16": 2}
+
+
+def _ptr(t):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _stream():
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def _f32(t):
+    if t is None:
+        return None
+    if not (t.is_cuda and t.dtype == torch.float32):
+        raise TypeError("brosoundml: expected a float32 CUDA tensor")
+    return t.contiguous()
+
+
+class Decoder:
+    # math modes smoke() exercises (the tensor-core modes join once built)
+    SMOKE_MATH = ("fp32",)
+    # math mode bench.py uses by default
+    DEFAULT_MATH = "fp32"
+
+    def __init__(self, cfg: dict, device: int = 0, math: str = "fp32"):
+        self.cfg = dict(cfg)
+        self._c = _lib.make_config(cfg)
+        L = _lib.lib()
+        h = ctypes.c_void_p()
+        _lib.check(L.bsml_decoder_create(ctypes.byref(self._c), int(device), ctypes.byref(h)))
+        self._h = h
+        self.device = torch.device("cuda", device)
+        n, ne, na, apc = ctypes.c_int64(), ctypes.c_int(), ctypes.c_int(), ctypes.c_int64()
+        _lib.check(L.bsml_decoder_param_count(h, ctypes.byref(n), ctypes.byref(ne), ctypes.byref(na), ctypes.byref(apc)))
+        self.n_params, self.n_affine, self.aff_per_clip = n.value, na.value, apc.value
+        arr = (_lib.BsmlParamEntry * ne.value)()
+        affc = (ctypes.c_int * na.value)()
+        rc = L.bsml_decoder_param_table(h, ctypes.cast(arr, ctypes.c_void_p), ne.value, ctypes.cast(affc, ctypes.c_void_p))
+        if rc < 0:
+            _lib.check(rc)
+        self.table = [dict(name=e.name.decode(), offset=e.offset, numel=e.numel, shape=tuple(e.shape[:e.ndim]),
+                           trainable=bool(e.trainable)) for e in arr]
+        self.aff_C = list(affc)
+        self.set_math(math)
+        self._last = None
+
+    def __del__(self):
+        h = getattr(self, "_h", None)
+        if h is not None and _lib._lib is not None:
+            _lib.lib().bsml_decoder_destroy(h)
+            self._h = None
+
+    def set_math(self, math: str) -> None:
+        _lib.check(_lib.lib().bsml_decoder_set_math(self._h, MATH[math]))
+        self.math = math
+
+    def audio_len(self, T: int, frames: int | None = None) -> int:
+        c = self.cfg
+        if frames is None:
+            frames = (2 * T * c["upsample_scale"]) // c["hop"] + 1
+        return c["hop"] * (frames - 1)
+
+    def workspace_bytes(self) -> int:
+        return int(_lib.lib().bsml_decoder_workspace_bytes(self._h))
+
+    def set_profiling(self, on: bool) -> None:
+        _lib.check(_lib.lib().bsml_decoder_set_profiling(self._h, 1 if on else 0))
+
+    PROFILE_CLASSES = ("conv", "wgrad", "norm_fwd", "norm_bwd")
+
+    def read_profile(self) -> dict:
+        """{class: (ms, algorithmic FLOPs or bytes, launches)} since the last read."""
+        buf = (ctypes.c_double * 12)()
+        _lib.check(_lib.lib().bsml_decoder_read_profile(self._h, ctypes.cast(buf, ctypes.c_void_p)))
+        return {k: (buf[3 * i], buf[3 * i + 1], int(buf[3 * i + 2])) for i, k in enumerate(self.PROFILE_CLASSES)}
+
+    def forward(self, params, asr, F0, N, style, har=None, aff_in=None, audio=None, aff_out=None):
+        params, asr, F0, N, style, har, aff_in = map(_f32, (params, asr, F0, N, style, har, aff_in))
+        B, _, T = asr.shape
+        frames = 0 if har is None else har.shape[2]
+        S = self.audio_len(T, frames if har is not None else None)
+        if audio is None:
+            audio = torch.empty((B, S), device=self.device, dtype=torch.float32)
+        self._last = (B, T)
+        # the engine borrows params until the matching backward (like the
+        # reference's borrowed weights): keep it alive here
+        self._borrowed = params
+        _lib.check(_lib.lib().bsml_decoder_forward(
+            self._h, B, T, _ptr(params), _ptr(asr), _ptr(F0), _ptr(N), _ptr(style), _ptr(har), frames,
+            _ptr(aff_in), _ptr(audio), _ptr(aff_out), _stream()))
+        return audio
+
+    def backward(self, daudio, grads=None, want_grads=True, want_inputs=True, want_aff=False):
+        B, T = self._last
+        daudio = _f32(daudio)
+        dev = self.device
+        if grads is None and want_grads:
+            grads = torch.empty(self.n_params, device=dev, dtype=torch.float32)
+        d_asr = torch.empty((B, self.cfg["asr_dim"], T), device=dev) if want_inputs else None
+        d_style = torch.empty((B, self.cfg["style_dim"]), device=dev) if want_inputs else None
+        d_aff = torch.empty(B * self.aff_per_clip, device=dev) if want_aff else None
+        _lib.check(_lib.lib().bsml_decoder_backward(self._h, _ptr(daudio), _ptr(grads), _ptr(d_asr),
+                                                   _ptr(d_style), _ptr(d_aff), _stream()))
+        return dict(grads=grads, d_asr=d_asr, d_style=d_style, d_aff=d_aff)
+
+
+def l1_loss(audio, target, loss=None, daudio=None):
+    audio, target = _f32(audio), _f32(target)
+    if loss is None:
+        loss = torch.empty(1, device=audio.device)
+    if daudio is None:
+        daudio = torch.empty_like(audio)
+    _lib.check(_lib.lib().bsml_loss_l1(_ptr(audio), _ptr(target), audio.numel(), _ptr(loss), _ptr(daudio), _stream()))
+    return loss, daudio
+
+
+def adam_step(param, grad, m, v, lr, step, beta1=0.9, beta2=0.999, eps=1e-8):
+    _lib.check(_lib.lib().bsml_adam_step(_ptr(param), _ptr(grad), _ptr(m), _ptr(v), param.numel(), lr, beta1, beta2,
+                                          eps, int(step), _stream()))

@@ -1,0 +1,187 @@
+/* bsml_decoder.h — C ABI of the B200-native Kokoro decoder training path.
+ *
+ * Drop-in boundary for the reference's decoder backward path
+ * (wlejon/brosoundml: src/kokoro_decoder_backward.h, include/brosoundml/decoder_lora.h).
+ * Every entry point takes plain device pointers and sizes; no C++ or torch type
+ * crosses it. All functions return 0 on success, a negative status on failure;
+ * bsml_last_error() gives the message ("brosoundml: <where>: <reason>", the
+ * reference's error format, src/kokoro_modules.cpp:90-92).
+ *
+ * Layouts follow the reference: activations NCL, element (b, c, l) at
+ * (b*C + c)*L + l (src/kokoro_decoder_backward.h:15-17, with a leading batch
+ * axis); conv weights (C_out, C_in, k) (include/brosoundml/modules.h:75);
+ * ConvTranspose1d weights (C_in, C_out, k) (include/brosoundml/kokoro_modules.h:321);
+ * AdaIN affines (gamma, beta) each (C) per clip (src/kokoro_decoder_backward.h:37-56).
+ * Streams are passed as void* (a cudaStream_t; NULL = legacy default stream).
+ */
+#ifndef BSML_DECODER_H
+#define BSML_DECODER_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Architecture. Field meanings follow DecoderBackbone::load_from
+ * (src/kokoro_modules.cpp:1021-1063), Generator::load_from (:1237-1347) and
+ * HarmonicSource::load_from (:1556-1572). */
+typedef struct bsml_decoder_config {
+    int asr_dim;          /* 512 */
+    int style_dim;        /* 128 */
+    int asr_res_dim;      /* 64 */
+    int enc_dim;          /* 1024 */
+    int n_decode;         /* 4 */
+    int dec_out[8];       /* 1024, 1024, 1024, 512 */
+    int upsample_block;   /* 3 */
+    int n_ups;            /* 2 */
+    int init_ch;          /* 512 */
+    int ups_rate[4];      /* 10, 6 */
+    int ups_kernel[4];    /* 20, 12 */
+    int noise_kernel[4];  /* 12, 1 */
+    int noise_stride[4];  /* 6, 1 */
+    int noise_pad[4];     /* 3, 0 */
+    int nr_kernel[4];     /* 7, 11 */
+    int nr_dil[4][3];     /* {1,3,5} */
+    int n_kernels;        /* 3 */
+    int rb_kernel[4];     /* 3, 7, 11 */
+    int rb_dil[4][3];     /* {1,3,5} */
+    int har_ch;           /* 22 */
+    int n_fft;            /* 20 */
+    int hop;              /* 5 */
+    int post_kernel;      /* 7 */
+    int harmonic_num;     /* 8 */
+    int sample_rate;      /* 24000 */
+    int upsample_scale;   /* 300 */
+} bsml_decoder_config;
+
+typedef struct bsml_param_entry {
+    char name[96];        /* upstream state-dict key below decoder.module. */
+    int64_t offset;       /* in floats, into the flat parameter / gradient buffer */
+    int64_t numel;
+    int ndim;
+    int shape[3];
+    int trainable;
+} bsml_param_entry;
+
+typedef struct bsml_decoder bsml_decoder;
+
+/* Arithmetic used for the conv / convT contractions. FP32_SIMT: fp32 CUDA-core
+ * kernels. TF32X3: tcgen05 tensor cores, each fp32 operand split hi+lo, three
+ * products (fp32-equivalent accuracy). BF16: tcgen05 with bf16 operands, fp32
+ * accumulation. Elementwise, normalisation and spectral work is fp32 in all modes. */
+enum { BSML_MATH_FP32_SIMT = 0, BSML_MATH_TF32X3 = 1, BSML_MATH_BF16 = 2 };
+
+const char* bsml_last_error(void);
+int bsml_version(void);
+
+/* ── whole-decoder engine ──────────────────────────────────────────────────
+ * Replaces DecoderLora::forward / ::backward (src/decoder_lora.cpp:211-296)
+ * and the assemblies they call (decoder_backbone_forward_train / _backward,
+ * generator_forward_train / _backward, src/kokoro_decoder_backward.h:213-293),
+ * batched over B clips. */
+int bsml_decoder_create(const bsml_decoder_config* cfg, int device, bsml_decoder** out);
+void bsml_decoder_destroy(bsml_decoder* d);
+int bsml_decoder_param_count(const bsml_decoder* d, int64_t* n_params, int* n_entries, int* n_affine,
+                             int64_t* aff_per_clip);
+/* aff_channels (optional) receives the channel count of each AdaIN, in
+ * DecoderLora::adapters() order (src/decoder_lora.cpp:173-179). */
+int bsml_decoder_param_table(const bsml_decoder* d, bsml_param_entry* out, int max_entries, int* aff_channels);
+int bsml_decoder_set_math(bsml_decoder* d, int math_mode);
+
+/* The same layout queries from a config alone (no device needed). */
+int bsml_config_param_count(const bsml_decoder_config* cfg, int64_t* n_params, int* n_entries, int* n_affine,
+                            int64_t* aff_per_clip);
+int bsml_config_param_table(const bsml_decoder_config* cfg, bsml_param_entry* out, int max_entries,
+                            int* aff_channels);
+
+/* Forward. params: flat (n_params). asr (B, asr_dim, T); F0, N (B, 2T);
+ * style (B, style_dim); har (B, har_ch, frames) or NULL to generate it from F0
+ * with the harmonic source (src/kokoro_modules.cpp:1574-1665). aff_in: NULL
+ * (gamma, beta) = fc(style) for every AdaIN) or packed per-AdaIN blocks
+ * [a][B][2*C_a] supplied by the caller (reference mode: the LoRA adapters sit
+ * outside, src/decoder_lora.cpp:184-194). audio (B, hop*(frames-1)).
+ * aff_out (optional) receives the resolved affines in the same packing.
+ * Caches every intermediate the matching backward needs (inputs are copied);
+ * params is borrowed: it must stay valid and unchanged until the matching
+ * backward has been enqueued, as the reference's weights must outlive its
+ * caches (include/brosoundml/decoder_lora.h:69-72). */
+int bsml_decoder_forward(bsml_decoder* d, int B, int T, const float* params, const float* asr, const float* F0,
+                         const float* N, const float* style, const float* har, int frames, const float* aff_in,
+                         float* audio, float* aff_out, void* stream);
+
+/* Backward of the last forward. daudio (B, S). grads (n_params) is
+ * OVERWRITTEN with d loss / d params (conv, convT, fc weights and biases,
+ * Snake alphas). d_asr (B, asr_dim, T), d_style (B, style_dim), d_aff
+ * (packed like aff_in) are optional outputs. In reference mode (aff_in given
+ * to the forward) fc gradients and d_style are zero: the affines are inputs. */
+int bsml_decoder_backward(bsml_decoder* d, const float* daudio, float* grads, float* d_asr, float* d_style,
+                          float* d_aff, void* stream);
+
+/* Bytes of device workspace the engine holds for the current (B, T). */
+int64_t bsml_decoder_workspace_bytes(const bsml_decoder* d);
+
+/* Optional per-kernel-class timing with CUDA events (no reference counterpart:
+ * instrumentation for the roofline report). Classes: 0 conv forward-like
+ * (fwd, dgrad, convT), 1 conv weight gradient, 2 AdaIN+Snake forward,
+ * 3 AdaIN+Snake backward. read_profile fills 12 doubles (per class: ms,
+ * algorithmic work in FLOPs (0-1) or bytes (2-3), launches), synchronises the
+ * device and clears the record. */
+int bsml_decoder_set_profiling(bsml_decoder* d, int on);
+/* Number of CUDA kernels this library has launched in the process so far. */
+int64_t bsml_launch_count(void);
+int bsml_decoder_read_profile(bsml_decoder* d, double* out12);
+
+/* ── loss and optimiser ─────────────────────────────────────────────────── */
+
+/* L1 loss: loss[0] = mean |audio - target|, daudio = sign(audio - target) / n. */
+int bsml_loss_l1(const float* audio, const float* target, int64_t n, float* loss, float* daudio, void* stream);
+
+/* Adam with bias correction, in place over n floats (bt::adam_step as used by
+ * DecoderLora::adam_step, src/decoder_lora.cpp:306-314). */
+int bsml_adam_step(float* param, const float* grad, float* m, float* v, int64_t n, float lr, float beta1,
+                   float beta2, float eps, int step, void* stream);
+
+/* ── atoms (the reference's detail:: functions, batched) ────────────────── */
+
+/* Conv1d forward (modules.cpp:103-108): x (B, Ci, L) -> y (B, Co, Lo). bias may be NULL. */
+int bsml_conv1d_forward(const float* x, int B, int Ci, int L, const float* W, const float* bias, int Co, int k,
+                        int stride, int pad, int dil, float* y, void* stream);
+/* conv1d_backward_input (kokoro_decoder_backward.cpp:230-234): dy (B, Co, Lo) -> dx (B, Ci, L). stride 1. */
+int bsml_conv1d_backward_input(const float* dy, int B, int Ci, int L, const float* W, int Co, int k, int stride,
+                               int pad, int dil, float* dx, void* stream);
+/* Weight / bias gradient (overwritten). db may be NULL. */
+int bsml_conv1d_backward_weight(const float* dy, const float* x, int B, int Ci, int L, int Co, int k, int stride,
+                                int pad, int dil, float* dW, float* db, void* stream);
+/* ConvTranspose1d, groups 1, output_padding 0 (kokoro_decoder_backward.cpp:627-629): W (Ci, Co, k). */
+int bsml_conv_transpose1d_forward(const float* x, int B, int Ci, int L, const float* W, const float* bias, int Co,
+                                  int k, int stride, int pad, float* y, void* stream);
+int bsml_conv_transpose1d_backward_input(const float* dy, int B, int Ci, int L, const float* W, int Co, int k,
+                                         int stride, int pad, float* dx, void* stream);
+int bsml_conv_transpose1d_backward_weight(const float* dy, const float* x, int B, int Ci, int L, int Co, int k,
+                                          int stride, int pad, float* dW, float* db, void* stream);
+
+/* adain_affine_forward / _backward (kokoro_decoder_backward.h:37-56), batched:
+ * x (B, C, L), gb (B, 2C) = (gamma ; beta) per clip. dgb overwritten. */
+int bsml_adain_affine_forward(const float* x, const float* gb, int B, int C, int L, float eps, float* y,
+                              void* stream);
+int bsml_adain_affine_backward(const float* x, const float* gb, const float* dy, int B, int C, int L, float eps,
+                               float* dx, float* dgb, void* stream);
+/* Snake1D (kokoro_modules.h:253) and its backward with the alpha gradient (overwritten). */
+int bsml_snake_forward(const float* x, const float* alpha, int B, int C, int L, float* y, void* stream);
+int bsml_snake_backward(const float* x, const float* alpha, const float* dy, int B, int C, int L, float* dx,
+                        float* dalpha, void* stream);
+/* iSTFT (center, periodic Hann n_fft, length hop*(L-1)) and its adjoint; re/im (B, n_fft/2+1, L). */
+int bsml_istft_forward(const float* re, const float* im, int B, int n_fft, int hop, int L, float* audio,
+                       void* stream);
+int bsml_istft_backward(const float* daudio, int B, int n_fft, int hop, int L, float* dre, float* dim,
+                        void* stream);
+/* HarmonicSource::forward (kokoro_modules.cpp:1574-1665): F0 (B, F) -> har (B, n_fft+2, F*scale/hop+1). */
+int bsml_harmonic_source(const bsml_decoder_config* cfg, const float* F0, int B, int F, const float* l_weight,
+                         const float* l_bias, float* har, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* BSML_DECODER_H */
