@@ -79,6 +79,7 @@ SIGNATURES = {
     "bsml_conv1d_forward": ([_P, _I, _I, _I, _P, _P, _I, _I, _I, _I, _I, _P, _P], _I),
     "bsml_conv1d_backward_input": ([_P, _I, _I, _I, _P, _I, _I, _I, _I, _I, _P, _P], _I),
     "bsml_conv1d_backward_weight": ([_P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _P, _P, _P], _I),
+    "bsml_conv1d_backward_weight_noalloc": ([_P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _P, _P, _P], _I),
     "bsml_conv_transpose1d_forward": ([_P, _I, _I, _I, _P, _P, _I, _I, _I, _I, _P, _P], _I),
     "bsml_conv_transpose1d_backward_input": ([_P, _I, _I, _I, _P, _I, _I, _I, _I, _P, _P], _I),
     "bsml_conv_transpose1d_backward_weight": ([_P, _P, _I, _I, _I, _I, _I, _I, _I, _P, _P, _P], _I),

@@ -66,6 +66,8 @@ int conv_out(int L, int k, int s, int p, int d) { return (L + 2 * p - d * (k - 1
 
 }  // namespace
 
+void bsml::set_last_error(const std::string& msg) { g_err = msg; }
+
 struct bsml_decoder {
     std::unique_ptr<bsml::Engine> eng;
 };

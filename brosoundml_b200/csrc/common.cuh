@@ -26,6 +26,9 @@ inline void check_cuda(cudaError_t e, const char* where) {
 #define BSML_CUDA(call) ::bsml::check_cuda((call), #call)
 #define BSML_LAUNCH(where) ::bsml::check_cuda(cudaGetLastError(), where)
 
+// Message returned by bsml_last_error() on this thread.
+void set_last_error(const std::string& msg);
+
 // Kernel launches issued by this library (every launch site counts itself).
 void count_launch();
 int64_t launch_count();

@@ -2,6 +2,8 @@
 // BSML_MATH_FP32_SIMT mode and, in the tensor-core modes, for the shapes the
 // tcgen05 kernels do not take (tiny channel counts: F0/N convs, conv_post,
 // noise_convs, asr_res).
+#include <algorithm>
+
 #include "kernels.h"
 
 namespace bsml {
@@ -334,6 +336,44 @@ void pack_convT_dgrad(const float* W, int Ci, int Co, int k, float* wp, cudaStre
     ::bsml::count_launch();
     pack_convT_dgrad_kernel<<<grid_for((int64_t)k * Co * Cip), 256, 0, st>>>(W, Ci, Co, k, Cip, wp);
     BSML_LAUNCH("pack_convT_dgrad");
+}
+
+}  // namespace bsml
+
+namespace bsml {
+
+bool conv_wgrad_simt_capped(const ConvWgrad& c, float* part, int64_t part_cap, cudaStream_t st) {
+    const int64_t rows = (int64_t)c.dy.B * c.dy.L;
+    const int64_t wsize = (int64_t)c.dy.C * c.x.C * c.k;
+    int64_t sp = std::min<int64_t>(wgrad_splits(rows, wsize), part_cap / std::max<int64_t>(wsize, 1));
+    int64_t sp_b = c.db ? std::min<int64_t>(wgrad_splits(rows, c.dy.C), part_cap / std::max(c.dy.C, 1)) : 1;
+    if (sp < 1 || sp_b < 1) return false;
+    WgK a;
+    a.dy = c.dy.p; a.dy_bs = c.dy.bstride; a.dy_ld = c.dy.ld; a.Lo = c.dy.L; a.Co = c.dy.C;
+    a.x = c.x.p; a.x_bs = c.x.bstride; a.x_ld = c.x.ld; a.L_in = c.x.L; a.Ci = c.x.C;
+    a.k = c.k; a.s = c.s; a.p = c.p; a.d = c.d; a.B = c.dy.B;
+    a.rows_total = rows;
+    a.rows_per_split = (int)ceil_div(rows, sp);
+    sp = ceil_div(rows, a.rows_per_split);
+    a.part = part;
+    dim3 grid((unsigned)ceil_div(a.Co, TC), (unsigned)(ceil_div(a.Ci, TC) * c.k), (unsigned)sp);
+    ::bsml::count_launch();
+    conv_wgrad_kernel<<<grid, 256, 0, st>>>(a);
+    BSML_LAUNCH("conv_wgrad_simt_capped");
+    ::bsml::count_launch();
+    reduce_splits_kernel<<<grid_for(wsize), 256, 0, st>>>(part, (int)sp, wsize, c.dW, c.accum ? 1 : 0);
+    BSML_LAUNCH("reduce_splits");
+    if (c.db) {
+        const int rps = (int)ceil_div(rows, sp_b);
+        sp_b = ceil_div(rows, rps);
+        dim3 g2((unsigned)ceil_div(c.dy.C, 128), (unsigned)sp_b);
+        ::bsml::count_launch();
+        colsum_kernel<<<g2, 128, 0, st>>>(c.dy.p, c.dy.bstride, c.dy.ld, c.dy.L, c.dy.C, c.dy.B, rps, part);
+        ::bsml::count_launch();
+        reduce_splits_kernel<<<grid_for(c.dy.C), 256, 0, st>>>(part, (int)sp_b, c.dy.C, c.db, c.accum ? 1 : 0);
+        BSML_LAUNCH("colsum_capped");
+    }
+    return true;
 }
 
 }  // namespace bsml

@@ -122,3 +122,10 @@ void adam(float* p, const float* g, float* m, float* v, int64_t n, float lr, flo
           cudaStream_t st);
 
 }  // namespace bsml
+
+namespace bsml {
+// Weight gradient with the split-K partials bounded by `part_cap` floats (fewer
+// splits when the cap is small); the bias column sums use the same bound.
+// Returns false, launching nothing, when even one split does not fit.
+bool conv_wgrad_simt_capped(const ConvWgrad& a, float* part, int64_t part_cap, cudaStream_t st);
+}  // namespace bsml

@@ -153,6 +153,23 @@ int bsml_conv1d_backward_input(const float* dy, int B, int Ci, int L, const floa
 /* Weight / bias gradient (overwritten). db may be NULL. */
 int bsml_conv1d_backward_weight(const float* dy, const float* x, int B, int Ci, int L, int Co, int k, int stride,
                                 int pad, int dil, float* dW, float* db, void* stream);
+/* Conv1d weight / bias gradient that allocates nothing. No counterpart in the
+ * reference: it is for callers that may not call cudaMalloc while computing
+ * gradients (a real-time audio thread that must not block on the driver's
+ * allocator, or an application whose device memory is all reserved up front by
+ * its own arena). Same arguments and results as bsml_conv1d_backward_weight, but
+ * its scratch (channels-last copies of dy and x, split-K partial sums) lives in
+ * one static device array of BSML_NOALLOC_SCRATCH_FLOATS floats (16 MiB) that
+ * every GPU loading this library holds until exit. A problem whose scratch
+ * (B*Lo*round_up(Co,4) + B*L*round_up(Ci,4) + Co*Ci*k floats, roughly) exceeds
+ * it is rejected with an error. The first call on each device looks the array's
+ * device address up (cudaGetSymbolAddress): make that first call before any
+ * stream capture. All calls share the array, so calls that overlap on the GPU
+ * (other streams, other threads) race; serialise them on one stream. */
+#define BSML_NOALLOC_SCRATCH_FLOATS (4ll * 1024 * 1024)
+int bsml_conv1d_backward_weight_noalloc(const float* dy, const float* x, int B, int Ci, int L, int Co, int k,
+                                        int stride, int pad, int dil, float* dW, float* db, void* stream);
+
 /* ConvTranspose1d, groups 1, output_padding 0 (kokoro_decoder_backward.cpp:627-629): W (Ci, Co, k). */
 int bsml_conv_transpose1d_forward(const float* x, int B, int Ci, int L, const float* W, const float* bias, int Co,
                                   int k, int stride, int pad, float* y, void* stream);
