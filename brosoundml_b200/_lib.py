@@ -73,6 +73,8 @@ SIGNATURES = {
     "bsml_decoder_workspace_bytes": ([_P], _L),
     "bsml_decoder_set_profiling": ([_P, _I], _I),
     "bsml_launch_count": ([], _L),
+    "bsml_set_atom_math": ([_I], _I),
+    "bsml_device_error": ([], _I),
     "bsml_decoder_read_profile": ([_P, _P], _I),
     "bsml_loss_l1": ([_P, _P, _L, _P, _P, _P], _I),
     "bsml_adam_step": ([_P, _P, _P, _P, _L, _F, _F, _F, _F, _I, _P], _I),

@@ -4,7 +4,10 @@
 #include <memory>
 #include <string>
 
+#include <atomic>
+
 #include "bsml_decoder.h"
+#include "conv_tc.h"
 #include "engine.h"
 #include "kernels.h"
 
@@ -63,6 +66,32 @@ void need(bool ok, const char* where, const char* why) {
 }
 
 int conv_out(int L, int k, int s, int p, int d) { return (L + 2 * p - d * (k - 1) - 1) / s + 1; }
+
+std::atomic<int> g_atom_math{BSML_MATH_FP32_SIMT};
+
+bool atom_tc(int K, int M, int s) { return g_atom_math.load() != BSML_MATH_FP32_SIMT && s == 1 && K >= 32 && M >= 64; }
+int atom_tc_mode() { return g_atom_math.load() == BSML_MATH_BF16 ? bsml::TC_BF16 : bsml::TC_TF32X3; }
+
+// Tensor-core forward-like conv for the atoms: planes of x, packed weight planes, launch.
+void atom_tc_conv(Scratch& sc, const bsml::Act& xa, const float* W, int kind, int Co_w, int Ci_w, int k, int s_ph,
+                  int r_ph, int taps, int M, const bsml::Act& ya, const float* bias, int p, int d, int No, int o_base,
+                  int orow_mul, int orow_off, cudaStream_t st) {
+    const int mode = atom_tc_mode();
+    float* xh = sc.f((int64_t)xa.B * xa.L * bsml::tc_pitch(xa.C, mode));
+    float* xl = sc.f((int64_t)xa.B * xa.L * bsml::tc_pitch(xa.C, mode));
+    const int64_t wn = (int64_t)taps * M * bsml::round_up(xa.C, 8);
+    float* wh = sc.f(wn);
+    float* wl = sc.f(wn);
+    bsml::make_act_planes(xa, mode, xh, xl, st);
+    bsml::pack_w_tc(W, kind, Co_w, Ci_w, k, s_ph, r_ph, mode, wh, wl, st);
+    bsml::TcConvFwd a;
+    a.x.hi = xh; a.x.lo = xl; a.x.ld = bsml::tc_pitch(xa.C, mode);
+    a.B = xa.B; a.L_in = xa.L; a.Ci = xa.C;
+    a.w.hi = wh; a.w.lo = wl; a.w.ld = (int)bsml::round_up(xa.C, 8);
+    a.taps = taps; a.Co = M; a.p = p; a.d = d; a.No = No; a.o_base = o_base;
+    a.y = ya; a.bias = bias; a.orow_mul = orow_mul; a.orow_off = orow_off;
+    bsml::conv_fwd_tc(a, mode, st);
+}
 
 }  // namespace
 
@@ -172,6 +201,20 @@ int64_t bsml_decoder_workspace_bytes(const bsml_decoder* d) { return d ? d->eng-
 
 int64_t bsml_launch_count(void) { return bsml::launch_count(); }
 
+int bsml_set_atom_math(int math_mode) {
+    return guarded([&] {
+        need(math_mode == BSML_MATH_FP32_SIMT || math_mode == BSML_MATH_TF32X3 || math_mode == BSML_MATH_BF16,
+             "bsml_set_atom_math", "unknown math mode");
+        g_atom_math.store(math_mode);
+    });
+}
+
+int bsml_device_error(void) {
+    int v = 0;
+    const int rc = guarded([&] { v = bsml::tc_error_flag(); });
+    return rc ? rc : v;
+}
+
 int bsml_decoder_set_profiling(bsml_decoder* d, int on) {
     return guarded([&] {
         need(d != nullptr, "bsml_decoder_set_profiling", "null handle");
@@ -212,12 +255,16 @@ int bsml_conv1d_forward(const float* x, int B, int Ci, int L, const float* W, co
         cudaStream_t st = S(stream);
         Scratch sc(st);
         bsml::Act xa = sc.act(B, L, Ci), ya = sc.act(B, Lo, Co);
-        float* wp = sc.f((int64_t)k * Ci * bsml::round_up(Co, 4));
         bsml::ncl_to_cl(x, xa, st);
-        bsml::pack_conv_fwd(W, Co, Ci, k, wp, st);
-        bsml::ConvFwd a;
-        a.x = xa; a.y = ya; a.wp = wp; a.bias = bias; a.k = k; a.s = stride; a.p = pad; a.d = dil; a.No = Lo;
-        bsml::conv_fwd_simt(a, st);
+        if (atom_tc(Ci, Co, stride)) {
+            atom_tc_conv(sc, xa, W, bsml::PACK_CONV_FWD, Co, Ci, k, 1, 0, k, Co, ya, bias, pad, dil, Lo, 0, 1, 0, st);
+        } else {
+            float* wp = sc.f((int64_t)k * Ci * bsml::round_up(Co, 4));
+            bsml::pack_conv_fwd(W, Co, Ci, k, wp, st);
+            bsml::ConvFwd a;
+            a.x = xa; a.y = ya; a.wp = wp; a.bias = bias; a.k = k; a.s = stride; a.p = pad; a.d = dil; a.No = Lo;
+            bsml::conv_fwd_simt(a, st);
+        }
         bsml::cl_to_ncl(ya, y, st);
     });
 }
@@ -231,12 +278,17 @@ int bsml_conv1d_backward_input(const float* dy, int B, int Ci, int L, const floa
         cudaStream_t st = S(stream);
         Scratch sc(st);
         bsml::Act ga = sc.act(B, Lo, Co), xa = sc.act(B, L, Ci);
-        float* wp = sc.f((int64_t)k * Co * bsml::round_up(Ci, 4));
         bsml::ncl_to_cl(dy, ga, st);
-        bsml::pack_conv_dgrad(W, Co, Ci, k, wp, st);
-        bsml::ConvFwd a;
-        a.x = ga; a.y = xa; a.wp = wp; a.k = k; a.s = 1; a.p = dil * (k - 1) - pad; a.d = dil; a.No = L;
-        bsml::conv_fwd_simt(a, st);
+        if (atom_tc(Co, Ci, 1)) {
+            atom_tc_conv(sc, ga, W, bsml::PACK_CONV_DGRAD, Co, Ci, k, 1, 0, k, Ci, xa, nullptr, dil * (k - 1) - pad, dil,
+                         L, 0, 1, 0, st);
+        } else {
+            float* wp = sc.f((int64_t)k * Co * bsml::round_up(Ci, 4));
+            bsml::pack_conv_dgrad(W, Co, Ci, k, wp, st);
+            bsml::ConvFwd a;
+            a.x = ga; a.y = xa; a.wp = wp; a.k = k; a.s = 1; a.p = dil * (k - 1) - pad; a.d = dil; a.No = L;
+            bsml::conv_fwd_simt(a, st);
+        }
         bsml::cl_to_ncl(xa, dx, st);
     });
 }
@@ -251,6 +303,25 @@ int bsml_conv1d_backward_weight(const float* dy, const float* x, int B, int Ci, 
         bsml::Act ga = sc.act(B, Lo, Co), xa = sc.act(B, L, Ci);
         bsml::ncl_to_cl(dy, ga, st);
         bsml::ncl_to_cl(x, xa, st);
+        if (atom_tc(Ci, Co, stride)) {
+            const int mode = atom_tc_mode();
+            float* yh = sc.f((int64_t)B * Lo * bsml::tc_pitch(Co, mode));
+            float* yl = sc.f((int64_t)B * Lo * bsml::tc_pitch(Co, mode));
+            float* xh = sc.f((int64_t)B * L * bsml::tc_pitch(Ci, mode));
+            float* xl = sc.f((int64_t)B * L * bsml::tc_pitch(Ci, mode));
+            bsml::make_act_planes(ga, mode, yh, yl, st);
+            bsml::make_act_planes(xa, mode, xh, xl, st);
+            bsml::TcConvWgrad w;
+            w.dy.hi = yh; w.dy.lo = yl; w.dy.ld = bsml::tc_pitch(Co, mode);
+            w.x.hi = xh; w.x.lo = xl; w.x.ld = bsml::tc_pitch(Ci, mode);
+            w.B = B; w.Lo = Lo; w.Co = Co; w.L_in = L; w.Ci = Ci; w.taps = k; w.p = pad; w.d = dil; w.dW = dW;
+            const int64_t cap = std::max<int64_t>(std::min<int64_t>(48ll << 20, 296ll * Co * Ci * k),
+                                                  bsml::colsum_partial_floats(ga));
+            float* part = sc.f(cap);
+            bsml::conv_wgrad_tc(w, mode, part, cap, st);
+            if (db) bsml::colsum(ga, db, false, part, st);
+            return;
+        }
         bsml::ConvWgrad a;
         a.dy = ga; a.x = xa; a.k = k; a.s = stride; a.p = pad; a.d = dil; a.dW = dW; a.db = db;
         float* part = sc.f(std::max(bsml::wgrad_partial_floats(a), bsml::colsum_partial_floats(ga)));
@@ -273,6 +344,11 @@ int bsml_conv_transpose1d_forward(const float* x, int B, int Ci, int L, const fl
             const int qmin = (int)bsml::ceil_div(std::max(pad - ph, 0), stride);
             const int qmax = (Lu - 1 + pad - ph) >= 0 ? (Lu - 1 + pad - ph) / stride : -1;
             if (qmax < qmin) continue;
+            if (atom_tc(Ci, Co, 1)) {
+                atom_tc_conv(sc, xa, W, bsml::PACK_CONVT_PHASE, Co, Ci, k, stride, ph, kr, Co, ya, bias, kr - 1, 1,
+                             qmax - qmin + 1, qmin, stride, ph - pad, st);
+                continue;
+            }
             float* wp = sc.f((int64_t)kr * Ci * bsml::round_up(Co, 4));
             bsml::pack_convT_phase(W, Ci, Co, k, stride, ph, wp, st);
             bsml::ConvFwd a;

@@ -1,0 +1,526 @@
+// tcgen05 implicit-GEMM convolution kernels (sm_100a).
+//
+// Forward-like form (conv fwd, conv input gradient with flipped/transposed
+// weights, ConvTranspose1d stride phases):
+//   D[co, o] = sum_{t, ci} W_t[co, ci] * X[b, (o + o_base) + t*d - p, ci]
+// K runs over (tap, 128-byte chunk of input channels); both operands are
+// K-major (channels contiguous), so one TMA box per operand plane per K step,
+// and a tap shift only moves the activation box's row coordinate.
+//
+// Weight-gradient form (stride-1 convs):
+//   D[co, ci] (tap t) = sum_{b, o} dY[b, o, co] * X[b, o + t*d - p, ci]
+// K runs over chunks of positions; both operands are MN-major (positions are
+// rows, channels contiguous), staged as 128-byte-wide column blocks. Split-K
+// over position chunks writes fp32 partial tiles, reduced in double afterwards.
+//
+// One CTA computes a 128 x 128 fp32 tile in TMEM (M = output channels on the
+// TMEM lanes). Warp roles (192 threads): warp 0 issues TMA, warp 1 owns TMEM
+// and one thread issues tcgen05.mma, warps 2-5 read the accumulator (each warp
+// its 32-lane quarter) and run the epilogue.
+//
+// Promotion (TF32x3): the tensor core's in-TMEM fp32 accumulation is not
+// round-to-nearest, and its error grows with K. With PROMOTE the MMA warp
+// alternates between two TMEM accumulators, one K step each, and the epilogue
+// warps fold every finished partial into fp32 registers, so each TMEM sum spans
+// only 12 instructions and the long sum is formed with ordinary fp32 adds.
+#include <cuda_bf16.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <mutex>
+
+#include "conv_tc.h"
+#include "tc_ptx.cuh"
+
+namespace bsml {
+
+namespace {
+
+__device__ int g_tc_err = 0;
+
+constexpr int BM = 128, BN = 128, TILE_BYTES = 16384;
+
+template <bool TF32>
+struct Cfg {
+    static constexpr int S = TF32 ? 3 : 6;            // pipeline stages
+    static constexpr int TILES = TF32 ? 4 : 2;        // A_hi, A_lo, B_hi, B_lo | A, B
+    static constexpr int BKE = TF32 ? 32 : 64;        // elements per 128-byte row
+    static constexpr int STAGE_BYTES = TILES * TILE_BYTES;
+    static constexpr int SMEM = S * STAGE_BYTES + 1024 + 256;
+    // weight-grad: positions (K rows) per stage; one MMA consumes 32 bytes of K
+    // = 8 (tf32) or 16 (bf16) rows; 128-byte column blocks per 128-wide operand
+    static constexpr int KROWS = TF32 ? 32 : 64;
+    static constexpr int MN_BLOCKS = 128 / BKE;
+};
+
+struct Args {
+    // forward-like
+    int No, o_base, p, d, taps, kchunks, Co;
+    float* y; int64_t y_bs; int y_ld; int orow_mul, orow_off, y_rows;
+    const float* bias;
+    const float* r; int64_t r_bs; int r_ld; int r_shift;
+    float alpha; int accum;
+    // weight-grad: Ci tiles, chunks per clip, total chunks, chunks per split, Ci
+    int n_ci_tiles, chunks_pc, chunks_total, chunks_per_split, Ci;
+    float* part;   // [split][tap][Co][Ci]
+};
+
+template <bool TF32, bool PROMOTE, bool WGRAD>
+__global__ void __launch_bounds__(192, 1)
+    conv_tc_kernel(const __grid_constant__ CUtensorMap mAh, const __grid_constant__ CUtensorMap mAl,
+                   const __grid_constant__ CUtensorMap mBh, const __grid_constant__ CUtensorMap mBl, const Args a) {
+    using C = Cfg<TF32>;
+    constexpr uint32_t TCOLS = PROMOTE ? 2 * BN : BN;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::S * C::STAGE_BYTES);
+    uint64_t* empty = full + C::S;
+    uint64_t* accf = empty + C::S;   // [2]
+    uint64_t* acce = accf + 2;       // [2]
+    uint32_t* tslot = reinterpret_cast<uint32_t*>(acce + 2);
+    int* err = &g_tc_err;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    int m0, n0, b = 0, t = 0, it0 = 0, n_iters;
+    if constexpr (WGRAD) {
+        m0 = blockIdx.x * BM;                              // co
+        t = blockIdx.y / a.n_ci_tiles;
+        n0 = (blockIdx.y - t * a.n_ci_tiles) * BN;         // ci
+        it0 = blockIdx.z * a.chunks_per_split;
+        const int it1 = min(a.chunks_total, it0 + a.chunks_per_split);
+        n_iters = it1 > it0 ? it1 - it0 : 0;
+    } else {
+        n0 = blockIdx.x * BN;                              // positions
+        m0 = blockIdx.y * BM;                              // co
+        b = blockIdx.z;
+        n_iters = a.taps * a.kchunks;
+    }
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < C::S; ++s) {
+            tc::mbar_init(&full[s], 1);
+            tc::mbar_init(&empty[s], 1);
+        }
+        tc::mbar_init(&accf[0], 1);
+        tc::mbar_init(&accf[1], 1);
+        tc::mbar_init(&acce[0], 4);
+        tc::mbar_init(&acce[1], 4);
+        tc::fence_barrier_init();
+        tc::prefetch_tmap(&mAh);
+        tc::prefetch_tmap(&mBh);
+        if (TF32) {
+            tc::prefetch_tmap(&mAl);
+            tc::prefetch_tmap(&mBl);
+        }
+    }
+    if (warp == 1) {
+        tc::tmem_alloc(tslot, TCOLS);
+        tc::tmem_relinquish();
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+    const uint32_t tbase = *tslot;
+
+    if (warp == 0 && lane == 0) {
+        // ── TMA producer
+        int issued = 0;
+        bool ok = true;
+        for (int it = 0; it < n_iters; ++it) {
+            const int s = it % C::S;
+            const uint32_t ph = (it / C::S) & 1;
+            if (!tc::mbar_wait(&empty[s], ph ^ 1, err, tc::TC_ERR_WAIT_EMPTY)) { ok = false; break; }
+            uint8_t* st = smem + s * C::STAGE_BYTES;
+            uint8_t* sB = st + (TF32 ? 2 : 1) * TILE_BYTES;
+            tc::mbar_arrive_expect_tx(&full[s], C::STAGE_BYTES);
+            if constexpr (WGRAD) {
+                const int q = it0 + it;
+                const int bb = q / a.chunks_pc;
+                const int orow = (q - bb * a.chunks_pc) * C::KROWS;
+                const int xrow = orow + t * a.d - a.p;
+#pragma unroll
+                for (int j = 0; j < C::MN_BLOCKS; ++j) {
+                    const int boff = j * C::KROWS * 128;
+                    tc::tma_load_3d(st + boff, &mAh, &full[s], m0 + j * C::BKE, orow, bb);
+                    tc::tma_load_3d(sB + boff, &mBh, &full[s], n0 + j * C::BKE, xrow, bb);
+                    if (TF32) {
+                        tc::tma_load_3d(st + TILE_BYTES + boff, &mAl, &full[s], m0 + j * C::BKE, orow, bb);
+                        tc::tma_load_3d(sB + TILE_BYTES + boff, &mBl, &full[s], n0 + j * C::BKE, xrow, bb);
+                    }
+                }
+            } else {
+                const int tt = it / a.kchunks, c = it - tt * a.kchunks;
+                const int kx = c * C::BKE;
+                const int brow = n0 + a.o_base + tt * a.d - a.p;
+                tc::tma_load_3d(st, &mAh, &full[s], kx, m0, tt);
+                tc::tma_load_3d(sB, &mBh, &full[s], kx, brow, b);
+                if (TF32) {
+                    tc::tma_load_3d(st + TILE_BYTES, &mAl, &full[s], kx, m0, tt);
+                    tc::tma_load_3d(sB + TILE_BYTES, &mBl, &full[s], kx, brow, b);
+                }
+            }
+            issued = it + 1;
+        }
+        if (!ok) {   // drain: the last S issued stages may still have copies in flight
+            for (int it = issued - C::S < 0 ? 0 : issued - C::S; it < issued; ++it)
+                tc::mbar_wait(&full[it % C::S], (it / C::S) & 1, nullptr, tc::TC_ERR_DRAIN);
+        }
+    } else if (warp == 1 && lane == 0) {
+        // ── MMA issuer
+        constexpr uint32_t idesc = tc::make_idesc(TF32 ? 2u : 1u, WGRAD ? 1u : 0u, WGRAD ? 1u : 0u, BM, BN);
+        for (int it = 0; it < n_iters; ++it) {
+            const int s = it % C::S;
+            const uint32_t ph = (it / C::S) & 1;
+            const int buf = PROMOTE ? (it & 1) : 0;
+            if (PROMOTE && it >= 2 && !tc::mbar_wait(&acce[buf], ((it >> 1) - 1) & 1, err, tc::TC_ERR_WAIT_ACC))
+                break;
+            if (!tc::mbar_wait(&full[s], ph, err, tc::TC_ERR_WAIT_FULL)) break;
+            tc::tc_fence_after();
+            const uint32_t base = tc::smem_u32(smem + s * C::STAGE_BYTES);
+            const uint32_t aH = base, aL = base + TILE_BYTES;
+            const uint32_t bH = base + (TF32 ? 2 : 1) * TILE_BYTES, bL = bH + TILE_BYTES;
+            const uint32_t d_tmem = tbase + (uint32_t)(buf * BN);
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+                // K-major: +32 bytes along the 128-byte row. MN-major: +32 bytes of K
+                // = 8 rows (tf32) or 16 rows (bf16) = 1024 / 2048 B; LBO = column-block stride
+                uint64_t dAh, dAl, dBh, dBl;
+                if constexpr (WGRAD) {
+                    const uint32_t off = kk * (TF32 ? 1024 : 2048);
+                    const uint32_t lbo = C::KROWS * 128;
+                    dAh = tc::desc_mnmajor(aH + off, lbo, TF32);
+                    dBh = tc::desc_mnmajor(bH + off, lbo, TF32);
+                    dAl = tc::desc_mnmajor(aL + off, lbo, TF32);
+                    dBl = tc::desc_mnmajor(bL + off, lbo, TF32);
+                } else {
+                    const uint32_t off = kk * 32;
+                    dAh = tc::desc_kmajor_sw128(aH + off);
+                    dBh = tc::desc_kmajor_sw128(bH + off);
+                    dAl = tc::desc_kmajor_sw128(aL + off);
+                    dBl = tc::desc_kmajor_sw128(bL + off);
+                }
+                const uint32_t acc = PROMOTE ? (kk > 0 ? 1u : 0u) : ((it > 0 || kk > 0) ? 1u : 0u);
+                tc::umma<TF32>(d_tmem, dAh, dBh, idesc, acc);
+                if (TF32) {
+                    tc::umma<TF32>(d_tmem, dAh, dBl, idesc, 1u);
+                    tc::umma<TF32>(d_tmem, dAl, dBh, idesc, 1u);
+                }
+            }
+            tc::umma_commit(&empty[s]);           // frees the stage once these MMAs have read it
+            if (PROMOTE) tc::umma_commit(&accf[buf]);
+        }
+        if (!PROMOTE) tc::umma_commit(&accf[0]);
+    } else if (warp >= 2) {
+        // ── epilogue
+        const int q = warp & 3;
+        const int mrow = m0 + q * 32 + lane;   // co
+        const uint32_t trow = tbase + ((uint32_t)(q * 32) << 16);
+        float R[BN];
+#pragma unroll
+        for (int j = 0; j < BN; ++j) R[j] = 0.f;
+        bool ok = true;
+        if (PROMOTE) {
+            for (int it = 0; it < n_iters; ++it) {
+                const int buf = it & 1;
+                bool w = true;
+                if (lane == 0) w = tc::mbar_wait(&accf[buf], (it >> 1) & 1, err, tc::TC_ERR_WAIT_ACC);
+                ok = __shfl_sync(0xffffffffu, w ? 1 : 0, 0) != 0;
+                if (!ok) break;
+                tc::tc_fence_after();
+#pragma unroll
+                for (int c0 = 0; c0 < BN; c0 += 16) {
+                    float v[16];
+                    tc::tmem_ld16(trow + buf * BN + c0, v);
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) R[c0 + j] += v[j];
+                }
+                tc::tc_fence_before();
+                __syncwarp();
+                if (lane == 0) tc::mbar_arrive(&acce[buf]);
+            }
+        } else if (n_iters > 0) {
+            bool w = true;
+            if (lane == 0) w = tc::mbar_wait(&accf[0], 0, err, tc::TC_ERR_WAIT_ACC);
+            ok = __shfl_sync(0xffffffffu, w ? 1 : 0, 0) != 0;
+            tc::tc_fence_after();
+            if (ok) {
+#pragma unroll
+                for (int c0 = 0; c0 < BN; c0 += 16) {
+                    float v[16];
+                    tc::tmem_ld16(trow + c0, v);
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) R[c0 + j] = v[j];
+                }
+            }
+        }
+        const bool valid = ok && *(volatile int*)err == tc::TC_OK;
+        if constexpr (WGRAD) {
+            if (valid && mrow < a.Co) {
+                float* pp = a.part + (((int64_t)blockIdx.z * a.taps + t) * a.Co + mrow) * (int64_t)a.Ci;
+#pragma unroll
+                for (int j = 0; j < BN; ++j)
+                    if (n0 + j < a.Ci) pp[n0 + j] = R[j];
+            }
+        } else {
+            if (valid && mrow < a.Co) {
+                const float bv = a.bias ? a.bias[mrow] : 0.f;
+#pragma unroll
+                for (int j = 0; j < BN; ++j) {
+                    const int o = n0 + j;
+                    if (o >= a.No) break;
+                    const int row = (o + a.o_base) * a.orow_mul + a.orow_off;
+                    if (row < 0 || row >= a.y_rows) continue;
+                    float val = R[j] + bv;
+                    if (a.r) val += a.r[(int64_t)b * a.r_bs + (int64_t)(row >> a.r_shift) * a.r_ld + mrow];
+                    val *= a.alpha;
+                    float* yp = a.y + (int64_t)b * a.y_bs + (int64_t)row * a.y_ld + mrow;
+                    if (a.accum) val += *yp;
+                    *yp = val;
+                }
+            }
+        }
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        __syncwarp();
+        tc::tc_fence_after();
+        tc::tmem_dealloc(tbase, TCOLS);
+    }
+}
+
+// ── operand planes
+__device__ __forceinline__ float tf32_rna(float x) {
+    uint32_t r;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+    return __uint_as_float(r);
+}
+
+template <bool TF32>
+__global__ void act_planes_kernel(Act x, void* hi, void* lo, int ld) {
+    const int64_t n = x.numel();
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const int c = (int)(i % x.C);
+        const int64_t r = i / x.C;
+        const int l = (int)(r % x.L), b = (int)(r / x.L);
+        const float v = x.row(b, l)[c];
+        const int64_t o = ((int64_t)b * x.L + l) * ld + c;
+        if (TF32) {
+            const float h = tf32_rna(v);
+            static_cast<float*>(hi)[o] = h;
+            static_cast<float*>(lo)[o] = v - h;
+        } else {
+            static_cast<__nv_bfloat16*>(hi)[o] = __float2bfloat16_rn(v);
+        }
+    }
+}
+
+template <bool TF32>
+__global__ void pack_w_kernel(const float* W, int kind, int Co, int Ci, int k, int s, int r, int taps, int M, int K,
+                              int Kp, void* hi, void* lo) {
+    const int64_t n = (int64_t)taps * M * Kp;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const int kk = (int)(i % Kp);
+        const int64_t q = i / Kp;
+        const int m = (int)(q % M), t = (int)(q / M);
+        float v = 0.f;
+        if (kk < K) {
+            if (kind == PACK_CONV_FWD) {            // m = co, kk = ci
+                v = W[((int64_t)m * Ci + kk) * k + t];
+            } else if (kind == PACK_CONV_DGRAD) {   // m = ci, kk = co
+                v = W[((int64_t)kk * Ci + m) * k + (k - 1 - t)];
+            } else {                                // convT phase: m = co, kk = ci
+                const int tt = r + (taps - 1 - t) * s;
+                v = W[((int64_t)kk * Co + m) * k + tt];
+            }
+        }
+        if (TF32) {
+            const float h = tf32_rna(v);
+            static_cast<float*>(hi)[i] = h;
+            static_cast<float*>(lo)[i] = v - h;
+        } else {
+            static_cast<__nv_bfloat16*>(hi)[i] = __float2bfloat16_rn(v);
+        }
+    }
+}
+
+// dW[(co*Ci + ci)*k + t] (+)= sum_split part[split][t][co][ci]
+__global__ void wgrad_reduce_kernel(const float* part, int splits, int taps, int Co, int Ci, float* dW, int accum) {
+    const int64_t n = (int64_t)Co * Ci * taps;
+    const int64_t stride_split = (int64_t)taps * Co * Ci;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const int t = (int)(i % taps);
+        const int64_t q = i / taps;
+        const int ci = (int)(q % Ci), co = (int)(q / Ci);
+        const int64_t src = ((int64_t)t * Co + co) * Ci + ci;
+        double s = 0;
+        for (int sp = 0; sp < splits; ++sp) s += part[sp * stride_split + src];
+        dW[i] = (float)(accum ? dW[i] + s : s);
+    }
+}
+
+inline int grid_for(int64_t n, int threads = 256) {
+    int64_t g = ceil_div(n, threads);
+    if (g > 148 * 32) g = 148 * 32;
+    return (int)(g < 1 ? 1 : g);
+}
+
+// ── tensor maps
+PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    if (!fn) fail("conv_tc", "cuTensorMapEncodeTiled is unavailable");
+    return fn;
+}
+
+// 3-D map over [d2][d1][d0] (d0 contiguous), box {box0, box1, 1}, 128-byte swizzle
+// span (16-byte chunks, or 32-byte chunks for MN-major tf32 operands).
+CUtensorMap make_map(const void* base, int mode, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t pitch0_elems,
+                     uint64_t d1_elems_per_d2, uint32_t box0, uint32_t box1, bool atom32 = false) {
+    CUtensorMap m;
+    const uint64_t es = (uint64_t)tc_esize(mode);
+    cuuint64_t dims[3] = {d0, d1, d2};
+    cuuint64_t strides[2] = {pitch0_elems * es, pitch0_elems * d1_elems_per_d2 * es};
+    cuuint32_t box[3] = {box0, box1, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    const CUtensorMapDataType dt =
+        mode == TC_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+    if ((reinterpret_cast<uintptr_t>(base) & 15) != 0) fail("conv_tc", "operand base not 16-byte aligned");
+    if (box0 * es != 128) fail("conv_tc", "box inner extent must be 128 bytes");
+    const CUresult rc = get_encode()(&m, dt, 3, const_cast<void*>(base), dims, strides, box, estr,
+                                     CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                     atom32 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
+                                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (rc != CUDA_SUCCESS) fail("conv_tc", "cuTensorMapEncodeTiled failed (" + std::to_string((int)rc) + ")");
+    return m;
+}
+
+template <bool TF32, bool PROMOTE, bool WGRAD>
+void set_smem_attr() {
+    static bool done = false;
+    if (!done) {
+        BSML_CUDA(cudaFuncSetAttribute(conv_tc_kernel<TF32, PROMOTE, WGRAD>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<TF32>::SMEM));
+        done = true;
+    }
+}
+
+template <bool TF32>
+void launch_fwd(const TcConvFwd& c, int mode, cudaStream_t st) {
+    using CF = Cfg<TF32>;
+    constexpr bool PROMOTE = TF32;
+    set_smem_attr<TF32, PROMOTE, false>();
+    const uint32_t bke = CF::BKE;
+    const CUtensorMap mAh = make_map(c.w.hi, mode, c.Ci, c.Co, c.taps, c.w.ld, c.Co, bke, BM);
+    const CUtensorMap mAl = TF32 ? make_map(c.w.lo, mode, c.Ci, c.Co, c.taps, c.w.ld, c.Co, bke, BM) : mAh;
+    const CUtensorMap mBh = make_map(c.x.hi, mode, c.Ci, c.L_in, c.B, c.x.ld, c.L_in, bke, BN);
+    const CUtensorMap mBl = TF32 ? make_map(c.x.lo, mode, c.Ci, c.L_in, c.B, c.x.ld, c.L_in, bke, BN) : mBh;
+    Args a{};
+    a.No = c.No; a.o_base = c.o_base; a.p = c.p; a.d = c.d; a.taps = c.taps;
+    a.kchunks = (int)ceil_div(c.Ci, CF::BKE);
+    a.Co = c.Co;
+    a.y = c.y.p; a.y_bs = c.y.bstride; a.y_ld = c.y.ld; a.orow_mul = c.orow_mul; a.orow_off = c.orow_off;
+    a.y_rows = c.y.L;
+    a.bias = c.bias;
+    a.r = c.r ? c.r->p : nullptr; a.r_bs = c.r ? c.r->bstride : 0; a.r_ld = c.r ? c.r->ld : 0; a.r_shift = c.r_shift;
+    a.alpha = c.alpha; a.accum = c.accum ? 1 : 0;
+    dim3 grid((unsigned)ceil_div(c.No, BN), (unsigned)ceil_div(c.Co, BM), (unsigned)c.B);
+    ::bsml::count_launch();
+    conv_tc_kernel<TF32, PROMOTE, false><<<grid, 192, CF::SMEM, st>>>(mAh, mAl, mBh, mBl, a);
+    BSML_LAUNCH("conv_fwd_tc");
+}
+
+template <bool TF32>
+void launch_wgrad(const TcConvWgrad& c, int mode, float* part, int64_t part_cap, cudaStream_t st) {
+    using CF = Cfg<TF32>;
+    constexpr bool PROMOTE = TF32;
+    set_smem_attr<TF32, PROMOTE, true>();
+    const uint32_t bke = CF::BKE, kr = CF::KROWS;
+    // A: dY planes [B][Lo][ld] (M = Co along the contiguous dim); B: X planes (N = Ci)
+    const CUtensorMap mAh = make_map(c.dy.hi, mode, c.Co, c.Lo, c.B, c.dy.ld, c.Lo, bke, kr, TF32);
+    const CUtensorMap mAl = TF32 ? make_map(c.dy.lo, mode, c.Co, c.Lo, c.B, c.dy.ld, c.Lo, bke, kr, TF32) : mAh;
+    const CUtensorMap mBh = make_map(c.x.hi, mode, c.Ci, c.L_in, c.B, c.x.ld, c.L_in, bke, kr, TF32);
+    const CUtensorMap mBl = TF32 ? make_map(c.x.lo, mode, c.Ci, c.L_in, c.B, c.x.ld, c.L_in, bke, kr, TF32) : mBh;
+    Args a{};
+    a.taps = c.taps; a.p = c.p; a.d = c.d; a.Co = c.Co; a.Ci = c.Ci;
+    a.n_ci_tiles = (int)ceil_div(c.Ci, BN);
+    a.chunks_pc = (int)ceil_div(c.Lo, CF::KROWS);
+    a.chunks_total = a.chunks_pc * c.B;
+    const int tiles = (int)ceil_div(c.Co, BM) * a.n_ci_tiles * c.taps;
+    // ~2 waves of CTAs on 148 SMs, each with >= 8 chunks of K, within the partial budget
+    int64_t splits = ceil_div(2 * 148, tiles);
+    splits = std::min<int64_t>(splits, ceil_div(a.chunks_total, 8));
+    splits = std::min<int64_t>(splits, part_cap / ((int64_t)c.taps * c.Co * c.Ci));
+    if (splits < 1) fail("conv_wgrad_tc", "split-K partial buffer too small");
+    a.chunks_per_split = (int)ceil_div(a.chunks_total, splits);
+    splits = ceil_div(a.chunks_total, a.chunks_per_split);
+    a.part = part;
+    dim3 grid((unsigned)ceil_div(c.Co, BM), (unsigned)(a.n_ci_tiles * c.taps), (unsigned)splits);
+    ::bsml::count_launch();
+    conv_tc_kernel<TF32, PROMOTE, true><<<grid, 192, CF::SMEM, st>>>(mAh, mAl, mBh, mBl, a);
+    BSML_LAUNCH("conv_wgrad_tc");
+    ::bsml::count_launch();
+    wgrad_reduce_kernel<<<grid_for((int64_t)c.Co * c.Ci * c.taps), 256, 0, st>>>(part, (int)splits, c.taps, c.Co,
+                                                                                    c.Ci, c.dW, c.accum ? 1 : 0);
+    BSML_LAUNCH("wgrad_reduce");
+}
+
+}  // namespace
+
+void make_act_planes(const Act& x, int mode, void* hi, void* lo, cudaStream_t st) {
+    const int ld = tc_pitch(x.C, mode);
+    ::bsml::count_launch();
+    if (mode == TC_TF32X3)
+        act_planes_kernel<true><<<grid_for(x.numel()), 256, 0, st>>>(x, hi, lo, ld);
+    else
+        act_planes_kernel<false><<<grid_for(x.numel()), 256, 0, st>>>(x, hi, lo, ld);
+    BSML_LAUNCH("make_act_planes");
+}
+
+void pack_w_tc(const float* W, int kind, int Co, int Ci, int k, int s, int r, int mode, void* hi, void* lo,
+               cudaStream_t st) {
+    int taps = k, M = Co, K = Ci;
+    if (kind == PACK_CONV_DGRAD) { M = Ci; K = Co; }
+    if (kind == PACK_CONVT_PHASE) taps = (k - r + s - 1) / s;
+    const int Kp = (int)round_up(K, 8);
+    const int64_t n = (int64_t)taps * M * Kp;
+    ::bsml::count_launch();
+    if (mode == TC_TF32X3)
+        pack_w_kernel<true><<<grid_for(n), 256, 0, st>>>(W, kind, Co, Ci, k, s, r, taps, M, K, Kp, hi, lo);
+    else
+        pack_w_kernel<false><<<grid_for(n), 256, 0, st>>>(W, kind, Co, Ci, k, s, r, taps, M, K, Kp, hi, lo);
+    BSML_LAUNCH("pack_w_tc");
+}
+
+void conv_fwd_tc(const TcConvFwd& c, int mode, cudaStream_t st) {
+    if (c.No <= 0) return;
+    if (mode == TC_TF32X3)
+        launch_fwd<true>(c, mode, st);
+    else
+        launch_fwd<false>(c, mode, st);
+}
+
+void conv_wgrad_tc(const TcConvWgrad& c, int mode, float* part, int64_t part_cap, cudaStream_t st) {
+    if (c.Lo <= 0) return;
+    if (mode == TC_TF32X3)
+        launch_wgrad<true>(c, mode, part, part_cap, st);
+    else
+        launch_wgrad<false>(c, mode, part, part_cap, st);
+}
+
+int tc_error_flag() {
+    int v = 0, zero = 0;
+    BSML_CUDA(cudaDeviceSynchronize());
+    BSML_CUDA(cudaMemcpyFromSymbol(&v, g_tc_err, sizeof(int)));
+    BSML_CUDA(cudaMemcpyToSymbol(g_tc_err, &zero, sizeof(int)));
+    return v;
+}
+
+}  // namespace bsml

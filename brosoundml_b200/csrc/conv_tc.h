@@ -1,0 +1,75 @@
+// tcgen05 implicit-GEMM convolution (sm_100a): TMA-staged K-major tiles,
+// TMEM accumulators, fused epilogue.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include "common.cuh"
+
+namespace bsml {
+
+// Operand arithmetic of the tensor-core path.
+//   TC_TF32X3: each fp32 operand is split hi + lo (hi = tf32-rounded value,
+//              lo = exact fp32 remainder) and D += Ahi*Bhi + Ahi*Blo + Alo*Bhi.
+//   TC_BF16:   bf16 operands, one product, fp32 accumulation.
+enum TcMode { TC_BF16 = 0, TC_TF32X3 = 1 };
+
+// Operand planes in global memory: fp32 (tf32 hi/lo) or bf16, row pitch `ld`
+// elements (16-byte multiple).
+struct TcPlanes {
+    const void* hi = nullptr;
+    const void* lo = nullptr;   // TC_TF32X3 only
+    int ld = 0;
+};
+
+inline int tc_pitch(int C, int mode) { return (int)round_up(C, mode == TC_BF16 ? 8 : 4); }
+inline int tc_esize(int mode) { return mode == TC_BF16 ? 2 : 4; }
+
+// Activation x (B, L, C) -> planes (same geometry, pitch tc_pitch(C)).
+void make_act_planes(const Act& x, int mode, void* hi, void* lo, cudaStream_t st);
+// Weight planes [taps][M][round_up(K, 8)] (K contiguous):
+//   conv fwd:       M = Co, K = Ci, tap t   = W[co][ci][t]
+//   conv dgrad:     M = Ci, K = Co, tap t'  = W[co][ci][k-1-t']
+//   convT phase r:  M = Co, K = Ci, tap m'  = W[ci][co][r + (kr-1-m')*s]
+void pack_w_tc(const float* W, int kind, int Co, int Ci, int k, int s, int r, int mode, void* hi, void* lo,
+               cudaStream_t st);
+enum { PACK_CONV_FWD = 0, PACK_CONV_DGRAD = 1, PACK_CONVT_PHASE = 2 };
+
+struct TcConvFwd {
+    // activations (B, L_in, Ci) as planes
+    TcPlanes x;
+    int B = 0, L_in = 0, Ci = 0;
+    // weights [taps][Co][Kp]
+    TcPlanes w;
+    int taps = 0, Co = 0;
+    // geometry (stride 1): input row = (o + o_base) + t*d - p
+    int p = 0, d = 1, No = 0, o_base = 0;
+    // epilogue (as ConvFwd): y[b, (o+o_base)*orow_mul + orow_off, co] =
+    //   alpha*(acc + bias + r[row >> r_shift]) + (accum ? y : 0)
+    Act y;
+    const float* bias = nullptr;
+    const Act* r = nullptr;
+    int r_shift = 0, orow_mul = 1, orow_off = 0;
+    float alpha = 1.f;
+    bool accum = false;
+};
+void conv_fwd_tc(const TcConvFwd& a, int mode, cudaStream_t st);
+
+// Weight gradient of a stride-1 conv: dW[(co*Ci + ci)*taps + t] (+)=
+//   sum_{b,o} dY[b, o, co] * X[b, o + t*d - p, ci]
+// over operand planes of dY (B, Lo, Co) and X (B, L_in, Ci). Split-K partials
+// go to `part` (at most part_cap floats) and are reduced in double.
+struct TcConvWgrad {
+    TcPlanes dy, x;
+    int B = 0, Lo = 0, Co = 0, L_in = 0, Ci = 0;
+    int taps = 1, p = 0, d = 1;
+    float* dW = nullptr;
+    bool accum = false;
+};
+void conv_wgrad_tc(const TcConvWgrad& a, int mode, float* part, int64_t part_cap, cudaStream_t st);
+
+// Reads and clears the device error word the tensor-core kernels set when a
+// bounded wait gives up (0 = no error). Synchronises the device.
+int tc_error_flag();
+
+}  // namespace bsml

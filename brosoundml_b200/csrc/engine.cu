@@ -76,6 +76,43 @@ Engine::Engine(const bsml_decoder_config& cfg, int device) : lay_(cfg), device_(
         for (int r = 0; r < u.s; ++r) wp_up_[u.id].push_back(take((int64_t)((u.k - r + u.s - 1) / u.s) * u.cin * round_up(u.cout, 4)));
         wp_up_dgrad_[u.id] = take((int64_t)u.k * u.cout * round_up(u.cin, 4));
     }
+    // tensor-core weight planes: 2 fp32 planes per layout (bf16 uses the first half)
+    {
+        int64_t tb = 0;
+        auto tsz = [&](int64_t floats) { tb = round_up(tb, 256) + floats * 4; };
+        for (auto* c : lay_.convs) {
+            tsz((int64_t)c->k * c->cout * round_up(c->cin, 8)); tsz((int64_t)c->k * c->cout * round_up(c->cin, 8));
+            tsz((int64_t)c->k * c->cin * round_up(c->cout, 8)); tsz((int64_t)c->k * c->cin * round_up(c->cout, 8));
+        }
+        for (auto& u : lay_.ups)
+            for (int r = 0; r < u.s; ++r)
+                for (int h = 0; h < 2; ++h) tsz((int64_t)((u.k - r + u.s - 1) / u.s) * u.cout * round_up(u.cin, 8));
+        tcw_bytes_ = round_up(tb, 256);
+        BSML_CUDA(cudaMalloc(&tcw_mem_, tcw_bytes_));
+        int64_t toff = 0;
+        auto ttake = [&](int64_t floats) {
+            toff = round_up(toff, 256);
+            float* p = (float*)(tcw_mem_ + toff);
+            toff += floats * 4;
+            return p;
+        };
+        const size_t nc = lay_.convs.size();
+        tcw_fwd_hi_.resize(nc); tcw_fwd_lo_.resize(nc); tcw_dg_hi_.resize(nc); tcw_dg_lo_.resize(nc);
+        for (auto* c : lay_.convs) {
+            tcw_fwd_hi_[c->id] = ttake((int64_t)c->k * c->cout * round_up(c->cin, 8));
+            tcw_fwd_lo_[c->id] = ttake((int64_t)c->k * c->cout * round_up(c->cin, 8));
+            tcw_dg_hi_[c->id] = ttake((int64_t)c->k * c->cin * round_up(c->cout, 8));
+            tcw_dg_lo_[c->id] = ttake((int64_t)c->k * c->cin * round_up(c->cout, 8));
+        }
+        tcw_up_hi_.resize(lay_.ups.size());
+        tcw_up_lo_.resize(lay_.ups.size());
+        for (auto& u : lay_.ups)
+            for (int r = 0; r < u.s; ++r) {
+                const int64_t n = (int64_t)((u.k - r + u.s - 1) / u.s) * u.cout * round_up(u.cin, 8);
+                tcw_up_hi_[u.id].push_back(ttake(n));
+                tcw_up_lo_[u.id].push_back(ttake(n));
+            }
+    }
     // fc row table (out offsets depend on B: rebuilt in ensure_plan)
     fc_rows_ = 0;
     for (int c : lay_.aff_C) fc_rows_ += 2 * c;
@@ -92,6 +129,7 @@ Engine::~Engine() {
     cudaSetDevice(device_);
     for (auto ev : ev_pool_) cudaEventDestroy(ev);
     cudaFree(wp_mem_);
+    cudaFree(tcw_mem_);
     cudaFree(ws_);
     cudaFree(fc_tab_);
     cudaFree(fc_row_entry_);
@@ -275,6 +313,11 @@ void Engine::plan(Planner& P) {
         s.B = B;
         s.p = P.f(max_elems);
     }
+    // activation operand planes for the tensor-core path (largest conv input)
+    tc_xh_ = P.f(max_elems);
+    tc_xl_ = P.f(max_elems);
+    tc_yh_ = P.f(max_elems);
+    tc_yl_ = P.f(max_elems);
 }
 
 void Engine::ensure_plan(int B, int T, int frames, bool have_har) {
@@ -314,14 +357,48 @@ void Engine::ensure_plan(int B, int T, int frames, bool have_har) {
 
 // ── weight packing (every step: the parameters may have changed)
 void Engine::pack_weights(cudaStream_t st) {
-    for (auto* c : lay_.convs) pack_conv_fwd(params_ + c->w, c->cout, c->cin, c->k, wp_fwd_[c->id], st);
+    for (auto* c : lay_.convs) {
+        if (tc_ok(c->cin, c->cout, c->s))
+            pack_w_tc(params_ + c->w, PACK_CONV_FWD, c->cout, c->cin, c->k, 1, 0, tc_mode(), tcw_fwd_hi_[c->id],
+                      tcw_fwd_lo_[c->id], st);
+        else
+            pack_conv_fwd(params_ + c->w, c->cout, c->cin, c->k, wp_fwd_[c->id], st);
+    }
     for (auto& u : lay_.ups)
-        for (int r = 0; r < u.s; ++r) pack_convT_phase(params_ + u.w, u.cin, u.cout, u.k, u.s, r, wp_up_[u.id][r], st);
+        for (int r = 0; r < u.s; ++r) {
+            if (tc_ok(u.cin, u.cout, 1))
+                pack_w_tc(params_ + u.w, PACK_CONVT_PHASE, u.cout, u.cin, u.k, u.s, r, tc_mode(), tcw_up_hi_[u.id][r],
+                          tcw_up_lo_[u.id][r], st);
+            else
+                pack_convT_phase(params_ + u.w, u.cin, u.cout, u.k, u.s, r, wp_up_[u.id][r], st);
+        }
 }
 void Engine::pack_dgrad_weights(cudaStream_t st) {
-    for (auto* c : lay_.convs)
-        if (c->s == 1) pack_conv_dgrad(params_ + c->w, c->cout, c->cin, c->k, wp_dgrad_[c->id], st);
+    for (auto* c : lay_.convs) {
+        if (c->s != 1) continue;
+        if (tc_ok(c->cout, c->cin, 1))
+            pack_w_tc(params_ + c->w, PACK_CONV_DGRAD, c->cout, c->cin, c->k, 1, 0, tc_mode(), tcw_dg_hi_[c->id],
+                      tcw_dg_lo_[c->id], st);
+        else
+            pack_conv_dgrad(params_ + c->w, c->cout, c->cin, c->k, wp_dgrad_[c->id], st);
+    }
     for (auto& u : lay_.ups) pack_convT_dgrad(params_ + u.w, u.cin, u.cout, u.k, wp_up_dgrad_[u.id], st);
+}
+
+void Engine::tc_planes(const Act& x, cudaStream_t st) { make_act_planes(x, tc_mode(), tc_xh_, tc_xl_, st); }
+
+void Engine::tc_launch(const Act& x, const float* whi, const float* wlo, int taps, int M, const Act& y,
+                       const float* bias, const Act* r, int r_shift, int p, int d, int No, int o_base, int orow_mul,
+                       int orow_off, float alpha, bool accum, cudaStream_t st) {
+    TcConvFwd a;
+    a.x.hi = tc_xh_; a.x.lo = tc_xl_; a.x.ld = tc_pitch(x.C, tc_mode());
+    a.B = x.B; a.L_in = x.L; a.Ci = x.C;
+    a.w.hi = whi; a.w.lo = wlo; a.w.ld = (int)round_up(x.C, 8);
+    a.taps = taps; a.Co = M;
+    a.p = p; a.d = d; a.No = No; a.o_base = o_base;
+    a.y = y; a.bias = bias; a.r = r; a.r_shift = r_shift; a.orow_mul = orow_mul; a.orow_off = orow_off;
+    a.alpha = alpha; a.accum = accum;
+    conv_fwd_tc(a, tc_mode(), st);
 }
 
 // ── conv wrappers
@@ -333,6 +410,14 @@ void Engine::conv(const ConvP& c, const Act& x, const Act& y, const Act* r, int 
     a.No = conv_out(x.L, c);
     a.alpha = alpha; a.accum = accum;
     if (a.No != y.L) fail("conv", "output length mismatch");
+    if (tc_ok(c.cin, c.cout, c.s)) {
+        tc_planes(x, st);
+        const int id = prof_begin(PROF_CONV, 2.0 * c.cin * c.cout * c.k * (double)a.No * x.B, st);
+        tc_launch(x, tcw_fwd_hi_[c.id], tcw_fwd_lo_[c.id], c.k, c.cout, y, a.bias, r, r_shift, c.p, c.d, a.No, 0, 1, 0,
+                  alpha, accum, st);
+        prof_end(id, st);
+        return;
+    }
     const int id = prof_begin(PROF_CONV, 2.0 * c.cin * c.cout * c.k * (double)a.No * x.B, st);
     conv_fwd_simt(a, st);
     prof_end(id, st);
@@ -347,6 +432,14 @@ void Engine::conv_dgrad(const ConvP& c, const Act& dy, const Act& dx, bool accum
     a.k = c.k; a.s = 1; a.p = c.d * (c.k - 1) - c.p; a.d = c.d;
     a.No = dx.L;
     a.accum = accum;
+    if (tc_ok(c.cout, c.cin, 1)) {
+        tc_planes(dy, st);
+        const int id = prof_begin(PROF_CONV, 2.0 * c.cin * c.cout * c.k * (double)dy.L * dy.B, st);
+        tc_launch(dy, tcw_dg_hi_[c.id], tcw_dg_lo_[c.id], c.k, c.cin, dx, nullptr, nullptr, 0, a.p, c.d, a.No, 0, 1, 0,
+                  1.f, accum, st);
+        prof_end(id, st);
+        return;
+    }
     const int id = prof_begin(PROF_CONV, 2.0 * c.cin * c.cout * c.k * (double)dy.L * dy.B, st);
     conv_fwd_simt(a, st);
     prof_end(id, st);
@@ -354,6 +447,21 @@ void Engine::conv_dgrad(const ConvP& c, const Act& dy, const Act& dx, bool accum
 
 void Engine::conv_wgrad(const ConvP& c, const Act& dy, const Act& x, cudaStream_t st) {
     if (!grads_) return;
+    if (tc_ok(c.cin, c.cout, c.s)) {
+        const int mode = tc_mode();
+        make_act_planes(dy, mode, tc_yh_, tc_yl_, st);
+        make_act_planes(x, mode, tc_xh_, tc_xl_, st);
+        TcConvWgrad w;
+        w.dy.hi = tc_yh_; w.dy.lo = tc_yl_; w.dy.ld = tc_pitch(dy.C, mode);
+        w.x.hi = tc_xh_; w.x.lo = tc_xl_; w.x.ld = tc_pitch(x.C, mode);
+        w.B = dy.B; w.Lo = dy.L; w.Co = dy.C; w.L_in = x.L; w.Ci = x.C;
+        w.taps = c.k; w.p = c.p; w.d = c.d; w.dW = grads_ + c.w;
+        const int id = prof_begin(PROF_WGRAD, 2.0 * c.cin * c.cout * c.k * (double)dy.L * dy.B, st);
+        conv_wgrad_tc(w, mode, part_, part_floats_, st);
+        if (c.b >= 0) colsum(dy, grads_ + c.b, false, part_, st);
+        prof_end(id, st);
+        return;
+    }
     ConvWgrad a;
     a.dy = dy; a.x = x; a.k = c.k; a.s = c.s; a.p = c.p; a.d = c.d;
     a.dW = grads_ + c.w;
@@ -368,6 +476,8 @@ void Engine::conv_wgrad(const ConvP& c, const Act& dy, const Act& x, cudaStream_
 //   y[q*s + r - p] = sum_m sum_ci W[ci, co, r + m*s] x[q - m, ci]
 void Engine::convT(const UpP& u, const Act& x, const Act& y, int row_off, const Act* r, cudaStream_t st) {
     const int Lu = (x.L - 1) * u.s - 2 * u.p + u.k;
+    const bool tc = tc_ok(u.cin, u.cout, 1);
+    if (tc) tc_planes(x, st);
     for (int ph = 0; ph < u.s; ++ph) {
         const int kr = (u.k - ph + u.s - 1) / u.s;
         if (kr <= 0) continue;
@@ -381,7 +491,11 @@ void Engine::convT(const UpP& u, const Act& x, const Act& y, int row_off, const 
         a.No = qmax - qmin + 1; a.o_base = qmin;
         a.orow_mul = u.s; a.orow_off = ph - u.p + row_off;
         const int id = prof_begin(PROF_CONV, 2.0 * u.cin * u.cout * kr * (double)a.No * x.B, st);
-        conv_fwd_simt(a, st);
+        if (tc)
+            tc_launch(x, tcw_up_hi_[u.id][ph], tcw_up_lo_[u.id][ph], kr, u.cout, y, a.bias, r, 0, a.p, 1, a.No, a.o_base,
+                      a.orow_mul, a.orow_off, 1.f, false, st);
+        else
+            conv_fwd_simt(a, st);
         prof_end(id, st);
     }
 }

@@ -7,6 +7,7 @@
 #include <vector>
 
 #include "common.cuh"
+#include "conv_tc.h"
 #include "kernels.h"
 #include "layout.h"
 
@@ -27,7 +28,7 @@ class Engine {
                  const float* style, const float* har, int frames, const float* aff_in, float* audio,
                  float* aff_out, cudaStream_t st);
     void backward(const float* daudio, float* grads, float* d_asr, float* d_style, float* d_aff, cudaStream_t st);
-    int64_t workspace_bytes() const { return ws_bytes_ + wp_bytes_; }
+    int64_t workspace_bytes() const { return ws_bytes_ + wp_bytes_ + tcw_bytes_; }
 
     // Per-kernel-class timing with CUDA events (off by default). Classes:
     // 0 conv fwd-like (fwd, dgrad, convT), 1 conv wgrad, 2 AdaIN/Snake forward,
@@ -111,6 +112,21 @@ class Engine {
     std::vector<float*> wp_fwd_, wp_dgrad_;       // per conv id
     std::vector<std::vector<float*>> wp_up_;      // per ups: phases
     std::vector<float*> wp_up_dgrad_;
+    // tensor-core weight planes (hi, lo) per conv id, per convT phase
+    char* tcw_mem_ = nullptr;
+    int64_t tcw_bytes_ = 0;
+    std::vector<float*> tcw_fwd_hi_, tcw_fwd_lo_, tcw_dg_hi_, tcw_dg_lo_;
+    std::vector<std::vector<float*>> tcw_up_hi_, tcw_up_lo_;
+    float* tc_xh_ = nullptr;          // activation planes of the current tensor-core call
+    float* tc_xl_ = nullptr;
+    float* tc_yh_ = nullptr;          // second operand's planes (weight gradients)
+    float* tc_yl_ = nullptr;
+    int tc_mode() const { return math_ == BSML_MATH_BF16 ? TC_BF16 : TC_TF32X3; }
+    bool tc_ok(int K, int M, int s) const { return math_ != BSML_MATH_FP32_SIMT && s == 1 && K >= 32 && M >= 64; }
+    void tc_planes(const Act& x, cudaStream_t st);
+    void tc_launch(const Act& x, const float* whi, const float* wlo, int taps, int M, const Act& y, const float* bias,
+                   const Act* r, int r_shift, int p, int d, int No, int o_base, int orow_mul, int orow_off,
+                   float alpha, bool accum, cudaStream_t st);
     FcRow* fc_tab_ = nullptr;                     // device
     int* fc_row_entry_ = nullptr;                 // device
     int fc_rows_ = 0;

@@ -35,9 +35,9 @@ def _f32(t):
 
 class Decoder:
     # math modes smoke() exercises (the tensor-core modes join once built)
-    SMOKE_MATH = ("fp32",)
-    # math mode bench.py uses by default
-    DEFAULT_MATH = "fp32"
+    SMOKE_MATH = ("fp32", "tf32x3")
+    # math mode bench.py uses by default (fp32-grade accuracy on the tensor cores)
+    DEFAULT_MATH = "tf32x3"
 
     def __init__(self, cfg: dict, device: int = 0, math: str = "fp32"):
         self.cfg = dict(cfg)

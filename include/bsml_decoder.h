@@ -144,6 +144,14 @@ int bsml_adam_step(float* param, const float* grad, float* m, float* v, int64_t 
 
 /* ── atoms (the reference's detail:: functions, batched) ────────────────── */
 
+/* Arithmetic of the conv / convT atoms below (process-wide, default
+ * BSML_MATH_FP32_SIMT). Tensor-core modes apply to stride-1 contractions with
+ * >= 32 input and >= 64 output channels; others stay on the fp32 kernels. */
+int bsml_set_atom_math(int math_mode);
+/* Reads and clears the error word a tensor-core kernel sets when one of its
+ * bounded waits gives up (0 = none). Synchronises the device. */
+int bsml_device_error(void);
+
 /* Conv1d forward (modules.cpp:103-108): x (B, Ci, L) -> y (B, Co, Lo). bias may be NULL. */
 int bsml_conv1d_forward(const float* x, int B, int Ci, int L, const float* W, const float* bias, int Co, int k,
                         int stride, int pad, int dil, float* y, void* stream);
