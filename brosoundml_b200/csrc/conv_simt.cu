@@ -295,22 +295,54 @@ void conv_wgrad_simt(const ConvWgrad& c, float* part, cudaStream_t st) {
     if (c.db) colsum(c.dy, c.db, c.accum, part, st);
 }
 
-int64_t colsum_partial_floats(const Act& dy) {
-    return (int64_t)wgrad_splits((int64_t)dy.B * dy.L, dy.C) * dy.C;
+// Column sums of a channels-last tensor: 256-row chunks, 4 warps per CTA, each
+// lane owning 4 consecutive channels (float4 loads, coalesced 512-byte rows),
+// fp32 within a chunk, double across chunks.
+namespace {
+constexpr int CS_ROWS = 256;
+__global__ void __launch_bounds__(128) colsum_chunk_kernel(const float* dy, int64_t bs, int ld, int L, int C,
+                                                          int64_t rows, float* part) {
+    __shared__ float red[4][128];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int c0 = blockIdx.y * 128 + lane * 4;
+    const int64_t r0 = (int64_t)blockIdx.x * CS_ROWS;
+    const int64_t r1 = min(rows, r0 + CS_ROWS);
+    float s[4] = {0.f, 0.f, 0.f, 0.f};
+    const bool vec = (c0 + 3 < C) && ((ld & 3) == 0);
+    for (int64_t r = r0 + warp; r < r1; r += 4) {
+        const int b = (int)(r / L), l = (int)(r - (int64_t)b * L);
+        const float* p = dy + (int64_t)b * bs + (int64_t)l * ld + c0;
+        if (vec) {
+            const float4 v = *reinterpret_cast<const float4*>(p);
+            s[0] += v.x; s[1] += v.y; s[2] += v.z; s[3] += v.w;
+        } else {
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                if (c0 + j < C) s[j] += p[j];
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) red[warp][lane * 4 + j] = s[j];
+    __syncthreads();
+    const int c = blockIdx.y * 128 + threadIdx.x;
+    if (c < C) part[(int64_t)blockIdx.x * C + c] = red[0][threadIdx.x] + red[1][threadIdx.x] + red[2][threadIdx.x] +
+                                                   red[3][threadIdx.x];
 }
+}  // namespace
 
 void colsum(const Act& dy, float* db, bool accum, float* part, cudaStream_t st) {
     const int64_t rows = (int64_t)dy.B * dy.L;
-    const int sp = wgrad_splits(rows, dy.C);
-    const int rps = (int)ceil_div(rows, sp);
-    dim3 grid((unsigned)ceil_div(dy.C, 128), (unsigned)sp);
+    const int chunks = (int)ceil_div(rows, CS_ROWS);
+    dim3 grid((unsigned)chunks, (unsigned)ceil_div(dy.C, 128));
     ::bsml::count_launch();
-    colsum_kernel<<<grid, 128, 0, st>>>(dy.p, dy.bstride, dy.ld, dy.L, dy.C, dy.B, rps, part);
+    colsum_chunk_kernel<<<grid, 128, 0, st>>>(dy.p, dy.bstride, dy.ld, dy.L, dy.C, rows, part);
     BSML_LAUNCH("colsum");
     ::bsml::count_launch();
-    reduce_splits_kernel<<<grid_for(dy.C), 256, 0, st>>>(part, sp, dy.C, db, accum ? 1 : 0);
+    reduce_splits_kernel<<<grid_for(dy.C), 256, 0, st>>>(part, chunks, dy.C, db, accum ? 1 : 0);
     BSML_LAUNCH("colsum_reduce");
 }
+
+int64_t colsum_partial_floats(const Act& dy) { return ceil_div((int64_t)dy.B * dy.L, CS_ROWS) * dy.C; }
 
 void pack_conv_fwd(const float* W, int Co, int Ci, int k, float* wp, cudaStream_t st) {
     const int Cop = (int)round_up(Co, 4);

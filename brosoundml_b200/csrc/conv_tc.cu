@@ -20,9 +20,9 @@
 //
 // Promotion (TF32x3): the tensor core's in-TMEM fp32 accumulation is not
 // round-to-nearest, and its error grows with K. With PROMOTE the MMA warp
-// alternates between two TMEM accumulators, one K step each, and the epilogue
+// alternates between two TMEM accumulators, PG K steps each, and the epilogue
 // warps fold every finished partial into fp32 registers, so each TMEM sum spans
-// only 12 instructions and the long sum is formed with ordinary fp32 adds.
+// only 12*PG instructions and the long sum is formed with ordinary fp32 adds.
 #include <cuda_bf16.h>
 #include <cudaTypedefs.h>
 
@@ -39,6 +39,8 @@ namespace {
 __device__ int g_tc_err = 0;
 
 constexpr int BM = 128, BN = 128, TILE_BYTES = 16384;
+// promoted accumulation: K steps summed in TMEM before the epilogue folds them into registers
+constexpr int PG = 2;
 
 template <bool TF32>
 struct Cfg {
@@ -171,8 +173,12 @@ __global__ void __launch_bounds__(192, 1)
         for (int it = 0; it < n_iters; ++it) {
             const int s = it % C::S;
             const uint32_t ph = (it / C::S) & 1;
-            const int buf = PROMOTE ? (it & 1) : 0;
-            if (PROMOTE && it >= 2 && !tc::mbar_wait(&acce[buf], ((it >> 1) - 1) & 1, err, tc::TC_ERR_WAIT_ACC))
+            const int g = it / PG;                          // promotion group
+            const bool g_first = (it % PG) == 0;
+            const bool g_last = (it % PG) == PG - 1 || it == n_iters - 1;
+            const int buf = PROMOTE ? (g & 1) : 0;
+            if (PROMOTE && g_first && g >= 2 &&
+                !tc::mbar_wait(&acce[buf], ((g >> 1) - 1) & 1, err, tc::TC_ERR_WAIT_ACC))
                 break;
             if (!tc::mbar_wait(&full[s], ph, err, tc::TC_ERR_WAIT_FULL)) break;
             tc::tc_fence_after();
@@ -199,7 +205,8 @@ __global__ void __launch_bounds__(192, 1)
                     dAl = tc::desc_kmajor_sw128(aL + off);
                     dBl = tc::desc_kmajor_sw128(bL + off);
                 }
-                const uint32_t acc = PROMOTE ? (kk > 0 ? 1u : 0u) : ((it > 0 || kk > 0) ? 1u : 0u);
+                const uint32_t acc =
+                    PROMOTE ? ((g_first && kk == 0) ? 0u : 1u) : ((it > 0 || kk > 0) ? 1u : 0u);
                 tc::umma<TF32>(d_tmem, dAh, dBh, idesc, acc);
                 if (TF32) {
                     tc::umma<TF32>(d_tmem, dAh, dBl, idesc, 1u);
@@ -207,7 +214,7 @@ __global__ void __launch_bounds__(192, 1)
                 }
             }
             tc::umma_commit(&empty[s]);           // frees the stage once these MMAs have read it
-            if (PROMOTE) tc::umma_commit(&accf[buf]);
+            if (PROMOTE && g_last) tc::umma_commit(&accf[buf]);
         }
         if (!PROMOTE) tc::umma_commit(&accf[0]);
     } else if (warp >= 2) {
@@ -220,19 +227,24 @@ __global__ void __launch_bounds__(192, 1)
         for (int j = 0; j < BN; ++j) R[j] = 0.f;
         bool ok = true;
         if (PROMOTE) {
-            for (int it = 0; it < n_iters; ++it) {
-                const int buf = it & 1;
+            const int n_groups = (n_iters + PG - 1) / PG;
+            for (int g = 0; g < n_groups; ++g) {
+                const int buf = g & 1;
                 bool w = true;
-                if (lane == 0) w = tc::mbar_wait(&accf[buf], (it >> 1) & 1, err, tc::TC_ERR_WAIT_ACC);
+                if (lane == 0) w = tc::mbar_wait(&accf[buf], (g >> 1) & 1, err, tc::TC_ERR_WAIT_ACC);
                 ok = __shfl_sync(0xffffffffu, w ? 1 : 0, 0) != 0;
                 if (!ok) break;
                 tc::tc_fence_after();
 #pragma unroll
-                for (int c0 = 0; c0 < BN; c0 += 16) {
-                    float v[16];
-                    tc::tmem_ld16(trow + buf * BN + c0, v);
+                for (int half = 0; half < BN; half += 64) {   // 4 loads in flight, one wait
+                    uint32_t v[4][16];
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) R[c0 + j] += v[j];
+                    for (int q4 = 0; q4 < 4; ++q4) tc::tmem_ld16_nowait(trow + buf * BN + half + q4 * 16, v[q4]);
+                    tc::tmem_wait_ld();
+#pragma unroll
+                    for (int q4 = 0; q4 < 4; ++q4)
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) R[half + q4 * 16 + j] += __uint_as_float(v[q4][j]);
                 }
                 tc::tc_fence_before();
                 __syncwarp();
