@@ -30,6 +30,8 @@
 #include <mutex>
 
 #include "conv_tc.h"
+#include "kernels.h"
+#include "planes.cuh"
 #include "tc_ptx.cuh"
 
 namespace bsml {
@@ -62,6 +64,7 @@ struct Args {
     const float* bias;
     const float* r; int64_t r_bs; int r_ld; int r_shift;
     float alpha; int accum;
+    double* stats;   // per-(b, co) sum and sum of squares of the stored outputs (nullable)
     // weight-grad: Ci tiles, chunks per clip, total chunks, chunks per split, Ci
     int n_ci_tiles, chunks_pc, chunks_total, chunks_per_split, Ci;
     float* part;   // [split][tap][Co][Ci]
@@ -276,6 +279,7 @@ __global__ void __launch_bounds__(192, 1)
         } else {
             if (valid && mrow < a.Co) {
                 const float bv = a.bias ? a.bias[mrow] : 0.f;
+                double s1 = 0.0, s2 = 0.0;
 #pragma unroll
                 for (int j = 0; j < BN; ++j) {
                     const int o = n0 + j;
@@ -288,6 +292,12 @@ __global__ void __launch_bounds__(192, 1)
                     float* yp = a.y + (int64_t)b * a.y_bs + (int64_t)row * a.y_ld + mrow;
                     if (a.accum) val += *yp;
                     *yp = val;
+                    s1 += val;
+                    s2 = fma((double)val, (double)val, s2);
+                }
+                if (a.stats) {
+                    atomicAdd(&a.stats[((int64_t)b * a.Co + mrow) * 2], s1);
+                    atomicAdd(&a.stats[((int64_t)b * a.Co + mrow) * 2 + 1], s2);
                 }
             }
         }
@@ -302,11 +312,6 @@ __global__ void __launch_bounds__(192, 1)
 }
 
 // ── operand planes
-__device__ __forceinline__ float tf32_rna(float x) {
-    uint32_t r;
-    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
-    return __uint_as_float(r);
-}
 
 template <bool TF32>
 __global__ void act_planes_kernel(Act x, void* hi, void* lo, int ld) {
@@ -443,6 +448,8 @@ void launch_fwd(const TcConvFwd& c, int mode, cudaStream_t st) {
     a.bias = c.bias;
     a.r = c.r ? c.r->p : nullptr; a.r_bs = c.r ? c.r->bstride : 0; a.r_ld = c.r ? c.r->ld : 0; a.r_shift = c.r_shift;
     a.alpha = c.alpha; a.accum = c.accum ? 1 : 0;
+    a.stats = c.stats;
+    if (c.stats && c.accum) fail("conv_fwd_tc", "output statistics need a non-accumulating output");
     dim3 grid((unsigned)ceil_div(c.No, BN), (unsigned)ceil_div(c.Co, BM), (unsigned)c.B);
     ::bsml::count_launch();
     conv_tc_kernel<TF32, PROMOTE, false><<<grid, 192, CF::SMEM, st>>>(mAh, mAl, mBh, mBl, a);
@@ -488,6 +495,12 @@ void launch_wgrad(const TcConvWgrad& c, int mode, float* part, int64_t part_cap,
 
 void make_act_planes(const Act& x, int mode, void* hi, void* lo, cudaStream_t st) {
     const int ld = tc_pitch(x.C, mode);
+    if ((reinterpret_cast<uintptr_t>(x.p) & 15) == 0 && (x.ld & 3) == 0 && (x.bstride & 3) == 0) {
+        PlaneOut po;
+        po.hi = hi; po.lo = lo; po.ld = ld; po.mode = mode;
+        scale_out_v(x, 1.f, nullptr, &po, nullptr, st);
+        return;
+    }
     ::bsml::count_launch();
     if (mode == TC_TF32X3)
         act_planes_kernel<true><<<grid_for(x.numel()), 256, 0, st>>>(x, hi, lo, ld);

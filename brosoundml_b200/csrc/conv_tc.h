@@ -52,6 +52,9 @@ struct TcConvFwd {
     int r_shift = 0, orow_mul = 1, orow_off = 0;
     float alpha = 1.f;
     bool accum = false;
+    // optional: stats[(b*Co + co)*2 + {0,1}] += sum, sum of squares of the
+    // stored outputs over the rows this call writes (accum must be false)
+    double* stats = nullptr;
 };
 void conv_fwd_tc(const TcConvFwd& a, int mode, cudaStream_t st);
 

@@ -22,31 +22,6 @@ __global__ void zero_d(double* p, int64_t n) {
         p[i] = 0.0;
 }
 
-__global__ void stats_kernel(Act x, double* acc) {
-    const int b = blockIdx.y;
-    const int l0 = blockIdx.x * ROWS, l1 = min(x.L, l0 + ROWS);
-    for (int c = threadIdx.x; c < x.C; c += blockDim.x) {
-        double s = 0, ss = 0;
-        for (int l = l0; l < l1; ++l) {
-            const double v = x.row(b, l)[c];
-            s += v;
-            ss += v * v;
-        }
-        atomicAdd(&acc[((int64_t)b * x.C + c) * 2], s);
-        atomicAdd(&acc[((int64_t)b * x.C + c) * 2 + 1], ss);
-    }
-}
-
-__global__ void stats_final_kernel(const double* acc, int64_t n, int L, float eps, float* mean, float* rstd) {
-    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
-        const double m = acc[2 * i] / L;
-        double v = acc[2 * i + 1] / L - m * m;
-        v = v > 0 ? v : 0;
-        mean[i] = (float)m;
-        rstd[i] = (float)(1.0 / sqrt(v + (double)eps));
-    }
-}
-
 __device__ __forceinline__ float act_fwd(float z, int act, float slope, float al) {
     if (act == ACT_LEAKY) return z > 0.f ? z : slope * z;
     if (act == ACT_SNAKE) {
@@ -54,101 +29,6 @@ __device__ __forceinline__ float act_fwd(float z, int act, float slope, float al
         return z + sn * sn / al;
     }
     return z;
-}
-
-__global__ void adain_fwd_kernel(Act x, const float* mean, const float* rstd, const float* gb, int act, float slope,
-                                 const float* alpha, Act y) {
-    const int64_t n = x.numel();
-    const int C = x.C;
-    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
-        const int c = (int)(i % C);
-        const int64_t r = i / C;
-        const int l = (int)(r % x.L), b = (int)(r / x.L);
-        const int64_t bc = (int64_t)b * C + c;
-        const float g1 = 1.f + gb[(int64_t)b * 2 * C + c], be = gb[(int64_t)b * 2 * C + C + c];
-        const float z = g1 * ((x.row(b, l)[c] - mean[bc]) * rstd[bc]) + be;
-        y.row(b, l)[c] = act_fwd(z, act, slope, alpha ? alpha[c] : 1.f);
-    }
-}
-
-// Per (b,c): S0 = sum dz, S1 = sum dz*xhat, S2 = sum dy * d act/d alpha, where
-// z = g1*xhat + beta and dz = dy * act'(z).
-__global__ void adain_bwd_reduce_kernel(Act x, const float* mean, const float* rstd, const float* gb, int act,
-                                        float slope, const float* alpha, Act dy, double* acc) {
-    const int b = blockIdx.y;
-    const int l0 = blockIdx.x * ROWS, l1 = min(x.L, l0 + ROWS);
-    const int C = x.C;
-    for (int c = threadIdx.x; c < C; c += blockDim.x) {
-        const int64_t bc = (int64_t)b * C + c;
-        const float g1 = 1.f + gb[(int64_t)b * 2 * C + c], be = gb[(int64_t)b * 2 * C + C + c];
-        const float m = mean[bc], rs = rstd[bc];
-        const float al = alpha ? alpha[c] : 1.f;
-        double s0 = 0, s1 = 0, s2 = 0;
-        for (int l = l0; l < l1; ++l) {
-            const float xh = (x.row(b, l)[c] - m) * rs;
-            const float z = g1 * xh + be;
-            const float g = dy.row(b, l)[c];
-            float dz = g;
-            if (act == ACT_LEAKY) {
-                dz = z > 0.f ? g : slope * g;
-            } else if (act == ACT_SNAKE) {
-                const float sn = sinf(al * z), s2a = sinf(2.f * al * z);
-                dz = g * (1.f + s2a);
-                s2 += (double)g * (double)(z * s2a / al - sn * sn / (al * al));
-            }
-            s0 += dz;
-            s1 += (double)dz * xh;
-        }
-        atomicAdd(&acc[bc * 3], s0);
-        atomicAdd(&acc[bc * 3 + 1], s1);
-        if (act == ACT_SNAKE) atomicAdd(&acc[bc * 3 + 2], s2);
-    }
-}
-
-__global__ void adain_bwd_apply_kernel(Act x, const float* mean, const float* rstd, const float* gb, int act,
-                                       float slope, const float* alpha, Act dy, const double* acc, Act dx, Act skip,
-                                       int has_skip) {
-    const int64_t n = x.numel();
-    const int C = x.C;
-    const float invL = 1.f / (float)x.L;
-    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
-        const int c = (int)(i % C);
-        const int64_t r = i / C;
-        const int l = (int)(r % x.L), b = (int)(r / x.L);
-        const int64_t bc = (int64_t)b * C + c;
-        const float g1 = 1.f + gb[(int64_t)b * 2 * C + c], be = gb[(int64_t)b * 2 * C + C + c];
-        const float m = mean[bc], rs = rstd[bc];
-        const float xh = (x.row(b, l)[c] - m) * rs;
-        const float g = dy.row(b, l)[c];
-        float dz = g;
-        if (act == ACT_LEAKY) {
-            const float z = g1 * xh + be;
-            dz = z > 0.f ? g : slope * g;
-        } else if (act == ACT_SNAKE) {
-            const float z = g1 * xh + be;
-            const float al = alpha[c];
-            dz = g * (1.f + sinf(2.f * al * z));
-        }
-        const float m0 = (float)(acc[bc * 3] * invL), m1 = (float)(acc[bc * 3 + 1] * invL);
-        float v = rs * g1 * (dz - m0 - xh * m1);
-        if (has_skip) v += skip.row(b, l)[c];
-        dx.row(b, l)[c] = v;
-    }
-}
-
-__global__ void adain_bwd_final_kernel(const double* acc, int B, int C, float* dgb, float* dalpha) {
-    const int c = blockIdx.x * blockDim.x + threadIdx.x;
-    if (c >= C) return;
-    double sa = 0;
-    for (int b = 0; b < B; ++b) {
-        const int64_t bc = (int64_t)b * C + c;
-        if (dgb) {
-            dgb[(int64_t)b * 2 * C + c] = (float)acc[bc * 3 + 1];
-            dgb[(int64_t)b * 2 * C + C + c] = (float)acc[bc * 3];
-        }
-        sa += acc[bc * 3 + 2];
-    }
-    if (dalpha) dalpha[c] += (float)sa;
 }
 
 __global__ void snake_fwd_kernel(Act x, const float* alpha, Act y) {
@@ -417,44 +297,6 @@ __global__ void fc_style_reduce_kernel(const float* part, int chunks, int n, flo
 }
 
 }  // namespace
-
-void in_stats(const Act& x, float eps, double* acc, float* mean, float* rstd, cudaStream_t st) {
-    const int64_t n = (int64_t)x.B * x.C;
-    ::bsml::count_launch();
-    zero_d<<<grid_for(2 * n), 256, 0, st>>>(acc, 2 * n);
-    dim3 grid((unsigned)ceil_div(x.L, ROWS), (unsigned)x.B);
-    ::bsml::count_launch();
-    stats_kernel<<<grid, x.C >= 256 ? 256 : (int)round_up(x.C, 32), 0, st>>>(x, acc);
-    ::bsml::count_launch();
-    stats_final_kernel<<<grid_for(n), 256, 0, st>>>(acc, n, x.L, eps, mean, rstd);
-    BSML_LAUNCH("in_stats");
-}
-
-void adain_act_fwd(const Act& x, const float* mean, const float* rstd, const float* gb, int act, float slope,
-                   const float* alpha, const Act& y, cudaStream_t st) {
-    ::bsml::count_launch();
-    adain_fwd_kernel<<<grid_for(x.numel()), 256, 0, st>>>(x, mean, rstd, gb, act, slope, alpha, y);
-    BSML_LAUNCH("adain_act_fwd");
-}
-
-void adain_act_bwd(const Act& x, const float* mean, const float* rstd, const float* gb, int act, float slope,
-                   const float* alpha, const Act& dy, const Act& dx, const Act* skip, float* dgb, float* dalpha,
-                   double* acc, cudaStream_t st) {
-    const int64_t n = (int64_t)x.B * x.C;
-    ::bsml::count_launch();
-    zero_d<<<grid_for(3 * n), 256, 0, st>>>(acc, 3 * n);
-    dim3 grid((unsigned)ceil_div(x.L, ROWS), (unsigned)x.B);
-    ::bsml::count_launch();
-    adain_bwd_reduce_kernel<<<grid, x.C >= 256 ? 256 : (int)round_up(x.C, 32), 0, st>>>(x, mean, rstd, gb, act,
-                                                                                       slope, alpha, dy, acc);
-    ::bsml::count_launch();
-    adain_bwd_apply_kernel<<<grid_for(x.numel()), 256, 0, st>>>(x, mean, rstd, gb, act, slope, alpha, dy, acc, dx,
-                                                                skip ? *skip : Act{}, skip ? 1 : 0);
-    ::bsml::count_launch();
-    adain_bwd_final_kernel<<<(unsigned)ceil_div(x.C, 128), 128, 0, st>>>(acc, x.B, x.C, dgb,
-                                                                       act == ACT_SNAKE ? dalpha : nullptr);
-    BSML_LAUNCH("adain_act_bwd");
-}
 
 void snake_fwd(const Act& x, const float* alpha, const Act& y, cudaStream_t st) {
     ::bsml::count_launch();

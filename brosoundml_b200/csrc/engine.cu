@@ -201,9 +201,7 @@ Engine::RB1C Engine::plan_rb1(Planner& P, int L, int C) {
     c.L = L;
     for (int i = 0; i < 3; ++i) {
         if (i > 0) c.x[i] = P.act(B_, L, C);
-        c.s1[i] = P.act(B_, L, C);
         c.c1[i] = P.act(B_, L, C);
-        c.s2[i] = P.act(B_, L, C);
         c.st1[i] = stats(P, B_, C);
         c.st2[i] = stats(P, B_, C);
     }
@@ -290,6 +288,7 @@ void Engine::plan(Planner& P) {
         for (int j = 0; j < K; ++j) {
             s.res[j] = plan_rb1(P, s.Lx, u.cout);
             s.res[j].x[0] = s.m;
+            if (j > 0) s.res[j].st1[0] = s.res[0].st1[0];   // same input, same statistics
         }
         note(L, u.cin);
         note(s.Lx, u.cout);
@@ -305,6 +304,8 @@ void Engine::plan(Planner& P) {
     dF0dn_ = P.act(B, T, 1);
     dNdn_ = P.act(B, T, 1);
     dacc_ = P.d((int64_t)B * std::max(max_c, 1) * 3);
+    ssum_ = P.d((int64_t)B * std::max(max_c, 1) * 2);
+    bsum_ = P.d(std::max(max_c, 1));
     part_floats_ = 48ll << 20;
     part_ = P.f(part_floats_);
     fc_part_ = P.f(ceil_div(fc_rows_, 256) * (int64_t)B * cf.style_dim + 64);
@@ -318,6 +319,8 @@ void Engine::plan(Planner& P) {
     tc_xl_ = P.f(max_elems);
     tc_yh_ = P.f(max_elems);
     tc_yl_ = P.f(max_elems);
+    tc_dh_ = P.f(max_elems);
+    tc_dl_ = P.f(max_elems);
 }
 
 void Engine::ensure_plan(int B, int T, int frames, bool have_har) {
@@ -385,47 +388,85 @@ void Engine::pack_dgrad_weights(cudaStream_t st) {
     for (auto& u : lay_.ups) pack_convT_dgrad(params_ + u.w, u.cin, u.cout, u.k, wp_up_dgrad_[u.id], st);
 }
 
-void Engine::tc_planes(const Act& x, cudaStream_t st) { make_act_planes(x, tc_mode(), tc_xh_, tc_xl_, st); }
+TcPlanes Engine::tc_planes(const Act& x, cudaStream_t st) {
+    if (!x.p) fail("conv", "internal: operand has neither fp32 data nor planes");
+    make_act_planes(x, tc_mode(), tc_xh_, tc_xl_, st);
+    TcPlanes t;
+    t.hi = tc_xh_; t.lo = tc_xl_; t.ld = tc_pitch(x.C, tc_mode());
+    return t;
+}
 
-void Engine::tc_launch(const Act& x, const float* whi, const float* wlo, int taps, int M, const Act& y,
-                       const float* bias, const Act* r, int r_shift, int p, int d, int No, int o_base, int orow_mul,
-                       int orow_off, float alpha, bool accum, cudaStream_t st) {
+Engine::Opnd Engine::operand(bool tc, int L, int C, const Act& fbuf, void* hi, void* lo) const {
+    Opnd o;
+    o.f = view(fbuf, L, C);
+    if (tc) {
+        o.f.p = nullptr;
+        o.tp.hi = hi; o.tp.lo = lo; o.tp.ld = tc_pitch(C, tc_mode());
+    }
+    return o;
+}
+
+void Engine::adain_fwd_to(const Act& x, const double* sums, const Stats& s, const float* gb, int act, float slope,
+                          const float* alpha, const Opnd& out, cudaStream_t st) {
+    PlaneOut po;
+    po.hi = const_cast<void*>(out.tp.hi); po.lo = const_cast<void*>(out.tp.lo); po.ld = out.tp.ld; po.mode = tc_mode();
+    adain_act_fwd_v(x, sums, 1e-5f, s.mean, s.rstd, gb, act, slope, alpha, out.f.p ? &out.f : nullptr,
+                    out.tp.hi ? &po : nullptr, st);
+}
+
+void Engine::adain_bwd_to(const Act& x, const Stats& s, const float* gb, int act, float slope, const float* alpha,
+                          const Act& dy, const Opnd& out, const Act* skip, double* colsum, float* dgb, float* dalpha,
+                          cudaStream_t st) {
+    PlaneOut po;
+    po.hi = const_cast<void*>(out.tp.hi); po.lo = const_cast<void*>(out.tp.lo); po.ld = out.tp.ld; po.mode = tc_mode();
+    adain_act_bwd_v(x, s.mean, s.rstd, gb, act, slope, alpha, dy, out.f.p ? &out.f : nullptr, skip,
+                    out.tp.hi ? &po : nullptr, colsum, dgb, dalpha, dacc_, st);
+}
+
+void Engine::tc_launch(const Act& x, const TcPlanes& xp, const float* whi, const float* wlo, int taps, int M,
+                       const Act& y, const float* bias, const Act* r, int r_shift, int p, int d, int No, int o_base,
+                       int orow_mul, int orow_off, float alpha, bool accum, double* stats, cudaStream_t st) {
     TcConvFwd a;
-    a.x.hi = tc_xh_; a.x.lo = tc_xl_; a.x.ld = tc_pitch(x.C, tc_mode());
+    a.x = xp;
     a.B = x.B; a.L_in = x.L; a.Ci = x.C;
     a.w.hi = whi; a.w.lo = wlo; a.w.ld = (int)round_up(x.C, 8);
     a.taps = taps; a.Co = M;
     a.p = p; a.d = d; a.No = No; a.o_base = o_base;
     a.y = y; a.bias = bias; a.r = r; a.r_shift = r_shift; a.orow_mul = orow_mul; a.orow_off = orow_off;
     a.alpha = alpha; a.accum = accum;
+    a.stats = stats;
     conv_fwd_tc(a, tc_mode(), st);
 }
 
 // ── conv wrappers
 void Engine::conv(const ConvP& c, const Act& x, const Act& y, const Act* r, int r_shift, float alpha, bool accum,
-                  cudaStream_t st) {
+                  cudaStream_t st, const TcPlanes* xp, double* stats) {
     ConvFwd a;
     a.x = x; a.y = y; a.wp = wp_fwd_[c.id]; a.bias = P(c.b); a.r = r; a.r_shift = r_shift;
     a.k = c.k; a.s = c.s; a.p = c.p; a.d = c.d;
     a.No = conv_out(x.L, c);
     a.alpha = alpha; a.accum = accum;
     if (a.No != y.L) fail("conv", "output length mismatch");
+    if (stats) BSML_CUDA(cudaMemsetAsync(stats, 0, sizeof(double) * 2 * (size_t)y.B * c.cout, st));
     if (tc_ok(c.cin, c.cout, c.s)) {
-        tc_planes(x, st);
+        const TcPlanes tp = xp ? *xp : tc_planes(x, st);
         const int id = prof_begin(PROF_CONV, 2.0 * c.cin * c.cout * c.k * (double)a.No * x.B, st);
-        tc_launch(x, tcw_fwd_hi_[c.id], tcw_fwd_lo_[c.id], c.k, c.cout, y, a.bias, r, r_shift, c.p, c.d, a.No, 0, 1, 0,
-                  alpha, accum, st);
+        tc_launch(x, tp, tcw_fwd_hi_[c.id], tcw_fwd_lo_[c.id], c.k, c.cout, y, a.bias, r, r_shift, c.p, c.d, a.No, 0,
+                  1, 0, alpha, accum, stats, st);
         prof_end(id, st);
         return;
     }
+    if (!x.p) fail("conv", "internal: fp32 operand missing on the CUDA-core path");
     const int id = prof_begin(PROF_CONV, 2.0 * c.cin * c.cout * c.k * (double)a.No * x.B, st);
     conv_fwd_simt(a, st);
     prof_end(id, st);
+    if (stats) norm_sums(y, stats, st);
 }
 
 // dx[j] = sum_{t,co} W[co,ci,t] dy[j + p - t*d]: a forward conv over dy with the
 // flipped, transposed weight and padding d*(k-1) - p (stride 1 only).
-void Engine::conv_dgrad(const ConvP& c, const Act& dy, const Act& dx, bool accum, cudaStream_t st) {
+void Engine::conv_dgrad(const ConvP& c, const Act& dy, const Act& dx, bool accum, cudaStream_t st,
+                        const TcPlanes* dyp) {
     if (c.s != 1) fail("conv_dgrad", "strided conv input gradients are not needed on this path");
     ConvFwd a;
     a.x = dy; a.y = dx; a.wp = wp_dgrad_[c.id];
@@ -433,42 +474,54 @@ void Engine::conv_dgrad(const ConvP& c, const Act& dy, const Act& dx, bool accum
     a.No = dx.L;
     a.accum = accum;
     if (tc_ok(c.cout, c.cin, 1)) {
-        tc_planes(dy, st);
+        const TcPlanes tp = dyp ? *dyp : tc_planes(dy, st);
         const int id = prof_begin(PROF_CONV, 2.0 * c.cin * c.cout * c.k * (double)dy.L * dy.B, st);
-        tc_launch(dy, tcw_dg_hi_[c.id], tcw_dg_lo_[c.id], c.k, c.cin, dx, nullptr, nullptr, 0, a.p, c.d, a.No, 0, 1, 0,
-                  1.f, accum, st);
+        tc_launch(dy, tp, tcw_dg_hi_[c.id], tcw_dg_lo_[c.id], c.k, c.cin, dx, nullptr, nullptr, 0, a.p, c.d, a.No, 0,
+                  1, 0, 1.f, accum, nullptr, st);
         prof_end(id, st);
         return;
     }
+    if (!dy.p) fail("conv_dgrad", "internal: fp32 operand missing on the CUDA-core path");
     const int id = prof_begin(PROF_CONV, 2.0 * c.cin * c.cout * c.k * (double)dy.L * dy.B, st);
     conv_fwd_simt(a, st);
     prof_end(id, st);
 }
 
-void Engine::conv_wgrad(const ConvP& c, const Act& dy, const Act& x, cudaStream_t st) {
+void Engine::conv_wgrad(const ConvP& c, const Act& dy, const Act& x, cudaStream_t st, const TcPlanes* dyp,
+                        const TcPlanes* xp, const double* bias_sum) {
     if (!grads_) return;
     if (tc_ok(c.cin, c.cout, c.s)) {
         const int mode = tc_mode();
-        make_act_planes(dy, mode, tc_yh_, tc_yl_, st);
-        make_act_planes(x, mode, tc_xh_, tc_xl_, st);
         TcConvWgrad w;
-        w.dy.hi = tc_yh_; w.dy.lo = tc_yl_; w.dy.ld = tc_pitch(dy.C, mode);
-        w.x.hi = tc_xh_; w.x.lo = tc_xl_; w.x.ld = tc_pitch(x.C, mode);
+        if (dyp) {
+            w.dy = *dyp;
+        } else {
+            if (!dy.p) fail("conv_wgrad", "internal: operand has neither fp32 data nor planes");
+            make_act_planes(dy, mode, tc_yh_, tc_yl_, st);
+            w.dy.hi = tc_yh_; w.dy.lo = tc_yl_; w.dy.ld = tc_pitch(dy.C, mode);
+        }
+        w.x = xp ? *xp : tc_planes(x, st);
         w.B = dy.B; w.Lo = dy.L; w.Co = dy.C; w.L_in = x.L; w.Ci = x.C;
         w.taps = c.k; w.p = c.p; w.d = c.d; w.dW = grads_ + c.w;
         const int id = prof_begin(PROF_WGRAD, 2.0 * c.cin * c.cout * c.k * (double)dy.L * dy.B, st);
         conv_wgrad_tc(w, mode, part_, part_floats_, st);
-        if (c.b >= 0) colsum(dy, grads_ + c.b, false, part_, st);
+        if (c.b >= 0) {
+            if (bias_sum) d2f(bias_sum, c.cout, grads_ + c.b, false, st);
+            else if (dy.p) colsum(dy, grads_ + c.b, false, part_, st);
+            else fail("conv_wgrad", "internal: bias gradient needs fp32 dy or its column sums");
+        }
         prof_end(id, st);
         return;
     }
+    if (!dy.p || !x.p) fail("conv_wgrad", "internal: fp32 operand missing on the CUDA-core path");
     ConvWgrad a;
     a.dy = dy; a.x = x; a.k = c.k; a.s = c.s; a.p = c.p; a.d = c.d;
     a.dW = grads_ + c.w;
-    a.db = G(c.b);
+    a.db = bias_sum ? nullptr : G(c.b);
     if (wgrad_partial_floats(a) > part_floats_) fail("conv_wgrad", "split-K partial buffer too small");
     const int id = prof_begin(PROF_WGRAD, 2.0 * c.cin * c.cout * c.k * (double)dy.L * dy.B, st);
     conv_wgrad_simt(a, part_, st);
+    if (bias_sum && c.b >= 0) d2f(bias_sum, c.cout, grads_ + c.b, false, st);
     prof_end(id, st);
 }
 
@@ -477,7 +530,8 @@ void Engine::conv_wgrad(const ConvP& c, const Act& dy, const Act& x, cudaStream_
 void Engine::convT(const UpP& u, const Act& x, const Act& y, int row_off, const Act* r, cudaStream_t st) {
     const int Lu = (x.L - 1) * u.s - 2 * u.p + u.k;
     const bool tc = tc_ok(u.cin, u.cout, 1);
-    if (tc) tc_planes(x, st);
+    TcPlanes tp;
+    if (tc) tp = tc_planes(x, st);
     for (int ph = 0; ph < u.s; ++ph) {
         const int kr = (u.k - ph + u.s - 1) / u.s;
         if (kr <= 0) continue;
@@ -492,8 +546,8 @@ void Engine::convT(const UpP& u, const Act& x, const Act& y, int row_off, const 
         a.orow_mul = u.s; a.orow_off = ph - u.p + row_off;
         const int id = prof_begin(PROF_CONV, 2.0 * u.cin * u.cout * kr * (double)a.No * x.B, st);
         if (tc)
-            tc_launch(x, tcw_up_hi_[u.id][ph], tcw_up_lo_[u.id][ph], kr, u.cout, y, a.bias, r, 0, a.p, 1, a.No, a.o_base,
-                      a.orow_mul, a.orow_off, 1.f, false, st);
+            tc_launch(x, tp, tcw_up_hi_[u.id][ph], tcw_up_lo_[u.id][ph], kr, u.cout, y, a.bias, r, 0, a.p, 1, a.No,
+                      a.o_base, a.orow_mul, a.orow_off, 1.f, false, nullptr, st);
         else
             conv_fwd_simt(a, st);
         prof_end(id, st);
@@ -587,47 +641,101 @@ void Engine::blk_bwd(const BlkP& w, BlkC& c, const Act& dY, const Act& dX, cudaS
 }
 
 // ── AdaINResBlock1 (kokoro_decoder_backward.cpp:287-376)
-void Engine::rb1_fwd(const RB1P& w, RB1C& c, const Act& x0, const Act& out, float out_alpha, bool out_accum,
-                     cudaStream_t st) {
+// Forward: each AdaIN+Snake writes its output straight into the operand form the
+// following conv reads (planes on the tensor-core path); the conv epilogue
+// returns the statistics of its output for the next AdaIN.
+void Engine::rb1_fwd(const RB1P& w, RB1C& c, const Act& x0, bool x0_stats, const Act& out, float out_alpha,
+                     bool out_accum, cudaStream_t st) {
     c.x[0] = x0;
-    // algorithmic bytes of one fused AdaIN+Snake forward: read x, write y
-    const double nb = 8.0 * (double)x0.numel();
+    const int L = c.L, C = w.C;
+    const bool tc = tc_ok(C, C, 1);   // every conv of the block is C -> C, stride 1
+    // bytes of one AdaIN+Snake forward: read x, write the conv operand
+    const double out_b = !tc ? 4.0 : tc_mode() == TC_BF16 ? 2.0 : 8.0;
+    const double nb = (4.0 + out_b) * (double)x0.numel();
     for (int i = 0; i < 3; ++i) {
         int id = prof_begin(PROF_NORM_FWD, nb, st);
-        stats_of(c.x[i], c.st1[i], st);
-        adain_act_fwd(c.x[i], c.st1[i].mean, c.st1[i].rstd, aff(w.a1[i]), ACT_SNAKE, 0.f, P(w.al1[i]), c.s1[i], st);
+        const double* sums = ssum_;   // from the previous conv's epilogue
+        if (i == 0) {
+            sums = nullptr;
+            if (!x0_stats) {
+                BSML_CUDA(cudaMemsetAsync(ssum_, 0, sizeof(double) * 2 * (size_t)B_ * C, st));
+                norm_sums(x0, ssum_, st);
+                sums = ssum_;
+            }
+        }
+        const Opnd s1 = operand(tc, L, C, S_[0], tc_xh_, tc_xl_);
+        adain_fwd_to(c.x[i], sums, c.st1[i], aff(w.a1[i]), ACT_SNAKE, 0.f, P(w.al1[i]), s1, st);
         prof_end(id, st);
-        conv(w.c1[i], c.s1[i], c.c1[i], nullptr, 0, 1.f, false, st);
+        conv(w.c1[i], s1.f, c.c1[i], nullptr, 0, 1.f, false, st, s1.planes(), ssum_);
         id = prof_begin(PROF_NORM_FWD, nb, st);
-        stats_of(c.c1[i], c.st2[i], st);
-        adain_act_fwd(c.c1[i], c.st2[i].mean, c.st2[i].rstd, aff(w.a2[i]), ACT_SNAKE, 0.f, P(w.al2[i]), c.s2[i], st);
+        const Opnd s2 = operand(tc, L, C, S_[0], tc_xh_, tc_xl_);
+        adain_fwd_to(c.c1[i], ssum_, c.st2[i], aff(w.a2[i]), ACT_SNAKE, 0.f, P(w.al2[i]), s2, st);
         prof_end(id, st);
         if (i < 2)
-            conv(w.c2[i], c.s2[i], c.x[i + 1], &c.x[i], 0, 1.f, false, st);
+            conv(w.c2[i], s2.f, c.x[i + 1], &c.x[i], 0, 1.f, false, st, s2.planes(), ssum_);
         else
-            conv(w.c2[i], c.s2[i], out, &c.x[i], 0, out_alpha, out_accum, st);
+            conv(w.c2[i], s2.f, out, &c.x[i], 0, out_alpha, out_accum, st, s2.planes(), nullptr);
     }
 }
 
+// Backward: the Snake outputs (conv operands of the weight gradients) are
+// recomputed from the cached inputs; each AdaIN backward writes its result as
+// the operand of the next input- and weight-gradient convs and sums its
+// columns for the preceding conv's bias gradient.
 void Engine::rb1_bwd(const RB1P& w, RB1C& c, const Act& dOut, float scale, const Act& D, cudaStream_t st) {
     const int L = c.L, C = w.C;
-    copy_act(dOut, D, st);
-    if (scale != 1.f) scale_act(D, scale, st);
-    Act t = view(S_[4], L, C), u = view(S_[5], L, C);
-    // algorithmic bytes of one fused AdaIN+Snake backward: read x and dy, write dx
-    const double nb = 12.0 * (double)D.numel();
+    const bool tc = tc_ok(C, C, 1);
+    const double pb = !tc ? 4.0 : tc_mode() == TC_BF16 ? 2.0 : 8.0;
+    const double n = (double)D.numel();
+    Act t = view(S_[4], L, C);
+    double* bs = grads_ ? bsum_ : nullptr;
+    auto zero_bs = [&]() {
+        if (bs) BSML_CUDA(cudaMemsetAsync(bs, 0, sizeof(double) * C, st));
+    };
+    // D = scale * dOut: fp32 (the running gradient), planes, bias sum of c2[2]
+    Opnd Dp;
+    Dp.f = D;
+    if (tc) { Dp.tp.hi = tc_dh_; Dp.tp.lo = tc_dl_; Dp.tp.ld = tc_pitch(C, tc_mode()); }
+    {
+        PlaneOut po;
+        po.hi = tc_dh_; po.lo = tc_dl_; po.ld = Dp.tp.ld; po.mode = tc_mode();
+        zero_bs();
+        scale_out_v(dOut, scale, &D, tc ? &po : nullptr, bs, st);
+    }
     for (int i = 2; i >= 0; --i) {
-        conv_dgrad(w.c2[i], D, t, false, st);
-        conv_wgrad(w.c2[i], D, c.s2[i], st);
-        int id = prof_begin(PROF_NORM_BWD, nb, st);
-        adain_act_bwd(c.c1[i], c.st2[i].mean, c.st2[i].rstd, aff(w.a2[i]), ACT_SNAKE, 0.f, P(w.al2[i]), t, u, nullptr,
-                      daff(w.a2[i]), G(w.al2[i]), dacc_, st);
+        conv_dgrad(w.c2[i], D, t, false, st, Dp.planes());
+        // s2[i] = Snake(AdaIN(c1[i])) again, as the weight-gradient operand
+        int id = prof_begin(PROF_NORM_BWD, (4.0 + pb) * n, st);
+        const Opnd s2 = operand(tc, L, C, S_[0], tc_xh_, tc_xl_);
+        adain_fwd_to(c.c1[i], nullptr, c.st2[i], aff(w.a2[i]), ACT_SNAKE, 0.f, P(w.al2[i]), s2, st);
         prof_end(id, st);
-        conv_dgrad(w.c1[i], u, t, false, st);
-        conv_wgrad(w.c1[i], u, c.s1[i], st);
-        id = prof_begin(PROF_NORM_BWD, nb, st);
-        adain_act_bwd(c.x[i], c.st1[i].mean, c.st1[i].rstd, aff(w.a1[i]), ACT_SNAKE, 0.f, P(w.al1[i]), t, D, &D,
-                      daff(w.a1[i]), G(w.al1[i]), dacc_, st);
+        conv_wgrad(w.c2[i], D, s2.f, st, Dp.planes(), s2.planes(), bs);
+        // u = gradient at conv1's output (operand of c1's dgrad and wgrad)
+        id = prof_begin(PROF_NORM_BWD, (8.0 + pb) * n, st);
+        const Opnd u = operand(tc, L, C, S_[5], tc_yh_, tc_yl_);
+        zero_bs();
+        adain_bwd_to(c.c1[i], c.st2[i], aff(w.a2[i]), ACT_SNAKE, 0.f, P(w.al2[i]), t, u, nullptr, bs, daff(w.a2[i]),
+                     G(w.al2[i]), st);
+        prof_end(id, st);
+        conv_dgrad(w.c1[i], u.f, t, false, st, u.planes());
+        id = prof_begin(PROF_NORM_BWD, (4.0 + pb) * n, st);
+        const Opnd s1 = operand(tc, L, C, S_[0], tc_xh_, tc_xl_);
+        adain_fwd_to(c.x[i], nullptr, c.st1[i], aff(w.a1[i]), ACT_SNAKE, 0.f, P(w.al1[i]), s1, st);
+        prof_end(id, st);
+        conv_wgrad(w.c1[i], u.f, s1.f, st, u.planes(), s1.planes(), bs);
+        // D += gradient at this pair's input: fp32, and (except for the last pair)
+        // planes and the bias sum of c2[i-1]
+        Opnd Dn = Dp;
+        double* bsn = nullptr;
+        if (i > 0) {
+            bsn = bs;
+            zero_bs();
+        } else {
+            Dn.tp = TcPlanes{};
+        }
+        id = prof_begin(PROF_NORM_BWD, (12.0 + 4.0 + (Dn.tp.hi ? pb : 0.0)) * n, st);
+        adain_bwd_to(c.x[i], c.st1[i], aff(w.a1[i]), ACT_SNAKE, 0.f, P(w.al1[i]), t, Dn, &D, bsn, daff(w.a1[i]),
+                     G(w.al1[i]), st);
         prof_end(id, st);
     }
 }
@@ -703,7 +811,7 @@ void Engine::forward(int B, int T, const float* params, const float* asr, const 
         const UpP& u = lay_.ups[i];
         leaky_fwd(s.x_in, 0.1f, s.a, st);
         conv(lay_.noise[i], har_, s.xsrc, nullptr, 0, 1.f, false, st);
-        rb1_fwd(lay_.nres[i], s.noise, s.xsrc, s.src, 1.f, false, st);
+        rb1_fwd(lay_.nres[i], s.noise, s.xsrc, false, s.src, 1.f, false, st);
         if (i == U - 1) {
             // u written to rows 1..Lu, row 0 = reflection of row 1 (pad1d mode 1), then m = u + src
             convT(u, s.a, s.m, 1, nullptr, st);
@@ -713,7 +821,7 @@ void Engine::forward(int B, int T, const float* params, const float* asr, const 
             convT(u, s.a, s.m, 0, &s.src, st);
         }
         for (int j = 0; j < K; ++j)
-            rb1_fwd(lay_.rbs[i * K + j], s.res[j], s.m, s.out, 1.f / (float)K, j > 0, st);
+            rb1_fwd(lay_.rbs[i * K + j], s.res[j], s.m, j > 0, s.out, 1.f / (float)K, j > 0, st);
     }
     // spectral head (kokoro_decoder_backward.cpp:378-410)
     const Act& xlast = stc_[U - 1].out;

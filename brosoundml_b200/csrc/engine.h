@@ -61,7 +61,10 @@ class Engine {
     };
     struct Stats { float* mean = nullptr; float* rstd = nullptr; };
     struct BlkC { Act x, r, pooled, c1, n2, sc; Stats s1, s2; int Lin = 0, Lout = 0; };
-    struct RB1C { Act x[3], s1[3], c1[3], s2[3]; Stats st1[3], st2[3]; int L = 0; };
+    // AdaINResBlock1 caches: block inputs x[i] and conv1 outputs c1[i] with
+    // their statistics. The Snake outputs are not kept: the backward recomputes
+    // them from x[i] / c1[i] and the statistics.
+    struct RB1C { Act x[3], c1[3]; Stats st1[3], st2[3]; int L = 0; };
     struct StageC { Act x_in, a, xsrc, src, m, out; RB1C noise; std::vector<RB1C> res; int Lin = 0, Lu = 0, Lx = 0; };
 
     void plan(Planner& P);
@@ -78,10 +81,32 @@ class Engine {
     const float* P(int64_t off) const { return off >= 0 ? params_ + off : nullptr; }
     float* G(int64_t off) const { return (grads_ && off >= 0) ? grads_ + off : nullptr; }
 
+    // A conv operand: the fp32 channels-last view (p may be null when only
+    // planes exist; the geometry is always set) and / or tensor-core planes.
+    struct Opnd {
+        Act f;
+        TcPlanes tp;
+        const TcPlanes* planes() const { return tp.hi ? &tp : nullptr; }
+    };
+    // Output buffer for an elementwise producer feeding a conv: operand planes
+    // (hi, lo) when that conv runs on the tensor cores, else fp32 in fbuf.
+    Opnd operand(bool tc, int L, int C, const Act& fbuf, void* hi, void* lo) const;
+    void adain_fwd_to(const Act& x, const double* sums, const Stats& s, const float* gb, int act, float slope,
+                      const float* alpha, const Opnd& out, cudaStream_t st);
+    void adain_bwd_to(const Act& x, const Stats& s, const float* gb, int act, float slope, const float* alpha,
+                      const Act& dy, const Opnd& out, const Act* skip, double* colsum, float* dgb, float* dalpha,
+                      cudaStream_t st);
+
+    // Conv wrappers. xp / dyp: the operand's planes when a producer already
+    // wrote them. stats: per-(b, co) sums of the output for the next norm
+    // (zeroed here). bias_sum: the bias gradient as per-channel double sums
+    // from the producer of dy (else it is summed from dy here).
     void conv(const ConvP& c, const Act& x, const Act& y, const Act* r, int r_shift, float alpha, bool accum,
-              cudaStream_t st);
-    void conv_dgrad(const ConvP& c, const Act& dy, const Act& dx, bool accum, cudaStream_t st);
-    void conv_wgrad(const ConvP& c, const Act& dy, const Act& x, cudaStream_t st);
+              cudaStream_t st, const TcPlanes* xp = nullptr, double* stats = nullptr);
+    void conv_dgrad(const ConvP& c, const Act& dy, const Act& dx, bool accum, cudaStream_t st,
+                    const TcPlanes* dyp = nullptr);
+    void conv_wgrad(const ConvP& c, const Act& dy, const Act& x, cudaStream_t st, const TcPlanes* dyp = nullptr,
+                    const TcPlanes* xp = nullptr, const double* bias_sum = nullptr);
     void convT(const UpP& u, const Act& x, const Act& y, int row_off, const Act* r, cudaStream_t st);
     void convT_dgrad(const UpP& u, const Act& dy, const Act& dx, cudaStream_t st);
     void convT_wgrad(const UpP& u, const Act& dy, const Act& x, cudaStream_t st);
@@ -89,8 +114,10 @@ class Engine {
 
     void blk_fwd(const BlkP& w, BlkC& c, const Act& y, cudaStream_t st);
     void blk_bwd(const BlkP& w, BlkC& c, const Act& dY, const Act& dX, cudaStream_t st);
-    void rb1_fwd(const RB1P& w, RB1C& c, const Act& x0, const Act& out, float out_alpha, bool out_accum,
-                 cudaStream_t st);
+    // x0_stats: the statistics of x0 are already in c.st1[0] (shared by the
+    // resblocks of one stage, which all read the same input)
+    void rb1_fwd(const RB1P& w, RB1C& c, const Act& x0, bool x0_stats, const Act& out, float out_alpha,
+                 bool out_accum, cudaStream_t st);
     // returns the gradient w.r.t. the block input in `D` (scratch, may alias nothing else)
     void rb1_bwd(const RB1P& w, RB1C& c, const Act& dOut, float scale, const Act& D, cudaStream_t st);
 
@@ -121,12 +148,14 @@ class Engine {
     float* tc_xl_ = nullptr;
     float* tc_yh_ = nullptr;          // second operand's planes (weight gradients)
     float* tc_yl_ = nullptr;
+    float* tc_dh_ = nullptr;          // planes of the running resblock input gradient
+    float* tc_dl_ = nullptr;
     int tc_mode() const { return math_ == BSML_MATH_BF16 ? TC_BF16 : TC_TF32X3; }
     bool tc_ok(int K, int M, int s) const { return math_ != BSML_MATH_FP32_SIMT && s == 1 && K >= 32 && M >= 64; }
-    void tc_planes(const Act& x, cudaStream_t st);
-    void tc_launch(const Act& x, const float* whi, const float* wlo, int taps, int M, const Act& y, const float* bias,
-                   const Act* r, int r_shift, int p, int d, int No, int o_base, int orow_mul, int orow_off,
-                   float alpha, bool accum, cudaStream_t st);
+    TcPlanes tc_planes(const Act& x, cudaStream_t st);   // x -> planes in tc_xh_ / tc_xl_
+    void tc_launch(const Act& x, const TcPlanes& xp, const float* whi, const float* wlo, int taps, int M,
+                   const Act& y, const float* bias, const Act* r, int r_shift, int p, int d, int No, int o_base,
+                   int orow_mul, int orow_off, float alpha, bool accum, double* stats, cudaStream_t st);
     FcRow* fc_tab_ = nullptr;                     // device
     int* fc_row_entry_ = nullptr;                 // device
     int fc_rows_ = 0;
@@ -162,6 +191,8 @@ class Engine {
     float* hs_src_ = nullptr;
     double* hs_phase_ = nullptr;
     double* dacc_ = nullptr;          // reduction scratch (B * max C * 3)
+    double* ssum_ = nullptr;          // per-(b, c) output sums of the last conv (B * max C * 2)
+    double* bsum_ = nullptr;          // bias-gradient column sums (max C)
     float* part_ = nullptr;           // split-K partials
     int64_t part_floats_ = 0;
     float* fc_part_ = nullptr;

@@ -56,8 +56,31 @@ void pack_convT_dgrad(const float* W, int Ci, int Co, int k, float* wp, cudaStre
 // ── normalisation and activations ────────────────────────────────────────────
 enum Activation { ACT_NONE = 0, ACT_LEAKY = 1, ACT_SNAKE = 2 };
 
+// Operand-plane output of an elementwise kernel, for the tensor-core convs:
+// planes share the (B, L) geometry of the fp32 tensor with row pitch `ld`
+// (mode 1: tf32 hi + fp32 lo planes, mode 0: one bf16 plane).
+struct PlaneOut { void* hi = nullptr; void* lo = nullptr; int ld = 0; int mode = 1; };
+
+// sums[(b*C + c)*2 + {0,1}] += sum_l x, sum_l x^2 (double; the caller zeroes sums)
+void norm_sums(const Act& x, double* sums, cudaStream_t st);
 // acc: (B*C*2) doubles, zeroed inside. mean/rstd: (B*C) floats.
 void in_stats(const Act& x, float eps, double* acc, float* mean, float* rstd, cudaStream_t st);
+// AdaIN + activation forward. With sums (norm_sums layout) the statistics come
+// from the sums and mean / rstd are written; with sums == nullptr they are read.
+// Writes y (fp32, nullable) and / or operand planes (nullable).
+void adain_act_fwd_v(const Act& x, const double* sums, float eps, float* mean, float* rstd, const float* gb, int act,
+                     float slope, const float* alpha, const Act* y, const PlaneOut* planes, cudaStream_t st);
+// Backward of adain_act_fwd_v. out = dx (+ skip; dx may alias skip) goes to dx
+// (nullable) and / or planes (nullable); colsum[c] += sum over (b, l) of out
+// (double, nullable, not zeroed here). dgb, dalpha as in adain_act_bwd.
+void adain_act_bwd_v(const Act& x, const float* mean, const float* rstd, const float* gb, int act, float slope,
+                     const float* alpha, const Act& dy, const Act* dx, const Act* skip, const PlaneOut* planes,
+                     double* colsum, float* dgb, float* dalpha, double* acc, cudaStream_t st);
+// out = alpha * src -> dst (nullable), planes (nullable), colsum (nullable, added to)
+void scale_out_v(const Act& src, float alpha, const Act* dst, const PlaneOut* planes, double* colsum,
+                 cudaStream_t st);
+// dst[i] (+)= (float) src[i]
+void d2f(const double* src, int n, float* dst, bool accum, cudaStream_t st);
 // y = act((1 + gamma) * (x - mean) * rstd + beta); gb = [B][2C] (gamma ; beta)
 void adain_act_fwd(const Act& x, const float* mean, const float* rstd, const float* gb, int act, float slope,
                    const float* alpha, const Act& y, cudaStream_t st);
