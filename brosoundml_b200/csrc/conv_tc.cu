@@ -3,9 +3,11 @@
 // Forward-like form (conv fwd, conv input gradient with flipped/transposed
 // weights, ConvTranspose1d stride phases):
 //   D[co, o] = sum_{t, ci} W_t[co, ci] * X[b, (o + o_base) + t*d - p, ci]
-// K runs over (tap, 128-byte chunk of input channels); both operands are
-// K-major (channels contiguous), so one TMA box per operand plane per K step,
-// and a tap shift only moves the activation box's row coordinate.
+// Persistent kernel, one 128 (co) x 256 (positions) fp32 tile at a time. K runs
+// over 128-byte chunks of input channels; for each chunk the CTA loads one
+// activation window of 256 + (taps-1)*d rows and reuses it for every tap: tap
+// t's operand is the same window shifted by t*d rows (a descriptor offset, not
+// a new load). Only the per-tap weight tiles stream through their own ring.
 //
 // Weight-gradient form (stride-1 convs):
 //   D[co, ci] (tap t) = sum_{b, o} dY[b, o, co] * X[b, o + t*d - p, ci]
@@ -13,16 +15,17 @@
 // rows, channels contiguous), staged as 128-byte-wide column blocks. Split-K
 // over position chunks writes fp32 partial tiles, reduced in double afterwards.
 //
-// One CTA computes a 128 x 128 fp32 tile in TMEM (M = output channels on the
-// TMEM lanes). Warp roles (192 threads): warp 0 issues TMA, warp 1 owns TMEM
-// and one thread issues tcgen05.mma, warps 2-5 read the accumulator (each warp
-// its 32-lane quarter) and run the epilogue.
+// Warp roles: warp 0 issues TMA, warp 1 owns TMEM and one thread issues
+// tcgen05.mma, the remaining warps read the accumulator (each warp its 32-lane
+// quarter of TMEM) and run the epilogue.
 //
 // Promotion (TF32x3): the tensor core's in-TMEM fp32 accumulation is not
-// round-to-nearest, and its error grows with K. With PROMOTE the MMA warp
-// alternates between two TMEM accumulators, PG K steps each, and the epilogue
-// warps fold every finished partial into fp32 registers, so each TMEM sum spans
-// only 12*PG instructions and the long sum is formed with ordinary fp32 adds.
+// round-to-nearest, and its error grows with K. The MMA warp alternates between
+// two TMEM accumulators, PG K steps each, and the epilogue warps fold every
+// finished partial into fp32 registers, so each TMEM sum spans only 12*PG
+// instructions and the long sum is formed with ordinary fp32 adds. In the
+// persistent forward kernel the same two buffers carry on into the next tile,
+// so the epilogue's stores of one tile overlap the next tile's MMAs.
 #include <cuda_bf16.h>
 #include <cudaTypedefs.h>
 
@@ -40,66 +43,326 @@ namespace {
 
 __device__ int g_tc_err = 0;
 
-constexpr int BM = 128, BN = 128, TILE_BYTES = 16384;
+constexpr int TILE_BYTES = 16384;   // 128 rows x 128 bytes
 // promoted accumulation: K steps summed in TMEM before the epilogue folds them into registers
 constexpr int PG = 2;
+constexpr int SMEM_OPTIN = 232448;  // opt-in dynamic shared memory per block on sm_100
 
+__device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
+    return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
+}
+
+// ── forward-like kernel ──────────────────────────────────────────────────────
 template <bool TF32>
-struct Cfg {
-    static constexpr int S = TF32 ? 3 : 6;            // pipeline stages
-    static constexpr int TILES = TF32 ? 4 : 2;        // A_hi, A_lo, B_hi, B_lo | A, B
-    static constexpr int BKE = TF32 ? 32 : 64;        // elements per 128-byte row
-    static constexpr int STAGE_BYTES = TILES * TILE_BYTES;
-    static constexpr int SMEM = S * STAGE_BYTES + 1024 + 256;
-    // weight-grad: positions (K rows) per stage; one MMA consumes 32 bytes of K
-    // = 8 (tf32) or 16 (bf16) rows; 128-byte column blocks per 128-wide operand
-    static constexpr int KROWS = TF32 ? 32 : 64;
-    static constexpr int MN_BLOCKS = 128 / BKE;
+struct FCfg {
+    static constexpr int BKE = TF32 ? 32 : 64;            // channels per 128-byte row
+    static constexpr int PLANES = TF32 ? 2 : 1;
+    static constexpr int NPOS = 256;                       // positions per tile (MMA N)
+    static constexpr int WT_BYTES = PLANES * TILE_BYTES;   // one weight stage: 128 co x 128 B per plane
+    static constexpr int NEPI = 8;                         // epilogue warps: 4 lane quarters x 2 column halves
+    static constexpr int THREADS = 64 + NEPI * 32;
+    static constexpr int MAX_SW = 8;
 };
 
-struct Args {
-    // forward-like
+struct FArgs {
     int No, o_base, p, d, taps, kchunks, Co;
+    int n_co, n_pt, n_tiles;
+    int wbox;        // rows per window box; a window is two boxes (2 * wbox rows)
+    int win_bytes;   // one window stage, all planes
+    int sw;          // weight stages
     float* y; int64_t y_bs; int y_ld; int orow_mul, orow_off, y_rows;
     const float* bias;
     const float* r; int64_t r_bs; int r_ld; int r_shift;
     float alpha; int accum;
     double* stats;   // per-(b, co) sum and sum of squares of the stored outputs (nullable)
-    // weight-grad: Ci tiles, chunks per clip, total chunks, chunks per split, Ci
-    int n_ci_tiles, chunks_pc, chunks_total, chunks_per_split, Ci;
+};
+
+// 320 threads = 10 warps, so one SM sub-partition holds 3 of them: 168
+// registers per thread at most (3 x 32 x 168 <= 16384).
+template <bool TF32>
+__global__ void __launch_bounds__(FCfg<TF32>::THREADS, 1)
+    conv_fwd_tc_kernel(const __grid_constant__ CUtensorMap mWh, const __grid_constant__ CUtensorMap mWl,
+                       const __grid_constant__ CUtensorMap mXh, const __grid_constant__ CUtensorMap mXl,
+                       const FArgs a) {
+    using F = FCfg<TF32>;
+    constexpr int NP = F::NPOS;
+    constexpr uint32_t TCOLS = 2 * NP;   // two promotion buffers of NP fp32 columns
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = align1024(smem_raw);
+    uint8_t* win = smem;                          // [2 stages][PLANES][2 * wbox rows][128 B]
+    uint8_t* wst = smem + 2 * a.win_bytes;        // [sw][PLANES][128 rows][128 B]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(wst + a.sw * F::WT_BYTES);
+    uint64_t* wfull = bars;                       // [MAX_SW]
+    uint64_t* wempty = bars + F::MAX_SW;          // [MAX_SW]
+    uint64_t* xfull = bars + 2 * F::MAX_SW;       // [2]
+    uint64_t* xempty = xfull + 2;                 // [2]
+    uint64_t* accf = xempty + 2;                  // [2]
+    uint64_t* acce = accf + 2;                    // [2]
+    uint64_t* mdone = acce + 2;
+    uint32_t* tslot = reinterpret_cast<uint32_t*>(mdone + 1);
+    int* err = &g_tc_err;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n_iters = a.taps * a.kchunks;          // K steps per tile
+    const int n_groups = (n_iters + PG - 1) / PG;    // promotion groups per tile
+    const int plane_bytes = 2 * a.wbox * 128;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < a.sw; ++s) {
+            tc::mbar_init(&wfull[s], 1);
+            tc::mbar_init(&wempty[s], 1);
+        }
+        for (int s = 0; s < 2; ++s) {
+            tc::mbar_init(&xfull[s], 1);
+            tc::mbar_init(&xempty[s], 1);
+            tc::mbar_init(&accf[s], 1);
+            tc::mbar_init(&acce[s], F::NEPI);
+        }
+        tc::mbar_init(mdone, 1);
+        tc::fence_barrier_init();
+        tc::prefetch_tmap(&mWh);
+        tc::prefetch_tmap(&mXh);
+        if (TF32) {
+            tc::prefetch_tmap(&mWl);
+            tc::prefetch_tmap(&mXl);
+        }
+    }
+    if (warp == 1) {
+        tc::tmem_alloc(tslot, TCOLS);
+        tc::tmem_relinquish();
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+    const uint32_t tbase = *tslot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ── TMA producer: per chunk one window, then one weight tile per tap
+            int kit = 0, cw = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; ok && tile < a.n_tiles; tile += gridDim.x) {
+                const int ct = tile % a.n_co, rest = tile / a.n_co;
+                const int pt = rest % a.n_pt, b = rest / a.n_pt;
+                const int m0 = ct * 128, row0 = pt * NP + a.o_base - a.p;
+                for (int c = 0; ok && c < a.kchunks; ++c) {
+                    const int kx = c * F::BKE;
+                    const int xs = cw & 1;
+                    if (!tc::mbar_wait(&xempty[xs], ((cw >> 1) & 1) ^ 1, err, tc::TC_ERR_WAIT_EMPTY)) {
+                        ok = false;
+                        break;
+                    }
+                    uint8_t* wb = win + xs * a.win_bytes;
+                    tc::mbar_arrive_expect_tx(&xfull[xs], a.win_bytes);
+                    tc::tma_load_3d(wb, &mXh, &xfull[xs], kx, row0, b);
+                    tc::tma_load_3d(wb + a.wbox * 128, &mXh, &xfull[xs], kx, row0 + a.wbox, b);
+                    if (TF32) {
+                        tc::tma_load_3d(wb + plane_bytes, &mXl, &xfull[xs], kx, row0, b);
+                        tc::tma_load_3d(wb + plane_bytes + a.wbox * 128, &mXl, &xfull[xs], kx, row0 + a.wbox, b);
+                    }
+                    ++cw;
+                    for (int t = 0; t < a.taps; ++t) {
+                        const int s = kit % a.sw;
+                        if (!tc::mbar_wait(&wempty[s], ((kit / a.sw) & 1) ^ 1, err, tc::TC_ERR_WAIT_EMPTY)) {
+                            ok = false;
+                            break;
+                        }
+                        uint8_t* ws = wst + s * F::WT_BYTES;
+                        tc::mbar_arrive_expect_tx(&wfull[s], F::WT_BYTES);
+                        tc::tma_load_3d(ws, &mWh, &wfull[s], kx, m0, t);
+                        if (TF32) tc::tma_load_3d(ws + TILE_BYTES, &mWl, &wfull[s], kx, m0, t);
+                        ++kit;
+                    }
+                }
+            }
+            if (!ok) {   // drain: copies issued into the rings may still be in flight
+                for (int i = kit - a.sw < 0 ? 0 : kit - a.sw; i < kit; ++i)
+                    tc::mbar_wait(&wfull[i % a.sw], (i / a.sw) & 1, nullptr, tc::TC_ERR_DRAIN);
+                for (int i = cw - 2 < 0 ? 0 : cw - 2; i < cw; ++i)
+                    tc::mbar_wait(&xfull[i & 1], (i >> 1) & 1, nullptr, tc::TC_ERR_DRAIN);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ── MMA issuer
+            constexpr uint32_t idesc = tc::make_idesc(TF32 ? 2u : 1u, 0u, 0u, 128, NP);
+            int kit = 0, cw = 0, G = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; ok && tile < a.n_tiles; tile += gridDim.x) {
+                for (int c = 0; ok && c < a.kchunks; ++c) {
+                    const int xs = cw & 1;
+                    if (!tc::mbar_wait(&xfull[xs], (cw >> 1) & 1, err, tc::TC_ERR_WAIT_FULL)) {
+                        ok = false;
+                        break;
+                    }
+                    tc::tc_fence_after();
+                    const uint32_t xh = tc::smem_u32(win + xs * a.win_bytes);
+                    const uint32_t xl = xh + plane_bytes;
+                    for (int t = 0; t < a.taps; ++t) {
+                        const int li = c * a.taps + t;
+                        const bool g_first = (li % PG) == 0;
+                        const bool g_last = (li % PG) == PG - 1 || li == n_iters - 1;
+                        const int g = G + li / PG;
+                        const int buf = g & 1;
+                        if (g_first && g >= 2 &&
+                            !tc::mbar_wait(&acce[buf], ((g >> 1) - 1) & 1, err, tc::TC_ERR_WAIT_ACC)) {
+                            ok = false;
+                            break;
+                        }
+                        const int s = kit % a.sw;
+                        if (!tc::mbar_wait(&wfull[s], (kit / a.sw) & 1, err, tc::TC_ERR_WAIT_FULL)) {
+                            ok = false;
+                            break;
+                        }
+                        tc::tc_fence_after();
+                        const uint32_t wa = tc::smem_u32(wst + s * F::WT_BYTES);
+                        const uint32_t roff = (uint32_t)(t * a.d) * 128u;   // tap shift inside the window
+                        const uint32_t d_tmem = tbase + (uint32_t)(buf * NP);
+#pragma unroll
+                        for (int kk = 0; kk < 4; ++kk) {
+                            const uint64_t dAh = tc::desc_kmajor_sw128(wa + kk * 32);
+                            const uint64_t dBh = tc::desc_kmajor_sw128(xh + roff + kk * 32);
+                            const uint32_t acc = (g_first && kk == 0) ? 0u : 1u;
+                            tc::umma<TF32>(d_tmem, dAh, dBh, idesc, acc);
+                            if (TF32) {
+                                const uint64_t dAl = tc::desc_kmajor_sw128(wa + TILE_BYTES + kk * 32);
+                                const uint64_t dBl = tc::desc_kmajor_sw128(xl + roff + kk * 32);
+                                tc::umma<TF32>(d_tmem, dAh, dBl, idesc, 1u);
+                                tc::umma<TF32>(d_tmem, dAl, dBh, idesc, 1u);
+                            }
+                        }
+                        tc::umma_commit(&wempty[s]);   // frees the weight stage once these MMAs have read it
+                        ++kit;
+                        if (g_last) tc::umma_commit(&accf[buf]);
+                    }
+                    if (!ok) break;
+                    tc::umma_commit(&xempty[xs]);      // frees the window after its last tap
+                    ++cw;
+                }
+                G += n_groups;
+            }
+            // every issued MMA has completed before TMEM is released
+            tc::umma_commit(mdone);
+            tc::mbar_wait(mdone, 0, nullptr, tc::TC_ERR_DRAIN);
+        }
+    } else {
+        // ── epilogue: warp (q, h) folds lanes 32q..32q+31, columns 128h..128h+127
+        const int ew = warp - 2;
+        const int q = warp & 3;   // the TMEM lane quarter this warp may access
+        const int h = ew >> 2;
+        const uint32_t trow = tbase + ((uint32_t)(q * 32) << 16) + (uint32_t)(h * 128);
+        int G = 0;
+        bool ok = true;
+        for (int tile = blockIdx.x; ok && tile < a.n_tiles; tile += gridDim.x) {
+            const int ct = tile % a.n_co, rest = tile / a.n_co;
+            const int pt = rest % a.n_pt, b = rest / a.n_pt;
+            const int mrow = ct * 128 + q * 32 + lane;   // co
+            const int o0 = pt * NP + h * 128;
+            float R[128];
+#pragma unroll
+            for (int j = 0; j < 128; ++j) R[j] = 0.f;
+            for (int gi = 0; gi < n_groups; ++gi) {
+                const int g = G + gi, buf = g & 1;
+                bool w = true;
+                if (lane == 0) w = tc::mbar_wait(&accf[buf], (g >> 1) & 1, err, tc::TC_ERR_WAIT_ACC);
+                ok = __shfl_sync(0xffffffffu, w ? 1 : 0, 0) != 0;
+                if (!ok) break;
+                tc::tc_fence_after();
+#pragma unroll
+                for (int c16 = 0; c16 < 128; c16 += 16) {
+                    uint32_t v[16];
+                    tc::tmem_ld16_nowait(trow + (uint32_t)(buf * NP + c16), v);
+                    tc::tmem_wait_ld();
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) R[c16 + j] += __uint_as_float(v[j]);
+                }
+                tc::tc_fence_before();
+                __syncwarp();
+                if (lane == 0) tc::mbar_arrive(&acce[buf]);
+            }
+            G += n_groups;
+            if (!ok || *(volatile int*)err != tc::TC_OK) break;
+            if (mrow < a.Co) {
+                const float bv = a.bias ? a.bias[mrow] : 0.f;
+                double s1 = 0.0, s2 = 0.0;
+#pragma unroll
+                for (int j = 0; j < 128; ++j) {
+                    const int o = o0 + j;
+                    if (o >= a.No) break;
+                    const int row = (o + a.o_base) * a.orow_mul + a.orow_off;
+                    if (row < 0 || row >= a.y_rows) continue;
+                    float val = R[j] + bv;
+                    if (a.r) val += a.r[(int64_t)b * a.r_bs + (int64_t)(row >> a.r_shift) * a.r_ld + mrow];
+                    val *= a.alpha;
+                    float* yp = a.y + (int64_t)b * a.y_bs + (int64_t)row * a.y_ld + mrow;
+                    if (a.accum) val += *yp;
+                    *yp = val;
+                    s1 += val;
+                    s2 = fma((double)val, (double)val, s2);
+                }
+                if (a.stats) {
+                    atomicAdd(&a.stats[((int64_t)b * a.Co + mrow) * 2], s1);
+                    atomicAdd(&a.stats[((int64_t)b * a.Co + mrow) * 2 + 1], s2);
+                }
+            }
+        }
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        __syncwarp();
+        tc::tc_fence_after();
+        tc::tmem_dealloc(tbase, TCOLS);
+    }
+}
+
+// ── weight-gradient kernel ───────────────────────────────────────────────────
+constexpr int BM = 128, BN = 128;
+
+template <bool TF32>
+struct WCfg {
+    static constexpr int S = TF32 ? 3 : 6;            // pipeline stages
+    static constexpr int TILES = TF32 ? 4 : 2;        // A_hi, A_lo, B_hi, B_lo | A, B
+    static constexpr int BKE = TF32 ? 32 : 64;        // elements per 128-byte row
+    static constexpr int STAGE_BYTES = TILES * TILE_BYTES;
+    static constexpr int SMEM = S * STAGE_BYTES + 1024 + 256;
+    // positions (K rows) per stage; one MMA consumes 32 bytes of K = 8 (tf32)
+    // or 16 (bf16) rows; 128-byte column blocks per 128-wide operand
+    static constexpr int KROWS = TF32 ? 32 : 64;
+    static constexpr int MN_BLOCKS = 128 / BKE;
+};
+
+struct WArgs {
+    int taps, p, d, Co, Ci;
+    // Ci tiles, chunks per clip, total chunks, chunks per split
+    int n_ci_tiles, chunks_pc, chunks_total, chunks_per_split;
     float* part;   // [split][tap][Co][Ci]
 };
 
-template <bool TF32, bool PROMOTE, bool WGRAD>
+template <bool TF32>
 __global__ void __launch_bounds__(192, 1)
-    conv_tc_kernel(const __grid_constant__ CUtensorMap mAh, const __grid_constant__ CUtensorMap mAl,
-                   const __grid_constant__ CUtensorMap mBh, const __grid_constant__ CUtensorMap mBl, const Args a) {
-    using C = Cfg<TF32>;
-    constexpr uint32_t TCOLS = PROMOTE ? 2 * BN : BN;
+    conv_wgrad_tc_kernel(const __grid_constant__ CUtensorMap mAh, const __grid_constant__ CUtensorMap mAl,
+                         const __grid_constant__ CUtensorMap mBh, const __grid_constant__ CUtensorMap mBl,
+                         const WArgs a) {
+    using C = WCfg<TF32>;
+    constexpr uint32_t TCOLS = 2 * BN;
     extern __shared__ uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* smem = align1024(smem_raw);
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::S * C::STAGE_BYTES);
     uint64_t* empty = full + C::S;
     uint64_t* accf = empty + C::S;   // [2]
     uint64_t* acce = accf + 2;       // [2]
-    uint32_t* tslot = reinterpret_cast<uint32_t*>(acce + 2);
+    uint64_t* mdone = acce + 2;
+    uint32_t* tslot = reinterpret_cast<uint32_t*>(mdone + 1);
     int* err = &g_tc_err;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    int m0, n0, b = 0, t = 0, it0 = 0, n_iters;
-    if constexpr (WGRAD) {
-        m0 = blockIdx.x * BM;                              // co
-        t = blockIdx.y / a.n_ci_tiles;
-        n0 = (blockIdx.y - t * a.n_ci_tiles) * BN;         // ci
-        it0 = blockIdx.z * a.chunks_per_split;
-        const int it1 = min(a.chunks_total, it0 + a.chunks_per_split);
-        n_iters = it1 > it0 ? it1 - it0 : 0;
-    } else {
-        n0 = blockIdx.x * BN;                              // positions
-        m0 = blockIdx.y * BM;                              // co
-        b = blockIdx.z;
-        n_iters = a.taps * a.kchunks;
-    }
+    const int m0 = blockIdx.x * BM;                              // co
+    const int t = blockIdx.y / a.n_ci_tiles;
+    const int n0 = (blockIdx.y - t * a.n_ci_tiles) * BN;         // ci
+    const int it0 = blockIdx.z * a.chunks_per_split;
+    const int it1 = min(a.chunks_total, it0 + a.chunks_per_split);
+    const int n_iters = it1 > it0 ? it1 - it0 : 0;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < C::S; ++s) {
@@ -110,6 +373,7 @@ __global__ void __launch_bounds__(192, 1)
         tc::mbar_init(&accf[1], 1);
         tc::mbar_init(&acce[0], 4);
         tc::mbar_init(&acce[1], 4);
+        tc::mbar_init(mdone, 1);
         tc::fence_barrier_init();
         tc::prefetch_tmap(&mAh);
         tc::prefetch_tmap(&mBh);
@@ -138,30 +402,18 @@ __global__ void __launch_bounds__(192, 1)
             uint8_t* st = smem + s * C::STAGE_BYTES;
             uint8_t* sB = st + (TF32 ? 2 : 1) * TILE_BYTES;
             tc::mbar_arrive_expect_tx(&full[s], C::STAGE_BYTES);
-            if constexpr (WGRAD) {
-                const int q = it0 + it;
-                const int bb = q / a.chunks_pc;
-                const int orow = (q - bb * a.chunks_pc) * C::KROWS;
-                const int xrow = orow + t * a.d - a.p;
+            const int q = it0 + it;
+            const int bb = q / a.chunks_pc;
+            const int orow = (q - bb * a.chunks_pc) * C::KROWS;
+            const int xrow = orow + t * a.d - a.p;
 #pragma unroll
-                for (int j = 0; j < C::MN_BLOCKS; ++j) {
-                    const int boff = j * C::KROWS * 128;
-                    tc::tma_load_3d(st + boff, &mAh, &full[s], m0 + j * C::BKE, orow, bb);
-                    tc::tma_load_3d(sB + boff, &mBh, &full[s], n0 + j * C::BKE, xrow, bb);
-                    if (TF32) {
-                        tc::tma_load_3d(st + TILE_BYTES + boff, &mAl, &full[s], m0 + j * C::BKE, orow, bb);
-                        tc::tma_load_3d(sB + TILE_BYTES + boff, &mBl, &full[s], n0 + j * C::BKE, xrow, bb);
-                    }
-                }
-            } else {
-                const int tt = it / a.kchunks, c = it - tt * a.kchunks;
-                const int kx = c * C::BKE;
-                const int brow = n0 + a.o_base + tt * a.d - a.p;
-                tc::tma_load_3d(st, &mAh, &full[s], kx, m0, tt);
-                tc::tma_load_3d(sB, &mBh, &full[s], kx, brow, b);
+            for (int j = 0; j < C::MN_BLOCKS; ++j) {
+                const int boff = j * C::KROWS * 128;
+                tc::tma_load_3d(st + boff, &mAh, &full[s], m0 + j * C::BKE, orow, bb);
+                tc::tma_load_3d(sB + boff, &mBh, &full[s], n0 + j * C::BKE, xrow, bb);
                 if (TF32) {
-                    tc::tma_load_3d(st + TILE_BYTES, &mAl, &full[s], kx, m0, tt);
-                    tc::tma_load_3d(sB + TILE_BYTES, &mBl, &full[s], kx, brow, b);
+                    tc::tma_load_3d(st + TILE_BYTES + boff, &mAl, &full[s], m0 + j * C::BKE, orow, bb);
+                    tc::tma_load_3d(sB + TILE_BYTES + boff, &mBl, &full[s], n0 + j * C::BKE, xrow, bb);
                 }
             }
             issued = it + 1;
@@ -172,16 +424,15 @@ __global__ void __launch_bounds__(192, 1)
         }
     } else if (warp == 1 && lane == 0) {
         // ── MMA issuer
-        constexpr uint32_t idesc = tc::make_idesc(TF32 ? 2u : 1u, WGRAD ? 1u : 0u, WGRAD ? 1u : 0u, BM, BN);
+        constexpr uint32_t idesc = tc::make_idesc(TF32 ? 2u : 1u, 1u, 1u, BM, BN);
         for (int it = 0; it < n_iters; ++it) {
             const int s = it % C::S;
             const uint32_t ph = (it / C::S) & 1;
             const int g = it / PG;                          // promotion group
             const bool g_first = (it % PG) == 0;
             const bool g_last = (it % PG) == PG - 1 || it == n_iters - 1;
-            const int buf = PROMOTE ? (g & 1) : 0;
-            if (PROMOTE && g_first && g >= 2 &&
-                !tc::mbar_wait(&acce[buf], ((g >> 1) - 1) & 1, err, tc::TC_ERR_WAIT_ACC))
+            const int buf = g & 1;
+            if (g_first && g >= 2 && !tc::mbar_wait(&acce[buf], ((g >> 1) - 1) & 1, err, tc::TC_ERR_WAIT_ACC))
                 break;
             if (!tc::mbar_wait(&full[s], ph, err, tc::TC_ERR_WAIT_FULL)) break;
             tc::tc_fence_after();
@@ -191,35 +442,26 @@ __global__ void __launch_bounds__(192, 1)
             const uint32_t d_tmem = tbase + (uint32_t)(buf * BN);
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk) {
-                // K-major: +32 bytes along the 128-byte row. MN-major: +32 bytes of K
-                // = 8 rows (tf32) or 16 rows (bf16) = 1024 / 2048 B; LBO = column-block stride
-                uint64_t dAh, dAl, dBh, dBl;
-                if constexpr (WGRAD) {
-                    const uint32_t off = kk * (TF32 ? 1024 : 2048);
-                    const uint32_t lbo = C::KROWS * 128;
-                    dAh = tc::desc_mnmajor(aH + off, lbo, TF32);
-                    dBh = tc::desc_mnmajor(bH + off, lbo, TF32);
-                    dAl = tc::desc_mnmajor(aL + off, lbo, TF32);
-                    dBl = tc::desc_mnmajor(bL + off, lbo, TF32);
-                } else {
-                    const uint32_t off = kk * 32;
-                    dAh = tc::desc_kmajor_sw128(aH + off);
-                    dBh = tc::desc_kmajor_sw128(bH + off);
-                    dAl = tc::desc_kmajor_sw128(aL + off);
-                    dBl = tc::desc_kmajor_sw128(bL + off);
-                }
-                const uint32_t acc =
-                    PROMOTE ? ((g_first && kk == 0) ? 0u : 1u) : ((it > 0 || kk > 0) ? 1u : 0u);
+                // +32 bytes of K = 8 rows (tf32) or 16 rows (bf16) = 1024 / 2048 B;
+                // LBO = column-block stride
+                const uint32_t off = kk * (TF32 ? 1024 : 2048);
+                const uint32_t lbo = C::KROWS * 128;
+                const uint64_t dAh = tc::desc_mnmajor(aH + off, lbo, TF32);
+                const uint64_t dBh = tc::desc_mnmajor(bH + off, lbo, TF32);
+                const uint32_t acc = (g_first && kk == 0) ? 0u : 1u;
                 tc::umma<TF32>(d_tmem, dAh, dBh, idesc, acc);
                 if (TF32) {
+                    const uint64_t dAl = tc::desc_mnmajor(aL + off, lbo, TF32);
+                    const uint64_t dBl = tc::desc_mnmajor(bL + off, lbo, TF32);
                     tc::umma<TF32>(d_tmem, dAh, dBl, idesc, 1u);
                     tc::umma<TF32>(d_tmem, dAl, dBh, idesc, 1u);
                 }
             }
             tc::umma_commit(&empty[s]);           // frees the stage once these MMAs have read it
-            if (PROMOTE && g_last) tc::umma_commit(&accf[buf]);
+            if (g_last) tc::umma_commit(&accf[buf]);
         }
-        if (!PROMOTE) tc::umma_commit(&accf[0]);
+        tc::umma_commit(mdone);
+        tc::mbar_wait(mdone, 0, nullptr, tc::TC_ERR_DRAIN);
     } else if (warp >= 2) {
         // ── epilogue
         const int q = warp & 3;
@@ -229,77 +471,35 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
         for (int j = 0; j < BN; ++j) R[j] = 0.f;
         bool ok = true;
-        if (PROMOTE) {
-            const int n_groups = (n_iters + PG - 1) / PG;
-            for (int g = 0; g < n_groups; ++g) {
-                const int buf = g & 1;
-                bool w = true;
-                if (lane == 0) w = tc::mbar_wait(&accf[buf], (g >> 1) & 1, err, tc::TC_ERR_WAIT_ACC);
-                ok = __shfl_sync(0xffffffffu, w ? 1 : 0, 0) != 0;
-                if (!ok) break;
-                tc::tc_fence_after();
-#pragma unroll
-                for (int half = 0; half < BN; half += 64) {   // 4 loads in flight, one wait
-                    uint32_t v[4][16];
-#pragma unroll
-                    for (int q4 = 0; q4 < 4; ++q4) tc::tmem_ld16_nowait(trow + buf * BN + half + q4 * 16, v[q4]);
-                    tc::tmem_wait_ld();
-#pragma unroll
-                    for (int q4 = 0; q4 < 4; ++q4)
-#pragma unroll
-                        for (int j = 0; j < 16; ++j) R[half + q4 * 16 + j] += __uint_as_float(v[q4][j]);
-                }
-                tc::tc_fence_before();
-                __syncwarp();
-                if (lane == 0) tc::mbar_arrive(&acce[buf]);
-            }
-        } else if (n_iters > 0) {
+        const int n_groups = (n_iters + PG - 1) / PG;
+        for (int g = 0; g < n_groups; ++g) {
+            const int buf = g & 1;
             bool w = true;
-            if (lane == 0) w = tc::mbar_wait(&accf[0], 0, err, tc::TC_ERR_WAIT_ACC);
+            if (lane == 0) w = tc::mbar_wait(&accf[buf], (g >> 1) & 1, err, tc::TC_ERR_WAIT_ACC);
             ok = __shfl_sync(0xffffffffu, w ? 1 : 0, 0) != 0;
+            if (!ok) break;
             tc::tc_fence_after();
-            if (ok) {
 #pragma unroll
-                for (int c0 = 0; c0 < BN; c0 += 16) {
-                    float v[16];
-                    tc::tmem_ld16(trow + c0, v);
+            for (int half = 0; half < BN; half += 64) {   // 4 loads in flight, one wait
+                uint32_t v[4][16];
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) R[c0 + j] = v[j];
-                }
+                for (int q4 = 0; q4 < 4; ++q4) tc::tmem_ld16_nowait(trow + buf * BN + half + q4 * 16, v[q4]);
+                tc::tmem_wait_ld();
+#pragma unroll
+                for (int q4 = 0; q4 < 4; ++q4)
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) R[half + q4 * 16 + j] += __uint_as_float(v[q4][j]);
             }
+            tc::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(&acce[buf]);
         }
         const bool valid = ok && *(volatile int*)err == tc::TC_OK;
-        if constexpr (WGRAD) {
-            if (valid && mrow < a.Co) {
-                float* pp = a.part + (((int64_t)blockIdx.z * a.taps + t) * a.Co + mrow) * (int64_t)a.Ci;
+        if (valid && mrow < a.Co) {
+            float* pp = a.part + (((int64_t)blockIdx.z * a.taps + t) * a.Co + mrow) * (int64_t)a.Ci;
 #pragma unroll
-                for (int j = 0; j < BN; ++j)
-                    if (n0 + j < a.Ci) pp[n0 + j] = R[j];
-            }
-        } else {
-            if (valid && mrow < a.Co) {
-                const float bv = a.bias ? a.bias[mrow] : 0.f;
-                double s1 = 0.0, s2 = 0.0;
-#pragma unroll
-                for (int j = 0; j < BN; ++j) {
-                    const int o = n0 + j;
-                    if (o >= a.No) break;
-                    const int row = (o + a.o_base) * a.orow_mul + a.orow_off;
-                    if (row < 0 || row >= a.y_rows) continue;
-                    float val = R[j] + bv;
-                    if (a.r) val += a.r[(int64_t)b * a.r_bs + (int64_t)(row >> a.r_shift) * a.r_ld + mrow];
-                    val *= a.alpha;
-                    float* yp = a.y + (int64_t)b * a.y_bs + (int64_t)row * a.y_ld + mrow;
-                    if (a.accum) val += *yp;
-                    *yp = val;
-                    s1 += val;
-                    s2 = fma((double)val, (double)val, s2);
-                }
-                if (a.stats) {
-                    atomicAdd(&a.stats[((int64_t)b * a.Co + mrow) * 2], s1);
-                    atomicAdd(&a.stats[((int64_t)b * a.Co + mrow) * 2 + 1], s2);
-                }
-            }
+            for (int j = 0; j < BN; ++j)
+                if (n0 + j < a.Ci) pp[n0 + j] = R[j];
         }
     }
     tc::tc_fence_before();
@@ -419,30 +619,47 @@ CUtensorMap make_map(const void* base, int mode, uint64_t d0, uint64_t d1, uint6
     return m;
 }
 
-template <bool TF32, bool PROMOTE, bool WGRAD>
-void set_smem_attr() {
-    static bool done = false;
-    if (!done) {
-        BSML_CUDA(cudaFuncSetAttribute(conv_tc_kernel<TF32, PROMOTE, WGRAD>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<TF32>::SMEM));
-        done = true;
+int sm_count() {
+    static int n = 0;
+    if (n == 0) {
+        int dev = 0;
+        BSML_CUDA(cudaGetDevice(&dev));
+        BSML_CUDA(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev));
     }
+    return n;
 }
 
 template <bool TF32>
 void launch_fwd(const TcConvFwd& c, int mode, cudaStream_t st) {
-    using CF = Cfg<TF32>;
-    constexpr bool PROMOTE = TF32;
-    set_smem_attr<TF32, PROMOTE, false>();
-    const uint32_t bke = CF::BKE;
-    const CUtensorMap mAh = make_map(c.w.hi, mode, c.Ci, c.Co, c.taps, c.w.ld, c.Co, bke, BM);
-    const CUtensorMap mAl = TF32 ? make_map(c.w.lo, mode, c.Ci, c.Co, c.taps, c.w.ld, c.Co, bke, BM) : mAh;
-    const CUtensorMap mBh = make_map(c.x.hi, mode, c.Ci, c.L_in, c.B, c.x.ld, c.L_in, bke, BN);
-    const CUtensorMap mBl = TF32 ? make_map(c.x.lo, mode, c.Ci, c.L_in, c.B, c.x.ld, c.L_in, bke, BN) : mBh;
-    Args a{};
+    using F = FCfg<TF32>;
+    static bool attr = false;
+    if (!attr) {
+        BSML_CUDA(cudaFuncSetAttribute(conv_fwd_tc_kernel<TF32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       SMEM_OPTIN));
+        attr = true;
+    }
+    const int halo = (c.taps - 1) * c.d;
+    FArgs a{};
+    a.wbox = (int)round_up(ceil_div(F::NPOS + halo, 2), 8);
+    if (a.wbox > 256) fail("conv_fwd_tc", "tap span too large for the activation window");
+    a.win_bytes = F::PLANES * 2 * a.wbox * 128;
+    const int fixed = 1024 + 256;   // alignment slack + barriers
+    a.sw = std::min(F::MAX_SW, (SMEM_OPTIN - fixed - 2 * a.win_bytes) / F::WT_BYTES);
+    if (a.sw < 2) fail("conv_fwd_tc", "activation window too large for shared memory");
+    const int smem = 2 * a.win_bytes + a.sw * F::WT_BYTES + fixed;
+    const uint32_t bke = F::BKE;
+    const CUtensorMap mWh = make_map(c.w.hi, mode, c.Ci, c.Co, c.taps, c.w.ld, c.Co, bke, 128);
+    const CUtensorMap mWl = TF32 ? make_map(c.w.lo, mode, c.Ci, c.Co, c.taps, c.w.ld, c.Co, bke, 128) : mWh;
+    const CUtensorMap mXh = make_map(c.x.hi, mode, c.Ci, c.L_in, c.B, c.x.ld, c.L_in, bke, a.wbox);
+    const CUtensorMap mXl = TF32 ? make_map(c.x.lo, mode, c.Ci, c.L_in, c.B, c.x.ld, c.L_in, bke, a.wbox) : mXh;
     a.No = c.No; a.o_base = c.o_base; a.p = c.p; a.d = c.d; a.taps = c.taps;
-    a.kchunks = (int)ceil_div(c.Ci, CF::BKE);
+    a.kchunks = (int)ceil_div(c.Ci, F::BKE);
     a.Co = c.Co;
+    a.n_co = (int)ceil_div(c.Co, 128);
+    a.n_pt = (int)ceil_div(c.No, F::NPOS);
+    const int64_t tiles = (int64_t)a.n_co * a.n_pt * c.B;
+    if (tiles > (1ll << 30)) fail("conv_fwd_tc", "too many tiles");
+    a.n_tiles = (int)tiles;
     a.y = c.y.p; a.y_bs = c.y.bstride; a.y_ld = c.y.ld; a.orow_mul = c.orow_mul; a.orow_off = c.orow_off;
     a.y_rows = c.y.L;
     a.bias = c.bias;
@@ -450,31 +667,35 @@ void launch_fwd(const TcConvFwd& c, int mode, cudaStream_t st) {
     a.alpha = c.alpha; a.accum = c.accum ? 1 : 0;
     a.stats = c.stats;
     if (c.stats && c.accum) fail("conv_fwd_tc", "output statistics need a non-accumulating output");
-    dim3 grid((unsigned)ceil_div(c.No, BN), (unsigned)ceil_div(c.Co, BM), (unsigned)c.B);
+    const int grid = (int)std::min<int64_t>(tiles, sm_count());
     ::bsml::count_launch();
-    conv_tc_kernel<TF32, PROMOTE, false><<<grid, 192, CF::SMEM, st>>>(mAh, mAl, mBh, mBl, a);
+    conv_fwd_tc_kernel<TF32><<<grid, F::THREADS, smem, st>>>(mWh, mWl, mXh, mXl, a);
     BSML_LAUNCH("conv_fwd_tc");
 }
 
 template <bool TF32>
 void launch_wgrad(const TcConvWgrad& c, int mode, float* part, int64_t part_cap, cudaStream_t st) {
-    using CF = Cfg<TF32>;
-    constexpr bool PROMOTE = TF32;
-    set_smem_attr<TF32, PROMOTE, true>();
+    using CF = WCfg<TF32>;
+    static bool attr = false;
+    if (!attr) {
+        BSML_CUDA(cudaFuncSetAttribute(conv_wgrad_tc_kernel<TF32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       CF::SMEM));
+        attr = true;
+    }
     const uint32_t bke = CF::BKE, kr = CF::KROWS;
     // A: dY planes [B][Lo][ld] (M = Co along the contiguous dim); B: X planes (N = Ci)
     const CUtensorMap mAh = make_map(c.dy.hi, mode, c.Co, c.Lo, c.B, c.dy.ld, c.Lo, bke, kr, TF32);
     const CUtensorMap mAl = TF32 ? make_map(c.dy.lo, mode, c.Co, c.Lo, c.B, c.dy.ld, c.Lo, bke, kr, TF32) : mAh;
     const CUtensorMap mBh = make_map(c.x.hi, mode, c.Ci, c.L_in, c.B, c.x.ld, c.L_in, bke, kr, TF32);
     const CUtensorMap mBl = TF32 ? make_map(c.x.lo, mode, c.Ci, c.L_in, c.B, c.x.ld, c.L_in, bke, kr, TF32) : mBh;
-    Args a{};
+    WArgs a{};
     a.taps = c.taps; a.p = c.p; a.d = c.d; a.Co = c.Co; a.Ci = c.Ci;
     a.n_ci_tiles = (int)ceil_div(c.Ci, BN);
     a.chunks_pc = (int)ceil_div(c.Lo, CF::KROWS);
     a.chunks_total = a.chunks_pc * c.B;
     const int tiles = (int)ceil_div(c.Co, BM) * a.n_ci_tiles * c.taps;
-    // ~2 waves of CTAs on 148 SMs, each with >= 8 chunks of K, within the partial budget
-    int64_t splits = ceil_div(2 * 148, tiles);
+    // ~2 waves of CTAs on the SMs, each with >= 8 chunks of K, within the partial budget
+    int64_t splits = ceil_div(2 * sm_count(), tiles);
     splits = std::min<int64_t>(splits, ceil_div(a.chunks_total, 8));
     splits = std::min<int64_t>(splits, part_cap / ((int64_t)c.taps * c.Co * c.Ci));
     if (splits < 1) fail("conv_wgrad_tc", "split-K partial buffer too small");
@@ -483,7 +704,7 @@ void launch_wgrad(const TcConvWgrad& c, int mode, float* part, int64_t part_cap,
     a.part = part;
     dim3 grid((unsigned)ceil_div(c.Co, BM), (unsigned)(a.n_ci_tiles * c.taps), (unsigned)splits);
     ::bsml::count_launch();
-    conv_tc_kernel<TF32, PROMOTE, true><<<grid, 192, CF::SMEM, st>>>(mAh, mAl, mBh, mBl, a);
+    conv_wgrad_tc_kernel<TF32><<<grid, 192, CF::SMEM, st>>>(mAh, mAl, mBh, mBl, a);
     BSML_LAUNCH("conv_wgrad_tc");
     ::bsml::count_launch();
     wgrad_reduce_kernel<<<grid_for((int64_t)c.Co * c.Ci * c.taps), 256, 0, st>>>(part, (int)splits, c.taps, c.Co,

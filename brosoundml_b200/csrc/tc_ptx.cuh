@@ -156,6 +156,10 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
 
 // Shared-memory matrix descriptor, K-major operand with the 128-byte swizzle:
 // rows of 128 B, 8-row (1024 B) swizzle atoms, SBO = 1024 B between atoms.
+// The swizzle follows the absolute shared-memory address (as the TMA wrote it),
+// so the start may be any 128-byte row of a 1024-byte-aligned loaded region
+// (a row-shifted view) with the base-offset field left at 0; setting it to the
+// row's phase in the pattern gives wrong products (checked on B200).
 __device__ __forceinline__ uint64_t desc_kmajor_sw128(uint32_t saddr) {
     uint64_t d = 0;
     d |= (uint64_t)((saddr & 0x3FFFFu) >> 4);   // start address

@@ -100,6 +100,8 @@ TC_CONV_CASES = [  # (B, Ci, L, Co, k, pad, dil): stride-1 shapes the tensor-cor
     (2, 514, 37, 1024, 3, 1, 1),       # backbone encode conv1: K tail (514 = 16*32 + 2)
     (3, 1090, 20, 512, 3, 1, 1),       # decode.3 conv1: K tail, 4 M tiles
     (2, 64, 129, 96, 1, 0, 1),         # 1x1, partial M tile
+    (8, 128, 24000, 128, 7, 9, 3),     # several 256-position tiles per persistent CTA
+    (16, 96, 3000, 128, 3, 1, 1),      # odd promotion-group count per tile, two tiles on some CTAs
 ]
 # tf32x3 with promoted accumulation is fp32-grade; bf16 is one bf16 product
 TC_TOL = {"tf32x3": 1e-5, "bf16": 1e-2}
