@@ -26,6 +26,9 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = "Kokoro decoder fwd+bwd audio-seconds/sec at 1/2/4/8 B200; % tensor/HBM roofline"
+# ncu capture (gpu__time_duration, dram__bytes_read/write) of conv_fwd_tc_kernel<tf32x3> on the probe
+# case B=16, Ci=Co=128, L=24001, k=7, d=3: 465.8 us, 395.6 MB read + 163.0 MB written
+NCU_CONV_FWD_TC = {"dram_bytes": 395.6e6 + 163.0e6, "flops": 2.0 * 16 * 128 * 128 * 7 * 24001}
 UNIT = "audio-s/s"
 WORKLOADS = {
     # name: (B per GPU, T asr frames, description)
@@ -298,24 +301,32 @@ def main():
     for k, (pms, work, n) in prof.items():
         if pms <= 0:
             continue
-        if k in ("conv", "wgrad"):
-            rl_all[k] = {"ms": pms, "launches": n, "tflops": work / (pms / 1e3) / 1e12, "share": pms / ms}
+        if k.startswith(("conv", "wgrad")):
+            rl_all[k] = {"ms": pms, "launches": n, "tflops": work / (pms / 1e3) / 1e12, "share": pms / ms,
+                         "flops_per_launch": work / max(n, 1)}
         else:
             rl_all[k] = {"ms": pms, "launches": n, "gbs": work / (pms / 1e3) / 1e9, "share": pms / ms}
     dom = max(rl_all, key=lambda k: rl_all[k]["ms"])
     tensor_peak = peaks["bf16_tflops"] if math == "bf16" else peaks["bf16_tflops"] / 2.0
-    if dom in ("conv", "wgrad"):
+    if dom.startswith(("conv", "wgrad")):
         ach = rl_all[dom]["tflops"]
-        if math == "fp32":
-            roofline = {"bound": "tensor", "achieved": ach, "peak": tensor_peak, "unit": "TFLOP/s",
-                        "frac": ach / tensor_peak, "traffic": None,
-                        "note": f"dominant class '{dom}' runs on fp32 CUDA cores; peak = tf32 dense "
-                                f"(half the {peaks['source']} bf16 cuBLAS figure)"}
+        traffic = None
+        note = f"dominant kernel class '{dom}'; achieved = useful conv FLOPs / CUDA-event time; "
+        if dom.endswith("_simt"):
+            note += f"runs on fp32 CUDA cores; peak = tf32 dense (half the {peaks['source']} bf16 cuBLAS figure)"
+        elif math == "bf16":
+            note += f"peak = {peaks['source']} bf16 dense"
         else:
-            roofline = {"bound": "tensor", "achieved": ach, "peak": tensor_peak, "unit": "TFLOP/s",
-                        "frac": ach / tensor_peak, "traffic": None,
-                        "note": f"dominant class '{dom}'; peak of {peaks['source']} "
-                                + ("bf16" if math == "bf16" else "tf32 dense = bf16/2")}
+            note += (f"peak = {peaks['source']} tf32 dense (bf16/2); TF32x3 issues 3 tensor products per useful "
+                     f"one, so the tensor pipe runs {3 * ach / tensor_peak:.0%} busy at this rate")
+            if dom == "conv_tc":
+                # DRAM bytes per FLOP of conv_fwd_tc_kernel from one ncu capture of the probe case
+                # (python -m brosoundml_b200.kernel_probe --B 16 --C 128 --L 24001 --k 7 --d 3 --math tf32x3),
+                # scaled to this class's average launch by its FLOPs
+                traffic = NCU_CONV_FWD_TC["dram_bytes"] / NCU_CONV_FWD_TC["flops"] * rl_all[dom]["flops_per_launch"]
+                note += "; traffic scaled from the ncu capture of the probe case by FLOPs"
+        roofline = {"bound": "tensor", "achieved": ach, "peak": tensor_peak, "unit": "TFLOP/s",
+                    "frac": ach / tensor_peak, "traffic": traffic, "note": note}
     else:
         ach = rl_all[dom]["gbs"]
         roofline = {"bound": "hbm", "achieved": ach, "peak": peaks["hbm_gbs"], "unit": "GB/s",

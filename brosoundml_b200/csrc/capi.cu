@@ -222,10 +222,10 @@ int bsml_decoder_set_profiling(bsml_decoder* d, int on) {
     });
 }
 
-int bsml_decoder_read_profile(bsml_decoder* d, double* out12) {
+int bsml_decoder_read_profile(bsml_decoder* d, double* out) {
     return guarded([&] {
-        need(d != nullptr && out12 != nullptr, "bsml_decoder_read_profile", "null argument");
-        d->eng->read_profile(out12);
+        need(d != nullptr && out != nullptr, "bsml_decoder_read_profile", "null argument");
+        d->eng->read_profile(out);
     });
 }
 

@@ -450,14 +450,14 @@ void Engine::conv(const ConvP& c, const Act& x, const Act& y, const Act* r, int 
     if (stats) BSML_CUDA(cudaMemsetAsync(stats, 0, sizeof(double) * 2 * (size_t)y.B * c.cout, st));
     if (tc_ok(c.cin, c.cout, c.s)) {
         const TcPlanes tp = xp ? *xp : tc_planes(x, st);
-        const int id = prof_begin(PROF_CONV, 2.0 * c.cin * c.cout * c.k * (double)a.No * x.B, st);
+        const int id = prof_begin(PROF_CONV_TC, 2.0 * c.cin * c.cout * c.k * (double)a.No * x.B, st);
         tc_launch(x, tp, tcw_fwd_hi_[c.id], tcw_fwd_lo_[c.id], c.k, c.cout, y, a.bias, r, r_shift, c.p, c.d, a.No, 0,
                   1, 0, alpha, accum, stats, st);
         prof_end(id, st);
         return;
     }
     if (!x.p) fail("conv", "internal: fp32 operand missing on the CUDA-core path");
-    const int id = prof_begin(PROF_CONV, 2.0 * c.cin * c.cout * c.k * (double)a.No * x.B, st);
+    const int id = prof_begin(PROF_CONV_SIMT, 2.0 * c.cin * c.cout * c.k * (double)a.No * x.B, st);
     conv_fwd_simt(a, st);
     prof_end(id, st);
     if (stats) norm_sums(y, stats, st);
@@ -475,14 +475,14 @@ void Engine::conv_dgrad(const ConvP& c, const Act& dy, const Act& dx, bool accum
     a.accum = accum;
     if (tc_ok(c.cout, c.cin, 1)) {
         const TcPlanes tp = dyp ? *dyp : tc_planes(dy, st);
-        const int id = prof_begin(PROF_CONV, 2.0 * c.cin * c.cout * c.k * (double)dy.L * dy.B, st);
+        const int id = prof_begin(PROF_CONV_TC, 2.0 * c.cin * c.cout * c.k * (double)dy.L * dy.B, st);
         tc_launch(dy, tp, tcw_dg_hi_[c.id], tcw_dg_lo_[c.id], c.k, c.cin, dx, nullptr, nullptr, 0, a.p, c.d, a.No, 0,
                   1, 0, 1.f, accum, nullptr, st);
         prof_end(id, st);
         return;
     }
     if (!dy.p) fail("conv_dgrad", "internal: fp32 operand missing on the CUDA-core path");
-    const int id = prof_begin(PROF_CONV, 2.0 * c.cin * c.cout * c.k * (double)dy.L * dy.B, st);
+    const int id = prof_begin(PROF_CONV_SIMT, 2.0 * c.cin * c.cout * c.k * (double)dy.L * dy.B, st);
     conv_fwd_simt(a, st);
     prof_end(id, st);
 }
@@ -503,7 +503,7 @@ void Engine::conv_wgrad(const ConvP& c, const Act& dy, const Act& x, cudaStream_
         w.x = xp ? *xp : tc_planes(x, st);
         w.B = dy.B; w.Lo = dy.L; w.Co = dy.C; w.L_in = x.L; w.Ci = x.C;
         w.taps = c.k; w.p = c.p; w.d = c.d; w.dW = grads_ + c.w;
-        const int id = prof_begin(PROF_WGRAD, 2.0 * c.cin * c.cout * c.k * (double)dy.L * dy.B, st);
+        const int id = prof_begin(PROF_WGRAD_TC, 2.0 * c.cin * c.cout * c.k * (double)dy.L * dy.B, st);
         conv_wgrad_tc(w, mode, part_, part_floats_, st);
         if (c.b >= 0) {
             if (bias_sum) d2f(bias_sum, c.cout, grads_ + c.b, false, st);
@@ -519,7 +519,7 @@ void Engine::conv_wgrad(const ConvP& c, const Act& dy, const Act& x, cudaStream_
     a.dW = grads_ + c.w;
     a.db = bias_sum ? nullptr : G(c.b);
     if (wgrad_partial_floats(a) > part_floats_) fail("conv_wgrad", "split-K partial buffer too small");
-    const int id = prof_begin(PROF_WGRAD, 2.0 * c.cin * c.cout * c.k * (double)dy.L * dy.B, st);
+    const int id = prof_begin(PROF_WGRAD_SIMT, 2.0 * c.cin * c.cout * c.k * (double)dy.L * dy.B, st);
     conv_wgrad_simt(a, part_, st);
     if (bias_sum && c.b >= 0) d2f(bias_sum, c.cout, grads_ + c.b, false, st);
     prof_end(id, st);
@@ -544,7 +544,7 @@ void Engine::convT(const UpP& u, const Act& x, const Act& y, int row_off, const 
         a.k = kr; a.s = 1; a.p = kr - 1; a.d = 1;
         a.No = qmax - qmin + 1; a.o_base = qmin;
         a.orow_mul = u.s; a.orow_off = ph - u.p + row_off;
-        const int id = prof_begin(PROF_CONV, 2.0 * u.cin * u.cout * kr * (double)a.No * x.B, st);
+        const int id = prof_begin(tc ? PROF_CONV_TC : PROF_CONV_SIMT, 2.0 * u.cin * u.cout * kr * (double)a.No * x.B, st);
         if (tc)
             tc_launch(x, tp, tcw_up_hi_[u.id][ph], tcw_up_lo_[u.id][ph], kr, u.cout, y, a.bias, r, 0, a.p, 1, a.No,
                       a.o_base, a.orow_mul, a.orow_off, 1.f, false, nullptr, st);
@@ -560,7 +560,7 @@ void Engine::convT_dgrad(const UpP& u, const Act& dy, const Act& dx, cudaStream_
     a.x = dy; a.y = dx; a.wp = wp_up_dgrad_[u.id];
     a.k = u.k; a.s = u.s; a.p = u.p; a.d = 1;
     a.No = dx.L;
-    const int id = prof_begin(PROF_CONV, 2.0 * u.cin * u.cout * u.k * (double)dx.L * dx.B, st);
+    const int id = prof_begin(PROF_CONV_SIMT, 2.0 * u.cin * u.cout * u.k * (double)dx.L * dx.B, st);
     conv_fwd_simt(a, st);
     prof_end(id, st);
 }
@@ -573,7 +573,7 @@ void Engine::convT_wgrad(const UpP& u, const Act& dy, const Act& x, cudaStream_t
     a.dW = grads_ + u.w;
     a.db = nullptr;
     if (wgrad_partial_floats(a) > part_floats_) fail("convT_wgrad", "split-K partial buffer too small");
-    const int id = prof_begin(PROF_WGRAD, 2.0 * u.cin * u.cout * u.k * (double)x.L * x.B, st);
+    const int id = prof_begin(PROF_WGRAD_SIMT, 2.0 * u.cin * u.cout * u.k * (double)x.L * x.B, st);
     conv_wgrad_simt(a, part_, st);
     colsum(dy, grads_ + u.b, false, part_, st);
     prof_end(id, st);

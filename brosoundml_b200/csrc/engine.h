@@ -30,11 +30,14 @@ class Engine {
     void backward(const float* daudio, float* grads, float* d_asr, float* d_style, float* d_aff, cudaStream_t st);
     int64_t workspace_bytes() const { return ws_bytes_ + wp_bytes_ + tcw_bytes_; }
 
-    // Per-kernel-class timing with CUDA events (off by default). Classes:
-    // 0 conv fwd-like (fwd, dgrad, convT), 1 conv wgrad, 2 AdaIN/Snake forward,
-    // 3 AdaIN/Snake backward. Per class: ms, algorithmic work (FLOPs for 0-1,
-    // bytes for 2-3), launches. Reading the profile synchronises the device.
-    enum { PROF_CONV = 0, PROF_WGRAD = 1, PROF_NORM_FWD = 2, PROF_NORM_BWD = 3, PROF_N = 4 };
+    // Per-kernel-class timing with CUDA events (off by default); the classes of
+    // bsml_decoder_read_profile. Per class: ms, algorithmic work (FLOPs for the
+    // convs, bytes for the norms), launches. Reading synchronises the device.
+    enum {
+        PROF_CONV_TC = BSML_PROF_CONV_TC, PROF_CONV_SIMT = BSML_PROF_CONV_SIMT, PROF_WGRAD_TC = BSML_PROF_WGRAD_TC,
+        PROF_WGRAD_SIMT = BSML_PROF_WGRAD_SIMT, PROF_NORM_FWD = BSML_PROF_NORM_FWD,
+        PROF_NORM_BWD = BSML_PROF_NORM_BWD, PROF_N = BSML_PROF_CLASSES
+    };
     void set_profiling(bool on);
     void read_profile(double* out);   // PROF_N * 3 doubles, then clears
 

@@ -83,11 +83,12 @@ class Decoder:
     def set_profiling(self, on: bool) -> None:
         _lib.check(_lib.lib().bsml_decoder_set_profiling(self._h, 1 if on else 0))
 
-    PROFILE_CLASSES = ("conv", "wgrad", "norm_fwd", "norm_bwd")
+    # the BSML_PROF_* classes of bsml_decoder_read_profile, in order
+    PROFILE_CLASSES = ("conv_tc", "conv_simt", "wgrad_tc", "wgrad_simt", "norm_fwd", "norm_bwd")
 
     def read_profile(self) -> dict:
         """{class: (ms, algorithmic FLOPs or bytes, launches)} since the last read."""
-        buf = (ctypes.c_double * 12)()
+        buf = (ctypes.c_double * (3 * len(self.PROFILE_CLASSES)))()
         _lib.check(_lib.lib().bsml_decoder_read_profile(self._h, ctypes.cast(buf, ctypes.c_void_p)))
         return {k: (buf[3 * i], buf[3 * i + 1], int(buf[3 * i + 2])) for i, k in enumerate(self.PROFILE_CLASSES)}
 

@@ -122,15 +122,21 @@ int bsml_decoder_backward(bsml_decoder* d, const float* daudio, float* grads, fl
 int64_t bsml_decoder_workspace_bytes(const bsml_decoder* d);
 
 /* Optional per-kernel-class timing with CUDA events (no reference counterpart:
- * instrumentation for the roofline report). Classes: 0 conv forward-like
- * (fwd, dgrad, convT), 1 conv weight gradient, 2 AdaIN+Snake forward,
- * 3 AdaIN+Snake backward. read_profile fills 12 doubles (per class: ms,
- * algorithmic work in FLOPs (0-1) or bytes (2-3), launches), synchronises the
- * device and clears the record. */
+ * instrumentation for the roofline report). Classes (BSML_PROF_*): forward-like
+ * convs (fwd, dgrad, convT) on the tensor cores and on the CUDA cores, weight
+ * gradients on each, AdaIN+Snake forward, AdaIN+Snake backward. read_profile
+ * fills 3 doubles per class (ms, algorithmic work in FLOPs for the convs or
+ * bytes for the norms, launches), synchronises the device and clears the
+ * record. */
+enum {
+    BSML_PROF_CONV_TC = 0, BSML_PROF_CONV_SIMT = 1, BSML_PROF_WGRAD_TC = 2, BSML_PROF_WGRAD_SIMT = 3,
+    BSML_PROF_NORM_FWD = 4, BSML_PROF_NORM_BWD = 5, BSML_PROF_CLASSES = 6
+};
 int bsml_decoder_set_profiling(bsml_decoder* d, int on);
 /* Number of CUDA kernels this library has launched in the process so far. */
 int64_t bsml_launch_count(void);
-int bsml_decoder_read_profile(bsml_decoder* d, double* out12);
+/* out: 3 * BSML_PROF_CLASSES doubles */
+int bsml_decoder_read_profile(bsml_decoder* d, double* out);
 
 /* ── loss and optimiser ─────────────────────────────────────────────────── */
 
