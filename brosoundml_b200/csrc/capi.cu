@@ -70,6 +70,10 @@ int conv_out(int L, int k, int s, int p, int d) { return (L + 2 * p - d * (k - 1
 std::atomic<int> g_atom_math{BSML_MATH_FP32_SIMT};
 
 bool atom_tc(int K, int M, int s) { return g_atom_math.load() != BSML_MATH_FP32_SIMT && s == 1 && K >= 32 && M >= 64; }
+// ConvTranspose1d gradients on the tensor cores: dy viewed row-packed (K = s*Co per tap)
+bool atom_convT_tc(int Ci, int Co, int s, int Lu) {
+    return g_atom_math.load() != BSML_MATH_FP32_SIMT && Ci >= 64 && s * Co >= 32 && Co % 8 == 0 && Lu % s == 0;
+}
 int atom_tc_mode() { return g_atom_math.load() == BSML_MATH_BF16 ? bsml::TC_BF16 : bsml::TC_TF32X3; }
 
 // Tensor-core forward-like conv for the atoms: planes of x, packed weight planes, launch.
@@ -368,8 +372,29 @@ int bsml_conv_transpose1d_backward_input(const float* dy, int B, int Ci, int L, 
         cudaStream_t st = S(stream);
         Scratch sc(st);
         bsml::Act ga = sc.act(B, Lu, Co), xa = sc.act(B, L, Ci);
-        float* wp = sc.f((int64_t)k * Co * bsml::round_up(Ci, 4));
         bsml::ncl_to_cl(dy, ga, st);
+        if (atom_convT_tc(Ci, Co, stride, Lu)) {
+            const int mode = atom_tc_mode();
+            const bsml::ConvTPack pk = bsml::convT_pack(k, stride, pad);
+            const int K = stride * Co;
+            float* gh = sc.f((int64_t)B * Lu * Co);
+            float* gl = sc.f((int64_t)B * Lu * Co);
+            const int64_t wn = (int64_t)pk.taps * Ci * bsml::round_up(K, 8);
+            float* wh = sc.f(wn);
+            float* wl = sc.f(wn);
+            bsml::make_act_planes(ga, mode, gh, gl, st);
+            bsml::pack_w_tc(W, bsml::PACK_CONVT_DGRAD, Co, Ci, k, stride, pad, mode, wh, wl, st);
+            bsml::TcConvFwd a;
+            a.x.hi = gh; a.x.lo = gl; a.x.ld = K;
+            a.B = B; a.L_in = Lu / stride; a.Ci = K;
+            a.w.hi = wh; a.w.lo = wl; a.w.ld = (int)bsml::round_up(K, 8);
+            a.taps = pk.taps; a.Co = Ci; a.p = -pk.u_min; a.d = 1; a.No = L;
+            a.y = xa;
+            bsml::conv_fwd_tc(a, mode, st);
+            bsml::cl_to_ncl(xa, dx, st);
+            return;
+        }
+        float* wp = sc.f((int64_t)k * Co * bsml::round_up(Ci, 4));
         bsml::pack_convT_dgrad(W, Ci, Co, k, wp, st);
         bsml::ConvFwd a;
         a.x = ga; a.y = xa; a.wp = wp; a.k = k; a.s = stride; a.p = pad; a.d = 1; a.No = L;
@@ -388,6 +413,29 @@ int bsml_conv_transpose1d_backward_weight(const float* dy, const float* x, int B
         bsml::Act ga = sc.act(B, Lu, Co), xa = sc.act(B, L, Ci);
         bsml::ncl_to_cl(dy, ga, st);
         bsml::ncl_to_cl(x, xa, st);
+        if (atom_convT_tc(Ci, Co, stride, Lu)) {
+            const int mode = atom_tc_mode();
+            const bsml::ConvTPack pk = bsml::convT_pack(k, stride, pad);
+            const int K = stride * Co;
+            float* gh = sc.f((int64_t)B * Lu * Co);
+            float* gl = sc.f((int64_t)B * Lu * Co);
+            float* xh = sc.f((int64_t)B * L * bsml::tc_pitch(Ci, mode));
+            float* xl = sc.f((int64_t)B * L * bsml::tc_pitch(Ci, mode));
+            bsml::make_act_planes(ga, mode, gh, gl, st);
+            bsml::make_act_planes(xa, mode, xh, xl, st);
+            bsml::TcConvWgrad w;
+            w.dy.hi = xh; w.dy.lo = xl; w.dy.ld = bsml::tc_pitch(Ci, mode);
+            w.x.hi = gh; w.x.lo = gl; w.x.ld = K;
+            w.B = B; w.Lo = L; w.Co = Ci; w.L_in = Lu / stride; w.Ci = K;
+            w.taps = pk.taps; w.p = -pk.u_min; w.d = 1; w.dW = dW;
+            w.ct_s = stride; w.ct_p = pad; w.ct_k = k; w.ct_Co = Co;
+            const int64_t cap = std::max<int64_t>(std::min<int64_t>(48ll << 20, 296ll * Ci * K * pk.taps),
+                                                  bsml::colsum_partial_floats(ga));
+            float* part = sc.f(cap);
+            bsml::conv_wgrad_tc(w, mode, part, cap, st);
+            if (db) bsml::colsum(ga, db, false, part, st);
+            return;
+        }
         bsml::ConvWgrad a;
         a.dy = xa; a.x = ga; a.k = k; a.s = stride; a.p = pad; a.d = 1; a.dW = dW;
         float* part = sc.f(std::max(bsml::wgrad_partial_floats(a), bsml::colsum_partial_floats(ga)));

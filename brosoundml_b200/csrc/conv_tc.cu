@@ -546,9 +546,14 @@ __global__ void pack_w_kernel(const float* W, int kind, int Co, int Ci, int k, i
                 v = W[((int64_t)m * Ci + kk) * k + t];
             } else if (kind == PACK_CONV_DGRAD) {   // m = ci, kk = co
                 v = W[((int64_t)kk * Ci + m) * k + (k - 1 - t)];
-            } else {                                // convT phase: m = co, kk = ci
+            } else if (kind == PACK_CONVT_PHASE) {  // convT phase: m = co, kk = ci
                 const int tt = r + (taps - 1 - t) * s;
                 v = W[((int64_t)kk * Co + m) * k + tt];
+            } else {                                // convT dgrad, row-packed: m = ci, kk = j*Co + co
+                const int u_min = -((r + s - 1) / s);
+                const int j = kk / Co, co = kk - j * Co;
+                const int tt = (t + u_min) * s + j + r;
+                if (tt >= 0 && tt < k) v = W[((int64_t)m * Co + co) * k + tt];
             }
         }
         if (TF32) {
@@ -573,6 +578,26 @@ __global__ void wgrad_reduce_kernel(const float* part, int splits, int taps, int
         double s = 0;
         for (int sp = 0; sp < splits; ++sp) s += part[sp * stride_split + src];
         dW[i] = (float)(accum ? dW[i] + s : s);
+    }
+}
+
+// ConvTranspose1d weight gradient from the row-packed partials:
+// dW[(ci*CoT + co)*k + t] (+)= sum_split part[split][tau][ci][j*CoT + co], t - p = (tau + u_min)*s + j
+__global__ void wgrad_reduce_convT_kernel(const float* part, int splits, int taps, int M, int N, int CoT, int k, int s,
+                                          int p, int u_min, float* dW, int accum) {
+    const int64_t n = (int64_t)M * CoT * k;
+    const int64_t stride_split = (int64_t)taps * M * N;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const int t = (int)(i % k);
+        const int64_t q = i / k;
+        const int co = (int)(q % CoT), m = (int)(q / CoT);
+        const int tp = t - p;
+        const int u = tp >= 0 ? tp / s : -((-tp + s - 1) / s);
+        const int j = tp - u * s, tau = u - u_min;
+        const int64_t src = ((int64_t)tau * M + m) * N + (int64_t)j * CoT + co;
+        double acc = 0;
+        for (int sp = 0; sp < splits; ++sp) acc += part[sp * stride_split + src];
+        dW[i] = (float)(accum ? dW[i] + acc : acc);
     }
 }
 
@@ -707,8 +732,15 @@ void launch_wgrad(const TcConvWgrad& c, int mode, float* part, int64_t part_cap,
     conv_wgrad_tc_kernel<TF32><<<grid, 192, CF::SMEM, st>>>(mAh, mAl, mBh, mBl, a);
     BSML_LAUNCH("conv_wgrad_tc");
     ::bsml::count_launch();
-    wgrad_reduce_kernel<<<grid_for((int64_t)c.Co * c.Ci * c.taps), 256, 0, st>>>(part, (int)splits, c.taps, c.Co,
-                                                                                    c.Ci, c.dW, c.accum ? 1 : 0);
+    if (c.ct_s > 0) {
+        const ConvTPack pk = convT_pack(c.ct_k, c.ct_s, c.ct_p);
+        if (pk.taps != c.taps || c.Ci != c.ct_s * c.ct_Co) fail("conv_wgrad_tc", "inconsistent ConvTranspose1d packing");
+        wgrad_reduce_convT_kernel<<<grid_for((int64_t)c.Co * c.ct_Co * c.ct_k), 256, 0, st>>>(
+            part, (int)splits, c.taps, c.Co, c.Ci, c.ct_Co, c.ct_k, c.ct_s, c.ct_p, pk.u_min, c.dW, c.accum ? 1 : 0);
+    } else {
+        wgrad_reduce_kernel<<<grid_for((int64_t)c.Co * c.Ci * c.taps), 256, 0, st>>>(part, (int)splits, c.taps, c.Co,
+                                                                                        c.Ci, c.dW, c.accum ? 1 : 0);
+    }
     BSML_LAUNCH("wgrad_reduce");
 }
 
@@ -735,6 +767,10 @@ void pack_w_tc(const float* W, int kind, int Co, int Ci, int k, int s, int r, in
     int taps = k, M = Co, K = Ci;
     if (kind == PACK_CONV_DGRAD) { M = Ci; K = Co; }
     if (kind == PACK_CONVT_PHASE) taps = (k - r + s - 1) / s;
+    if (kind == PACK_CONVT_DGRAD) {
+        if (r < 0) fail("pack_w_tc", "negative ConvTranspose1d padding");
+        M = Ci; K = s * Co; taps = convT_pack(k, s, r).taps;
+    }
     const int Kp = (int)round_up(K, 8);
     const int64_t n = (int64_t)taps * M * Kp;
     ::bsml::count_launch();

@@ -31,9 +31,26 @@ void make_act_planes(const Act& x, int mode, void* hi, void* lo, cudaStream_t st
 //   conv fwd:       M = Co, K = Ci, tap t   = W[co][ci][t]
 //   conv dgrad:     M = Ci, K = Co, tap t'  = W[co][ci][k-1-t']
 //   convT phase r:  M = Co, K = Ci, tap m'  = W[ci][co][r + (kr-1-m')*s]
+//   convT dgrad:    M = Ci, K = s*Co (row-packed, see ConvTPack), r = the convT padding p
 void pack_w_tc(const float* W, int kind, int Co, int Ci, int k, int s, int r, int mode, void* hi, void* lo,
                cudaStream_t st);
-enum { PACK_CONV_FWD = 0, PACK_CONV_DGRAD = 1, PACK_CONVT_PHASE = 2 };
+enum { PACK_CONV_FWD = 0, PACK_CONV_DGRAD = 1, PACK_CONVT_PHASE = 2, PACK_CONVT_DGRAD = 3 };
+
+// ConvTranspose1d (weight W[Ci][Co][k], stride s, padding p, output length Lu)
+// input and weight gradients as stride-1 problems over dy viewed row-packed:
+//   dy2[b, m, j*Co + co] = dy[b, m*s + j, co]      (Lu % s == 0, compact rows)
+// With t - p = u*s + j (0 <= j < s), u in [u_min, u_max]:
+//   dx[q, ci]       = sum_{u, j, co} W[ci, co, u*s + j + p] * dy2[q + u, j*Co + co]
+//   dW[ci, co, t]   = sum_q x[q, ci] * dy2[q + u, j*Co + co]
+// i.e. a conv with taps = u_max - u_min + 1, padding -u_min and K = s*Co.
+struct ConvTPack {
+    int taps, u_min;
+};
+inline int floor_div(int a, int b) { return a >= 0 ? a / b : -((-a + b - 1) / b); }
+inline ConvTPack convT_pack(int k, int s, int p) {
+    const int u_min = floor_div(-p, s), u_max = floor_div(k - 1 - p, s);
+    return ConvTPack{u_max - u_min + 1, u_min};
+}
 
 struct TcConvFwd {
     // activations (B, L_in, Ci) as planes
@@ -66,6 +83,10 @@ struct TcConvWgrad {
     TcPlanes dy, x;
     int B = 0, Lo = 0, Co = 0, L_in = 0, Ci = 0;
     int taps = 1, p = 0, d = 1;
+    // ConvTranspose1d mode (ct_s > 0): x is dy2 of ConvTPack (Ci = ct_s * ct_Co
+    // row-packed channels), dy is the convT input, and dW is the convT weight
+    // [Co][ct_Co][ct_k] (Co = convT input channels)
+    int ct_s = 0, ct_p = 0, ct_k = 0, ct_Co = 0;
     float* dW = nullptr;
     bool accum = false;
 };

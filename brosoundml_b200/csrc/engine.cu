@@ -84,9 +84,12 @@ Engine::Engine(const bsml_decoder_config& cfg, int device) : lay_(cfg), device_(
             tsz((int64_t)c->k * c->cout * round_up(c->cin, 8)); tsz((int64_t)c->k * c->cout * round_up(c->cin, 8));
             tsz((int64_t)c->k * c->cin * round_up(c->cout, 8)); tsz((int64_t)c->k * c->cin * round_up(c->cout, 8));
         }
-        for (auto& u : lay_.ups)
+        for (auto& u : lay_.ups) {
             for (int r = 0; r < u.s; ++r)
                 for (int h = 0; h < 2; ++h) tsz((int64_t)((u.k - r + u.s - 1) / u.s) * u.cout * round_up(u.cin, 8));
+            for (int h = 0; h < 2; ++h)
+                tsz((int64_t)convT_pack(u.k, u.s, u.p).taps * u.cin * round_up((int64_t)u.s * u.cout, 8));
+        }
         tcw_bytes_ = round_up(tb, 256);
         BSML_CUDA(cudaMalloc(&tcw_mem_, tcw_bytes_));
         int64_t toff = 0;
@@ -106,12 +109,18 @@ Engine::Engine(const bsml_decoder_config& cfg, int device) : lay_(cfg), device_(
         }
         tcw_up_hi_.resize(lay_.ups.size());
         tcw_up_lo_.resize(lay_.ups.size());
-        for (auto& u : lay_.ups)
+        tcw_updg_hi_.resize(lay_.ups.size());
+        tcw_updg_lo_.resize(lay_.ups.size());
+        for (auto& u : lay_.ups) {
             for (int r = 0; r < u.s; ++r) {
                 const int64_t n = (int64_t)((u.k - r + u.s - 1) / u.s) * u.cout * round_up(u.cin, 8);
                 tcw_up_hi_[u.id].push_back(ttake(n));
                 tcw_up_lo_[u.id].push_back(ttake(n));
             }
+            const int64_t n = (int64_t)convT_pack(u.k, u.s, u.p).taps * u.cin * round_up((int64_t)u.s * u.cout, 8);
+            tcw_updg_hi_[u.id] = ttake(n);
+            tcw_updg_lo_[u.id] = ttake(n);
+        }
     }
     // fc row table (out offsets depend on B: rebuilt in ensure_plan)
     fc_rows_ = 0;
@@ -385,7 +394,12 @@ void Engine::pack_dgrad_weights(cudaStream_t st) {
         else
             pack_conv_dgrad(params_ + c->w, c->cout, c->cin, c->k, wp_dgrad_[c->id], st);
     }
-    for (auto& u : lay_.ups) pack_convT_dgrad(params_ + u.w, u.cin, u.cout, u.k, wp_up_dgrad_[u.id], st);
+    for (auto& u : lay_.ups) {
+        pack_convT_dgrad(params_ + u.w, u.cin, u.cout, u.k, wp_up_dgrad_[u.id], st);
+        if (convT_tc(u))
+            pack_w_tc(params_ + u.w, PACK_CONVT_DGRAD, u.cout, u.cin, u.k, u.s, u.p, tc_mode(), tcw_updg_hi_[u.id],
+                      tcw_updg_lo_[u.id], st);
+    }
 }
 
 TcPlanes Engine::tc_planes(const Act& x, cudaStream_t st) {
@@ -554,8 +568,24 @@ void Engine::convT(const UpP& u, const Act& x, const Act& y, int row_off, const 
     }
 }
 
-// dx[l, ci] = sum_{t, co} W[ci, co, t] dy[l*s - p + t, co]: a strided forward conv over dy
-void Engine::convT_dgrad(const UpP& u, const Act& dy, const Act& dx, cudaStream_t st) {
+// dx[l, ci] = sum_{t, co} W[ci, co, t] dy[l*s - p + t, co]. Tensor cores: a stride-1
+// conv over dy viewed row-packed (ConvTPack: K = s*Co, taps u_min..u_max); CUDA
+// cores: a strided forward conv over dy.
+void Engine::convT_dgrad(const UpP& u, const Act& dy, const Act& dx, cudaStream_t st, const TcPlanes* dyp) {
+    if (dyp) {
+        const ConvTPack pk = convT_pack(u.k, u.s, u.p);
+        TcConvFwd a;
+        a.x.hi = dyp->hi; a.x.lo = dyp->lo; a.x.ld = u.s * u.cout;
+        a.B = dy.B; a.L_in = dy.L / u.s; a.Ci = u.s * u.cout;
+        a.w.hi = tcw_updg_hi_[u.id]; a.w.lo = tcw_updg_lo_[u.id]; a.w.ld = (int)round_up((int64_t)u.s * u.cout, 8);
+        a.taps = pk.taps; a.Co = u.cin;
+        a.p = -pk.u_min; a.d = 1; a.No = dx.L; a.o_base = 0;
+        a.y = dx;
+        const int id = prof_begin(PROF_CONV_TC, 2.0 * u.cin * u.cout * u.k * (double)dx.L * dx.B, st);
+        conv_fwd_tc(a, tc_mode(), st);
+        prof_end(id, st);
+        return;
+    }
     ConvFwd a;
     a.x = dy; a.y = dx; a.wp = wp_up_dgrad_[u.id];
     a.k = u.k; a.s = u.s; a.p = u.p; a.d = 1;
@@ -565,9 +595,27 @@ void Engine::convT_dgrad(const UpP& u, const Act& dy, const Act& dx, cudaStream_
     prof_end(id, st);
 }
 
-// dW[ci, co, t] = sum x[l, ci] dy[l*s - p + t, co]  (conv wgrad with roles swapped), db = colsum(dy)
-void Engine::convT_wgrad(const UpP& u, const Act& dy, const Act& x, cudaStream_t st) {
+// dW[ci, co, t] = sum x[l, ci] dy[l*s - p + t, co] (conv wgrad with roles swapped; on
+// the tensor cores over the row-packed dy), db = colsum(dy)
+void Engine::convT_wgrad(const UpP& u, const Act& dy, const Act& x, cudaStream_t st, const TcPlanes* dyp) {
     if (!grads_) return;
+    if (dyp) {
+        const ConvTPack pk = convT_pack(u.k, u.s, u.p);
+        const int mode = tc_mode();
+        TcConvWgrad w;
+        w.dy = tc_planes(x, st);   // the convT input plays dY's role (M = Ci of the convT)
+        w.x = *dyp;
+        w.x.ld = u.s * u.cout;
+        w.B = x.B; w.Lo = x.L; w.Co = u.cin; w.L_in = dy.L / u.s; w.Ci = u.s * u.cout;
+        w.taps = pk.taps; w.p = -pk.u_min; w.d = 1;
+        w.dW = grads_ + u.w;
+        w.ct_s = u.s; w.ct_p = u.p; w.ct_k = u.k; w.ct_Co = u.cout;
+        const int id = prof_begin(PROF_WGRAD_TC, 2.0 * u.cin * u.cout * u.k * (double)x.L * x.B, st);
+        conv_wgrad_tc(w, mode, part_, part_floats_, st);
+        colsum(dy, grads_ + u.b, false, part_, st);
+        prof_end(id, st);
+        return;
+    }
     ConvWgrad a;
     a.dy = x; a.x = dy; a.k = u.k; a.s = u.s; a.p = u.p; a.d = 1;
     a.dW = grads_ + u.w;
@@ -577,6 +625,16 @@ void Engine::convT_wgrad(const UpP& u, const Act& dy, const Act& x, cudaStream_t
     conv_wgrad_simt(a, part_, st);
     colsum(dy, grads_ + u.b, false, part_, st);
     prof_end(id, st);
+}
+
+// Row-packed tensor-core operand of a ConvTranspose1d gradient: planes of dy in
+// tc_yh_ / tc_yl_ (compact rows), or nullptr when the CUDA-core path applies.
+const TcPlanes* Engine::convT_dy_planes(const UpP& u, const Act& dy, TcPlanes& tp, cudaStream_t st) {
+    if (!convT_tc(u) || dy.L % u.s != 0) return nullptr;
+    make_act_planes(dy, tc_mode(), tc_yh_, tc_yl_, st);
+    tp.hi = tc_yh_; tp.lo = tc_yl_; tp.ld = tc_pitch(dy.C, tc_mode());
+    if (tp.ld != dy.C) fail("convT_dgrad", "internal: row-packed planes need compact rows");
+    return &tp;
 }
 
 void Engine::stats_of(const Act& x, const Stats& s, cudaStream_t st) { in_stats(x, 1e-5f, dacc_, s.mean, s.rstd, st); }
@@ -877,8 +935,10 @@ void Engine::backward(const float* daudio, float* grads, float* d_asr, float* d_
             du = rows(dm, 1, s.Lu);
         }
         Act da = view(S_[xbuf ^ 1], s.Lin, u.cin);
-        convT_dgrad(u, du, da, st);
-        convT_wgrad(u, du, s.a, st);
+        TcPlanes dup;
+        const TcPlanes* dupp = convT_dy_planes(u, du, dup, st);
+        convT_dgrad(u, du, da, st, dupp);
+        convT_wgrad(u, du, s.a, st, dupp);
         Act dprev = view(S_[xbuf], s.Lin, u.cin);
         leaky_bwd(s.x_in, 0.1f, da, dprev, st);
         dX = dprev;

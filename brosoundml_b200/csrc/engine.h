@@ -111,8 +111,14 @@ class Engine {
     void conv_wgrad(const ConvP& c, const Act& dy, const Act& x, cudaStream_t st, const TcPlanes* dyp = nullptr,
                     const TcPlanes* xp = nullptr, const double* bias_sum = nullptr);
     void convT(const UpP& u, const Act& x, const Act& y, int row_off, const Act* r, cudaStream_t st);
-    void convT_dgrad(const UpP& u, const Act& dy, const Act& dx, cudaStream_t st);
-    void convT_wgrad(const UpP& u, const Act& dy, const Act& x, cudaStream_t st);
+    // dyp: row-packed planes of dy from convT_dy_planes (tensor cores), else CUDA cores
+    void convT_dgrad(const UpP& u, const Act& dy, const Act& dx, cudaStream_t st, const TcPlanes* dyp = nullptr);
+    void convT_wgrad(const UpP& u, const Act& dy, const Act& x, cudaStream_t st, const TcPlanes* dyp = nullptr);
+    const TcPlanes* convT_dy_planes(const UpP& u, const Act& dy, TcPlanes& tp, cudaStream_t st);
+    // ConvTranspose1d gradients on the tensor cores (row-packed form; needs Lu % s == 0 at run time)
+    bool convT_tc(const UpP& u) const {
+        return math_ != BSML_MATH_FP32_SIMT && u.cin >= 64 && u.s * u.cout >= 32 && u.cout % 8 == 0;
+    }
     void stats_of(const Act& x, const Stats& s, cudaStream_t st);
 
     void blk_fwd(const BlkP& w, BlkC& c, const Act& y, cudaStream_t st);
@@ -147,6 +153,7 @@ class Engine {
     int64_t tcw_bytes_ = 0;
     std::vector<float*> tcw_fwd_hi_, tcw_fwd_lo_, tcw_dg_hi_, tcw_dg_lo_;
     std::vector<std::vector<float*>> tcw_up_hi_, tcw_up_lo_;
+    std::vector<float*> tcw_updg_hi_, tcw_updg_lo_;   // convT input gradient, row-packed
     float* tc_xh_ = nullptr;          // activation planes of the current tensor-core call
     float* tc_xl_ = nullptr;
     float* tc_yh_ = nullptr;          // second operand's planes (weight gradients)

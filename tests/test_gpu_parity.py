@@ -160,21 +160,35 @@ def test_tc_wgrad_atoms(orc, atom_math, math, case):
 
 
 @pytest.mark.parametrize("math", ["tf32x3", "bf16"])
-@pytest.mark.parametrize("case", [(2, 512, 40, 256, 20, 10, 5), (2, 256, 100, 128, 12, 6, 3)])
+@pytest.mark.parametrize("case", [(2, 512, 40, 256, 20, 10, 5), (2, 256, 100, 128, 12, 6, 3),
+                                  (16, 256, 400, 128, 12, 6, 3)])
 def test_tc_convT_atoms(orc, atom_math, math, case):
-    """ConvTranspose1d stride phases on the tcgen05 kernel (strided output rows)."""
+    """ConvTranspose1d on the tcgen05 kernels: forward by stride phases (strided output
+    rows); input and weight gradients as stride-1 problems over the row-packed dy."""
     B, Ci, L, Co, k, s, p = case
     rng = np.random.default_rng(5 + k)
     x = rng.normal(0, 1, (B, Ci, L)).astype(np.float32)
     W = rng.normal(0, 0.05, (Ci, Co, k)).astype(np.float32)
     b = rng.normal(0, 0.1, Co).astype(np.float32)
     Lu = (L - 1) * s - 2 * p + k
+    dy = rng.normal(0, 1, (B, Co, Lu)).astype(np.float32)
+    lib = _lib.lib()
     atom_math(math)
-    xd, Wd, bd = dev(x), dev(W), dev(b)
+    xd, Wd, bd, dyd = dev(x), dev(W), dev(b), dev(dy)
     y = torch.empty((B, Co, Lu), device="cuda")
-    _lib.check(_lib.lib().bsml_conv_transpose1d_forward(P(xd), B, Ci, L, P(Wd), P(bd), Co, k, s, p, P(y), stream()))
+    _lib.check(lib.bsml_conv_transpose1d_forward(P(xd), B, Ci, L, P(Wd), P(bd), Co, k, s, p, P(y), stream()))
     assert rel_l2(host(y), orc.convT_fwd(x, W, b, s, p)) < TC_TOL[math]
-    assert _lib.lib().bsml_device_error() == 0
+    dx = torch.empty((B, Ci, L), device="cuda")
+    _lib.check(lib.bsml_conv_transpose1d_backward_input(P(dyd), B, Ci, L, P(Wd), Co, k, s, p, P(dx), stream()))
+    assert rel_l2(host(dx), orc.convT_dgrad(dy, W, L, s, p)) < TC_TOL[math]
+    dW = torch.empty((Ci, Co, k), device="cuda")
+    db = torch.empty(Co, device="cuda")
+    _lib.check(lib.bsml_conv_transpose1d_backward_weight(P(dyd), P(xd), B, Ci, L, Co, k, s, p, P(dW), P(db),
+                                                          stream()))
+    rW, rb = orc.convT_wgrad(dy, x, k, s, p)
+    assert rel_l2(host(dW), rW) < TC_TOL[math]
+    assert rel_l2(host(db), rb) < 1e-5
+    assert lib.bsml_device_error() == 0
 
 
 CONVT_CASES = [  # (B, Ci, L, Co, k, stride, pad)
