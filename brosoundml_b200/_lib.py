@@ -76,6 +76,7 @@ SIGNATURES = {
     "bsml_set_atom_math": ([_I], _I),
     "bsml_device_error": ([], _I),
     "bsml_decoder_read_profile": ([_P, _P], _I),
+    "bsml_decoder_read_profile_records": ([_P, _P, _I, _P], _I),
     "bsml_loss_l1": ([_P, _P, _L, _P, _P, _P], _I),
     "bsml_adam_step": ([_P, _P, _P, _P, _L, _F, _F, _F, _F, _I, _P], _I),
     "bsml_conv1d_forward": ([_P, _I, _I, _I, _P, _P, _I, _I, _I, _I, _I, _P, _P], _I),

@@ -233,6 +233,14 @@ int bsml_decoder_read_profile(bsml_decoder* d, double* out) {
     });
 }
 
+int bsml_decoder_read_profile_records(bsml_decoder* d, double* out, int max_records, int* n_records) {
+    return guarded([&] {
+        need(d != nullptr && out != nullptr && n_records != nullptr && max_records >= 0,
+             "bsml_decoder_read_profile_records", "bad argument");
+        d->eng->read_profile_records(out, max_records, n_records);
+    });
+}
+
 int bsml_loss_l1(const float* audio, const float* target, int64_t n, float* loss, float* daudio, void* stream) {
     return guarded([&] {
         need(audio && target && loss && daudio && n > 0, "bsml_loss_l1", "bad argument");

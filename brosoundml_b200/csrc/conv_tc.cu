@@ -3,9 +3,9 @@
 // Forward-like form (conv fwd, conv input gradient with flipped/transposed
 // weights, ConvTranspose1d stride phases):
 //   D[co, o] = sum_{t, ci} W_t[co, ci] * X[b, (o + o_base) + t*d - p, ci]
-// Persistent kernel, one 128 (co) x 256 (positions) fp32 tile at a time. K runs
-// over 128-byte chunks of input channels; for each chunk the CTA loads one
-// activation window of 256 + (taps-1)*d rows and reuses it for every tap: tap
+// Persistent kernel, one 128 (co) x NP (positions, 192..256) fp32 tile at a time.
+// K runs over 128-byte chunks of input channels; for each chunk the CTA loads one
+// activation window of NP + (taps-1)*d rows and reuses it for every tap: tap
 // t's operand is the same window shifted by t*d rows (a descriptor offset, not
 // a new load). Only the per-tap weight tiles stream through their own ring.
 //
@@ -53,11 +53,12 @@ __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
 }
 
 // ── forward-like kernel ──────────────────────────────────────────────────────
-template <bool TF32>
+template <bool TF32, int NP>
 struct FCfg {
     static constexpr int BKE = TF32 ? 32 : 64;            // channels per 128-byte row
     static constexpr int PLANES = TF32 ? 2 : 1;
-    static constexpr int NPOS = 256;                       // positions per tile (MMA N)
+    static constexpr int NPOS = NP;                        // positions per tile (MMA N): 256, 224 or 192
+    static constexpr int HALF = NP / 2;                    // columns per epilogue warp (multiple of 16)
     static constexpr int WT_BYTES = PLANES * TILE_BYTES;   // one weight stage: 128 co x 128 B per plane
     static constexpr int NEPI = 8;                         // epilogue warps: 4 lane quarters x 2 column halves
     static constexpr int THREADS = 64 + NEPI * 32;
@@ -79,14 +80,14 @@ struct FArgs {
 
 // 320 threads = 10 warps, so one SM sub-partition holds 3 of them: 168
 // registers per thread at most (3 x 32 x 168 <= 16384).
-template <bool TF32>
-__global__ void __launch_bounds__(FCfg<TF32>::THREADS, 1)
+template <bool TF32, int NPT>
+__global__ void __launch_bounds__(FCfg<TF32, NPT>::THREADS, 1)
     conv_fwd_tc_kernel(const __grid_constant__ CUtensorMap mWh, const __grid_constant__ CUtensorMap mWl,
                        const __grid_constant__ CUtensorMap mXh, const __grid_constant__ CUtensorMap mXl,
                        const FArgs a) {
-    using F = FCfg<TF32>;
-    constexpr int NP = F::NPOS;
-    constexpr uint32_t TCOLS = 2 * NP;   // two promotion buffers of NP fp32 columns
+    using F = FCfg<TF32, NPT>;
+    constexpr int NP = F::NPOS, HC = F::HALF;
+    constexpr uint32_t TCOLS = 512;   // two promotion buffers of NP fp32 columns (allocation: a power of 2)
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = align1024(smem_raw);
     uint8_t* win = smem;                          // [2 stages][PLANES][2 * wbox rows][128 B]
@@ -246,21 +247,21 @@ __global__ void __launch_bounds__(FCfg<TF32>::THREADS, 1)
             tc::mbar_wait(mdone, 0, nullptr, tc::TC_ERR_DRAIN);
         }
     } else {
-        // ── epilogue: warp (q, h) folds lanes 32q..32q+31, columns 128h..128h+127
+        // ── epilogue: warp (q, h) folds lanes 32q..32q+31, columns HC*h..HC*h+HC-1
         const int ew = warp - 2;
         const int q = warp & 3;   // the TMEM lane quarter this warp may access
         const int h = ew >> 2;
-        const uint32_t trow = tbase + ((uint32_t)(q * 32) << 16) + (uint32_t)(h * 128);
+        const uint32_t trow = tbase + ((uint32_t)(q * 32) << 16) + (uint32_t)(h * HC);
         int G = 0;
         bool ok = true;
         for (int tile = blockIdx.x; ok && tile < a.n_tiles; tile += gridDim.x) {
             const int ct = tile % a.n_co, rest = tile / a.n_co;
             const int pt = rest % a.n_pt, b = rest / a.n_pt;
             const int mrow = ct * 128 + q * 32 + lane;   // co
-            const int o0 = pt * NP + h * 128;
-            float R[128];
+            const int o0 = pt * NP + h * HC;
+            float R[HC];
 #pragma unroll
-            for (int j = 0; j < 128; ++j) R[j] = 0.f;
+            for (int j = 0; j < HC; ++j) R[j] = 0.f;
             for (int gi = 0; gi < n_groups; ++gi) {
                 const int g = G + gi, buf = g & 1;
                 bool w = true;
@@ -269,7 +270,7 @@ __global__ void __launch_bounds__(FCfg<TF32>::THREADS, 1)
                 if (!ok) break;
                 tc::tc_fence_after();
 #pragma unroll
-                for (int c16 = 0; c16 < 128; c16 += 16) {
+                for (int c16 = 0; c16 < HC; c16 += 16) {
                     uint32_t v[16];
                     tc::tmem_ld16_nowait(trow + (uint32_t)(buf * NP + c16), v);
                     tc::tmem_wait_ld();
@@ -284,19 +285,33 @@ __global__ void __launch_bounds__(FCfg<TF32>::THREADS, 1)
             if (!ok || *(volatile int*)err != tc::TC_OK) break;
             if (mrow < a.Co) {
                 const float bv = a.bias ? a.bias[mrow] : 0.f;
+                // every read (residual, accumulated output) before the first store: with
+                // no store in between, the loads are issued back to back
+                if (a.r || a.accum) {
+#pragma unroll
+                    for (int j = 0; j < HC; ++j) {
+                        const int o = o0 + j;
+                        const int row = (o + a.o_base) * a.orow_mul + a.orow_off;
+                        if (o >= a.No || row < 0 || row >= a.y_rows) continue;
+                        float val = R[j] + bv;
+                        if (a.r) val += a.r[(int64_t)b * a.r_bs + (int64_t)(row >> a.r_shift) * a.r_ld + mrow];
+                        val *= a.alpha;
+                        if (a.accum) val += a.y[(int64_t)b * a.y_bs + (int64_t)row * a.y_ld + mrow];
+                        R[j] = val;
+                    }
+                } else {
+#pragma unroll
+                    for (int j = 0; j < HC; ++j) R[j] = (R[j] + bv) * a.alpha;
+                }
                 double s1 = 0.0, s2 = 0.0;
 #pragma unroll
-                for (int j = 0; j < 128; ++j) {
+                for (int j = 0; j < HC; ++j) {
                     const int o = o0 + j;
                     if (o >= a.No) break;
                     const int row = (o + a.o_base) * a.orow_mul + a.orow_off;
                     if (row < 0 || row >= a.y_rows) continue;
-                    float val = R[j] + bv;
-                    if (a.r) val += a.r[(int64_t)b * a.r_bs + (int64_t)(row >> a.r_shift) * a.r_ld + mrow];
-                    val *= a.alpha;
-                    float* yp = a.y + (int64_t)b * a.y_bs + (int64_t)row * a.y_ld + mrow;
-                    if (a.accum) val += *yp;
-                    *yp = val;
+                    const float val = R[j];
+                    a.y[(int64_t)b * a.y_bs + (int64_t)row * a.y_ld + mrow] = val;
                     s1 += val;
                     s2 = fma((double)val, (double)val, s2);
                 }
@@ -654,24 +669,40 @@ int sm_count() {
     return n;
 }
 
-template <bool TF32>
-void launch_fwd(const TcConvFwd& c, int mode, cudaStream_t st) {
-    using F = FCfg<TF32>;
+// Tile width: the widest of 256 / 224 / 192 positions whose activation windows
+// (two stages) still leave room for three weight stages.
+struct FwdGeom {
+    int np, wbox, win_bytes, sw, smem;
+};
+FwdGeom fwd_geom(bool tf32, int halo) {
+    const int planes = tf32 ? 2 : 1, wt = planes * TILE_BYTES, fixed = 1024 + 256;
+    FwdGeom g{};
+    for (int np : {256, 224, 192}) {
+        g.np = np;
+        g.wbox = (int)round_up(ceil_div(np + halo, 2), 8);
+        g.win_bytes = planes * 2 * g.wbox * 128;
+        g.sw = std::min(8, (SMEM_OPTIN - fixed - 2 * g.win_bytes) / wt);
+        if (g.wbox <= 256 && g.sw >= 3) break;
+    }
+    if (g.wbox > 256) fail("conv_fwd_tc", "tap span too large for the activation window");
+    if (g.sw < 2) fail("conv_fwd_tc", "activation window too large for shared memory");
+    g.smem = 2 * g.win_bytes + g.sw * wt + fixed;
+    return g;
+}
+
+template <bool TF32, int NPT>
+void launch_fwd_np(const TcConvFwd& c, int mode, const FwdGeom& g, cudaStream_t st) {
+    using F = FCfg<TF32, NPT>;
     static bool attr = false;
     if (!attr) {
-        BSML_CUDA(cudaFuncSetAttribute(conv_fwd_tc_kernel<TF32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        BSML_CUDA(cudaFuncSetAttribute(conv_fwd_tc_kernel<TF32, NPT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        SMEM_OPTIN));
         attr = true;
     }
-    const int halo = (c.taps - 1) * c.d;
     FArgs a{};
-    a.wbox = (int)round_up(ceil_div(F::NPOS + halo, 2), 8);
-    if (a.wbox > 256) fail("conv_fwd_tc", "tap span too large for the activation window");
-    a.win_bytes = F::PLANES * 2 * a.wbox * 128;
-    const int fixed = 1024 + 256;   // alignment slack + barriers
-    a.sw = std::min(F::MAX_SW, (SMEM_OPTIN - fixed - 2 * a.win_bytes) / F::WT_BYTES);
-    if (a.sw < 2) fail("conv_fwd_tc", "activation window too large for shared memory");
-    const int smem = 2 * a.win_bytes + a.sw * F::WT_BYTES + fixed;
+    a.wbox = g.wbox;
+    a.win_bytes = g.win_bytes;
+    a.sw = g.sw;
     const uint32_t bke = F::BKE;
     const CUtensorMap mWh = make_map(c.w.hi, mode, c.Ci, c.Co, c.taps, c.w.ld, c.Co, bke, 128);
     const CUtensorMap mWl = TF32 ? make_map(c.w.lo, mode, c.Ci, c.Co, c.taps, c.w.ld, c.Co, bke, 128) : mWh;
@@ -694,8 +725,19 @@ void launch_fwd(const TcConvFwd& c, int mode, cudaStream_t st) {
     if (c.stats && c.accum) fail("conv_fwd_tc", "output statistics need a non-accumulating output");
     const int grid = (int)std::min<int64_t>(tiles, sm_count());
     ::bsml::count_launch();
-    conv_fwd_tc_kernel<TF32><<<grid, F::THREADS, smem, st>>>(mWh, mWl, mXh, mXl, a);
+    conv_fwd_tc_kernel<TF32, NPT><<<grid, F::THREADS, g.smem, st>>>(mWh, mWl, mXh, mXl, a);
     BSML_LAUNCH("conv_fwd_tc");
+}
+
+template <bool TF32>
+void launch_fwd(const TcConvFwd& c, int mode, cudaStream_t st) {
+    const FwdGeom g = fwd_geom(TF32, (c.taps - 1) * c.d);
+    if (g.np == 256)
+        launch_fwd_np<TF32, 256>(c, mode, g, st);
+    else if (g.np == 224)
+        launch_fwd_np<TF32, 224>(c, mode, g, st);
+    else
+        launch_fwd_np<TF32, 192>(c, mode, g, st);
 }
 
 template <bool TF32>

@@ -170,6 +170,23 @@ void Engine::prof_end(int id, cudaStream_t st) {
     if (id >= 0) BSML_CUDA(cudaEventRecord(prof_[id].b, st));
 }
 
+void Engine::read_profile_records(double* out, int max_records, int* n_records) {
+    BSML_CUDA(cudaDeviceSynchronize());
+    int n = 0;
+    for (auto& r : prof_) {
+        if (n >= max_records) break;
+        float ms = 0;
+        BSML_CUDA(cudaEventElapsedTime(&ms, r.a, r.b));
+        out[3 * n] = r.cls;
+        out[3 * n + 1] = r.work;
+        out[3 * n + 2] = ms;
+        ++n;
+    }
+    *n_records = n;
+    prof_.clear();
+    ev_used_ = 0;
+}
+
 void Engine::read_profile(double* out) {
     for (int i = 0; i < PROF_N * 3; ++i) out[i] = 0;
     BSML_CUDA(cudaDeviceSynchronize());

@@ -40,6 +40,8 @@ class Engine {
     };
     void set_profiling(bool on);
     void read_profile(double* out);   // PROF_N * 3 doubles, then clears
+    // per launch in issue order: (class, work, ms), at most max_records; then clears
+    void read_profile_records(double* out, int max_records, int* n_records);
 
    private:
     // ── planning

@@ -23,6 +23,7 @@ namespace bsml {
 namespace {
 
 constexpr int NT = 256;   // threads per CTA
+constexpr int UNR = 4;    // rows whose loads a thread issues before it stores (memory-level parallelism)
 
 struct Out4 {
     float* y = nullptr; int64_t y_bs = 0; int y_ld = 0;                 // fp32 output (nullable)
@@ -153,11 +154,19 @@ __device__ __forceinline__ void load_chan(Chan& k, int b, int c0, int C, int L, 
     }
 }
 
+// Snake's sine and cosine: Cody-Waite reduction by 2*pi to [-pi, pi] (2*pi split
+// as C1 + C2 with C1 = 201/32, exact in 8 bits, so k*C1 is exact for |k| < 2^16),
+// then the SFU sine / cosine, whose absolute error on [-pi, pi] is about 2^-21.4.
+__device__ __forceinline__ float reduce_2pi(float x) {
+    const float k = rintf(x * 0.15915494309189535f);
+    return fmaf(-k, 1.9353071795864769e-3f, fmaf(-k, 6.28125f, x));
+}
+
 template <int ACT>
 __device__ __forceinline__ float act_f(float z, float slope, float al, float ial) {
     if (ACT == ACT_LEAKY) return z > 0.f ? z : slope * z;
     if (ACT == ACT_SNAKE) {
-        const float sn = sinf(al * z);
+        const float sn = __sinf(reduce_2pi(al * z));
         return fmaf(sn * sn, ial, z);
     }
     return z;
@@ -177,8 +186,7 @@ __global__ void __launch_bounds__(NT) adain_fwd_kernel(Act x, int rows, const do
         load_chan<ACT>(k, b, c0, C, x.L, sums, eps, mean, rstd, mean, rstd, gb, alpha,
                        blockIdx.x == 0 && threadIdx.y == 0);
         const float* base = x.p + (int64_t)b * x.bstride + c0;
-        for (int l = l0 + threadIdx.y; l < l1; l += blockDim.y) {
-            const float4 a = ldg4(base + (int64_t)l * x.ld);
+        auto row = [&](const float4& a, int l) {
             float r[4];
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
@@ -186,7 +194,18 @@ __global__ void __launch_bounds__(NT) adain_fwd_kernel(Act x, int rows, const do
                 r[j] = act_f<ACT>(z, slope, k.al[j], k.ial[j]);
             }
             put(o, b, l, c0, make_float4(r[0], r[1], r[2], r[3]), nv);
+        };
+        // UNR rows per step, all loads issued before any store
+        const int dl = blockDim.y;
+        int l = l0 + threadIdx.y;
+        for (; l + (UNR - 1) * dl < l1; l += UNR * dl) {
+            float4 a[UNR];
+#pragma unroll
+            for (int u = 0; u < UNR; ++u) a[u] = ldg4(base + (int64_t)(l + u * dl) * x.ld);
+#pragma unroll
+            for (int u = 0; u < UNR; ++u) row(a[u], l + u * dl);
         }
+        for (; l < l1; l += dl) row(ldg4(base + (int64_t)l * x.ld), l);
     }
 }
 
@@ -195,8 +214,8 @@ template <int ACT>
 __device__ __forceinline__ float act_b(float z, float g, float slope, float al, float ial, float& dal) {
     if (ACT == ACT_LEAKY) return z > 0.f ? g : slope * g;
     if (ACT == ACT_SNAKE) {
-        float sn, cs;
-        sincosf(al * z, &sn, &cs);
+        const float r = reduce_2pi(al * z);
+        const float sn = __sinf(r), cs = __cosf(r);
         const float s2a = 2.f * sn * cs;   // sin(2 alpha z)
         dal = g * (z * s2a * ial - sn * sn * ial * ial);
         return fmaf(g, s2a, g);
@@ -219,23 +238,39 @@ __global__ void __launch_bounds__(NT) adain_bwd_reduce_kernel(Act x, int rows, c
             const int c0 = 4 * v;
             Chan k;
             load_chan<ACT>(k, b, c0, C, x.L, nullptr, 0.f, nullptr, nullptr, mean, rstd, gb, alpha, false);
+            // a thread's rows (at most a few dozen) are summed in fp32, then combined in double
+            float f[3][4] = {};
             const float* xb = x.p + (int64_t)b * x.bstride + c0;
             const float* gbp = dy.p + (int64_t)b * dy.bstride + c0;
-            const int dl = blockDim.y;
-            for (int l = l0 + threadIdx.y; l < l1; l += dl) {
-                const float4 a = ldg4(xb + (int64_t)l * x.ld);
-                const float4 g = ldg4(gbp + (int64_t)l * dy.ld);
+            auto row = [&](const float4& a, const float4& g) {
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
                     const float xh = (get(a, j) - k.m[j]) * k.rs[j];
                     const float z = fmaf(k.g1[j], xh, k.be[j]);
                     float dal = 0.f;
                     const float dz = act_b<ACT>(z, get(g, j), slope, k.al[j], k.ial[j], dal);
-                    s[0][j] += dz;
-                    s[1][j] = fma((double)dz, (double)xh, s[1][j]);
-                    if (ACT == ACT_SNAKE) s[2][j] += dal;
+                    f[0][j] += dz;
+                    f[1][j] = fmaf(dz, xh, f[1][j]);
+                    if (ACT == ACT_SNAKE) f[2][j] += dal;
                 }
+            };
+            const int dl = blockDim.y;
+            int l = l0 + threadIdx.y;
+            for (; l + (UNR - 1) * dl < l1; l += UNR * dl) {
+                float4 a[UNR], g[UNR];
+#pragma unroll
+                for (int u = 0; u < UNR; ++u) {
+                    a[u] = ldg4(xb + (int64_t)(l + u * dl) * x.ld);
+                    g[u] = ldg4(gbp + (int64_t)(l + u * dl) * dy.ld);
+                }
+#pragma unroll
+                for (int u = 0; u < UNR; ++u) row(a[u], g[u]);
             }
+            for (; l < l1; l += dl) row(ldg4(xb + (int64_t)l * x.ld), ldg4(gbp + (int64_t)l * dy.ld));
+#pragma unroll
+            for (int q = 0; q < 3; ++q)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) s[q][j] = f[q][j];
         }
         combine_rows<3>(s, v, C4, C, acc + (int64_t)b * C * 3);
     }
@@ -267,11 +302,7 @@ __global__ void __launch_bounds__(NT) adain_bwd_apply_kernel(Act x, int rows, co
             }
             const float* xb = x.p + (int64_t)b * x.bstride + c0;
             const float* gbp = dy.p + (int64_t)b * dy.bstride + c0;
-            for (int l = l0 + threadIdx.y; l < l1; l += blockDim.y) {
-                const float4 a = ldg4(xb + (int64_t)l * x.ld);
-                const float4 g = ldg4(gbp + (int64_t)l * dy.ld);
-                float4 sk = make_float4(0.f, 0.f, 0.f, 0.f);
-                if (o.skip) sk = ld4(o.skip + (int64_t)b * o.s_bs + (int64_t)l * o.s_ld + c0);
+            auto row = [&](const float4& a, const float4& g, const float4& sk, int l) {
                 float r[4];
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
@@ -283,7 +314,27 @@ __global__ void __launch_bounds__(NT) adain_bwd_apply_kernel(Act x, int rows, co
                     cs[0][j] += r[j];
                 }
                 put(o, b, l, c0, make_float4(r[0], r[1], r[2], r[3]), nv);
+            };
+            auto skip_at = [&](int l) {
+                return o.skip ? ld4(o.skip + (int64_t)b * o.s_bs + (int64_t)l * o.s_ld + c0)
+                              : make_float4(0.f, 0.f, 0.f, 0.f);
+            };
+            constexpr int U2 = UNR / 2;   // three loads per row
+            const int dl = blockDim.y;
+            int l = l0 + threadIdx.y;
+            for (; l + (U2 - 1) * dl < l1; l += U2 * dl) {
+                float4 a[U2], g[U2], sk[U2];
+#pragma unroll
+                for (int u = 0; u < U2; ++u) {
+                    a[u] = ldg4(xb + (int64_t)(l + u * dl) * x.ld);
+                    g[u] = ldg4(gbp + (int64_t)(l + u * dl) * dy.ld);
+                    sk[u] = skip_at(l + u * dl);
+                }
+#pragma unroll
+                for (int u = 0; u < U2; ++u) row(a[u], g[u], sk[u], l + u * dl);
             }
+            for (; l < l1; l += dl)
+                row(ldg4(xb + (int64_t)l * x.ld), ldg4(gbp + (int64_t)l * dy.ld), skip_at(l), l);
         }
         if (colsum) combine_rows<1>(cs, v, C4, C, colsum);
     }
@@ -315,13 +366,22 @@ __global__ void __launch_bounds__(NT) scale_out_kernel(Act s, int rows, float al
         if (v < C4) {
             const int c0 = 4 * v, nv = min(4, C - c0);
             const float* base = s.p + (int64_t)b * s.bstride + c0;
-            for (int l = l0 + threadIdx.y; l < l1; l += blockDim.y) {
-                const float4 a = ldg4(base + (int64_t)l * s.ld);
+            auto row = [&](const float4& a, int l) {
                 const float4 r = make_float4(alpha * a.x, alpha * a.y, alpha * a.z, alpha * a.w);
 #pragma unroll
                 for (int j = 0; j < 4; ++j) cs[0][j] += get(r, j);
                 put(o, b, l, c0, r, nv);
+            };
+            const int dl = blockDim.y;
+            int l = l0 + threadIdx.y;
+            for (; l + (UNR - 1) * dl < l1; l += UNR * dl) {
+                float4 a[UNR];
+#pragma unroll
+                for (int u = 0; u < UNR; ++u) a[u] = ldg4(base + (int64_t)(l + u * dl) * s.ld);
+#pragma unroll
+                for (int u = 0; u < UNR; ++u) row(a[u], l + u * dl);
             }
+            for (; l < l1; l += dl) row(ldg4(base + (int64_t)l * s.ld), l);
         }
         if (colsum) combine_rows<1>(cs, v, C4, C, colsum);
     }
@@ -342,9 +402,10 @@ Geo geo(const Act& x) {
     const int C4 = (int)ceil_div(x.C, 4);
     const int bx = (int)std::min<int64_t>(round_up(C4, 32), NT);
     const int by = std::max(1, NT / bx);
-    // about 6 CTAs per SM over the whole tensor, whole multiples of by rows, 32..1024 rows
+    // about 6 CTAs per SM over the whole tensor, whole multiples of by rows, at least
+    // 32 rows and at most 64 rows per thread (the per-thread fp32 partial sums)
     int64_t rows = ceil_div((int64_t)x.B * x.L, 148 * 6);
-    rows = std::min<int64_t>(std::max<int64_t>(round_up(rows, by), 32), 1024);
+    rows = std::min<int64_t>(std::max<int64_t>(round_up(rows, by), 32), 64 * by);
     Geo g;
     g.rows = (int)rows;
     g.block = dim3((unsigned)bx, (unsigned)by);

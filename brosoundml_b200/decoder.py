@@ -92,6 +92,14 @@ class Decoder:
         _lib.check(_lib.lib().bsml_decoder_read_profile(self._h, ctypes.cast(buf, ctypes.c_void_p)))
         return {k: (buf[3 * i], buf[3 * i + 1], int(buf[3 * i + 2])) for i, k in enumerate(self.PROFILE_CLASSES)}
 
+    def read_profile_records(self, max_records: int = 4096) -> list:
+        """[(class, algorithmic FLOPs or bytes, ms)] per profiled launch, in issue order."""
+        buf = (ctypes.c_double * (3 * max_records))()
+        n = ctypes.c_int(0)
+        _lib.check(_lib.lib().bsml_decoder_read_profile_records(self._h, ctypes.cast(buf, ctypes.c_void_p),
+                                                                 max_records, ctypes.byref(n)))
+        return [(self.PROFILE_CLASSES[int(buf[3 * i])], buf[3 * i + 1], buf[3 * i + 2]) for i in range(n.value)]
+
     def forward(self, params, asr, F0, N, style, har=None, aff_in=None, audio=None, aff_out=None):
         params, asr, F0, N, style, har, aff_in = map(_f32, (params, asr, F0, N, style, har, aff_in))
         B, _, T = asr.shape

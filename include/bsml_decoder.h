@@ -137,6 +137,10 @@ int bsml_decoder_set_profiling(bsml_decoder* d, int on);
 int64_t bsml_launch_count(void);
 /* out: 3 * BSML_PROF_CLASSES doubles */
 int bsml_decoder_read_profile(bsml_decoder* d, double* out);
+/* The same record launch by launch, in issue order: 3 doubles per launch (class,
+ * work, ms), at most max_records; *n_records = how many were written. Clears the
+ * record like read_profile. */
+int bsml_decoder_read_profile_records(bsml_decoder* d, double* out, int max_records, int* n_records);
 
 /* ── loss and optimiser ─────────────────────────────────────────────────── */
 
