@@ -259,6 +259,22 @@ __global__ void __launch_bounds__(FCfg<TF32, NPT>::THREADS, 1)
             const int pt = rest % a.n_pt, b = rest / a.n_pt;
             const int mrow = ct * 128 + q * 32 + lane;   // co
             const int o0 = pt * NP + h * HC;
+            // columns j in [jlo, jhi) map to output rows inside y: row(j) = row0 + j*orow_mul
+            const int row0 = (o0 + a.o_base) * a.orow_mul + a.orow_off;
+            const int jlo = row0 >= 0 ? 0 : (-row0 + a.orow_mul - 1) / a.orow_mul;
+            int jhi = min(HC, a.No - o0);
+            jhi = a.y_rows > row0 ? min(jhi, (a.y_rows - row0 + a.orow_mul - 1) / a.orow_mul) : 0;
+            if (mrow >= a.Co) jhi = 0;
+            const float* rb = a.r ? a.r + (int64_t)b * a.r_bs + mrow : nullptr;
+            float* yb = a.y + (int64_t)b * a.y_bs + mrow;
+            // the residual / prior-output rows this tile reads at its end go to L2 now,
+            // while its MMAs run (a warp's 32 lanes share each 128-byte line)
+            if (rb || a.accum) {
+                for (int j = jlo; j < jhi; ++j) {
+                    if (rb) tc::prefetch_l2(rb + ((row0 + j * a.orow_mul) >> a.r_shift) * a.r_ld);
+                    if (a.accum) tc::prefetch_l2(yb + (row0 + j * a.orow_mul) * a.y_ld);
+                }
+            }
             float R[HC];
 #pragma unroll
             for (int j = 0; j < HC; ++j) R[j] = 0.f;
@@ -285,35 +301,38 @@ __global__ void __launch_bounds__(FCfg<TF32, NPT>::THREADS, 1)
             if (!ok || *(volatile int*)err != tc::TC_OK) break;
             if (mrow < a.Co) {
                 const float bv = a.bias ? a.bias[mrow] : 0.f;
-                // every read (residual, accumulated output) before the first store: with
-                // no store in between, the loads are issued back to back
-                if (a.r || a.accum) {
-#pragma unroll
-                    for (int j = 0; j < HC; ++j) {
-                        const int o = o0 + j;
-                        const int row = (o + a.o_base) * a.orow_mul + a.orow_off;
-                        if (o >= a.No || row < 0 || row >= a.y_rows) continue;
-                        float val = R[j] + bv;
-                        if (a.r) val += a.r[(int64_t)b * a.r_bs + (int64_t)(row >> a.r_shift) * a.r_ld + mrow];
-                        val *= a.alpha;
-                        if (a.accum) val += a.y[(int64_t)b * a.y_bs + (int64_t)row * a.y_ld + mrow];
-                        R[j] = val;
-                    }
-                } else {
-#pragma unroll
-                    for (int j = 0; j < HC; ++j) R[j] = (R[j] + bv) * a.alpha;
-                }
                 double s1 = 0.0, s2 = 0.0;
+                if (!rb && !a.accum) {
 #pragma unroll
-                for (int j = 0; j < HC; ++j) {
-                    const int o = o0 + j;
-                    if (o >= a.No) break;
-                    const int row = (o + a.o_base) * a.orow_mul + a.orow_off;
-                    if (row < 0 || row >= a.y_rows) continue;
-                    const float val = R[j];
-                    a.y[(int64_t)b * a.y_bs + (int64_t)row * a.y_ld + mrow] = val;
-                    s1 += val;
-                    s2 = fma((double)val, (double)val, s2);
+                    for (int jj = 0; jj < HC; ++jj) {
+                        if (jj < jlo || jj >= jhi) continue;
+                        const float val = (R[jj] + bv) * a.alpha;
+                        yb[(row0 + jj * a.orow_mul) * a.y_ld] = val;
+                        s1 += val;
+                        s2 = fma((double)val, (double)val, s2);
+                    }
+                }
+                // EB columns at a time: their reads are all issued before their stores
+                constexpr int EB = 8;
+#pragma unroll
+                for (int c16 = 0; (rb || a.accum) && c16 < HC; c16 += EB) {
+                    float t[EB], u[EB];
+#pragma unroll
+                    for (int j = 0; j < EB; ++j) {
+                        const int jj = c16 + j, row = row0 + jj * a.orow_mul;
+                        const bool in = jj >= jlo && jj < jhi;
+                        t[j] = (rb && in) ? rb[(row >> a.r_shift) * a.r_ld] : 0.f;
+                        u[j] = (a.accum && in) ? yb[row * a.y_ld] : 0.f;
+                    }
+#pragma unroll
+                    for (int j = 0; j < EB; ++j) {
+                        const int jj = c16 + j;
+                        if (jj < jlo || jj >= jhi) continue;
+                        const float val = (R[jj] + bv + t[j]) * a.alpha + u[j];
+                        yb[(row0 + jj * a.orow_mul) * a.y_ld] = val;
+                        s1 += val;
+                        s2 = fma((double)val, (double)val, s2);
+                    }
                 }
                 if (a.stats) {
                     atomicAdd(&a.stats[((int64_t)b * a.Co + mrow) * 2], s1);
@@ -723,6 +742,9 @@ void launch_fwd_np(const TcConvFwd& c, int mode, const FwdGeom& g, cudaStream_t 
     a.alpha = c.alpha; a.accum = c.accum ? 1 : 0;
     a.stats = c.stats;
     if (c.stats && c.accum) fail("conv_fwd_tc", "output statistics need a non-accumulating output");
+    // the epilogue forms in-clip offsets (row * ld) in 32 bits
+    if ((int64_t)c.y.L * c.y.ld >= (1ll << 31) || (c.r && (int64_t)c.r->L * c.r->ld >= (1ll << 31)))
+        fail("conv_fwd_tc", "clip too long for 32-bit row offsets");
     const int grid = (int)std::min<int64_t>(tiles, sm_count());
     ::bsml::count_launch();
     conv_fwd_tc_kernel<TF32, NPT><<<grid, F::THREADS, g.smem, st>>>(mWh, mWl, mXh, mXl, a);
