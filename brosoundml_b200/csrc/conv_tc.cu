@@ -12,8 +12,9 @@
 // Weight-gradient form (stride-1 convs):
 //   D[co, ci] (tap t) = sum_{b, o} dY[b, o, co] * X[b, o + t*d - p, ci]
 // K runs over chunks of positions; both operands are MN-major (positions are
-// rows, channels contiguous), staged as 128-byte-wide column blocks. Split-K
-// over position chunks writes fp32 partial tiles, reduced in double afterwards.
+// rows, channels contiguous), staged as 128-byte-wide column blocks. A CTA
+// computes two taps from one dY chunk and one X window. Split-K over position
+// chunks writes fp32 partial tiles, reduced in double afterwards.
 //
 // Warp roles: warp 0 issues TMA, warp 1 owns TMEM and one thread issues
 // tcgen05.mma, the remaining warps read the accumulator (each warp its 32-lane
@@ -351,62 +352,76 @@ __global__ void __launch_bounds__(FCfg<TF32, NPT>::THREADS, 1)
 }
 
 // ── weight-gradient kernel ───────────────────────────────────────────────────
+// One CTA: a 128 (co) x 128 (ci) tile for a pair of taps (t0, t0+1) over a split
+// of the position chunks. Per K step it stages one dY chunk (KROWS positions) and
+// one X window of KROWS + d rows: tap t0 + u reads the window shifted by u*d rows
+// (a descriptor offset), so the dY chunk and the X rows serve both taps.
 constexpr int BM = 128, BN = 128;
 
 template <bool TF32>
 struct WCfg {
-    static constexpr int S = TF32 ? 3 : 6;            // pipeline stages
-    static constexpr int TILES = TF32 ? 4 : 2;        // A_hi, A_lo, B_hi, B_lo | A, B
+    static constexpr int PLANES = TF32 ? 2 : 1;
     static constexpr int BKE = TF32 ? 32 : 64;        // elements per 128-byte row
-    static constexpr int STAGE_BYTES = TILES * TILE_BYTES;
-    static constexpr int SMEM = S * STAGE_BYTES + 1024 + 256;
     // positions (K rows) per stage; one MMA consumes 32 bytes of K = 8 (tf32)
     // or 16 (bf16) rows; 128-byte column blocks per 128-wide operand
     static constexpr int KROWS = TF32 ? 32 : 64;
     static constexpr int MN_BLOCKS = 128 / BKE;
+    static constexpr int A_BYTES = PLANES * MN_BLOCKS * KROWS * 128;   // dY chunk, all planes
+    static constexpr int NEPI = 8;                                      // 4 lane quarters x 2 taps
+    static constexpr int THREADS = 64 + NEPI * 32;
+    static constexpr int MAX_S = 8;
 };
 
 struct WArgs {
     int taps, p, d, Co, Ci;
-    // Ci tiles, chunks per clip, total chunks, chunks per split
-    int n_ci_tiles, chunks_pc, chunks_total, chunks_per_split;
-    float* part;   // [split][tap][Co][Ci]
+    // Ci tiles, tap pairs, chunks per clip, total chunks, chunks per split
+    int n_ci_tiles, n_pairs, chunks_pc, chunks_total, chunks_per_split;
+    int wrows;        // X window rows per column block (KROWS + d, rounded up to 8)
+    int stage_bytes;  // A_BYTES + X window (all planes)
+    int stages;
+    float* part;      // [split][tap][Co][Ci]
 };
 
 template <bool TF32>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(WCfg<TF32>::THREADS, 1)
     conv_wgrad_tc_kernel(const __grid_constant__ CUtensorMap mAh, const __grid_constant__ CUtensorMap mAl,
                          const __grid_constant__ CUtensorMap mBh, const __grid_constant__ CUtensorMap mBl,
                          const WArgs a) {
     using C = WCfg<TF32>;
-    constexpr uint32_t TCOLS = 2 * BN;
+    constexpr uint32_t TCOLS = 4 * BN;   // 2 taps x 2 promotion buffers
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = align1024(smem_raw);
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::S * C::STAGE_BYTES);
-    uint64_t* empty = full + C::S;
-    uint64_t* accf = empty + C::S;   // [2]
-    uint64_t* acce = accf + 2;       // [2]
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + a.stages * a.stage_bytes);
+    uint64_t* empty = full + C::MAX_S;
+    uint64_t* accf = empty + C::MAX_S;   // [2]
+    uint64_t* acce = accf + 2;           // [2]
     uint64_t* mdone = acce + 2;
     uint32_t* tslot = reinterpret_cast<uint32_t*>(mdone + 1);
     int* err = &g_tc_err;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int m0 = blockIdx.x * BM;                              // co
-    const int t = blockIdx.y / a.n_ci_tiles;
-    const int n0 = (blockIdx.y - t * a.n_ci_tiles) * BN;         // ci
-    const int it0 = blockIdx.z * a.chunks_per_split;
-    const int it1 = min(a.chunks_total, it0 + a.chunks_per_split);
+    const int pair = blockIdx.y / a.n_ci_tiles;
+    const int n0 = (blockIdx.y - pair * a.n_ci_tiles) * BN;      // ci
+    const int t0 = 2 * pair;
+    const int ntap = min(2, a.taps - t0);
+    // a lone last tap (odd tap count) takes twice the chunks, so every CTA has the
+    // same MMA work; its splits beyond the end write zero partials
+    const int cps = (ntap == 1 && a.taps > 1) ? 2 * a.chunks_per_split : a.chunks_per_split;
+    const int it0 = min(a.chunks_total, blockIdx.z * cps);
+    const int it1 = min(a.chunks_total, it0 + cps);
     const int n_iters = it1 > it0 ? it1 - it0 : 0;
+    const int xplane = C::MN_BLOCKS * a.wrows * 128;             // one X plane in a stage
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < C::S; ++s) {
+        for (int s = 0; s < a.stages; ++s) {
             tc::mbar_init(&full[s], 1);
             tc::mbar_init(&empty[s], 1);
         }
         tc::mbar_init(&accf[0], 1);
         tc::mbar_init(&accf[1], 1);
-        tc::mbar_init(&acce[0], 4);
-        tc::mbar_init(&acce[1], 4);
+        tc::mbar_init(&acce[0], C::NEPI);
+        tc::mbar_init(&acce[1], C::NEPI);
         tc::mbar_init(mdone, 1);
         tc::fence_barrier_init();
         tc::prefetch_tmap(&mAh);
@@ -425,82 +440,90 @@ __global__ void __launch_bounds__(192, 1)
     tc::tc_fence_after();
     const uint32_t tbase = *tslot;
 
-    if (warp == 0 && lane == 0) {
-        // ── TMA producer
-        int issued = 0;
-        bool ok = true;
-        for (int it = 0; it < n_iters; ++it) {
-            const int s = it % C::S;
-            const uint32_t ph = (it / C::S) & 1;
-            if (!tc::mbar_wait(&empty[s], ph ^ 1, err, tc::TC_ERR_WAIT_EMPTY)) { ok = false; break; }
-            uint8_t* st = smem + s * C::STAGE_BYTES;
-            uint8_t* sB = st + (TF32 ? 2 : 1) * TILE_BYTES;
-            tc::mbar_arrive_expect_tx(&full[s], C::STAGE_BYTES);
-            const int q = it0 + it;
-            const int bb = q / a.chunks_pc;
-            const int orow = (q - bb * a.chunks_pc) * C::KROWS;
-            const int xrow = orow + t * a.d - a.p;
+    if (warp == 0) {
+        if (lane == 0) {
+            // ── TMA producer
+            int issued = 0;
+            bool ok = true;
+            for (int it = 0; it < n_iters; ++it) {
+                const int s = it % a.stages;
+                const uint32_t ph = (it / a.stages) & 1;
+                if (!tc::mbar_wait(&empty[s], ph ^ 1, err, tc::TC_ERR_WAIT_EMPTY)) { ok = false; break; }
+                uint8_t* st = smem + s * a.stage_bytes;
+                uint8_t* sB = st + C::A_BYTES;
+                tc::mbar_arrive_expect_tx(&full[s], a.stage_bytes);
+                const int q = it0 + it;
+                const int bb = q / a.chunks_pc;
+                const int orow = (q - bb * a.chunks_pc) * C::KROWS;
+                const int xrow = orow + t0 * a.d - a.p;
 #pragma unroll
-            for (int j = 0; j < C::MN_BLOCKS; ++j) {
-                const int boff = j * C::KROWS * 128;
-                tc::tma_load_3d(st + boff, &mAh, &full[s], m0 + j * C::BKE, orow, bb);
-                tc::tma_load_3d(sB + boff, &mBh, &full[s], n0 + j * C::BKE, xrow, bb);
-                if (TF32) {
-                    tc::tma_load_3d(st + TILE_BYTES + boff, &mAl, &full[s], m0 + j * C::BKE, orow, bb);
-                    tc::tma_load_3d(sB + TILE_BYTES + boff, &mBl, &full[s], n0 + j * C::BKE, xrow, bb);
+                for (int j = 0; j < C::MN_BLOCKS; ++j) {
+                    tc::tma_load_3d(st + j * C::KROWS * 128, &mAh, &full[s], m0 + j * C::BKE, orow, bb);
+                    tc::tma_load_3d(sB + j * a.wrows * 128, &mBh, &full[s], n0 + j * C::BKE, xrow, bb);
+                    if (TF32) {
+                        tc::tma_load_3d(st + C::A_BYTES / 2 + j * C::KROWS * 128, &mAl, &full[s], m0 + j * C::BKE,
+                                        orow, bb);
+                        tc::tma_load_3d(sB + xplane + j * a.wrows * 128, &mBl, &full[s], n0 + j * C::BKE, xrow, bb);
+                    }
                 }
+                issued = it + 1;
             }
-            issued = it + 1;
+            if (!ok) {   // drain: the last issued stages may still have copies in flight
+                for (int it = issued - a.stages < 0 ? 0 : issued - a.stages; it < issued; ++it)
+                    tc::mbar_wait(&full[it % a.stages], (it / a.stages) & 1, nullptr, tc::TC_ERR_DRAIN);
+            }
         }
-        if (!ok) {   // drain: the last S issued stages may still have copies in flight
-            for (int it = issued - C::S < 0 ? 0 : issued - C::S; it < issued; ++it)
-                tc::mbar_wait(&full[it % C::S], (it / C::S) & 1, nullptr, tc::TC_ERR_DRAIN);
-        }
-    } else if (warp == 1 && lane == 0) {
-        // ── MMA issuer
-        constexpr uint32_t idesc = tc::make_idesc(TF32 ? 2u : 1u, 1u, 1u, BM, BN);
-        for (int it = 0; it < n_iters; ++it) {
-            const int s = it % C::S;
-            const uint32_t ph = (it / C::S) & 1;
-            const int g = it / PG;                          // promotion group
-            const bool g_first = (it % PG) == 0;
-            const bool g_last = (it % PG) == PG - 1 || it == n_iters - 1;
-            const int buf = g & 1;
-            if (g_first && g >= 2 && !tc::mbar_wait(&acce[buf], ((g >> 1) - 1) & 1, err, tc::TC_ERR_WAIT_ACC))
-                break;
-            if (!tc::mbar_wait(&full[s], ph, err, tc::TC_ERR_WAIT_FULL)) break;
-            tc::tc_fence_after();
-            const uint32_t base = tc::smem_u32(smem + s * C::STAGE_BYTES);
-            const uint32_t aH = base, aL = base + TILE_BYTES;
-            const uint32_t bH = base + (TF32 ? 2 : 1) * TILE_BYTES, bL = bH + TILE_BYTES;
-            const uint32_t d_tmem = tbase + (uint32_t)(buf * BN);
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ── MMA issuer
+            constexpr uint32_t idesc = tc::make_idesc(TF32 ? 2u : 1u, 1u, 1u, BM, BN);
+            const uint32_t lbo_a = C::KROWS * 128, lbo_b = (uint32_t)a.wrows * 128;
+            for (int it = 0; it < n_iters; ++it) {
+                const int s = it % a.stages;
+                const uint32_t ph = (it / a.stages) & 1;
+                const int g = it / PG;                          // promotion group
+                const bool g_first = (it % PG) == 0;
+                const bool g_last = (it % PG) == PG - 1 || it == n_iters - 1;
+                const int buf = g & 1;
+                if (g_first && g >= 2 &&
+                    !tc::mbar_wait(&acce[buf], ((g >> 1) - 1) & 1, err, tc::TC_ERR_WAIT_ACC))
+                    break;
+                if (!tc::mbar_wait(&full[s], ph, err, tc::TC_ERR_WAIT_FULL)) break;
+                tc::tc_fence_after();
+                const uint32_t base = tc::smem_u32(smem + s * a.stage_bytes);
+                const uint32_t aH = base, aL = base + C::A_BYTES / 2;
+                const uint32_t bH = base + C::A_BYTES, bL = bH + xplane;
+                for (int u = 0; u < ntap; ++u) {
+                    const uint32_t d_tmem = tbase + (uint32_t)((u * 2 + buf) * BN);
+                    const uint32_t bshift = (uint32_t)(u * a.d) * 128u;   // tap t0 + u: window shifted by u*d rows
 #pragma unroll
-            for (int kk = 0; kk < 4; ++kk) {
-                // +32 bytes of K = 8 rows (tf32) or 16 rows (bf16) = 1024 / 2048 B;
-                // LBO = column-block stride
-                const uint32_t off = kk * (TF32 ? 1024 : 2048);
-                const uint32_t lbo = C::KROWS * 128;
-                const uint64_t dAh = tc::desc_mnmajor(aH + off, lbo, TF32);
-                const uint64_t dBh = tc::desc_mnmajor(bH + off, lbo, TF32);
-                const uint32_t acc = (g_first && kk == 0) ? 0u : 1u;
-                tc::umma<TF32>(d_tmem, dAh, dBh, idesc, acc);
-                if (TF32) {
-                    const uint64_t dAl = tc::desc_mnmajor(aL + off, lbo, TF32);
-                    const uint64_t dBl = tc::desc_mnmajor(bL + off, lbo, TF32);
-                    tc::umma<TF32>(d_tmem, dAh, dBl, idesc, 1u);
-                    tc::umma<TF32>(d_tmem, dAl, dBh, idesc, 1u);
+                    for (int kk = 0; kk < 4; ++kk) {
+                        // +32 bytes of K = 8 rows (tf32) or 16 rows (bf16) = 1024 / 2048 B
+                        const uint32_t off = kk * (TF32 ? 1024 : 2048);
+                        const uint64_t dAh = tc::desc_mnmajor(aH + off, lbo_a, TF32);
+                        const uint64_t dBh = tc::desc_mnmajor(bH + bshift + off, lbo_b, TF32);
+                        const uint32_t acc = (g_first && kk == 0) ? 0u : 1u;
+                        tc::umma<TF32>(d_tmem, dAh, dBh, idesc, acc);
+                        if (TF32) {
+                            const uint64_t dAl = tc::desc_mnmajor(aL + off, lbo_a, TF32);
+                            const uint64_t dBl = tc::desc_mnmajor(bL + bshift + off, lbo_b, TF32);
+                            tc::umma<TF32>(d_tmem, dAh, dBl, idesc, 1u);
+                            tc::umma<TF32>(d_tmem, dAl, dBh, idesc, 1u);
+                        }
+                    }
                 }
+                tc::umma_commit(&empty[s]);           // frees the stage once these MMAs have read it
+                if (g_last) tc::umma_commit(&accf[buf]);
             }
-            tc::umma_commit(&empty[s]);           // frees the stage once these MMAs have read it
-            if (g_last) tc::umma_commit(&accf[buf]);
+            tc::umma_commit(mdone);
+            tc::mbar_wait(mdone, 0, nullptr, tc::TC_ERR_DRAIN);
         }
-        tc::umma_commit(mdone);
-        tc::mbar_wait(mdone, 0, nullptr, tc::TC_ERR_DRAIN);
-    } else if (warp >= 2) {
-        // ── epilogue
+    } else {
+        // ── epilogue: warp (q, u) folds lanes 32q..32q+31 of tap t0 + u
         const int q = warp & 3;
+        const int u = (warp - 2) >> 2;
         const int mrow = m0 + q * 32 + lane;   // co
-        const uint32_t trow = tbase + ((uint32_t)(q * 32) << 16);
+        const uint32_t trow = tbase + ((uint32_t)(q * 32) << 16) + (uint32_t)(u * 2 * BN);
         float R[BN];
 #pragma unroll
         for (int j = 0; j < BN; ++j) R[j] = 0.f;
@@ -513,24 +536,23 @@ __global__ void __launch_bounds__(192, 1)
             ok = __shfl_sync(0xffffffffu, w ? 1 : 0, 0) != 0;
             if (!ok) break;
             tc::tc_fence_after();
+            if (u < ntap) {
 #pragma unroll
-            for (int half = 0; half < BN; half += 64) {   // 4 loads in flight, one wait
-                uint32_t v[4][16];
+                for (int c16 = 0; c16 < BN; c16 += 16) {
+                    uint32_t v[16];
+                    tc::tmem_ld16_nowait(trow + (uint32_t)(buf * BN + c16), v);
+                    tc::tmem_wait_ld();
 #pragma unroll
-                for (int q4 = 0; q4 < 4; ++q4) tc::tmem_ld16_nowait(trow + buf * BN + half + q4 * 16, v[q4]);
-                tc::tmem_wait_ld();
-#pragma unroll
-                for (int q4 = 0; q4 < 4; ++q4)
-#pragma unroll
-                    for (int j = 0; j < 16; ++j) R[half + q4 * 16 + j] += __uint_as_float(v[q4][j]);
+                    for (int j = 0; j < 16; ++j) R[c16 + j] += __uint_as_float(v[j]);
+                }
             }
             tc::tc_fence_before();
             __syncwarp();
             if (lane == 0) tc::mbar_arrive(&acce[buf]);
         }
         const bool valid = ok && *(volatile int*)err == tc::TC_OK;
-        if (valid && mrow < a.Co) {
-            float* pp = a.part + (((int64_t)blockIdx.z * a.taps + t) * a.Co + mrow) * (int64_t)a.Ci;
+        if (valid && u < ntap && mrow < a.Co) {
+            float* pp = a.part + (((int64_t)blockIdx.z * a.taps + t0 + u) * a.Co + mrow) * (int64_t)a.Ci;
 #pragma unroll
             for (int j = 0; j < BN; ++j)
                 if (n0 + j < a.Ci) pp[n0 + j] = R[j];
@@ -768,32 +790,44 @@ void launch_wgrad(const TcConvWgrad& c, int mode, float* part, int64_t part_cap,
     static bool attr = false;
     if (!attr) {
         BSML_CUDA(cudaFuncSetAttribute(conv_wgrad_tc_kernel<TF32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       CF::SMEM));
+                                       SMEM_OPTIN));
         attr = true;
     }
+    WArgs a{};
+    a.taps = c.taps; a.p = c.p; a.d = c.d; a.Co = c.Co; a.Ci = c.Ci;
+    // X window: KROWS positions plus the second tap's shift
+    a.wrows = (int)round_up(CF::KROWS + (c.taps > 1 ? c.d : 0), 8);
+    if (a.wrows > 256) fail("conv_wgrad_tc", "dilation too large for the position window");
+    a.stage_bytes = CF::A_BYTES + CF::PLANES * CF::MN_BLOCKS * a.wrows * 128;
+    const int fixed = 1024 + 256;
+    a.stages = std::min(CF::MAX_S, (SMEM_OPTIN - fixed) / a.stage_bytes);
+    if (a.stages < 2) fail("conv_wgrad_tc", "stage too large for shared memory");
+    const int smem = a.stages * a.stage_bytes + fixed;
     const uint32_t bke = CF::BKE, kr = CF::KROWS;
     // A: dY planes [B][Lo][ld] (M = Co along the contiguous dim); B: X planes (N = Ci)
     const CUtensorMap mAh = make_map(c.dy.hi, mode, c.Co, c.Lo, c.B, c.dy.ld, c.Lo, bke, kr, TF32);
     const CUtensorMap mAl = TF32 ? make_map(c.dy.lo, mode, c.Co, c.Lo, c.B, c.dy.ld, c.Lo, bke, kr, TF32) : mAh;
-    const CUtensorMap mBh = make_map(c.x.hi, mode, c.Ci, c.L_in, c.B, c.x.ld, c.L_in, bke, kr, TF32);
-    const CUtensorMap mBl = TF32 ? make_map(c.x.lo, mode, c.Ci, c.L_in, c.B, c.x.ld, c.L_in, bke, kr, TF32) : mBh;
-    WArgs a{};
-    a.taps = c.taps; a.p = c.p; a.d = c.d; a.Co = c.Co; a.Ci = c.Ci;
+    const CUtensorMap mBh = make_map(c.x.hi, mode, c.Ci, c.L_in, c.B, c.x.ld, c.L_in, bke, a.wrows, TF32);
+    const CUtensorMap mBl =
+        TF32 ? make_map(c.x.lo, mode, c.Ci, c.L_in, c.B, c.x.ld, c.L_in, bke, a.wrows, TF32) : mBh;
     a.n_ci_tiles = (int)ceil_div(c.Ci, BN);
+    a.n_pairs = (int)ceil_div(c.taps, 2);
     a.chunks_pc = (int)ceil_div(c.Lo, CF::KROWS);
     a.chunks_total = a.chunks_pc * c.B;
-    const int tiles = (int)ceil_div(c.Co, BM) * a.n_ci_tiles * c.taps;
-    // ~2 waves of CTAs on the SMs, each with >= 8 chunks of K, within the partial budget
-    int64_t splits = ceil_div(2 * sm_count(), tiles);
+    // CTAs of equal work: a tap pair counts 1, a lone last tap (odd count, twice the
+    // chunks) 1/2. Splits for ~2 full waves, each CTA >= 8 chunks, within the partial budget.
+    const int full_pairs = c.taps / 2, lone = (c.taps % 2 == 1 && c.taps > 1) ? 1 : 0;
+    const double units = (double)ceil_div(c.Co, BM) * a.n_ci_tiles * (full_pairs + 0.5 * lone + (c.taps == 1 ? 1 : 0));
+    int64_t splits = std::max<int64_t>(1, (int64_t)(2 * sm_count() / units));
     splits = std::min<int64_t>(splits, ceil_div(a.chunks_total, 8));
     splits = std::min<int64_t>(splits, part_cap / ((int64_t)c.taps * c.Co * c.Ci));
     if (splits < 1) fail("conv_wgrad_tc", "split-K partial buffer too small");
     a.chunks_per_split = (int)ceil_div(a.chunks_total, splits);
     splits = ceil_div(a.chunks_total, a.chunks_per_split);
     a.part = part;
-    dim3 grid((unsigned)ceil_div(c.Co, BM), (unsigned)(a.n_ci_tiles * c.taps), (unsigned)splits);
+    dim3 grid((unsigned)ceil_div(c.Co, BM), (unsigned)(a.n_ci_tiles * a.n_pairs), (unsigned)splits);
     ::bsml::count_launch();
-    conv_wgrad_tc_kernel<TF32><<<grid, 192, CF::SMEM, st>>>(mAh, mAl, mBh, mBl, a);
+    conv_wgrad_tc_kernel<TF32><<<grid, CF::THREADS, smem, st>>>(mAh, mAl, mBh, mBl, a);
     BSML_LAUNCH("conv_wgrad_tc");
     ::bsml::count_launch();
     if (c.ct_s > 0) {
