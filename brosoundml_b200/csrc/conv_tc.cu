@@ -405,11 +405,12 @@ __global__ void __launch_bounds__(WCfg<TF32>::THREADS, 1)
     const int n0 = (blockIdx.y - pair * a.n_ci_tiles) * BN;      // ci
     const int t0 = 2 * pair;
     const int ntap = min(2, a.taps - t0);
-    // a lone last tap (odd tap count) takes twice the chunks, so every CTA has the
-    // same MMA work; its splits beyond the end write zero partials
-    const int cps = (ntap == 1 && a.taps > 1) ? 2 * a.chunks_per_split : a.chunks_per_split;
-    const int it0 = min(a.chunks_total, blockIdx.z * cps);
-    const int it1 = min(a.chunks_total, it0 + cps);
+    // A lone last tap (odd tap count > 1) still issues the second tap's MMAs (into a
+    // TMEM buffer nobody reads): every CTA then runs at the same pace, so the CTAs
+    // of one split stream the same dY / X rows together and share them in L2.
+    const int nmma = a.taps > 1 ? 2 : 1;
+    const int it0 = blockIdx.z * a.chunks_per_split;
+    const int it1 = min(a.chunks_total, it0 + a.chunks_per_split);
     const int n_iters = it1 > it0 ? it1 - it0 : 0;
     const int xplane = C::MN_BLOCKS * a.wrows * 128;             // one X plane in a stage
 
@@ -493,7 +494,7 @@ __global__ void __launch_bounds__(WCfg<TF32>::THREADS, 1)
                 const uint32_t base = tc::smem_u32(smem + s * a.stage_bytes);
                 const uint32_t aH = base, aL = base + C::A_BYTES / 2;
                 const uint32_t bH = base + C::A_BYTES, bL = bH + xplane;
-                for (int u = 0; u < ntap; ++u) {
+                for (int u = 0; u < nmma; ++u) {
                     const uint32_t d_tmem = tbase + (uint32_t)((u * 2 + buf) * BN);
                     const uint32_t bshift = (uint32_t)(u * a.d) * 128u;   // tap t0 + u: window shifted by u*d rows
 #pragma unroll
@@ -814,11 +815,9 @@ void launch_wgrad(const TcConvWgrad& c, int mode, float* part, int64_t part_cap,
     a.n_pairs = (int)ceil_div(c.taps, 2);
     a.chunks_pc = (int)ceil_div(c.Lo, CF::KROWS);
     a.chunks_total = a.chunks_pc * c.B;
-    // CTAs of equal work: a tap pair counts 1, a lone last tap (odd count, twice the
-    // chunks) 1/2. Splits for ~2 full waves, each CTA >= 8 chunks, within the partial budget.
-    const int full_pairs = c.taps / 2, lone = (c.taps % 2 == 1 && c.taps > 1) ? 1 : 0;
-    const double units = (double)ceil_div(c.Co, BM) * a.n_ci_tiles * (full_pairs + 0.5 * lone + (c.taps == 1 ? 1 : 0));
-    int64_t splits = std::max<int64_t>(1, (int64_t)(2 * sm_count() / units));
+    // ~2 full waves of equal CTAs, each with >= 8 chunks of K, within the partial budget
+    const int64_t tiles = ceil_div(c.Co, BM) * a.n_ci_tiles * a.n_pairs;
+    int64_t splits = std::max<int64_t>(1, 2 * sm_count() / tiles);
     splits = std::min<int64_t>(splits, ceil_div(a.chunks_total, 8));
     splits = std::min<int64_t>(splits, part_cap / ((int64_t)c.taps * c.Co * c.Ci));
     if (splits < 1) fail("conv_wgrad_tc", "split-K partial buffer too small");
