@@ -163,7 +163,9 @@ class Engine {
     float* tc_dh_ = nullptr;          // planes of the running resblock input gradient
     float* tc_dl_ = nullptr;
     int tc_mode() const { return math_ == BSML_MATH_BF16 ? TC_BF16 : TC_TF32X3; }
-    bool tc_ok(int K, int M, int s) const { return math_ != BSML_MATH_FP32_SIMT && s == 1 && K >= 32 && M >= 64; }
+    // stride-1 convs run on the tensor cores; narrow channel counts (conv_post's 22
+    // outputs, the 22 harmonic channels) are zero-padded to the tile by TMA
+    bool tc_ok(int K, int M, int s) const { return math_ != BSML_MATH_FP32_SIMT && s == 1 && K >= 8 && M >= 16; }
     TcPlanes tc_planes(const Act& x, cudaStream_t st);   // x -> planes in tc_xh_ / tc_xl_
     void tc_launch(const Act& x, const TcPlanes& xp, const float* whi, const float* wlo, int taps, int M,
                    const Act& y, const float* bias, const Act* r, int r_shift, int p, int d, int No, int o_base,
