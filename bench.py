@@ -203,7 +203,7 @@ def main():
     import torch.distributed as dist
     from datetime import timedelta
 
-    from brosoundml_b200 import config, synth
+    from brosoundml_b200 import config, dp, synth
     from brosoundml_b200 import _lib
     from brosoundml_b200.decoder import Decoder, adam_step, l1_loss
 
@@ -236,8 +236,7 @@ def main():
         dec.forward(params, inp["asr"], inp["F0"], inp["N"], inp["style"], audio=audio)
         l1_loss(audio, inp["target"], lossbuf, dabuf)
         dec.backward(dabuf, grads=grads)
-        if world > 1:
-            dist.all_reduce(grads, op=dist.ReduceOp.AVG)
+        dp.average_gradients(grads)   # one NCCL all-reduce of the flat gradient (N > 1)
         state["step"] += 1
         adam_step(params, grads, m, v, 1e-5, state["step"])
 

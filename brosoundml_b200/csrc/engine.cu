@@ -822,6 +822,9 @@ void Engine::forward(int B, int T, const float* params, const float* asr, const 
     if (B < 1 || T < 1) fail("bsml_decoder_forward", "B and T must be positive");
     if (!params || !asr || !F0 || !N || !audio) fail("bsml_decoder_forward", "null input");
     if (!aff_in && !style) fail("bsml_decoder_forward", "style is required unless aff_in is given");
+    if (!har && lay_.cfg.har_ch != lay_.cfg.n_fft + 2)
+        fail("bsml_decoder_forward", "the harmonic source makes n_fft + 2 channels but har_ch = " +
+                                         std::to_string(lay_.cfg.har_ch) + ": pass har");
     BSML_CUDA(cudaSetDevice(device_));
     ensure_plan(B, T, frames, har != nullptr);
     const auto& cf = lay_.cfg;

@@ -1175,6 +1175,8 @@ int run(const orc_cfg* cfg, int B, int T, const R* params, const R* asr, const R
     d.N_in = N;
     std::vector<R> har_local;
     if (!har) {
+        // the harmonic source makes n_fft + 2 channels (|X| and angle X per bin)
+        if (cfg->har_ch != cfg->n_fft + 2) return -2;
         const int S = 2 * T * cfg->upsample_scale;
         frames = S / cfg->hop + 1;
         har_local.resize((size_t)B * cfg->har_ch * frames);

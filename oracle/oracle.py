@@ -126,6 +126,9 @@ class Oracle:
         """
         c = self.cfg_dict
         B, _, T = asr.shape
+        if har is None and c["har_ch"] != c["n_fft"] + 2:
+            raise ValueError("oracle: the harmonic source makes n_fft + 2 channels; "
+                             f"this config has har_ch = {c['har_ch']}: pass har")
         f = (lambda a: None if a is None else np.ascontiguousarray(a, dtype=dtype))
         params, asr, F0, N, style, har, aff_in, daudio = map(f, (params, asr, F0, N, style, har, aff_in, daudio))
         L_last_frames = (2 * T * c["upsample_scale"]) // c["hop"] + 1 if har is None else har.shape[2]
@@ -139,10 +142,12 @@ class Oracle:
         if want_aff:
             out["aff"] = np.zeros(B * self.aff_per_clip, dtype)
         fn = lib().orc_decoder_run_f32 if dtype == np.float32 else lib().orc_decoder_run_f64
-        fn(ctypes.byref(self.cfg), B, T, _p(params), _p(asr), _p(F0), _p(N), _p(style), _p(har),
-           0 if har is None else har.shape[2], _p(aff_in), _p(daudio), _p(out["audio"]),
-           _p(out.get("grads")), _p(out.get("d_asr")), _p(out.get("d_style")), _p(out.get("d_aff")),
-           _p(out.get("aff")))
+        rc = fn(ctypes.byref(self.cfg), B, T, _p(params), _p(asr), _p(F0), _p(N), _p(style), _p(har),
+                0 if har is None else har.shape[2], _p(aff_in), _p(daudio), _p(out["audio"]),
+                _p(out.get("grads")), _p(out.get("d_asr")), _p(out.get("d_style")), _p(out.get("d_aff")),
+                _p(out.get("aff")))
+        if rc != 0:
+            raise RuntimeError(f"oracle: decoder run failed ({rc})")
         return out
 
     def harmonic_source(self, params, F0):

@@ -208,3 +208,14 @@ def test_fd_reference_mode_affines():
     r = o.run(p, x["asr"], x["F0"], x["N"], x["style"], har=har, aff_in=aff, daudio=a - tgt, dtype=np.float64)
     an, fd = _fd_dir(loss, aff, r["d_aff"], np.random.default_rng(1), h=1e-6)
     assert abs(an - fd) <= 1e-6 + 1e-5 * abs(fd)
+
+
+def test_harmonic_source_needs_matching_channels():
+    """The built-in harmonic source makes n_fft + 2 channels: a config with another
+    har_ch must be given har explicitly (the miniature config has har_ch = 1)."""
+    cfg = config.miniature()
+    o = Oracle(cfg)
+    x = synth.make_inputs(cfg, 1, 4, 1)
+    p = np.zeros(o.n_params, np.float32)
+    with pytest.raises(ValueError):
+        o.run(p, x["asr"], x["F0"], x["N"], x["style"])
