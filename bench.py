@@ -212,6 +212,9 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     if world > 1:
+        # rank 0's stdout carries only the JSON line: no NCCL version banner
+        if os.environ.get("NCCL_DEBUG", "VERSION").upper() == "VERSION":
+            os.environ["NCCL_DEBUG"] = "WARN"
         dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=torch.device("cuda", local))
     math = args.math or Decoder.DEFAULT_MATH
     cfg = config.kokoro_82m()
