@@ -379,7 +379,7 @@ struct WArgs {
     int wrows;        // X window rows per column block (KROWS + d, rounded up to 8)
     int stage_bytes;  // A_BYTES + X window (all planes)
     int stages;
-    float* part;      // [split][tap][Co][Ci]
+    float* part;      // [split][Co][Ci][tap]
 };
 
 template <bool TF32>
@@ -553,10 +553,11 @@ __global__ void __launch_bounds__(WCfg<TF32>::THREADS, 1)
         }
         const bool valid = ok && *(volatile int*)err == tc::TC_OK;
         if (valid && u < ntap && mrow < a.Co) {
-            float* pp = a.part + (((int64_t)blockIdx.z * a.taps + t0 + u) * a.Co + mrow) * (int64_t)a.Ci;
+            // partials [split][co][ci][tap]: the reduce then reads them in dW order
+            float* pp = a.part + (((int64_t)blockIdx.z * a.Co + mrow) * a.Ci + n0) * a.taps + t0 + u;
 #pragma unroll
             for (int j = 0; j < BN; ++j)
-                if (n0 + j < a.Ci) pp[n0 + j] = R[j];
+                if (n0 + j < a.Ci) pp[(int64_t)j * a.taps] = R[j];
         }
     }
     tc::tc_fence_before();
@@ -623,23 +624,18 @@ __global__ void pack_w_kernel(const float* W, int kind, int Co, int Ci, int k, i
     }
 }
 
-// dW[(co*Ci + ci)*k + t] (+)= sum_split part[split][t][co][ci]
+// dW[(co*Ci + ci)*k + t] (+)= sum_split part[split][co][ci][t]
 __global__ void wgrad_reduce_kernel(const float* part, int splits, int taps, int Co, int Ci, float* dW, int accum) {
     const int64_t n = (int64_t)Co * Ci * taps;
-    const int64_t stride_split = (int64_t)taps * Co * Ci;
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
-        const int t = (int)(i % taps);
-        const int64_t q = i / taps;
-        const int ci = (int)(q % Ci), co = (int)(q / Ci);
-        const int64_t src = ((int64_t)t * Co + co) * Ci + ci;
         double s = 0;
-        for (int sp = 0; sp < splits; ++sp) s += part[sp * stride_split + src];
+        for (int sp = 0; sp < splits; ++sp) s += part[sp * n + i];
         dW[i] = (float)(accum ? dW[i] + s : s);
     }
 }
 
 // ConvTranspose1d weight gradient from the row-packed partials:
-// dW[(ci*CoT + co)*k + t] (+)= sum_split part[split][tau][ci][j*CoT + co], t - p = (tau + u_min)*s + j
+// dW[(ci*CoT + co)*k + t] (+)= sum_split part[split][ci][j*CoT + co][tau], t - p = (tau + u_min)*s + j
 __global__ void wgrad_reduce_convT_kernel(const float* part, int splits, int taps, int M, int N, int CoT, int k, int s,
                                           int p, int u_min, float* dW, int accum) {
     const int64_t n = (int64_t)M * CoT * k;
@@ -651,7 +647,7 @@ __global__ void wgrad_reduce_convT_kernel(const float* part, int splits, int tap
         const int tp = t - p;
         const int u = tp >= 0 ? tp / s : -((-tp + s - 1) / s);
         const int j = tp - u * s, tau = u - u_min;
-        const int64_t src = ((int64_t)tau * M + m) * N + (int64_t)j * CoT + co;
+        const int64_t src = ((int64_t)m * N + (int64_t)j * CoT + co) * taps + tau;
         double acc = 0;
         for (int sp = 0; sp < splits; ++sp) acc += part[sp * stride_split + src];
         dW[i] = (float)(accum ? dW[i] + acc : acc);

@@ -210,27 +210,65 @@ __global__ void dwconvT_dgrad_kernel(Act dy, const float* W, int k, int s, int p
     }
 }
 // one thread per (c, t) + bias; rows reduced serially in double (C*k small)
-__global__ void dwconvT_wgrad_kernel(Act dy, Act x, int k, int s, int p, float* dW, float* db) {
-    const int idx = blockIdx.x * blockDim.x + threadIdx.x;
-    const int C = x.C;
-    if (idx >= C * (k + 1)) return;
-    const int c = idx % C, t = idx / C;
-    double acc = 0;
-    for (int b = 0; b < x.B; ++b) {
-        if (t == k) {
-            for (int j = 0; j < dy.L; ++j) acc += dy.row(b, j)[c];
-        } else {
-            for (int l = 0; l < x.L; ++l) {
-                const int j = l * s - p + t;
-                if (j >= 0 && j < dy.L) acc += (double)x.row(b, l)[c] * dy.row(b, j)[c];
-            }
+// dW[c*k + t] += sum over a chunk of input rows (b, l) of x[b, l, c] * dy[b, l*s - p + t, c]
+constexpr int DW_MAXK = 8;
+__global__ void dwconvT_wgrad_kernel(Act dy, Act x, int k, int s, int p, int rows_per, double* acc) {
+    const int c = blockIdx.x * blockDim.x + threadIdx.x;
+    if (c >= x.C) return;
+    const int r0 = blockIdx.y * rows_per, r1 = min(x.B * x.L, r0 + rows_per);
+    double a[DW_MAXK] = {};
+    for (int r = r0; r < r1; ++r) {
+        const int b = r / x.L, l = r - b * x.L;
+        const double xv = x.row(b, l)[c];
+#pragma unroll
+        for (int t = 0; t < DW_MAXK; ++t) {
+            const int j = l * s - p + t;
+            if (t < k && j >= 0 && j < dy.L) a[t] += xv * (double)dy.row(b, j)[c];
         }
     }
-    if (t == k) {
-        if (db) db[c] = (float)acc;
-    } else {
-        dW[c * k + t] = (float)acc;
+#pragma unroll
+    for (int t = 0; t < DW_MAXK; ++t)
+        if (t < k) atomicAdd(&acc[(int64_t)c * k + t], a[t]);
+}
+
+// d (op)= s on 4-channel groups (128-bit loads / stores), one clip per blockIdx.y
+enum { EW_COPY = 0, EW_ADD = 1, EW_SCALE = 2 };
+template <int OP>
+__global__ void ew4_kernel(Act s, Act d, float alpha) {
+    const int b = blockIdx.y;
+    const int C4 = (s.C + 3) >> 2, n = s.L * C4;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        const int l = i / C4, c = 4 * (i - l * C4), nv = min(4, s.C - c);
+        const float4 a = *reinterpret_cast<const float4*>(s.row(b, l) + c);
+        float4 r = a;
+        if (OP == EW_ADD) {
+            const float4 o = *reinterpret_cast<const float4*>(d.row(b, l) + c);
+            r = make_float4(fmaf(alpha, a.x, o.x), fmaf(alpha, a.y, o.y), fmaf(alpha, a.z, o.z), fmaf(alpha, a.w, o.w));
+        } else if (OP == EW_SCALE) {
+            r = make_float4(alpha * a.x, alpha * a.y, alpha * a.z, alpha * a.w);
+        }
+        float* dp = d.row(b, l) + c;
+        if (nv == 4) {
+            *reinterpret_cast<float4*>(dp) = r;
+        } else {
+            dp[0] = r.x;
+            if (nv > 1) dp[1] = r.y;
+            if (nv > 2) dp[2] = r.z;
+        }
     }
+}
+
+bool vec_ok(const Act& a) {
+    return (reinterpret_cast<uintptr_t>(a.p) & 15) == 0 && (a.ld & 3) == 0 && (a.bstride & 3) == 0;
+}
+
+template <int OP>
+void ew4(const Act& s, const Act& d, float alpha, cudaStream_t st) {
+    const int64_t n = (int64_t)s.L * ceil_div(s.C, 4);
+    const int gx = (int)std::min<int64_t>(std::max<int64_t>(ceil_div(n, 256), 1), std::max(1, 148 * 8 / std::max(s.B, 1)));
+    ::bsml::count_launch();
+    ew4_kernel<OP><<<dim3((unsigned)gx, (unsigned)s.B), 256, 0, st>>>(s, d, alpha);
+    BSML_LAUNCH("ew4");
 }
 
 // ── AdaIN fc: one warp per output row o of every AdaIN, all clips
@@ -327,16 +365,19 @@ void leaky_bwd(const Act& x, float slope, const Act& dy, const Act& dx, cudaStre
     BSML_LAUNCH("leaky_bwd");
 }
 void copy_act(const Act& s, const Act& d, cudaStream_t st) {
+    if (s.numel() > 0 && vec_ok(s) && vec_ok(d)) return ew4<EW_COPY>(s, d, 1.f, st);
     ::bsml::count_launch();
     copy_kernel<<<grid_for(s.numel()), 256, 0, st>>>(s, d);
     BSML_LAUNCH("copy_act");
 }
 void add_act(const Act& s, const Act& d, float alpha, cudaStream_t st) {
+    if (s.numel() > 0 && vec_ok(s) && vec_ok(d)) return ew4<EW_ADD>(s, d, alpha, st);
     ::bsml::count_launch();
     add_kernel<<<grid_for(s.numel()), 256, 0, st>>>(s, d, alpha);
     BSML_LAUNCH("add_act");
 }
 void scale_act(const Act& x, float alpha, cudaStream_t st) {
+    if (x.numel() > 0 && vec_ok(x)) return ew4<EW_SCALE>(x, x, alpha, st);
     ::bsml::count_launch();
     scale_kernel<<<grid_for(x.numel()), 256, 0, st>>>(x, alpha);
     BSML_LAUNCH("scale_act");
@@ -384,11 +425,17 @@ void dwconvT_dgrad(const Act& dy, const float* W, int k, int s, int p, const Act
     dwconvT_dgrad_kernel<<<grid_for(dx.numel()), 256, 0, st>>>(dy, W, k, s, p, dx);
     BSML_LAUNCH("dwconvT_dgrad");
 }
-void dwconvT_wgrad(const Act& dy, const Act& x, int k, int s, int p, float* dW, float* db, cudaStream_t st) {
-    const int n = x.C * (k + 1);
+void dwconvT_wgrad(const Act& dy, const Act& x, int k, int s, int p, float* dW, float* db, double* acc,
+                   float* part, cudaStream_t st) {
+    if (k > DW_MAXK) fail("dwconvT_wgrad", "kernel size above 8");
+    BSML_CUDA(cudaMemsetAsync(acc, 0, sizeof(double) * x.C * k, st));
+    const int rows_per = 64;
+    dim3 grid((unsigned)ceil_div(x.C, 128), (unsigned)ceil_div((int64_t)x.B * x.L, rows_per));
     ::bsml::count_launch();
-    dwconvT_wgrad_kernel<<<(unsigned)ceil_div(n, 128), 128, 0, st>>>(dy, x, k, s, p, dW, db);
+    dwconvT_wgrad_kernel<<<grid, 128, 0, st>>>(dy, x, k, s, p, rows_per, acc);
     BSML_LAUNCH("dwconvT_wgrad");
+    d2f(acc, x.C * k, dW, false, st);
+    if (db) colsum(dy, db, false, part, st);
 }
 
 void affine_fc_fwd(const FcRow* table, int n_entries, int total_rows, const int* row_entry, const float* params,

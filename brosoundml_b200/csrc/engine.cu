@@ -697,7 +697,7 @@ void Engine::blk_bwd(const BlkP& w, BlkC& c, const Act& dY, const Act& dX, cudaS
     if (w.up) {
         dr = view(S_[2], Lin, w.cin);
         dwconvT_dgrad(dpooled, P(w.pool_w), 3, 2, 1, dr, st);
-        if (grads_) dwconvT_wgrad(dpooled, c.r, 3, 2, 1, G(w.pool_w), G(w.pool_b), st);
+        if (grads_) dwconvT_wgrad(dpooled, c.r, 3, 2, 1, G(w.pool_w), G(w.pool_b), dacc_, part_, st);
     }
     adain_act_bwd(c.x, c.s1.mean, c.s1.rstd, aff(w.n1), ACT_LEAKY, 0.2f, nullptr, dr, dX, nullptr, daff(w.n1),
                   nullptr, dacc_, st);

@@ -111,7 +111,9 @@ void fill(float* p, int64_t n, float v, cudaStream_t st);
 // depthwise ConvTranspose1d (groups = C), weight (C, 1, k): the upsampling pool.
 void dwconvT_fwd(const Act& x, const float* W, const float* bias, int k, int s, int p, const Act& y, cudaStream_t st);
 void dwconvT_dgrad(const Act& dy, const float* W, int k, int s, int p, const Act& dx, cudaStream_t st);
-void dwconvT_wgrad(const Act& dy, const Act& x, int k, int s, int p, float* dW, float* db, cudaStream_t st);
+// acc: C*k doubles of scratch; part: colsum_partial_floats(dy) floats (bias sums)
+void dwconvT_wgrad(const Act& dy, const Act& x, int k, int s, int p, float* dW, float* db, double* acc,
+                   float* part, cudaStream_t st);
 
 // ── AdaIN fc (style -> gamma/beta) for many AdaINs at once ──────────────────
 // One AdaIN fc: weight/bias offsets into the flat params, output offset into the
