@@ -93,6 +93,18 @@ SIGNATURES = {
     "bsml_istft_forward": ([_P, _P, _I, _I, _I, _I, _P, _P], _I),
     "bsml_istft_backward": ([_P, _I, _I, _I, _I, _P, _P, _P], _I),
     "bsml_harmonic_source": ([_CFG, _P, _I, _I, _P, _P, _P, _P], _I),
+    "bsml_lora_create": ([_P, _I, _F, ctypes.c_uint64, ctypes.POINTER(_P)], _I),
+    "bsml_lora_destroy": ([_P], None),
+    "bsml_lora_layout": ([_P, ctypes.POINTER(_L), ctypes.POINTER(_I), ctypes.POINTER(_I), ctypes.POINTER(_I),
+                          ctypes.POINTER(_L), ctypes.POINTER(_L), _P, _P, _P], _I),
+    "bsml_lora_buffers": ([_P, ctypes.POINTER(_P), ctypes.POINTER(_P)], _I),
+    "bsml_lora_forward": ([_P, _I, _I, _P, _P, _P, _P, _P, _I, _P, _I, _P, _P, _P], _I),
+    "bsml_lora_backward": ([_P, _P, _P], _I),
+    "bsml_lora_zero_grad": ([_P, _P], _I),
+    "bsml_lora_adam_step": ([_P, _F, _F, _F, _F, _P], _I),
+    "bsml_lora_save": ([_P, ctypes.c_char_p], _I),
+    "bsml_lora_load": ([_P, ctypes.c_char_p], _I),
+    "bsml_lora_state": ([_P, ctypes.POINTER(_F), ctypes.POINTER(_I)], _I),
 }
 
 _lib = None

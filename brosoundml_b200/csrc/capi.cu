@@ -10,6 +10,7 @@
 #include "conv_tc.h"
 #include "engine.h"
 #include "kernels.h"
+#include "lora.h"
 
 namespace {
 
@@ -103,6 +104,10 @@ void bsml::set_last_error(const std::string& msg) { g_err = msg; }
 
 struct bsml_decoder {
     std::unique_ptr<bsml::Engine> eng;
+};
+
+struct bsml_lora {
+    std::unique_ptr<bsml::Lora> lora;
 };
 
 extern "C" {
@@ -238,6 +243,101 @@ int bsml_decoder_read_profile_records(bsml_decoder* d, double* out, int max_reco
         need(d != nullptr && out != nullptr && n_records != nullptr && max_records >= 0,
              "bsml_decoder_read_profile_records", "bad argument");
         d->eng->read_profile_records(out, max_records, n_records);
+    });
+}
+
+int bsml_lora_create(bsml_decoder* d, int rank, float scale, uint64_t seed, bsml_lora** out) {
+    return guarded([&] {
+        need(d && out, "bsml_lora_create", "null argument");
+        auto* l = new bsml_lora;
+        try {
+            l->lora = std::make_unique<bsml::Lora>(*d->eng, rank, scale, seed);
+        } catch (...) {
+            delete l;
+            throw;
+        }
+        *out = l;
+    });
+}
+
+void bsml_lora_destroy(bsml_lora* l) { delete l; }
+
+int bsml_lora_layout(const bsml_lora* l, int64_t* n_params, int* n_adapters, int* rank, int* style_dim,
+                     int64_t* off_W1, int64_t* off_W2, int64_t* off_A, int64_t* off_B, int* adapter_C) {
+    return guarded([&] {
+        need(l != nullptr, "bsml_lora_layout", "null handle");
+        const bsml::Lora& L = *l->lora;
+        if (n_params) *n_params = L.n_params();
+        if (n_adapters) *n_adapters = L.n_adapters();
+        if (rank) *rank = L.rank();
+        if (style_dim) *style_dim = L.style_dim();
+        if (off_W1) *off_W1 = L.off_W1();
+        if (off_W2) *off_W2 = L.off_W2();
+        for (int a = 0; a < L.n_adapters(); ++a) {
+            if (off_A) off_A[a] = L.adapters()[a].offA;
+            if (off_B) off_B[a] = L.adapters()[a].offB;
+            if (adapter_C) adapter_C[a] = L.adapters()[a].C;
+        }
+    });
+}
+
+int bsml_lora_buffers(bsml_lora* l, float** params, float** grads) {
+    return guarded([&] {
+        need(l != nullptr, "bsml_lora_buffers", "null handle");
+        if (params) *params = l->lora->params();
+        if (grads) *grads = l->lora->grads();
+    });
+}
+
+int bsml_lora_forward(bsml_lora* l, int B, int T, const float* params, const float* asr, const float* F0,
+                      const float* N, const float* ref_s, int ref_s_stride, const float* har, int frames,
+                      const float* cond, float* audio, void* stream) {
+    return guarded([&] {
+        need(l != nullptr, "bsml_lora_forward", "null handle");
+        l->lora->forward(B, T, params, asr, F0, N, ref_s, ref_s_stride, har, frames, cond, audio, S(stream));
+    });
+}
+
+int bsml_lora_backward(bsml_lora* l, const float* daudio, void* stream) {
+    return guarded([&] {
+        need(l != nullptr && daudio != nullptr, "bsml_lora_backward", "null argument");
+        l->lora->backward(daudio, S(stream));
+    });
+}
+
+int bsml_lora_zero_grad(bsml_lora* l, void* stream) {
+    return guarded([&] {
+        need(l != nullptr, "bsml_lora_zero_grad", "null handle");
+        l->lora->zero_grad(S(stream));
+    });
+}
+
+int bsml_lora_adam_step(bsml_lora* l, float lr, float beta1, float beta2, float eps, void* stream) {
+    return guarded([&] {
+        need(l != nullptr, "bsml_lora_adam_step", "null handle");
+        l->lora->adam_step(lr, beta1, beta2, eps, S(stream));
+    });
+}
+
+int bsml_lora_save(const bsml_lora* l, const char* path) {
+    return guarded([&] {
+        need(l != nullptr && path != nullptr, "bsml_lora_save", "null argument");
+        l->lora->save(path);
+    });
+}
+
+int bsml_lora_load(bsml_lora* l, const char* path) {
+    return guarded([&] {
+        need(l != nullptr && path != nullptr, "bsml_lora_load", "null argument");
+        l->lora->load(path);
+    });
+}
+
+int bsml_lora_state(const bsml_lora* l, float* scale, int* step) {
+    return guarded([&] {
+        need(l != nullptr, "bsml_lora_state", "null handle");
+        if (scale) *scale = l->lora->scale();
+        if (step) *step = l->lora->step();
     });
 }
 

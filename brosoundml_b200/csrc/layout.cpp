@@ -144,6 +144,7 @@ Layout::Layout(const bsml_decoder_config& c) : cfg(c) {
     // AdaIN order = DecoderLora::adapters() (decoder_lora.cpp:173-179)
     auto reg = [&](AdaP& a) {
         a.idx = (int)aff_C.size();
+        adains.push_back(&a);
         aff_C.push_back(a.C);
         aff_base.push_back(aff_per_clip);
         aff_per_clip += 2 * a.C;

@@ -42,6 +42,7 @@ struct Layout {
     ConvP post;
     std::vector<int> aff_C;
     std::vector<int64_t> aff_base;   // per AdaIN: sum of 2*C over earlier AdaINs (per clip)
+    std::vector<const AdaP*> adains; // per AdaIN index (= DecoderLora::adapters() order)
     int64_t aff_per_clip = 0;
     std::vector<ConvP*> convs;       // every regular conv (for weight packing)
 

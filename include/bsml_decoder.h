@@ -152,6 +152,47 @@ int bsml_loss_l1(const float* audio, const float* target, int64_t n, float* loss
 int bsml_adam_step(float* param, const float* grad, float* m, float* v, int64_t n, float lr, float beta1,
                    float beta2, float eps, int step, void* stream);
 
+/* ── DecoderLora (include/brosoundml/decoder_lora.h:36-164) ─────────────────
+ * LoRA adapters on every AdaIN's style -> (gamma, beta) fc, a shared
+ * conditioning gate g(v) = W2 tanh(W1 v) (in_dim 3, hidden 16, width = rank,
+ * W2 zero at creation), Adam and the ELRA1 checkpoint; batched over clips (the
+ * reference runs one clip). The decoder runs in reference mode under it: the
+ * base weights are frozen and no weight gradients are formed. A bsml_lora
+ * refers to its bsml_decoder and must be destroyed first. */
+typedef struct bsml_lora bsml_lora;
+
+/* DecoderLora::make (src/decoder_lora.cpp:115-147): rank 1..32, LoRA scale,
+ * seed (0 = the reference default) for the xavier-uniform A, B and gate W1. */
+int bsml_lora_create(bsml_decoder* d, int rank, float scale, uint64_t seed, bsml_lora** out);
+void bsml_lora_destroy(bsml_lora* l);
+/* Sizes. The flat parameter vector (device; gradients share the layout) holds
+ * gate W1 [16][3], gate W2 [rank][16], then per adapter (adapters() order)
+ * A [rank][style_dim] and B [2C][rank]. off_A / off_B: n_adapters entries each. */
+int bsml_lora_layout(const bsml_lora* l, int64_t* n_params, int* n_adapters, int* rank, int* style_dim,
+                     int64_t* off_W1, int64_t* off_W2, int64_t* off_A, int64_t* off_B, int* adapter_C);
+/* Device pointers to the parameter and gradient vectors (owned by the object). */
+int bsml_lora_buffers(bsml_lora* l, float** params, float** grads);
+/* DecoderLora::forward (src/decoder_lora.cpp:211-246), batched: style of clip b
+ * = ref_s[b*ref_s_stride .. + style_dim), cond (B, 3), har optional (NULL: the
+ * harmonic source). params = the frozen decoder weights, borrowed until the
+ * matching backward. */
+int bsml_lora_forward(bsml_lora* l, int B, int T, const float* params, const float* asr, const float* F0,
+                      const float* N, const float* ref_s, int ref_s_stride, const float* har, int frames,
+                      const float* cond, float* audio, void* stream);
+/* DecoderLora::backward (src/decoder_lora.cpp:248-296): accumulates the adapter
+ * and gate gradients (until bsml_lora_zero_grad). */
+int bsml_lora_backward(bsml_lora* l, const float* daudio, void* stream);
+int bsml_lora_zero_grad(bsml_lora* l, void* stream);
+/* DecoderLora::adam_step: one shared step count for every tensor. */
+int bsml_lora_adam_step(bsml_lora* l, float lr, float beta1, float beta2, float eps, void* stream);
+/* DecoderLora::save / load (src/decoder_lora.cpp:324-396): the ELRA1 byte
+ * format; load restores values into an object of the same architecture and
+ * takes the scale from the file. Synchronous. */
+int bsml_lora_save(const bsml_lora* l, const char* path);
+int bsml_lora_load(bsml_lora* l, const char* path);
+/* Current LoRA scale and Adam step count. */
+int bsml_lora_state(const bsml_lora* l, float* scale, int* step);
+
 /* ── atoms (the reference's detail:: functions, batched) ────────────────── */
 
 /* Arithmetic of the conv / convT atoms below (process-wide, default
