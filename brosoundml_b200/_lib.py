@@ -105,6 +105,14 @@ SIGNATURES = {
     "bsml_lora_save": ([_P, ctypes.c_char_p], _I),
     "bsml_lora_load": ([_P, ctypes.c_char_p], _I),
     "bsml_lora_state": ([_P, ctypes.POINTER(_F), ctypes.POINTER(_I)], _I),
+    "bsml_convlora_create": ([_P, _I, _F, ctypes.c_uint64, ctypes.POINTER(_P)], _I),
+    "bsml_convlora_destroy": ([_P], None),
+    "bsml_convlora_layout": ([_P, ctypes.POINTER(_L), ctypes.POINTER(_I), _P, _P, _P, _P, _P], _I),
+    "bsml_convlora_buffers": ([_P, ctypes.POINTER(_P), ctypes.POINTER(_P)], _I),
+    "bsml_convlora_forward": ([_P, _I, _I, _P, _P, _P, _P, _P, _P, _I, _P, _P], _I),
+    "bsml_convlora_backward": ([_P, _P, _P], _I),
+    "bsml_convlora_zero_grad": ([_P, _P], _I),
+    "bsml_convlora_adam_step": ([_P, _F, _F, _F, _F, _P], _I),
 }
 
 _lib = None

@@ -10,6 +10,7 @@
 #include "conv_tc.h"
 #include "engine.h"
 #include "kernels.h"
+#include "convlora.h"
 #include "lora.h"
 
 namespace {
@@ -108,6 +109,10 @@ struct bsml_decoder {
 
 struct bsml_lora {
     std::unique_ptr<bsml::Lora> lora;
+};
+
+struct bsml_convlora {
+    std::unique_ptr<bsml::ConvLora> lora;
 };
 
 extern "C" {
@@ -338,6 +343,77 @@ int bsml_lora_state(const bsml_lora* l, float* scale, int* step) {
         need(l != nullptr, "bsml_lora_state", "null handle");
         if (scale) *scale = l->lora->scale();
         if (step) *step = l->lora->step();
+    });
+}
+
+int bsml_convlora_create(bsml_decoder* d, int rank, float scale, uint64_t seed, bsml_convlora** out) {
+    return guarded([&] {
+        need(d && out, "bsml_convlora_create", "null argument");
+        auto* l = new bsml_convlora;
+        try {
+            l->lora = std::make_unique<bsml::ConvLora>(*d->eng, rank, scale, seed);
+        } catch (...) {
+            delete l;
+            throw;
+        }
+        *out = l;
+    });
+}
+
+void bsml_convlora_destroy(bsml_convlora* l) { delete l; }
+
+int bsml_convlora_layout(const bsml_convlora* l, int64_t* n_params, int* n_weights, int64_t* w_off, int* rows,
+                         int* cols, int64_t* off_A, int64_t* off_B) {
+    return guarded([&] {
+        need(l != nullptr, "bsml_convlora_layout", "null handle");
+        const auto& ws = l->lora->weights();
+        if (n_params) *n_params = l->lora->n_params();
+        if (n_weights) *n_weights = (int)ws.size();
+        for (size_t i = 0; i < ws.size(); ++i) {
+            if (w_off) w_off[i] = ws[i].w;
+            if (rows) rows[i] = ws[i].rows;
+            if (cols) cols[i] = ws[i].cols;
+            if (off_A) off_A[i] = ws[i].offA;
+            if (off_B) off_B[i] = ws[i].offB;
+        }
+    });
+}
+
+int bsml_convlora_buffers(bsml_convlora* l, float** params, float** grads) {
+    return guarded([&] {
+        need(l != nullptr, "bsml_convlora_buffers", "null handle");
+        if (params) *params = l->lora->params();
+        if (grads) *grads = l->lora->grads();
+    });
+}
+
+int bsml_convlora_forward(bsml_convlora* l, int B, int T, const float* params, const float* asr, const float* F0,
+                          const float* N, const float* style, const float* har, int frames, float* audio,
+                          void* stream) {
+    return guarded([&] {
+        need(l != nullptr, "bsml_convlora_forward", "null handle");
+        l->lora->forward(B, T, params, asr, F0, N, style, har, frames, audio, S(stream));
+    });
+}
+
+int bsml_convlora_backward(bsml_convlora* l, const float* daudio, void* stream) {
+    return guarded([&] {
+        need(l != nullptr && daudio != nullptr, "bsml_convlora_backward", "null argument");
+        l->lora->backward(daudio, S(stream));
+    });
+}
+
+int bsml_convlora_zero_grad(bsml_convlora* l, void* stream) {
+    return guarded([&] {
+        need(l != nullptr, "bsml_convlora_zero_grad", "null handle");
+        l->lora->zero_grad(S(stream));
+    });
+}
+
+int bsml_convlora_adam_step(bsml_convlora* l, float lr, float beta1, float beta2, float eps, void* stream) {
+    return guarded([&] {
+        need(l != nullptr, "bsml_convlora_adam_step", "null handle");
+        l->lora->adam_step(lr, beta1, beta2, eps, S(stream));
     });
 }
 

@@ -108,3 +108,58 @@ class _DeviceBuffer:
 
 def _device_view(ptr: int, n: int, device) -> torch.Tensor:
     return torch.as_tensor(_DeviceBuffer(ptr, n), device=device)
+
+
+class ConvLora:
+    """Conv-weight LoRA (no counterpart in the reference): a rank-r
+    adapter W + scale * B A on every Conv1d / ConvTranspose1d weight of ``decoder``,
+    base weights frozen. A weight stored (d0, d1, k) is viewed as [d0][d1*k];
+    A [rank][d1*k] starts N(0, 0.01), B [d0][rank] starts at zero."""
+
+    def __init__(self, decoder: Decoder, rank: int = 8, scale: float = 2.0, seed: int = 0):
+        L = _lib.lib()
+        h = ctypes.c_void_p()
+        _lib.check(L.bsml_convlora_create(decoder._h, int(rank), float(scale), int(seed), ctypes.byref(h)))
+        self._h, self.decoder, self.rank, self.scale = h, decoder, int(rank), float(scale)
+        n, nw = ctypes.c_int64(), ctypes.c_int()
+        _lib.check(L.bsml_convlora_layout(h, ctypes.byref(n), ctypes.byref(nw), None, None, None, None, None))
+        arrs = [(ctypes.c_int64 * nw.value)(), (ctypes.c_int * nw.value)(), (ctypes.c_int * nw.value)(),
+                (ctypes.c_int64 * nw.value)(), (ctypes.c_int64 * nw.value)()]
+        _lib.check(L.bsml_convlora_layout(h, None, None, *[ctypes.cast(a, ctypes.c_void_p) for a in arrs]))
+        self.n_params = n.value
+        self.weights = [dict(w=w, rows=r, cols=c, offA=a, offB=b) for w, r, c, a, b in zip(*[list(a) for a in arrs])]
+        pp, gp = ctypes.c_void_p(), ctypes.c_void_p()
+        _lib.check(L.bsml_convlora_buffers(h, ctypes.byref(pp), ctypes.byref(gp)))
+        self._pp, self._gp = pp.value, gp.value
+
+    def __del__(self):
+        h = getattr(self, "_h", None)
+        if h is not None and _lib._lib is not None:
+            _lib.lib().bsml_convlora_destroy(h)
+            self._h = None
+
+    def params(self) -> torch.Tensor:
+        return _device_view(self._pp, self.n_params, self.decoder.device)
+
+    def grads(self) -> torch.Tensor:
+        return _device_view(self._gp, self.n_params, self.decoder.device)
+
+    def forward(self, params, asr, F0, N, style, har=None, audio=None):
+        params, asr, F0, N, style, har = map(_f32, (params, asr, F0, N, style, har))
+        B, _, T = asr.shape
+        frames = 0 if har is None else har.shape[2]
+        if audio is None:
+            audio = torch.empty((B, self.decoder.audio_len(T, frames if har is not None else None)),
+                                device=self.decoder.device)
+        _lib.check(_lib.lib().bsml_convlora_forward(self._h, B, T, _ptr(params), _ptr(asr), _ptr(F0), _ptr(N),
+                                                    _ptr(style), _ptr(har), frames, _ptr(audio), _stream()))
+        return audio
+
+    def backward(self, daudio) -> None:
+        _lib.check(_lib.lib().bsml_convlora_backward(self._h, _ptr(_f32(daudio)), _stream()))
+
+    def zero_grad(self) -> None:
+        _lib.check(_lib.lib().bsml_convlora_zero_grad(self._h, _stream()))
+
+    def adam_step(self, lr: float, beta1: float = 0.9, beta2: float = 0.999, eps: float = 1e-8) -> None:
+        _lib.check(_lib.lib().bsml_convlora_adam_step(self._h, lr, beta1, beta2, eps, _stream()))

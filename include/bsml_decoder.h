@@ -193,6 +193,31 @@ int bsml_lora_load(bsml_lora* l, const char* path);
 /* Current LoRA scale and Adam step count. */
 int bsml_lora_state(const bsml_lora* l, float* scale, int* step);
 
+/* ── conv-weight LoRA (no counterpart in the reference) ──
+ * A rank-r adapter on every Conv1d / ConvTranspose1d weight, base weights frozen.
+ * A weight stored (d0, d1, k) is viewed as [d0][d1*k] and adapted to
+ * W + scale * B A, A [rank][d1*k] ~ N(0, 0.01) at creation, B [d0][rank] = 0.
+ * Refers to its bsml_decoder, which must outlive it. */
+typedef struct bsml_convlora bsml_convlora;
+
+int bsml_convlora_create(bsml_decoder* d, int rank, float scale, uint64_t seed, bsml_convlora** out);
+void bsml_convlora_destroy(bsml_convlora* l);
+/* n_weights adapted weights; per weight (arrays of n_weights): its offset in the
+ * decoder parameters, rows (d0), cols (d1*k), and the offsets of A and B in the
+ * flat LoRA parameter vector. */
+int bsml_convlora_layout(const bsml_convlora* l, int64_t* n_params, int* n_weights, int64_t* w_off, int* rows,
+                         int* cols, int64_t* off_A, int64_t* off_B);
+int bsml_convlora_buffers(bsml_convlora* l, float** params, float** grads);
+/* Forward of the adapted decoder; params = the frozen base weights (read during
+ * the call only: the adapters are folded into a private copy). */
+int bsml_convlora_forward(bsml_convlora* l, int B, int T, const float* params, const float* asr, const float* F0,
+                          const float* N, const float* style, const float* har, int frames, float* audio,
+                          void* stream);
+/* Accumulates dA, dB from the audio gradient (until bsml_convlora_zero_grad). */
+int bsml_convlora_backward(bsml_convlora* l, const float* daudio, void* stream);
+int bsml_convlora_zero_grad(bsml_convlora* l, void* stream);
+int bsml_convlora_adam_step(bsml_convlora* l, float lr, float beta1, float beta2, float eps, void* stream);
+
 /* ── atoms (the reference's detail:: functions, batched) ────────────────── */
 
 /* Arithmetic of the conv / convT atoms below (process-wide, default

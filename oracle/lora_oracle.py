@@ -151,3 +151,50 @@ def read_elra1(path: str):
         A, B = tensor(), tensor()
         ads.append((C, A, B))
     return rank, sd, scale, hidden, W1, W2, ads
+
+
+# ── conv-weight LoRA (no reference counterpart) ──────────────
+class ConvLoraLayout:
+    """Every 3-d ``*.weight`` of the decoder (Conv1d / ConvTranspose1d), viewed [d0][d1*k];
+    flat LoRA vector: per weight A [rank][d1*k] then B [d0][rank]."""
+
+    def __init__(self, table, rank: int):
+        self.rank = rank
+        self.ws = []
+        off = 0
+        for e in table:
+            if len(e["shape"]) != 3 or not e["name"].endswith(".weight"):
+                continue
+            rows, cols = e["shape"][0], e["shape"][1] * e["shape"][2]
+            self.ws.append(dict(w=e["offset"], rows=rows, cols=cols, offA=off, offB=off + rank * cols))
+            off += rank * cols + rows * rank
+        self.n_params = off
+
+
+def conv_lora_fold(lay: ConvLoraLayout, params, lp, scale):
+    eff = params.astype(np.float64).copy()
+    for w in lay.ws:
+        A = lp[w["offA"]:w["offA"] + lay.rank * w["cols"]].reshape(lay.rank, w["cols"])
+        B = lp[w["offB"]:w["offB"] + w["rows"] * lay.rank].reshape(w["rows"], lay.rank)
+        eff[w["w"]:w["w"] + w["rows"] * w["cols"]] += scale * (B @ A).reshape(-1)
+    return eff
+
+
+def conv_lora_grads(lay: ConvLoraLayout, lp, dW_full, scale):
+    g = np.zeros(lay.n_params)
+    for w in lay.ws:
+        A = lp[w["offA"]:w["offA"] + lay.rank * w["cols"]].reshape(lay.rank, w["cols"])
+        B = lp[w["offB"]:w["offB"] + w["rows"] * lay.rank].reshape(w["rows"], lay.rank)
+        dW = dW_full[w["w"]:w["w"] + w["rows"] * w["cols"]].reshape(w["rows"], w["cols"])
+        g[w["offA"]:w["offA"] + lay.rank * w["cols"]] = (scale * B.T @ dW).reshape(-1)
+        g[w["offB"]:w["offB"] + w["rows"] * lay.rank] = (scale * dW @ A.T).reshape(-1)
+    return g
+
+
+def conv_lora_run(oracle, lay: ConvLoraLayout, params, lp, asr, F0, N, style, scale, har=None, daudio=None):
+    eff = conv_lora_fold(lay, params, lp.astype(np.float64), scale)
+    out = oracle.run(eff, asr, F0, N, style, har=har, daudio=daudio, dtype=np.float64)
+    res = {"audio": out["audio"]}
+    if daudio is not None:
+        res["grads"] = conv_lora_grads(lay, lp.astype(np.float64), out["grads"], scale)
+    return res

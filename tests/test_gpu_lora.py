@@ -2,7 +2,9 @@
 reference's own LoRA properties: neutral identity at gate zero
 (tests/test_kokoro_decoder_backward.cpp:516-530), Adam with one shared step,
 gradient accumulation until zero_grad, and the ELRA1 checkpoint round trip
-(:562-577) with its error paths (src/decoder_lora.cpp:334-382)."""
+(:562-577) with its error paths (src/decoder_lora.cpp:334-382); and the conv-weight
+LoRA (bsml_convlora_*, BASELINE config 3) against the float64 oracle of the folded
+decoder, its zero-B identity, accumulation and Adam."""
 
 import numpy as np
 import pytest
@@ -158,3 +160,84 @@ def test_lora_checkpoint_roundtrip(tmp_path):
     _, other = _make(cfg, "fp32", rank=4)
     with pytest.raises(BsmlError, match="architecture mismatch"):
         other.load(path)
+
+
+# ── conv-weight LoRA ─────────────────────────────────────
+def _make_conv(cfg, math, seed=5, rank=RANK):
+    from brosoundml_b200.decoder import Decoder
+    from brosoundml_b200.lora import ConvLora
+    dec = Decoder(cfg, 0, math=math)
+    return dec, ConvLora(dec, rank=rank, scale=SCALE, seed=seed)
+
+
+@pytest.mark.parametrize("which,math", [("miniature", "fp32"), ("kokoro", "tf32x3")])
+def test_conv_lora_forward_backward_vs_oracle(which, math):
+    torch = _torch()
+    cfg, o, p, x, har, ref_s, cond = _case(which)
+    dec, cl = _make_conv(cfg, math)
+    lay = lo.ConvLoraLayout(o.table, RANK)
+    assert cl.n_params == lay.n_params and len(cl.weights) == len(lay.ws)
+    for w, e in zip(cl.weights, lay.ws):
+        assert (w["w"], w["rows"], w["cols"], w["offA"], w["offB"]) == (e["w"], e["rows"], e["cols"], e["offA"],
+                                                                        e["offB"])
+    lp = np.random.default_rng(3).normal(0, 0.02, lay.n_params).astype(np.float32)
+    cl.params().copy_(_dev(lp))
+    pd = _dev(p)
+    audio = cl.forward(pd, _dev(x["asr"]), _dev(x["F0"]), _dev(x["N"]), _dev(x["style"]), har=_dev(har))
+    da = np.random.default_rng(4).normal(0, 1, tuple(audio.shape)).astype(np.float32)
+    cl.zero_grad()
+    cl.backward(_dev(da))
+    torch.cuda.synchronize()
+    r = lo.conv_lora_run(o, lay, p.astype(np.float64), lp.astype(np.float64), x["asr"], x["F0"], x["N"],
+                         x["style"], SCALE, har=har, daudio=da.astype(np.float64))
+    tol = 1e-4   # fp32 / TF32x3 against the float64 oracle
+    assert rel_l2(audio.cpu().numpy(), r["audio"]) < tol
+    g = cl.grads().cpu().numpy()
+    assert rel_l2(g, r["grads"]) < tol
+    for i in (0, len(lay.ws) // 2, len(lay.ws) - 1):
+        w = lay.ws[i]
+        sA, sB = slice(w["offA"], w["offB"]), slice(w["offB"], w["offB"] + w["rows"] * RANK)
+        assert rel_l2(g[sA], r["grads"][sA]) < 10 * tol and rel_l2(g[sB], r["grads"][sB]) < 10 * tol, i
+
+
+def test_conv_lora_starts_as_the_base_decoder():
+    """B = 0 at creation: the adapted decoder equals the base decoder; A ~ N(0, 0.01)."""
+    torch = _torch()
+    cfg, o, p, x, har, ref_s, cond = _case("kokoro", 1)
+    dec, cl = _make_conv(cfg, "tf32x3")
+    P = cl.params()
+    for w in cl.weights[:4]:
+        assert float(P[w["offB"]:w["offB"] + w["rows"] * RANK].abs().max()) == 0.0
+    A = torch.cat([P[w["offA"]:w["offB"]] for w in cl.weights])
+    assert abs(float(A.std()) - 0.01) < 1e-3 and abs(float(A.mean())) < 1e-3
+    pd = _dev(p)
+    a_cl = cl.forward(pd, _dev(x["asr"]), _dev(x["F0"]), _dev(x["N"]), _dev(x["style"]), har=_dev(har)).clone()
+    a_base = dec.forward(pd, _dev(x["asr"]), _dev(x["F0"]), _dev(x["N"]), _dev(x["style"]), har=_dev(har))
+    torch.cuda.synchronize()
+    assert rel_l2(a_cl.cpu().numpy(), a_base.cpu().numpy()) < 1e-6   # atomics may reorder sums
+
+
+def test_conv_lora_adam_and_grad_accumulation():
+    torch = _torch()
+    cfg, o, p, x, har, ref_s, cond = _case("miniature", 2)
+    dec, cl = _make_conv(cfg, "fp32")
+    cl.params().normal_(0, 0.02)
+    pd = _dev(p)
+    args = (pd, _dev(x["asr"]), _dev(x["F0"]), _dev(x["N"]), _dev(x["style"]))
+    audio = cl.forward(*args, har=_dev(har))
+    da = torch.randn_like(audio)
+    cl.zero_grad()
+    cl.backward(da)
+    g1 = cl.grads().clone()
+    cl.forward(*args, har=_dev(har))
+    cl.backward(da)
+    torch.cuda.synchronize()
+    assert torch.allclose(cl.grads(), 2 * g1, rtol=1e-5, atol=1e-10)
+    cl.zero_grad()
+    cl.backward(da)
+    p0, g = cl.params().clone().double(), cl.grads().clone().double()
+    lr, b1, b2, eps = 1e-3, 0.9, 0.999, 1e-8
+    cl.adam_step(lr, b1, b2, eps)
+    torch.cuda.synchronize()
+    expect = p0 - lr * ((1 - b1) * g / (1 - b1)) / (torch.sqrt((1 - b2) * g * g / (1 - b2)) + eps)
+    assert torch.allclose(cl.params().double(), expect, rtol=1e-5, atol=1e-7)

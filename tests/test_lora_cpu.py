@@ -84,3 +84,29 @@ def test_elra1_reader_roundtrip(tmp_path):
     assert np.array_equal(W1, lay.W1(lp)) and np.array_equal(W2, lay.W2(lp))
     assert [c for c, _, _ in ads] == [3, 5]
     assert np.array_equal(ads[1][2], lay.B(lp, 1))
+
+
+def test_conv_lora_grads_directional_fd():
+    """Conv-weight LoRA (config 3): dA, dB from the decoder's weight gradients against
+    finite differences of the adapted miniature decoder."""
+    o, lay_, p, lp_, x, har, cond, tgt = _setup(3)
+    lay = lo.ConvLoraLayout(o.table, RANK)
+    assert len(lay.ws) > 0
+    lp = np.random.default_rng(8).normal(0, 0.05, lay.n_params)
+
+    def loss(q):
+        a = lo.conv_lora_run(o, lay, p, q, x["asr"], x["F0"], x["N"], x["style"], SCALE, har=har)["audio"]
+        return 0.5 * float(((a - tgt) ** 2).sum())
+
+    a = lo.conv_lora_run(o, lay, p, lp, x["asr"], x["F0"], x["N"], x["style"], SCALE, har=har)["audio"]
+    g = lo.conv_lora_run(o, lay, p, lp, x["asr"], x["F0"], x["N"], x["style"], SCALE, har=har, daudio=a - tgt)["grads"]
+    rng = np.random.default_rng(9)
+    for part in ("A", "B"):
+        v = np.zeros_like(lp)
+        for w in lay.ws:
+            s = slice(w["offA"], w["offB"]) if part == "A" else slice(w["offB"], w["offB"] + w["rows"] * RANK)
+            v[s] = rng.uniform(-1, 1, s.stop - s.start)
+        h = 1e-6
+        fd = (loss(lp + h * v) - loss(lp - h * v)) / (2 * h)
+        an = float((g * v).sum())
+        assert abs(an - fd) <= 1e-7 + 1e-5 * abs(fd), (part, an, fd)
