@@ -36,6 +36,24 @@ class BsmlParamEntry(ctypes.Structure):
                 ("ndim", ctypes.c_int), ("shape", ctypes.c_int * 3), ("trainable", ctypes.c_int)]
 
 
+class BsmlBlockSpec(ctypes.Structure):
+    """Mirror of bsml_block_spec (kind 1 = AdainResBlk1d, 2 = AdaINResBlock1)."""
+
+    _fields_ = [("kind", ctypes.c_int), ("style_dim", ctypes.c_int), ("cin", ctypes.c_int), ("cout", ctypes.c_int),
+                ("upsample", ctypes.c_int), ("kernel", ctypes.c_int), ("dil", ctypes.c_int * 3)]
+
+
+def make_block_spec(d: dict) -> BsmlBlockSpec:
+    s = BsmlBlockSpec()
+    for k, v in d.items():
+        if k == "dil":
+            for i, x in enumerate(v):
+                s.dil[i] = int(x)
+        else:
+            setattr(s, k, int(v))
+    return s
+
+
 def make_config(d: dict) -> BsmlConfig:
     c = BsmlConfig()
     for k, v in d.items():
@@ -56,6 +74,7 @@ def make_config(d: dict) -> BsmlConfig:
 # Every exported entry point with its argument types (restype int unless noted).
 _P, _I, _F, _L = ctypes.c_void_p, ctypes.c_int, ctypes.c_float, ctypes.c_int64
 _CFG = ctypes.POINTER(BsmlConfig)
+_BS = ctypes.POINTER(BsmlBlockSpec)
 SIGNATURES = {
     "bsml_last_error": ([], ctypes.c_char_p),
     "bsml_version": ([], _I),
@@ -71,6 +90,12 @@ SIGNATURES = {
     "bsml_decoder_forward": ([_P, _I, _I, _P, _P, _P, _P, _P, _P, _I, _P, _P, _P, _P], _I),
     "bsml_decoder_backward": ([_P, _P, _P, _P, _P, _P, _P], _I),
     "bsml_decoder_workspace_bytes": ([_P], _L),
+    "bsml_block_create": ([_BS, _I, ctypes.POINTER(_P)], _I),
+    "bsml_block_param_count": ([_BS, ctypes.POINTER(_L), ctypes.POINTER(_I), ctypes.POINTER(_I),
+                                ctypes.POINTER(_L)], _I),
+    "bsml_block_param_table": ([_BS, _P, _I, _P], _I),
+    "bsml_block_forward": ([_P, _I, _I, _P, _P, _P, _P, _P, _P, _P], _I),
+    "bsml_block_backward": ([_P, _P, _P, _P, _P, _P, _P], _I),
     "bsml_decoder_set_profiling": ([_P, _I], _I),
     "bsml_launch_count": ([], _L),
     "bsml_set_atom_math": ([_I], _I),
@@ -139,6 +164,24 @@ def lib():
 def check(rc: int) -> None:
     if rc != 0:
         raise BsmlError(lib().bsml_last_error().decode())
+
+
+def block_layout(spec: dict):
+    """Parameter table of one block without a device: (n_params, table, aff_C, aff_per_clip)."""
+    L = lib()
+    c = make_block_spec(spec)
+    n, ne, na, apc = ctypes.c_int64(), ctypes.c_int(), ctypes.c_int(), ctypes.c_int64()
+    check(L.bsml_block_param_count(ctypes.byref(c), ctypes.byref(n), ctypes.byref(ne), ctypes.byref(na),
+                                   ctypes.byref(apc)))
+    arr = (BsmlParamEntry * ne.value)()
+    affc = (ctypes.c_int * na.value)()
+    rc = L.bsml_block_param_table(ctypes.byref(c), ctypes.cast(arr, ctypes.c_void_p), ne.value,
+                                  ctypes.cast(affc, ctypes.c_void_p))
+    if rc < 0:
+        check(rc)
+    table = [dict(name=e.name.decode(), offset=e.offset, numel=e.numel, shape=tuple(e.shape[:e.ndim]),
+                  trainable=bool(e.trainable)) for e in arr]
+    return n.value, table, list(affc), apc.value
 
 
 def layout(cfg: dict):

@@ -211,6 +211,61 @@ int bsml_decoder_backward(bsml_decoder* d, const float* daudio, float* grads, fl
     });
 }
 
+int bsml_block_create(const bsml_block_spec* spec, int device, bsml_decoder** out) {
+    return guarded([&] {
+        need(spec && out, "bsml_block_create", "null argument");
+        auto* d = new bsml_decoder;
+        try {
+            d->eng = std::make_unique<bsml::Engine>(*spec, device);
+        } catch (...) {
+            delete d;
+            throw;
+        }
+        *out = d;
+    });
+}
+
+int bsml_block_param_count(const bsml_block_spec* spec, int64_t* n_params, int* n_entries, int* n_affine,
+                           int64_t* aff_per_clip) {
+    return guarded([&] {
+        need(spec != nullptr, "bsml_block_param_count", "null spec");
+        const bsml::Layout L(*spec);
+        if (n_params) *n_params = L.total;
+        if (n_entries) *n_entries = (int)L.table.size();
+        if (n_affine) *n_affine = (int)L.aff_C.size();
+        if (aff_per_clip) *aff_per_clip = L.aff_per_clip;
+    });
+}
+
+int bsml_block_param_table(const bsml_block_spec* spec, bsml_param_entry* out, int max_entries, int* aff_channels) {
+    int n = 0;
+    const int rc = guarded([&] {
+        need(spec != nullptr && out != nullptr, "bsml_block_param_table", "null argument");
+        const bsml::Layout L(*spec);
+        n = std::min<int>(max_entries, (int)L.table.size());
+        for (int i = 0; i < n; ++i) out[i] = L.table[i];
+        if (aff_channels)
+            for (size_t i = 0; i < L.aff_C.size(); ++i) aff_channels[i] = L.aff_C[i];
+    });
+    return rc ? rc : n;
+}
+
+int bsml_block_forward(bsml_decoder* d, int B, int L, const float* params, const float* x, const float* style,
+                       const float* aff_in, float* y, float* aff_out, void* stream) {
+    return guarded([&] {
+        need(d != nullptr, "bsml_block_forward", "null handle");
+        d->eng->forward_block(B, L, params, x, style, aff_in, y, aff_out, S(stream));
+    });
+}
+
+int bsml_block_backward(bsml_decoder* d, const float* dy, float* grads, float* dx, float* d_style, float* d_aff,
+                        void* stream) {
+    return guarded([&] {
+        need(d != nullptr, "bsml_block_backward", "null handle");
+        d->eng->backward_block(dy, grads, dx, d_style, d_aff, S(stream));
+    });
+}
+
 int64_t bsml_decoder_workspace_bytes(const bsml_decoder* d) { return d ? d->eng->workspace_bytes() : 0; }
 
 int64_t bsml_launch_count(void) { return bsml::launch_count(); }

@@ -42,8 +42,11 @@ int conv_out(int L, const ConvP& c) { return (L + 2 * c.p - c.d * (c.k - 1) - 1)
 
 }  // namespace
 
-Engine::Engine(const bsml_decoder_config& cfg, int device) : lay_(cfg), device_(device) {
-    BSML_CUDA(cudaSetDevice(device));
+Engine::Engine(const bsml_decoder_config& cfg, int device) : lay_(cfg), device_(device) { init(); }
+Engine::Engine(const bsml_block_spec& spec, int device) : lay_(spec), device_(device) { init(); }
+
+void Engine::init() {
+    BSML_CUDA(cudaSetDevice(device_));
     // packed weights: forward + dgrad layouts for every conv, phases + dgrad for every convT
     int64_t bytes = 0;
     auto sz = [&](int64_t floats) { bytes = round_up(bytes, 256) + floats * 4; };
@@ -329,6 +332,14 @@ void Engine::plan(Planner& P) {
     dasrres_ = P.act(B, T, cf.asr_res_dim);
     dF0dn_ = P.act(B, T, 1);
     dNdn_ = P.act(B, T, 1);
+    plan_scratch(P, max_elems, max_c);
+}
+
+// reduction scratch, split-K partials, the backward's scratch activations and
+// the tensor-core operand planes, sized for the largest activation
+void Engine::plan_scratch(Planner& P, int64_t max_elems, int max_c) {
+    const int B = B_;
+    const auto& cf = lay_.cfg;
     dacc_ = P.d((int64_t)B * std::max(max_c, 1) * 3);
     ssum_ = P.d((int64_t)B * std::max(max_c, 1) * 2);
     bsum_ = P.d(std::max(max_c, 1));
@@ -349,11 +360,40 @@ void Engine::plan(Planner& P) {
     tc_dl_ = P.f(max_elems);
 }
 
+// One block (block_kind != 0): T_ is the block's input length L
+void Engine::plan_block(Planner& P) {
+    const int B = B_, L = T_;
+    style_copy_ = P.f((int64_t)B * lay_.cfg.style_dim);
+    aff_ = P.f((int64_t)B * lay_.aff_per_clip);
+    daff_ = P.f((int64_t)B * lay_.aff_per_clip);
+    int64_t max_elems = 0;
+    int max_c = 0;
+    if (lay_.block_kind == BSML_BLOCK_RESBLK1D) {
+        const BlkP& w = lay_.enc;
+        blk_x_ = P.act(B, L, w.cin);
+        encc_ = plan_blk(P, w, L, true);
+        encc_.x = blk_x_;
+        blk_y_ = P.act(B, encc_.Lout, w.cout);
+        max_c = std::max(w.cin, w.cout);
+        max_elems = (int64_t)B * encc_.Lout * pitch(max_c);
+    } else {
+        const RB1P& w = lay_.rbs[0];
+        blk_x_ = P.act(B, L, w.C);
+        rb1c_ = plan_rb1(P, L, w.C);
+        rb1c_.x[0] = blk_x_;
+        blk_y_ = P.act(B, L, w.C);
+        max_c = w.C;
+        max_elems = (int64_t)B * L * pitch(w.C);
+    }
+    plan_scratch(P, max_elems, max_c);
+}
+
 void Engine::ensure_plan(int B, int T, int frames, bool have_har) {
     if (planned_ && B == B_ && T == T_ && have_har == have_har_ && (!have_har || frames == frames_)) return;
     B_ = B; T_ = T; frames_ = frames; have_har_ = have_har;
     Planner p0;
-    plan(p0);
+    if (lay_.block_kind) plan_block(p0);
+    else plan(p0);
     const int64_t need = round_up(p0.off, 1 << 20);
     if (need > ws_bytes_) {
         if (ws_) BSML_CUDA(cudaFree(ws_));
@@ -364,7 +404,8 @@ void Engine::ensure_plan(int B, int T, int frames, bool have_har) {
     }
     Planner p1;
     p1.base = ws_;
-    plan(p1);
+    if (lay_.block_kind) plan_block(p1);
+    else plan(p1);
     // fc table for this B
     std::vector<FcRow> tab(lay_.aff_C.size());
     int row0 = 0;
@@ -375,10 +416,7 @@ void Engine::ensure_plan(int B, int T, int frames, bool have_har) {
         f.out_off = (int64_t)B * lay_.aff_base[a.idx];
         f.n_out = 2 * a.C;
     };
-    fill_tab(lay_.enc.n1); fill_tab(lay_.enc.n2);
-    for (auto& d : lay_.dec) { fill_tab(d.n1); fill_tab(d.n2); }
-    for (auto& r : lay_.nres) for (int i = 0; i < 3; ++i) { fill_tab(r.a1[i]); fill_tab(r.a2[i]); }
-    for (auto& r : lay_.rbs) for (int i = 0; i < 3; ++i) { fill_tab(r.a1[i]); fill_tab(r.a2[i]); }
+    for (const AdaP* a : lay_.adains) fill_tab(*a);
     for (auto& f : tab) { f.row0 = row0; row0 += f.n_out; }
     BSML_CUDA(cudaMemcpy(fc_tab_, tab.data(), sizeof(FcRow) * tab.size(), cudaMemcpyHostToDevice));
     planned_ = true;
@@ -819,6 +857,7 @@ void Engine::rb1_bwd(const RB1P& w, RB1C& c, const Act& dOut, float scale, const
 void Engine::forward(int B, int T, const float* params, const float* asr, const float* F0, const float* N,
                      const float* style, const float* har, int frames, const float* aff_in, float* audio,
                      float* aff_out, cudaStream_t st) {
+    if (lay_.block_kind) fail("bsml_decoder_forward", "the handle holds a single block: use bsml_block_forward");
     if (B < 1 || T < 1) fail("bsml_decoder_forward", "B and T must be positive");
     if (!params || !asr || !F0 || !N || !audio) fail("bsml_decoder_forward", "null input");
     if (!aff_in && !style) fail("bsml_decoder_forward", "style is required unless aff_in is given");
@@ -914,6 +953,7 @@ void Engine::forward(int B, int T, const float* params, const float* asr, const 
 // ── backward
 void Engine::backward(const float* daudio, float* grads, float* d_asr, float* d_style, float* d_aff,
                       cudaStream_t st) {
+    if (lay_.block_kind) fail("bsml_decoder_backward", "the handle holds a single block: use bsml_block_backward");
     if (!fwd_done_) fail("bsml_decoder_backward", "no matching forward");
     if (!daudio) fail("bsml_decoder_backward", "null daudio");
     BSML_CUDA(cudaSetDevice(device_));
@@ -1005,6 +1045,73 @@ void Engine::backward(const float* daudio, float* grads, float* d_asr, float* d_
     } else {
         affine_fc_bwd(fc_tab_, (int)lay_.aff_C.size(), fc_rows_, fc_row_entry_, params_, style_, daff_, B,
                       cf.style_dim, grads_, d_style, fc_part_, st);
+    }
+    grads_ = nullptr;
+}
+
+// ── one block (detail::adain_resblk_1d_* / adain_resblock1_*, kokoro_decoder_backward.cpp:152-376)
+void Engine::forward_block(int B, int L, const float* params, const float* x, const float* style,
+                           const float* aff_in, float* y, float* aff_out, cudaStream_t st) {
+    if (!lay_.block_kind) fail("bsml_block_forward", "the handle holds a whole decoder: use bsml_decoder_forward");
+    if (B < 1 || L < 1) fail("bsml_block_forward", "B and L must be positive");
+    if (!params || !x || !y) fail("bsml_block_forward", "null input");
+    if (!aff_in && !style) fail("bsml_block_forward", "style is required unless aff_in is given");
+    BSML_CUDA(cudaSetDevice(device_));
+    ensure_plan(B, L, 0, false);
+    const int S = lay_.cfg.style_dim;
+    params_ = params;
+    if (style) BSML_CUDA(cudaMemcpyAsync(style_copy_, style, sizeof(float) * B * S, cudaMemcpyDeviceToDevice, st));
+    style_ = style ? style_copy_ : nullptr;
+    ref_mode_ = aff_in != nullptr;
+    fwd_done_ = false;
+    pack_weights(st);
+    if (ref_mode_)
+        BSML_CUDA(cudaMemcpyAsync(aff_, aff_in, sizeof(float) * B * lay_.aff_per_clip, cudaMemcpyDeviceToDevice, st));
+    else
+        affine_fc_fwd(fc_tab_, (int)lay_.aff_C.size(), fc_rows_, fc_row_entry_, params_, style_, B, S, aff_, st);
+    if (aff_out)
+        BSML_CUDA(cudaMemcpyAsync(aff_out, aff_, sizeof(float) * B * lay_.aff_per_clip, cudaMemcpyDeviceToDevice, st));
+    ncl_to_cl(x, blk_x_, st);
+    if (lay_.block_kind == BSML_BLOCK_RESBLK1D) blk_fwd(lay_.enc, encc_, blk_y_, st);
+    else rb1_fwd(lay_.rbs[0], rb1c_, blk_x_, false, blk_y_, 1.f, false, st);
+    cl_to_ncl(blk_y_, y, st);
+    fwd_done_ = true;
+}
+
+void Engine::backward_block(const float* dy, float* grads, float* dx, float* d_style, float* d_aff,
+                            cudaStream_t st) {
+    if (!lay_.block_kind) fail("bsml_block_backward", "the handle holds a whole decoder: use bsml_decoder_backward");
+    if (!fwd_done_) fail("bsml_block_backward", "no matching forward");
+    if (!dy) fail("bsml_block_backward", "null dy");
+    BSML_CUDA(cudaSetDevice(device_));
+    const int B = B_, S = lay_.cfg.style_dim;
+    grads_ = grads;
+    if (grads_) fill(grads_, lay_.total, 0.f, st);
+    pack_dgrad_weights(st);
+    Act dX;
+    if (lay_.block_kind == BSML_BLOCK_RESBLK1D) {
+        // blk_bwd works in S_[0..3]
+        const BlkP& w = lay_.enc;
+        Act dY = view(S_[4], encc_.Lout, w.cout);
+        ncl_to_cl(dy, dY, st);
+        dX = view(S_[5], encc_.Lin, w.cin);
+        blk_bwd(w, encc_, dY, dX, st);
+    } else {
+        // rb1_bwd works in S_[0], S_[4], S_[5] and D
+        const RB1P& w = lay_.rbs[0];
+        Act dO = view(S_[1], rb1c_.L, w.C);
+        ncl_to_cl(dy, dO, st);
+        dX = view(S_[2], rb1c_.L, w.C);
+        rb1_bwd(w, rb1c_, dO, 1.f, dX, st);
+    }
+    if (dx) cl_to_ncl(dX, dx, st);
+    if (d_aff)
+        BSML_CUDA(cudaMemcpyAsync(d_aff, daff_, sizeof(float) * B * lay_.aff_per_clip, cudaMemcpyDeviceToDevice, st));
+    if (ref_mode_) {
+        if (d_style) fill(d_style, (int64_t)B * S, 0.f, st);
+    } else {
+        affine_fc_bwd(fc_tab_, (int)lay_.aff_C.size(), fc_rows_, fc_row_entry_, params_, style_, daff_, B, S, grads_,
+                      d_style, fc_part_, st);
     }
     grads_ = nullptr;
 }

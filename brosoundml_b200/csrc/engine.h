@@ -16,6 +16,7 @@ namespace bsml {
 class Engine {
    public:
     Engine(const bsml_decoder_config& cfg, int device);
+    Engine(const bsml_block_spec& spec, int device);   // one block on its own
     ~Engine();
     Engine(const Engine&) = delete;
     Engine& operator=(const Engine&) = delete;
@@ -28,6 +29,10 @@ class Engine {
                  const float* style, const float* har, int frames, const float* aff_in, float* audio,
                  float* aff_out, cudaStream_t st);
     void backward(const float* daudio, float* grads, float* d_asr, float* d_style, float* d_aff, cudaStream_t st);
+    // one block (a handle made from a bsml_block_spec): x, y, dy, dx NCL
+    void forward_block(int B, int L, const float* params, const float* x, const float* style, const float* aff_in,
+                       float* y, float* aff_out, cudaStream_t st);
+    void backward_block(const float* dy, float* grads, float* dx, float* d_style, float* d_aff, cudaStream_t st);
     int64_t workspace_bytes() const { return ws_bytes_ + wp_bytes_ + tcw_bytes_; }
 
     // Per-kernel-class timing with CUDA events (off by default); the classes of
@@ -72,7 +77,10 @@ class Engine {
     struct RB1C { Act x[3], c1[3]; Stats st1[3], st2[3]; int L = 0; };
     struct StageC { Act x_in, a, xsrc, src, m, out; RB1C noise; std::vector<RB1C> res; int Lin = 0, Lu = 0, Lx = 0; };
 
+    void init();
     void plan(Planner& P);
+    void plan_block(Planner& P);
+    void plan_scratch(Planner& P, int64_t max_elems, int max_c);
     void ensure_plan(int B, int T, int frames, bool have_har);
     Stats stats(Planner& P, int B, int C);
     BlkC plan_blk(Planner& P, const BlkP& w, int Lin, bool input_owned);
@@ -195,6 +203,8 @@ class Engine {
     Act asr_, F0dn_, Ndn_, asrres_, enc_in_, har_, xl_, post_, genin_;
     std::vector<Act> dec_in_;
     BlkC encc_;
+    RB1C rb1c_;                       // block mode: the AdaINResBlock1's caches
+    Act blk_x_, blk_y_;               // block mode: channels-last input and output
     std::vector<BlkC> decc_;
     std::vector<char> res_applied_;
     std::vector<int> x_ch_;

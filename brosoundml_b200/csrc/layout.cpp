@@ -15,6 +15,11 @@ std::atomic<int64_t> g_launches{0};
 void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 int64_t launch_count() { return g_launches.load(std::memory_order_relaxed); }
 
+namespace {
+// "a.b" module-key join; an empty prefix gives the block-relative key
+std::string sub(const std::string& n, const std::string& s) { return n.empty() ? s : n + "." + s; }
+}  // namespace
+
 int64_t Layout::add(const std::string& name, int nd, int s0, int s1, int s2, bool train) {
     bsml_param_entry e{};
     std::snprintf(e.name, sizeof(e.name), "%s", name.c_str());
@@ -51,14 +56,14 @@ AdaP Layout::adain(const std::string& n, int C) {
 BlkP Layout::blk(const std::string& n, int cin, int cout, bool up) {
     BlkP b;
     b.cin = cin; b.cout = cout; b.up = up; b.sc = cin != cout;
-    b.n1 = adain(n + ".norm1", cin);
-    b.n2 = adain(n + ".norm2", cout);
-    b.c1 = conv(n + ".conv1", cout, cin, 3, 1, 1, 1, true);
-    b.c2 = conv(n + ".conv2", cout, cout, 3, 1, 1, 1, true);
-    if (b.sc) b.c1x1 = conv(n + ".conv1x1", cout, cin, 1, 1, 0, 1, false);
+    b.n1 = adain(sub(n, "norm1"), cin);
+    b.n2 = adain(sub(n, "norm2"), cout);
+    b.c1 = conv(sub(n, "conv1"), cout, cin, 3, 1, 1, 1, true);
+    b.c2 = conv(sub(n, "conv2"), cout, cout, 3, 1, 1, 1, true);
+    if (b.sc) b.c1x1 = conv(sub(n, "conv1x1"), cout, cin, 1, 1, 0, 1, false);
     if (up) {
-        b.pool_w = add(n + ".pool.weight", 3, cin, 1, 3, true);
-        b.pool_b = add(n + ".pool.bias", 1, cin, 1, 1, true);
+        b.pool_w = add(sub(n, "pool.weight"), 3, cin, 1, 3, true);
+        b.pool_b = add(sub(n, "pool.bias"), 1, cin, 1, 1, true);
     }
     return b;
 }
@@ -70,12 +75,12 @@ RB1P Layout::rb1(const std::string& n, int C, int k, const int* dil) {
     r.C = C; r.k = k;
     for (int i = 0; i < 3; ++i) r.dil[i] = dil[i];
     for (int i = 0; i < 3; ++i)
-        r.c1[i] = conv(n + ".convs1." + std::to_string(i), C, C, k, 1, (k * dil[i] - dil[i]) / 2, dil[i], true);
-    for (int i = 0; i < 3; ++i) r.c2[i] = conv(n + ".convs2." + std::to_string(i), C, C, k, 1, (k - 1) / 2, 1, true);
-    for (int i = 0; i < 3; ++i) r.a1[i] = adain(n + ".adain1." + std::to_string(i), C);
-    for (int i = 0; i < 3; ++i) r.a2[i] = adain(n + ".adain2." + std::to_string(i), C);
-    for (int i = 0; i < 3; ++i) r.al1[i] = add(n + ".alpha1." + std::to_string(i), 3, 1, C, 1, true);
-    for (int i = 0; i < 3; ++i) r.al2[i] = add(n + ".alpha2." + std::to_string(i), 3, 1, C, 1, true);
+        r.c1[i] = conv(sub(n, "convs1." + std::to_string(i)), C, C, k, 1, (k * dil[i] - dil[i]) / 2, dil[i], true);
+    for (int i = 0; i < 3; ++i) r.c2[i] = conv(sub(n, "convs2." + std::to_string(i)), C, C, k, 1, (k - 1) / 2, 1, true);
+    for (int i = 0; i < 3; ++i) r.a1[i] = adain(sub(n, "adain1." + std::to_string(i)), C);
+    for (int i = 0; i < 3; ++i) r.a2[i] = adain(sub(n, "adain2." + std::to_string(i)), C);
+    for (int i = 0; i < 3; ++i) r.al1[i] = add(sub(n, "alpha1." + std::to_string(i)), 3, 1, C, 1, true);
+    for (int i = 0; i < 3; ++i) r.al2[i] = add(sub(n, "alpha2." + std::to_string(i)), 3, 1, C, 1, true);
     return r;
 }
 
@@ -141,6 +146,32 @@ Layout::Layout(const bsml_decoder_config& c) : cfg(c) {
     post = conv("generator.conv_post", cfg.n_fft + 2, cfg.init_ch >> cfg.n_ups, cfg.post_kernel, 1,
                 (cfg.post_kernel - 1) / 2, 1, true);
 
+    finish();
+}
+
+void validate_block(const bsml_block_spec& b) {
+    auto bad = [](const char* why) { fail("bsml_block_create", why); };
+    if (b.kind != BSML_BLOCK_RESBLK1D && b.kind != BSML_BLOCK_RESBLOCK1) bad("unknown block kind");
+    if (b.style_dim <= 0 || b.cin <= 0 || b.cout <= 0) bad("non-positive channel count");
+    if (b.kind == BSML_BLOCK_RESBLOCK1) {
+        if (b.cin != b.cout) bad("an AdaINResBlock1 keeps its channel count (cin == cout)");
+        if (b.kernel < 1 || !(b.kernel & 1)) bad("kernel must be odd");
+        for (int i = 0; i < 3; ++i)
+            if (b.dil[i] < 1) bad("dilations must be positive");
+    }
+}
+
+// One block on its own: an AdainResBlk1d in `enc`, an AdaINResBlock1 in `rbs[0]`;
+// parameter keys relative to the block
+Layout::Layout(const bsml_block_spec& b) : block_kind(b.kind) {
+    validate_block(b);
+    cfg.style_dim = b.style_dim;
+    if (b.kind == BSML_BLOCK_RESBLK1D) enc = blk("", b.cin, b.cout, b.upsample != 0);
+    else rbs.push_back(rb1("", b.cin, b.kernel, b.dil));
+    finish();
+}
+
+void Layout::finish() {
     // AdaIN order = DecoderLora::adapters() (decoder_lora.cpp:173-179)
     auto reg = [&](AdaP& a) {
         a.idx = (int)aff_C.size();
@@ -149,20 +180,21 @@ Layout::Layout(const bsml_decoder_config& c) : cfg(c) {
         aff_base.push_back(aff_per_clip);
         aff_per_clip += 2 * a.C;
     };
-    reg(enc.n1); reg(enc.n2);
+    const bool decoder = block_kind == 0, with_enc = block_kind != BSML_BLOCK_RESBLOCK1;
+    if (with_enc) { reg(enc.n1); reg(enc.n2); }
     for (auto& d : dec) { reg(d.n1); reg(d.n2); }
     for (auto& r : nres) { for (auto& a : r.a1) reg(a); for (auto& a : r.a2) reg(a); }
     for (auto& r : rbs) { for (auto& a : r.a1) reg(a); for (auto& a : r.a2) reg(a); }
 
     auto regc = [&](ConvP& cp) { cp.id = (int)convs.size(); convs.push_back(&cp); };
-    regc(F0c); regc(Nc); regc(asr_res);
+    if (decoder) { regc(F0c); regc(Nc); regc(asr_res); }
     auto regb = [&](BlkP& b) { regc(b.c1); regc(b.c2); if (b.sc) regc(b.c1x1); };
-    regb(enc);
+    if (with_enc) regb(enc);
     for (auto& d : dec) regb(d);
     for (auto& n : noise) regc(n);
     for (auto& r : nres) for (int i = 0; i < 3; ++i) { regc(r.c1[i]); regc(r.c2[i]); }
     for (auto& r : rbs) for (int i = 0; i < 3; ++i) { regc(r.c1[i]); regc(r.c2[i]); }
-    regc(post);
+    if (decoder) regc(post);
     for (size_t i = 0; i < ups.size(); ++i) ups[i].id = (int)i;
 }
 

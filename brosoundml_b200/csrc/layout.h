@@ -30,6 +30,7 @@ struct UpP { int64_t w = -1, b = -1; int cin = 0, cout = 0, k = 0, s = 1, p = 0;
 
 struct Layout {
     bsml_decoder_config cfg{};
+    int block_kind = 0;              // 0 = full decoder, else BSML_BLOCK_* (block in enc / rbs[0])
     std::vector<bsml_param_entry> table;
     int64_t total = 0;
     ConvP F0c, Nc, asr_res;
@@ -47,10 +48,12 @@ struct Layout {
     std::vector<ConvP*> convs;       // every regular conv (for weight packing)
 
     explicit Layout(const bsml_decoder_config& c);
+    explicit Layout(const bsml_block_spec& b);
     Layout(const Layout&) = delete;
     Layout& operator=(const Layout&) = delete;
 
    private:
+    void finish();   // AdaIN and conv registries
     int64_t add(const std::string& name, int nd, int s0, int s1, int s2, bool train);
     ConvP conv(const std::string& n, int cout, int cin, int k, int s, int p, int d, bool bias);
     AdaP adain(const std::string& n, int C);
@@ -59,5 +62,6 @@ struct Layout {
 };
 
 void validate_config(const bsml_decoder_config& c);
+void validate_block(const bsml_block_spec& b);
 
 }  // namespace bsml

@@ -130,6 +130,59 @@ class Decoder:
         return dict(grads=grads, d_asr=d_asr, d_style=d_style, d_aff=d_aff)
 
 
+class Block(Decoder):
+    """One decoder block on its own over the same engine: ``spec`` =
+    dict(kind=1, style_dim, cin, cout, upsample) for an AdainResBlk1d
+    (``detail::adain_resblk_1d_forward_train`` / ``_backward``,
+    src/kokoro_decoder_backward.h:82-111) or dict(kind=2, style_dim, cin=C, cout=C,
+    kernel, dil) for an AdaINResBlock1 (``detail::adain_resblock1_forward_train`` /
+    ``_backward``, :125-144). Parameter keys are block-relative."""
+
+    RESBLK1D, RESBLOCK1 = 1, 2
+
+    def __init__(self, spec: dict, device: int = 0, math: str = "fp32"):
+        self.spec = dict(spec)
+        self.cfg = {"style_dim": spec["style_dim"]}
+        self._c = _lib.make_block_spec(spec)
+        L = _lib.lib()
+        h = ctypes.c_void_p()
+        _lib.check(L.bsml_block_create(ctypes.byref(self._c), int(device), ctypes.byref(h)))
+        self._h = h
+        self.device = torch.device("cuda", device)
+        self.n_params, self.table, self.aff_C, self.aff_per_clip = _lib.block_layout(spec)
+        self.n_affine = len(self.aff_C)
+        self.set_math(math)
+        self._last = None
+
+    def out_len(self, L: int) -> int:
+        return 2 * L if self.spec["kind"] == self.RESBLK1D and self.spec.get("upsample") else L
+
+    def forward(self, params, x, style=None, aff_in=None, y=None, aff_out=None):
+        """x (B, cin, L) -> y (B, cout, out_len(L))."""
+        params, x, style, aff_in = map(_f32, (params, x, style, aff_in))
+        B, _, L = x.shape
+        if y is None:
+            y = torch.empty((B, self.spec["cout"], self.out_len(L)), device=self.device, dtype=torch.float32)
+        self._last = (B, L)
+        self._borrowed = params
+        _lib.check(_lib.lib().bsml_block_forward(self._h, B, L, _ptr(params), _ptr(x), _ptr(style), _ptr(aff_in),
+                                                 _ptr(y), _ptr(aff_out), _stream()))
+        return y
+
+    def backward(self, dy, grads=None, want_grads=True, want_inputs=True, want_aff=False):
+        B, L = self._last
+        dy = _f32(dy)
+        dev = self.device
+        if grads is None and want_grads:
+            grads = torch.empty(self.n_params, device=dev, dtype=torch.float32)
+        dx = torch.empty((B, self.spec["cin"], L), device=dev) if want_inputs else None
+        d_style = torch.empty((B, self.spec["style_dim"]), device=dev) if want_inputs else None
+        d_aff = torch.empty(B * self.aff_per_clip, device=dev) if want_aff else None
+        _lib.check(_lib.lib().bsml_block_backward(self._h, _ptr(dy), _ptr(grads), _ptr(dx), _ptr(d_style),
+                                                  _ptr(d_aff), _stream()))
+        return dict(grads=grads, dx=dx, d_style=d_style, d_aff=d_aff)
+
+
 def l1_loss(audio, target, loss=None, daudio=None):
     audio, target = _f32(audio), _f32(target)
     if loss is None:

@@ -142,6 +142,44 @@ int bsml_decoder_read_profile(bsml_decoder* d, double* out);
  * record like read_profile. */
 int bsml_decoder_read_profile_records(bsml_decoder* d, double* out, int max_records, int* n_records);
 
+/* ── one decoder block on its own ──────────────────────────────────────────
+ * The reference's block-level atoms, batched:
+ *   BSML_BLOCK_RESBLK1D   detail::adain_resblk_1d_forward_train / _backward
+ *                         (src/kokoro_decoder_backward.h:82-111): AdainResBlk1d
+ *                         cin -> cout, optional x2 upsample (depthwise convT pool,
+ *                         nearest-2x shortcut), learned 1x1 shortcut when cin != cout
+ *   BSML_BLOCK_RESBLOCK1  detail::adain_resblock1_forward_train / _backward
+ *                         (:125-144): AdaINResBlock1 with Snake, C channels, kernel,
+ *                         convs1 dilations dil[3]
+ * The handle is a bsml_decoder: param_count / param_table, set_math, profiling
+ * and destroy apply; parameter keys are block-relative ("norm1.fc.weight",
+ * "convs1.0.weight", "alpha2.1", ...). The whole-decoder entry points reject a
+ * block handle and the block entry points reject a decoder handle. */
+enum { BSML_BLOCK_RESBLK1D = 1, BSML_BLOCK_RESBLOCK1 = 2 };
+typedef struct bsml_block_spec {
+    int kind;        /* BSML_BLOCK_* */
+    int style_dim;
+    int cin, cout;   /* RESBLOCK1: cin = cout = C */
+    int upsample;    /* RESBLK1D: 1 = x2 upsampling block */
+    int kernel;      /* RESBLOCK1: odd conv kernel */
+    int dil[3];      /* RESBLOCK1: convs1 dilations */
+} bsml_block_spec;
+int bsml_block_create(const bsml_block_spec* spec, int device, bsml_decoder** out);
+/* Layout queries from a spec alone (no device needed). */
+int bsml_block_param_count(const bsml_block_spec* spec, int64_t* n_params, int* n_entries, int* n_affine,
+                           int64_t* aff_per_clip);
+int bsml_block_param_table(const bsml_block_spec* spec, bsml_param_entry* out, int max_entries, int* aff_channels);
+/* Forward: x (B, cin, L) NCL -> y (B, cout, L_out), L_out = 2L for an upsampling
+ * AdainResBlk1d, else L. style (B, style_dim) or aff_in (packed [a][B][2*C_a],
+ * adapter order: norm1, norm2 / adain1[0..2], adain2[0..2]). Caches what the
+ * backward needs; params is borrowed until the backward has been enqueued. */
+int bsml_block_forward(bsml_decoder* d, int B, int L, const float* params, const float* x, const float* style,
+                       const float* aff_in, float* y, float* aff_out, void* stream);
+/* Backward of the last block forward: dy (B, cout, L_out). grads (n_params)
+ * OVERWRITTEN (optional); dx (B, cin, L), d_style, d_aff optional. */
+int bsml_block_backward(bsml_decoder* d, const float* dy, float* grads, float* dx, float* d_style, float* d_aff,
+                        void* stream);
+
 /* ── loss and optimiser ─────────────────────────────────────────────────── */
 
 /* L1 loss: loss[0] = mean |audio - target|, daudio = sign(audio - target) / n. */

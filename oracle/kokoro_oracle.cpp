@@ -74,6 +74,18 @@ typedef struct orc_cfg {
     int upsample_scale;   // prod(ups_rate) * hop = 300
 } orc_cfg;
 
+// One decoder block on its own (the reference's block-level atoms,
+// src/kokoro_decoder_backward.h:82-144). kind 1 = AdainResBlk1d (cin, cout,
+// upsample), kind 2 = AdaINResBlock1 (C = cin, kernel, dil).
+typedef struct orc_block_spec {
+    int kind;
+    int style_dim;
+    int cin, cout;
+    int upsample;
+    int kernel;
+    int dil[3];
+} orc_block_spec;
+
 typedef struct orc_param {
     char name[96];
     int64_t offset;
@@ -101,8 +113,12 @@ struct RB1 {
 };
 struct Up { int64_t w = -1, b = -1; int cin = 0, cout = 0, k = 0, s = 1, p = 0; };
 
+// "a.b" module-key join; an empty prefix gives the block-relative key
+inline std::string sub(const std::string& n, const std::string& s) { return n.empty() ? s : n + "." + s; }
+
 struct Layout {
     orc_cfg cfg;
+    int kind = 0;   // 0 = full decoder, else orc_block_spec::kind
     std::vector<orc_param> table;
     int64_t total = 0;
     Conv F0c, Nc, asr_res;
@@ -142,14 +158,14 @@ struct Layout {
     }
     Blk blk(const std::string& n, int cin, int cout, bool up) {
         Blk b; b.cin = cin; b.cout = cout; b.up = up; b.sc = cin != cout;
-        b.n1 = adain(n + ".norm1", cin);
-        b.n2 = adain(n + ".norm2", cout);
-        b.c1 = conv(n + ".conv1", cout, cin, 3, 1, 1, 1, true);
-        b.c2 = conv(n + ".conv2", cout, cout, 3, 1, 1, 1, true);
-        if (b.sc) b.c1x1 = conv(n + ".conv1x1", cout, cin, 1, 1, 0, 1, false);
+        b.n1 = adain(sub(n, "norm1"), cin);
+        b.n2 = adain(sub(n, "norm2"), cout);
+        b.c1 = conv(sub(n, "conv1"), cout, cin, 3, 1, 1, 1, true);
+        b.c2 = conv(sub(n, "conv2"), cout, cout, 3, 1, 1, 1, true);
+        if (b.sc) b.c1x1 = conv(sub(n, "conv1x1"), cout, cin, 1, 1, 0, 1, false);
         if (up) {
-            b.pool_w = add(n + ".pool.weight", 3, cin, 1, 3, true);
-            b.pool_b = add(n + ".pool.bias", 1, cin, 1, 1, true);
+            b.pool_w = add(sub(n, "pool.weight"), 3, cin, 1, 3, true);
+            b.pool_b = add(sub(n, "pool.bias"), 1, cin, 1, 1, true);
         }
         return b;
     }
@@ -157,13 +173,13 @@ struct Layout {
         RB1 r; r.C = C; r.k = k;
         for (int i = 0; i < 3; ++i) r.dil[i] = dil[i];
         for (int i = 0; i < 3; ++i)   // get_padding(k, d) = (k*d - d)/2, kokoro_modules.cpp:1155-1157
-            r.c1[i] = conv(n + ".convs1." + std::to_string(i), C, C, k, 1, (k * dil[i] - dil[i]) / 2, dil[i], true);
+            r.c1[i] = conv(sub(n, "convs1." + std::to_string(i)), C, C, k, 1, (k * dil[i] - dil[i]) / 2, dil[i], true);
         for (int i = 0; i < 3; ++i)
-            r.c2[i] = conv(n + ".convs2." + std::to_string(i), C, C, k, 1, (k - 1) / 2, 1, true);
-        for (int i = 0; i < 3; ++i) r.a1[i] = adain(n + ".adain1." + std::to_string(i), C);
-        for (int i = 0; i < 3; ++i) r.a2[i] = adain(n + ".adain2." + std::to_string(i), C);
-        for (int i = 0; i < 3; ++i) r.al1[i] = add(n + ".alpha1." + std::to_string(i), 3, 1, C, 1, true);
-        for (int i = 0; i < 3; ++i) r.al2[i] = add(n + ".alpha2." + std::to_string(i), 3, 1, C, 1, true);
+            r.c2[i] = conv(sub(n, "convs2." + std::to_string(i)), C, C, k, 1, (k - 1) / 2, 1, true);
+        for (int i = 0; i < 3; ++i) r.a1[i] = adain(sub(n, "adain1." + std::to_string(i)), C);
+        for (int i = 0; i < 3; ++i) r.a2[i] = adain(sub(n, "adain2." + std::to_string(i)), C);
+        for (int i = 0; i < 3; ++i) r.al1[i] = add(sub(n, "alpha1." + std::to_string(i)), 3, 1, C, 1, true);
+        for (int i = 0; i < 3; ++i) r.al2[i] = add(sub(n, "alpha2." + std::to_string(i)), 3, 1, C, 1, true);
         return r;
     }
 
@@ -202,12 +218,25 @@ struct Layout {
                                   cfg.init_ch >> (i + 1), cfg.rb_kernel[j], cfg.rb_dil[j]));
         post = conv("generator.conv_post", cfg.n_fft + 2, cfg.init_ch >> cfg.n_ups, cfg.post_kernel, 1,
                     (cfg.post_kernel - 1) / 2, 1, true);
-        // AdaIN order = DecoderLora::adapters() order (decoder_lora.cpp:173-179).
+        register_adains();
+    }
+
+    // a single block: AdainResBlk1d held in `enc`, AdaINResBlock1 in `rbs[0]`;
+    // keys are block-relative ("norm1.fc.weight", "convs1.0.weight", ...)
+    explicit Layout(const orc_block_spec& b) : cfg{}, kind(b.kind) {
+        cfg.style_dim = b.style_dim;
+        if (kind == 1) enc = blk("", b.cin, b.cout, b.upsample != 0);
+        else rbs.push_back(rb1("", b.cin, b.kernel, b.dil));
+        register_adains();
+    }
+
+    // AdaIN order = DecoderLora::adapters() order (decoder_lora.cpp:173-179).
+    void register_adains() {
         auto reg = [&](AdaIN& a) {
             a.idx = (int)aff_C.size(); aff_C.push_back(a.C); aff_base.push_back(aff_per_clip);
             aff_per_clip += 2 * a.C;
         };
-        reg(enc.n1); reg(enc.n2);
+        if (kind != 2) { reg(enc.n1); reg(enc.n2); }
         for (auto& d : dec) { reg(d.n1); reg(d.n2); }
         for (auto& r : nres) { for (auto& a : r.a1) reg(a); for (auto& a : r.a2) reg(a); }
         for (auto& r : rbs) { for (auto& a : r.a1) reg(a); for (auto& a : r.a2) reg(a); }
@@ -717,7 +746,7 @@ struct Decoder {
         for_each_adain(one);
     }
     template <class F> void for_each_adain(F f) {
-        f(lay.enc.n1); f(lay.enc.n2);
+        if (lay.kind != 2) { f(lay.enc.n1); f(lay.enc.n2); }
         for (auto& d : lay.dec) { f(d.n1); f(d.n2); }
         for (auto& r : lay.nres) { for (auto& a : r.a1) f(a); for (auto& a : r.a2) f(a); }
         for (auto& r : lay.rbs) { for (auto& a : r.a1) f(a); for (auto& a : r.a2) f(a); }
@@ -1193,9 +1222,71 @@ int run(const orc_cfg* cfg, int B, int T, const R* params, const R* asr, const R
     return 0;
 }
 
+// One block forward (+ backward when dy != NULL); x, y, dy, dx in NCL.
+template <class R>
+int run_block(const orc_block_spec* spec, int B, int L, const R* params, const R* x, const R* style, const R* aff_in,
+              const R* dy, R* y, R* grads, R* dx, R* d_style, R* d_aff, R* aff_out) {
+    if (spec->kind != 1 && spec->kind != 2) return -1;
+    orc::Layout lay(*spec);
+    orc::Decoder<R> d(lay, params, grads, B, L);
+    d.style = style;
+    d.aff_in = aff_in;
+    d.resolve_affines();
+    if (aff_out) std::memcpy(aff_out, d.aff.data(), sizeof(R) * d.aff.size());
+    if (grads) std::fill(grads, grads + lay.total, R(0));
+    if (d_style) std::fill(d_style, d_style + (int64_t)B * spec->style_dim, R(0));
+    std::vector<R> out, din;
+    if (spec->kind == 1) {
+        typename orc::Decoder<R>::BlkCache c;
+        d.blk_f(lay.enc, x, L, c, out);
+        if (dy) d.blk_b(lay.enc, c, dy, din);
+    } else {
+        typename orc::Decoder<R>::RB1Cache c;
+        d.rb1_f(lay.rbs[0], x, L, c, out);
+        if (dy) d.rb1_b(lay.rbs[0], c, dy, &din);
+    }
+    if (y) std::memcpy(y, out.data(), sizeof(R) * out.size());
+    if (dy) {
+        if (dx) std::memcpy(dx, din.data(), sizeof(R) * din.size());
+        d.affine_backward(d_style);
+        if (d_aff) std::memcpy(d_aff, d.daff.data(), sizeof(R) * d.daff.size());
+    }
+    return 0;
+}
+
 }  // namespace
 
 extern "C" {
+
+int orc_block_param_count(const orc_block_spec* spec, int64_t* total, int* n_entries, int* n_affine,
+                          int64_t* aff_per_clip) {
+    orc::Layout lay(*spec);
+    if (total) *total = lay.total;
+    if (n_entries) *n_entries = (int)lay.table.size();
+    if (n_affine) *n_affine = (int)lay.aff_C.size();
+    if (aff_per_clip) *aff_per_clip = lay.aff_per_clip;
+    return 0;
+}
+
+int orc_block_param_table(const orc_block_spec* spec, orc_param* out, int max_entries, int* aff_C) {
+    orc::Layout lay(*spec);
+    const int n = std::min<int>(max_entries, (int)lay.table.size());
+    for (int i = 0; i < n; ++i) out[i] = lay.table[i];
+    if (aff_C)
+        for (size_t i = 0; i < lay.aff_C.size(); ++i) aff_C[i] = lay.aff_C[i];
+    return n;
+}
+
+int orc_block_run_f32(const orc_block_spec* spec, int B, int L, const float* params, const float* x,
+                      const float* style, const float* aff_in, const float* dy, float* y, float* grads, float* dx,
+                      float* d_style, float* d_aff, float* aff_out) {
+    return run_block<float>(spec, B, L, params, x, style, aff_in, dy, y, grads, dx, d_style, d_aff, aff_out);
+}
+int orc_block_run_f64(const orc_block_spec* spec, int B, int L, const double* params, const double* x,
+                      const double* style, const double* aff_in, const double* dy, double* y, double* grads,
+                      double* dx, double* d_style, double* d_aff, double* aff_out) {
+    return run_block<double>(spec, B, L, params, x, style, aff_in, dy, y, grads, dx, d_style, d_aff, aff_out);
+}
 
 int orc_param_count(const orc_cfg* cfg, int64_t* total, int* n_entries, int* n_affine, int64_t* aff_per_clip) {
     orc::Layout lay(*cfg);

@@ -44,6 +44,24 @@ class OrcParam(ctypes.Structure):
                 ("ndim", ctypes.c_int), ("shape", ctypes.c_int * 3), ("trainable", ctypes.c_int)]
 
 
+class OrcBlockSpec(ctypes.Structure):
+    """Mirror of ``orc_block_spec``: kind 1 = AdainResBlk1d, kind 2 = AdaINResBlock1."""
+
+    _fields_ = [("kind", ctypes.c_int), ("style_dim", ctypes.c_int), ("cin", ctypes.c_int), ("cout", ctypes.c_int),
+                ("upsample", ctypes.c_int), ("kernel", ctypes.c_int), ("dil", ctypes.c_int * 3)]
+
+
+def make_block_spec(d: dict) -> OrcBlockSpec:
+    s = OrcBlockSpec()
+    for k, v in d.items():
+        if k == "dil":
+            for i, x in enumerate(v):
+                s.dil[i] = int(x)
+        else:
+            setattr(s, k, int(v))
+    return s
+
+
 def make_cfg(d: dict) -> OrcCfg:
     """Build an OrcCfg from a plain dict (the same dict the product accepts)."""
     c = OrcCfg()
@@ -85,6 +103,12 @@ def lib():
         for sfx in ("f32", "f64"):
             fn = getattr(_lib, f"orc_decoder_run_{sfx}")
             fn.argtypes = [ctypes.POINTER(OrcCfg), I, I] + [P] * 6 + [I] + [P] * 8
+        BS = ctypes.POINTER(OrcBlockSpec)
+        _lib.orc_block_param_count.argtypes = [BS, ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(I),
+                                               ctypes.POINTER(I), ctypes.POINTER(ctypes.c_int64)]
+        _lib.orc_block_param_table.argtypes = [BS, ctypes.POINTER(OrcParam), I, P]
+        for sfx in ("f32", "f64"):
+            getattr(_lib, f"orc_block_run_{sfx}").argtypes = [BS, I, I] + [P] * 11
         _lib.orc_harmonic_source_f32.argtypes = [ctypes.POINTER(OrcCfg), P, I, I, P, P, P]
         _lib.orc_threads.restype = I
         _lib.orc_set_threads.argtypes = [I]
@@ -93,6 +117,52 @@ def lib():
 
 def _p(a):
     return None if a is None else a.ctypes.data_as(ctypes.c_void_p)
+
+
+class BlockOracle:
+    """One decoder block on its own: ``spec`` = dict(kind=1, style_dim, cin, cout, upsample)
+    for an AdainResBlk1d or dict(kind=2, style_dim, cin=C, cout=C, kernel, dil) for an
+    AdaINResBlock1 (src/kokoro_decoder_backward.h:82-144)."""
+
+    def __init__(self, spec: dict):
+        self.spec_dict = dict(spec)
+        self.spec = make_block_spec(spec)
+        L = lib()
+        tot, ne, na, apc = ctypes.c_int64(), ctypes.c_int(), ctypes.c_int(), ctypes.c_int64()
+        L.orc_block_param_count(ctypes.byref(self.spec), ctypes.byref(tot), ctypes.byref(ne), ctypes.byref(na),
+                                ctypes.byref(apc))
+        self.n_params, self.n_affine, self.aff_per_clip = tot.value, na.value, apc.value
+        arr = (OrcParam * ne.value)()
+        affc = np.zeros(na.value, dtype=np.int32)
+        L.orc_block_param_table(ctypes.byref(self.spec), arr, ne.value, _p(affc))
+        self.table = [dict(name=p.name.decode(), offset=p.offset, numel=p.numel,
+                           shape=tuple(p.shape[:p.ndim]), trainable=bool(p.trainable)) for p in arr]
+        self.aff_C = [int(c) for c in affc]
+
+    def out_len(self, L: int) -> int:
+        return 2 * L if self.spec_dict["kind"] == 1 and self.spec_dict.get("upsample") else L
+
+    def run(self, params, x, style, aff_in=None, dy=None, dtype=np.float32, want_aff=False):
+        """x (B, cin, L) NCL; style (B, style_dim); aff_in packed (gamma, beta) or None; dy
+        (B, cout, L_out) for the backward. Returns y and, with dy, grads, dx, d_style, d_aff."""
+        B, _, L = x.shape
+        f = (lambda a: None if a is None else np.ascontiguousarray(a, dtype=dtype))
+        params, x, style, aff_in, dy = map(f, (params, x, style, aff_in, dy))
+        out = dict(y=np.zeros((B, self.spec_dict["cout"], self.out_len(L)), dtype))
+        if dy is not None:
+            out["grads"] = np.zeros(self.n_params, dtype)
+            out["dx"] = np.zeros_like(x)
+            out["d_style"] = np.zeros((B, self.spec_dict["style_dim"]), dtype)
+            out["d_aff"] = np.zeros(B * self.aff_per_clip, dtype)
+        if want_aff:
+            out["aff"] = np.zeros(B * self.aff_per_clip, dtype)
+        fn = lib().orc_block_run_f32 if dtype == np.float32 else lib().orc_block_run_f64
+        rc = fn(ctypes.byref(self.spec), B, L, _p(params), _p(x), _p(style), _p(aff_in), _p(dy), _p(out["y"]),
+                _p(out.get("grads")), _p(out.get("dx")), _p(out.get("d_style")), _p(out.get("d_aff")),
+                _p(out.get("aff")))
+        if rc != 0:
+            raise RuntimeError(f"oracle: block run failed ({rc})")
+        return out
 
 
 class Oracle:

@@ -24,12 +24,13 @@ def hann(n: int, dtype) -> torch.Tensor:
 
 
 class TorchDecoder:
-    def __init__(self, cfg: dict, table, params: np.ndarray, dtype=torch.float64):
+    def __init__(self, cfg: dict, table, params: np.ndarray, dtype=torch.float64, device=None):
         self.cfg = cfg
         self.dtype = dtype
         self.p = {}
         for e in table:
-            t = torch.tensor(params[e["offset"]:e["offset"] + e["numel"]], dtype=dtype).reshape(e["shape"])
+            t = torch.tensor(params[e["offset"]:e["offset"] + e["numel"]], dtype=dtype,
+                             device=device).reshape(e["shape"])
             t.requires_grad_(e["trainable"])
             self.p[e["name"]] = t
         self.table = table
@@ -39,7 +40,7 @@ class TorchDecoder:
         for e in self.table:
             t = self.p[e["name"]]
             if t.grad is not None:
-                g[e["offset"]:e["offset"] + e["numel"]] = t.grad.detach().reshape(-1).numpy()
+                g[e["offset"]:e["offset"] + e["numel"]] = t.grad.detach().reshape(-1).cpu().numpy()
         return g
 
     # ── pieces
