@@ -31,11 +31,17 @@ METRIC = "Kokoro decoder fwd+bwd audio-seconds/sec at 1/2/4/8 B200; % tensor/HBM
 NCU_CONV_FWD_TC = {"dram_bytes": 394.7e6 + 160.3e6, "flops": 2.0 * 16 * 128 * 128 * 7 * 24001}
 UNIT = "audio-s/s"
 WORKLOADS = {
-    # name: (B per GPU, T asr frames, description)
+    # name: (B per GPU, T asr frames (c1: samples L), description)
     "c2": (16, 200, "Kokoro-82M decoder fwd+bwd, B=16 x T=200 (5 s clips) per GPU, BASELINE config 2"),
     "c0": (1, 32, "Kokoro-82M decoder fwd+bwd, B=1 x T=32 (0.8 s), BASELINE config 0"),
     "c3": (64, 400, "Kokoro-82M decoder fwd+bwd, B=64 x T=400 (10 s clips) per GPU, BASELINE config 3 shapes"),
+    "c3lora": (64, 400, "Kokoro-82M decoder conv-weight LoRA step (rank 8, scale 2, base frozen), B=64 x T=400 "
+                        "(10 s clips) per GPU, BASELINE config 3"),
+    "c1": (8, 24000, "one generator AdaINResBlock1 (C=128, k=7, dilations 1,3,5, Snake, AdaIN style 128) "
+                     "fwd+bwd, x [8,128,24000], BASELINE config 1"),
 }
+# BASELINE config 1 reports conv throughput, not audio
+C1_METRIC = "AdaINResBlock1 [8,128,24000] k7 fwd+bwd conv TFLOP/s (fwd+dgrad+wgrad); Snake/AdaIN GB/s"
 
 
 def audio_seconds(B, T):
@@ -135,12 +141,192 @@ def run_cpu_baseline(cfg, T, threads=None):
                        f"(all grads) in the C++ oracle (oracle/kokoro_oracle.cpp), {dt:.1f} s")
 
 
+def setup_decoder(args, B, T, dev, rank, math):
+    """Full decoder training step: forward, L1, backward (all grads), all-reduce, Adam."""
+    import torch
+
+    from brosoundml_b200 import config, dp, synth
+    from brosoundml_b200.decoder import Decoder, adam_step, l1_loss
+
+    cfg = config.kokoro_82m()
+    dec = Decoder(cfg, dev.index, math=math)
+    params = torch.tensor(synth.init_params(dec.table, dec.n_params, 0), device=dev)
+    x = synth.make_inputs(cfg, B, T, 1 + rank)
+    tgt = synth.make_target(cfg, B, T, 1000 + rank)
+    host = {k: torch.from_numpy(v).pin_memory() for k, v in x.items()}
+    host["target"] = torch.from_numpy(tgt).pin_memory()
+    d = {k: v.to(dev) for k, v in host.items()}
+    grads = torch.empty(dec.n_params, device=dev)
+    m = torch.zeros(dec.n_params, device=dev)
+    v = torch.zeros(dec.n_params, device=dev)
+    audio = torch.empty((B, dec.audio_len(T)), device=dev)
+    lossbuf = torch.empty(1, device=dev)
+    dabuf = torch.empty_like(audio)
+    state = {"step": 0}
+
+    def step(inp):
+        dec.forward(params, inp["asr"], inp["F0"], inp["N"], inp["style"], audio=audio)
+        l1_loss(audio, inp["target"], lossbuf, dabuf)
+        dec.backward(dabuf, grads=grads)
+        dp.average_gradients(grads)   # one NCCL all-reduce of the flat gradient (N > 1)
+        state["step"] += 1
+        adam_step(params, grads, m, v, 1e-5, state["step"])
+
+    return dict(host=host, dev=d, step=step, result=lossbuf, prof=dec, metric=METRIC, unit=UNIT,
+                units_per_step=audio_seconds(B, T),
+                config={"audio_s_per_step_per_gpu": audio_seconds(B, T),
+                        "weights": "random init N(0,0.02), Snake alpha 1", "optimizer": "Adam lr 1e-5"})
+
+
+def setup_convlora(args, B, T, dev, rank, math):
+    """rank-8 LoRA (A ~ N(0, 0.01), B = 0, scale 16/8) on every
+    Conv1d / ConvTranspose1d weight, base frozen: forward of the adapted decoder, L1,
+    backward, dA/dB, all-reduce of the LoRA gradients (N > 1), Adam on A and B."""
+    import torch
+
+    from brosoundml_b200 import config, dp, synth
+    from brosoundml_b200.decoder import Decoder, l1_loss
+    from brosoundml_b200.lora import ConvLora
+
+    cfg = config.kokoro_82m()
+    dec = Decoder(cfg, dev.index, math=math)
+    lora = ConvLora(dec, rank=8, scale=16.0 / 8.0, seed=1)
+    params = torch.tensor(synth.init_params(dec.table, dec.n_params, 0), device=dev)
+    x = synth.make_inputs(cfg, B, T, 1 + rank)
+    tgt = synth.make_target(cfg, B, T, 1000 + rank)
+    host = {k: torch.from_numpy(v).pin_memory() for k, v in x.items()}
+    host["target"] = torch.from_numpy(tgt).pin_memory()
+    d = {k: v.to(dev) for k, v in host.items()}
+    audio = torch.empty((B, dec.audio_len(T)), device=dev)
+    lossbuf = torch.empty(1, device=dev)
+    dabuf = torch.empty_like(audio)
+    g = lora.grads()
+
+    def step(inp):
+        lora.forward(params, inp["asr"], inp["F0"], inp["N"], inp["style"], audio=audio)
+        l1_loss(audio, inp["target"], lossbuf, dabuf)
+        lora.zero_grad()
+        lora.backward(dabuf)
+        dp.average_gradients(g)       # one NCCL all-reduce of the flat LoRA gradient (N > 1)
+        lora.adam_step(1e-4)
+
+    return dict(host=host, dev=d, step=step, result=lossbuf, prof=dec, metric=METRIC, unit=UNIT,
+                units_per_step=audio_seconds(B, T),
+                config={"audio_s_per_step_per_gpu": audio_seconds(B, T), "lora_params": lora.n_params,
+                        "lora": "rank 8, scale 2, every conv/convT weight, base frozen",
+                        "weights": "random init N(0,0.02), Snake alpha 1", "optimizer": "Adam lr 1e-4 on A, B"})
+
+
+def block_flops(B, C, L, k):
+    """Algorithmic conv FLOPs of one AdaINResBlock1 fwd+bwd (6 stride-1 C->C convs,
+    forward + input gradient + weight gradient)."""
+    return 3 * 6 * 2.0 * B * C * C * k * L
+
+
+def setup_block(args, B, L, dev, rank, math):
+    """one AdaINResBlock1 (C=128, k=7, dilations 1,3,5) fwd+bwd
+    with every gradient (conv weights and biases, Snake alphas, AdaIN fc, dx, d_style)."""
+    import numpy as np
+    import torch
+
+    from brosoundml_b200 import _lib
+    from brosoundml_b200.decoder import Block
+
+    spec = dict(kind=2, style_dim=128, cin=128, cout=128, kernel=7, dil=[1, 3, 5])
+    blk = Block(spec, dev.index, math=math)
+    rng = np.random.default_rng(0)
+    p = np.zeros(blk.n_params, np.float32)
+    for e in blk.table:
+        sl = slice(e["offset"], e["offset"] + e["numel"])
+        p[sl] = 1.0 if e["name"].startswith("alpha") else rng.normal(0, 0.02, e["numel"])
+    params = torch.tensor(p, device=dev)
+    r = np.random.default_rng(1 + rank)
+    host = {"x": torch.from_numpy(r.standard_normal((B, 128, L), dtype=np.float32)).pin_memory(),
+            "style": torch.from_numpy(r.standard_normal((B, 128), dtype=np.float32)).pin_memory(),
+            "dy": torch.from_numpy(r.standard_normal((B, 128, L), dtype=np.float32)).pin_memory()}
+    d = {k: v.to(dev) for k, v in host.items()}
+    y = torch.empty((B, 128, L), device=dev)
+    grads = torch.empty(blk.n_params, device=dev)
+    dx = torch.empty((B, 128, L), device=dev)
+    d_style = torch.empty((B, 128), device=dev)
+    L_ = _lib.lib()
+    from brosoundml_b200.decoder import _ptr, _stream
+
+    def step(inp):
+        blk.forward(params, inp["x"], inp["style"], y=y)
+        _lib.check(L_.bsml_block_backward(blk._h, _ptr(inp["dy"]), _ptr(grads), _ptr(dx), _ptr(d_style), None,
+                                          _stream()))
+
+    fl = block_flops(B, 128, L, 7)
+    return dict(host=host, dev=d, step=step, result=d_style[0, :1], prof=blk, metric=C1_METRIC, unit="TFLOP/s",
+                units_per_step=fl / 1e12,
+                config={"conv_flops_per_step": fl, "weights": "N(0,0.02), Snake alpha 1",
+                        "inputs": "x, style, upstream grad N(0,1)"})
+
+
+def run_cpu_baseline_block(B, L):
+    """The block oracle on the whole config-1 workload (B clips x L samples), timed once."""
+    import numpy as np
+
+    from oracle import oracle as orc
+
+    spec = dict(kind=2, style_dim=128, cin=128, cout=128, kernel=7, dil=[1, 3, 5])
+    o = orc.BlockOracle(spec)
+    rng = np.random.default_rng(0)
+    p = rng.normal(0, 0.02, o.n_params).astype(np.float32)
+    x = rng.standard_normal((B, 128, L), dtype=np.float32)
+    s = rng.standard_normal((B, 128), dtype=np.float32)
+    dy = rng.standard_normal((B, 128, L), dtype=np.float32)
+    o.run(p, x[:1, :, :256], s[:1], dy=dy[:1, :, :256])
+    t0 = time.perf_counter()
+    o.run(p, x, s, dy=dy)
+    dt = time.perf_counter() - t0
+    return dict(value=block_flops(B, 128, L, 7) / dt / 1e12, unit="TFLOP/s", cores=orc.threads(), kind="port",
+                sample=f"the whole workload ({B} clips x L={L}) block fwd+bwd (all grads) in the C++ oracle, "
+                       f"{dt:.1f} s")
+
+
+def reference_arm_block(args):
+    """Config 1 on the host cores: the block oracle over the whole workload per step."""
+    import numpy as np
+
+    from oracle import oracle as orc
+
+    B, L, desc = WORKLOADS["c1"]
+    o = orc.BlockOracle(dict(kind=2, style_dim=128, cin=128, cout=128, kernel=7, dil=[1, 3, 5]))
+    rng = np.random.default_rng(0)
+    p = rng.normal(0, 0.02, o.n_params).astype(np.float32)
+    x = rng.standard_normal((B, 128, L), dtype=np.float32)
+    s = rng.standard_normal((B, 128), dtype=np.float32)
+    dy = rng.standard_normal((B, 128, L), dtype=np.float32)
+    for _ in range(args.warmup):
+        o.run(p, x, s, dy=dy)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        o.run(p, x, s, dy=dy)
+    dt = (time.perf_counter() - t0) / max(args.steps, 1)
+    v = block_flops(B, 128, L, 7) / dt / 1e12
+    sample = f"the whole workload ({B} clips x L={L}) block fwd+bwd (all grads) per step, oracle/kokoro_oracle.cpp"
+    line = {
+        "impl": "reference", "metric": C1_METRIC, "value": v, "unit": "TFLOP/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
+        "config": {"workload": desc, "sample": sample},
+        "cpu_baseline": {"value": v, "unit": "TFLOP/s", "cores": orc.threads(), "kind": "port", "sample": sample},
+        "e2e": {"value": v, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
 def reference_arm(args):
     """The reference's own CPU path cannot be built here (all its arithmetic is in
     the absent brotensor library), so this arm times the oracle port of it on the
     host cores, as the CPU baseline."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
+        return
+    if args.workload == "c1":
+        reference_arm_block(args)
         return
     from brosoundml_b200 import config
 
@@ -203,9 +389,9 @@ def main():
     import torch.distributed as dist
     from datetime import timedelta
 
-    from brosoundml_b200 import config, dp, synth
+    from brosoundml_b200 import config
     from brosoundml_b200 import _lib
-    from brosoundml_b200.decoder import Decoder, adam_step, l1_loss
+    from brosoundml_b200.decoder import Decoder
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -217,31 +403,16 @@ def main():
             os.environ["NCCL_DEBUG"] = "WARN"
         dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=torch.device("cuda", local))
     math = args.math or Decoder.DEFAULT_MATH
-    cfg = config.kokoro_82m()
     B, T, desc = WORKLOADS[args.workload]
     dev = torch.device("cuda", local)
-    dec = Decoder(cfg, local, math=math)
-    params = torch.tensor(synth.init_params(dec.table, dec.n_params, 0), device=dev)
-    x = synth.make_inputs(cfg, B, T, 1 + rank)
-    tgt = synth.make_target(cfg, B, T, 1000 + rank)
-    host = {k: torch.from_numpy(v).pin_memory() for k, v in x.items()}
-    host["target"] = torch.from_numpy(tgt).pin_memory()
-    d = {k: v.to(dev) for k, v in host.items()}
-    grads = torch.empty(dec.n_params, device=dev)
-    m = torch.zeros(dec.n_params, device=dev)
-    v = torch.zeros(dec.n_params, device=dev)
-    audio = torch.empty((B, dec.audio_len(T)), device=dev)
-    lossbuf = torch.empty(1, device=dev)
-    dabuf = torch.empty_like(audio)
-    state = {"step": 0}
-
-    def train_step(inp):
-        dec.forward(params, inp["asr"], inp["F0"], inp["N"], inp["style"], audio=audio)
-        l1_loss(audio, inp["target"], lossbuf, dabuf)
-        dec.backward(dabuf, grads=grads)
-        dp.average_gradients(grads)   # one NCCL all-reduce of the flat gradient (N > 1)
-        state["step"] += 1
-        adam_step(params, grads, m, v, 1e-5, state["step"])
+    if args.workload == "c1":
+        w = setup_block(args, B, T, dev, rank, math)
+    elif args.workload == "c3lora":
+        w = setup_convlora(args, B, T, dev, rank, math)
+    else:
+        w = setup_decoder(args, B, T, dev, rank, math)
+    host, d, train_step, result = w["host"], w["dev"], w["step"], w["result"]
+    prof_src = w["prof"]
 
     def barrier():
         if world > 1:
@@ -273,7 +444,8 @@ def main():
     launches = (_lib.lib().bsml_launch_count() - n0) // max(args.steps, 1)
     ms = max_over_ranks(e0.elapsed_time(e1)) / args.steps
     clk = clocks.stop() if rank == 0 else None
-    value = world * audio_seconds(B, T) / (ms / 1e3)
+    per_step, unit = w["units_per_step"], w["unit"]
+    value = world * per_step / (ms / 1e3)
 
     # e2e: the public API with host buffers, H2D of the step's inputs and D2H of the loss every step
     e2e = None
@@ -286,18 +458,18 @@ def main():
         for _ in range(e2e_steps):
             inp = {k: t.to(dev, non_blocking=True) for k, t in host.items()}
             train_step(inp)
-            loss_host.copy_(lossbuf, non_blocking=True)
+            loss_host.copy_(result, non_blocking=True)
         e1.record(st)
         barrier()
         ms_e2e = max_over_ranks(e0.elapsed_time(e1)) / e2e_steps
-        e2e = {"value": world * audio_seconds(B, T) / (ms_e2e / 1e3), "unit": UNIT, "h2d_bytes_per_step": h2d,
+        e2e = {"value": world * per_step / (ms_e2e / 1e3), "unit": unit, "h2d_bytes_per_step": h2d,
                "d2h_bytes_per_step": 4, "ms_per_step": ms_e2e}
 
     # roofline: one profiled step (per-class CUDA events), after the timed region
-    dec.set_profiling(True)
+    prof_src.set_profiling(True)
     train_step(d)
-    prof = dec.read_profile()
-    dec.set_profiling(False)
+    prof = prof_src.read_profile()
+    prof_src.set_profiling(False)
     peaks = load_peaks()
     rl_all = {}
     for k, (pms, work, n) in prof.items():
@@ -337,17 +509,18 @@ def main():
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline and args.workload in ("c2", "c0"):
-        cpu = run_cpu_baseline(cfg, T)
+        cpu = run_cpu_baseline(config.kokoro_82m(), T)
+    elif rank == 0 and world == 1 and not args.no_cpu_baseline and args.workload == "c1":
+        cpu = run_cpu_baseline_block(B, T)
 
     if rank == 0:
         line = {
-            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "metric": w["metric"], "value": value, "unit": unit, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": math, "data": "synthetic",
-            "config": {"workload": desc, "global_batch": B * world, "seq_len": T, "parallelism": f"dp{world}",
-                       "audio_s_per_step": world * audio_seconds(B, T),
-                       "l2": "working set (~GBs of cached activations) >> 126 MB L2; no flush needed",
-                       "weights": "random init N(0,0.02), Snake alpha 1", "optimizer": "Adam lr 1e-5"},
+            "config": dict({"workload": desc, "global_batch": B * world, "seq_len": T, "parallelism": f"dp{world}",
+                            "l2": "working set (GBs of cached activations) >> 126 MB L2; no flush needed"},
+                           **w["config"]),
             "clocks": clk, "e2e": e2e, "gpu_launches": int(launches), "roofline": roofline,
             "roofline_by_class": rl_all, "cpu_baseline": cpu,
         }
