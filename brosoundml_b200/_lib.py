@@ -90,6 +90,7 @@ SIGNATURES = {
     "bsml_decoder_forward": ([_P, _I, _I, _P, _P, _P, _P, _P, _P, _I, _P, _P, _P, _P], _I),
     "bsml_decoder_backward": ([_P, _P, _P, _P, _P, _P, _P], _I),
     "bsml_decoder_workspace_bytes": ([_P], _L),
+    "bsml_selftest_bounded_wait": ([_P], _I),
     "bsml_block_create": ([_BS, _I, ctypes.POINTER(_P)], _I),
     "bsml_block_param_count": ([_BS, ctypes.POINTER(_L), ctypes.POINTER(_I), ctypes.POINTER(_I),
                                 ctypes.POINTER(_L)], _I),

@@ -284,6 +284,10 @@ int bsml_device_error(void) {
     return rc ? rc : v;
 }
 
+int bsml_selftest_bounded_wait(void* stream) {
+    return guarded([&] { bsml::tc_wait_selftest(S(stream)); });
+}
+
 int bsml_decoder_set_profiling(bsml_decoder* d, int on) {
     return guarded([&] {
         need(d != nullptr, "bsml_decoder_set_profiling", "null handle");

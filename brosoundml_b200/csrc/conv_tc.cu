@@ -890,6 +890,23 @@ void conv_wgrad_tc(const TcConvWgrad& c, int mode, float* part, int64_t part_cap
         launch_wgrad<false>(c, mode, part, part_cap, st);
 }
 
+// One thread waits, through the same bounded wait every tensor-core kernel uses,
+// on an mbarrier phase that nothing completes: after the limit it leaves
+// TC_ERR_WAIT_FULL in the error word and returns (nothing in flight).
+__global__ void wait_selftest_kernel() {
+    __shared__ __align__(8) uint64_t bar;
+    if (threadIdx.x != 0) return;
+    tc::mbar_init(&bar, 1);
+    tc::fence_barrier_init();
+    tc::mbar_wait(&bar, 0, &g_tc_err, tc::TC_ERR_WAIT_FULL);
+}
+
+void tc_wait_selftest(cudaStream_t st) {
+    count_launch();
+    wait_selftest_kernel<<<1, 32, 0, st>>>();
+    BSML_LAUNCH("wait_selftest_kernel");
+}
+
 int tc_error_flag() {
     int v = 0, zero = 0;
     BSML_CUDA(cudaDeviceSynchronize());

@@ -95,5 +95,7 @@ void conv_wgrad_tc(const TcConvWgrad& a, int mode, float* part, int64_t part_cap
 // Reads and clears the device error word the tensor-core kernels set when a
 // bounded wait gives up (0 = no error). Synchronises the device.
 int tc_error_flag();
+// a kernel whose bounded wait runs out (about 2 s): checks the error-word path
+void tc_wait_selftest(cudaStream_t st);
 
 }  // namespace bsml

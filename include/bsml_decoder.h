@@ -265,6 +265,10 @@ int bsml_set_atom_math(int math_mode);
 /* Reads and clears the error word a tensor-core kernel sets when one of its
  * bounded waits gives up (0 = none). Synchronises the device. */
 int bsml_device_error(void);
+/* Self-test of that mechanism (no reference counterpart): launches one kernel
+ * whose bounded wait, on a barrier nothing completes, gives up after about 2 s
+ * and leaves code 1 (wait for data) in the error word; the context stays usable. */
+int bsml_selftest_bounded_wait(void* stream);
 
 /* Conv1d forward (modules.cpp:103-108): x (B, Ci, L) -> y (B, Co, Lo). bias may be NULL. */
 int bsml_conv1d_forward(const float* x, int B, int Ci, int L, const float* W, const float* bias, int Co, int k,

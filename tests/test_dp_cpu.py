@@ -92,3 +92,39 @@ def test_two_rank_gradient_average_matches_full_batch():
     inp, tgt = _batch(cfg)
     g_full = _shard_grads(cfg, params, inp, tgt, slice(0, B_GLOBAL))
     np.testing.assert_allclose(g_dp, g_full, rtol=1e-10, atol=1e-14)
+
+
+def _rank_leaves(rank, world, port, q):
+    from datetime import timedelta
+    import time
+
+    torch.set_num_threads(1)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=5))
+    if rank == 1:
+        os._exit(0)   # leaves between steps: never joins the gradient all-reduce
+    t0 = time.time()
+    try:
+        dp.average_gradients(torch.ones(16, dtype=torch.float64))
+        q.put(("ok", time.time() - t0, ""))
+    except Exception as e:  # noqa: BLE001 - any error is the expected outcome
+        q.put(("error", time.time() - t0, f"{type(e).__name__}: {str(e)[:200]}"))
+    q.close()
+    q.join_thread()
+    os._exit(0)
+
+
+def test_rank_that_leaves_gives_an_error_not_a_hang():
+    """A rank that exits between steps: the surviving rank's gradient all-reduce ends
+    with an error (peer gone or process-group timeout), never a hang."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    ps = [ctx.Process(target=_rank_leaves, args=(r, 2, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    outcome, dt, msg = q.get(timeout=120)
+    for p in ps:
+        p.join(timeout=60)
+    assert outcome == "error", msg
+    assert dt < 60, dt
