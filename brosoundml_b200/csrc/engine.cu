@@ -485,11 +485,19 @@ void Engine::adain_fwd_to(const Act& x, const double* sums, const Stats& s, cons
 
 void Engine::adain_bwd_to(const Act& x, const Stats& s, const float* gb, int act, float slope, const float* alpha,
                           const Act& dy, const Opnd& out, const Act* skip, double* colsum, float* dgb, float* dalpha,
-                          cudaStream_t st) {
+                          cudaStream_t st, bool acc_ready) {
     PlaneOut po;
     po.hi = const_cast<void*>(out.tp.hi); po.lo = const_cast<void*>(out.tp.lo); po.ld = out.tp.ld; po.mode = tc_mode();
     adain_act_bwd_v(x, s.mean, s.rstd, gb, act, slope, alpha, dy, out.f.p ? &out.f : nullptr, skip,
-                    out.tp.hi ? &po : nullptr, colsum, dgb, dalpha, dacc_, st);
+                    out.tp.hi ? &po : nullptr, colsum, dgb, dalpha, dacc_, st, acc_ready);
+}
+
+void Engine::recompute_reduce_to(const Act& x, const Stats& s, const float* gb, int act, float slope,
+                                 const float* alpha, const Act& dy, const Opnd& out, cudaStream_t st) {
+    PlaneOut po;
+    po.hi = const_cast<void*>(out.tp.hi); po.lo = const_cast<void*>(out.tp.lo); po.ld = out.tp.ld; po.mode = tc_mode();
+    adain_recompute_reduce(x, s.mean, s.rstd, gb, act, slope, alpha, out.f.p ? &out.f : nullptr,
+                           out.tp.hi ? &po : nullptr, dy, dacc_, st);
 }
 
 void Engine::tc_launch(const Act& x, const TcPlanes& xp, const float* whi, const float* wlo, int taps, int M,
@@ -815,25 +823,29 @@ void Engine::rb1_bwd(const RB1P& w, RB1C& c, const Act& dOut, float scale, const
         zero_bs();
         scale_out_v(dOut, scale, &D, tc ? &po : nullptr, bs, st);
     }
+    // Algorithmic bytes per element of one AdaIN+Snake backward with its recompute:
+    // x and dy read once, the recomputed operand and the gradient written (the
+    // second read of x and dy by the apply pass is implementation traffic).
     for (int i = 2; i >= 0; --i) {
         conv_dgrad(w.c2[i], D, t, false, st, Dp.planes());
-        // s2[i] = Snake(AdaIN(c1[i])) again, as the weight-gradient operand
-        int id = prof_begin(PROF_NORM_BWD, (4.0 + pb) * n, st);
+        // s2[i] = Snake(AdaIN(c1[i])) again, as the weight-gradient operand, in the
+        // same pass as the backward's reduction over (c1[i], t)
+        int id = prof_begin(PROF_NORM_BWD, (8.0 + pb) * n, st);
         const Opnd s2 = operand(tc, L, C, S_[0], tc_xh_, tc_xl_);
-        adain_fwd_to(c.c1[i], nullptr, c.st2[i], aff(w.a2[i]), ACT_SNAKE, 0.f, P(w.al2[i]), s2, st);
+        recompute_reduce_to(c.c1[i], c.st2[i], aff(w.a2[i]), ACT_SNAKE, 0.f, P(w.al2[i]), t, s2, st);
         prof_end(id, st);
         conv_wgrad(w.c2[i], D, s2.f, st, Dp.planes(), s2.planes(), bs);
         // u = gradient at conv1's output (operand of c1's dgrad and wgrad)
-        id = prof_begin(PROF_NORM_BWD, (8.0 + pb) * n, st);
+        id = prof_begin(PROF_NORM_BWD, pb * n, st);
         const Opnd u = operand(tc, L, C, S_[5], tc_yh_, tc_yl_);
         zero_bs();
         adain_bwd_to(c.c1[i], c.st2[i], aff(w.a2[i]), ACT_SNAKE, 0.f, P(w.al2[i]), t, u, nullptr, bs, daff(w.a2[i]),
-                     G(w.al2[i]), st);
+                     G(w.al2[i]), st, true);
         prof_end(id, st);
         conv_dgrad(w.c1[i], u.f, t, false, st, u.planes());
-        id = prof_begin(PROF_NORM_BWD, (4.0 + pb) * n, st);
+        id = prof_begin(PROF_NORM_BWD, (8.0 + pb) * n, st);
         const Opnd s1 = operand(tc, L, C, S_[0], tc_xh_, tc_xl_);
-        adain_fwd_to(c.x[i], nullptr, c.st1[i], aff(w.a1[i]), ACT_SNAKE, 0.f, P(w.al1[i]), s1, st);
+        recompute_reduce_to(c.x[i], c.st1[i], aff(w.a1[i]), ACT_SNAKE, 0.f, P(w.al1[i]), t, s1, st);
         prof_end(id, st);
         conv_wgrad(w.c1[i], u.f, s1.f, st, u.planes(), s1.planes(), bs);
         // D += gradient at this pair's input: fp32, and (except for the last pair)
@@ -846,9 +858,9 @@ void Engine::rb1_bwd(const RB1P& w, RB1C& c, const Act& dOut, float scale, const
         } else {
             Dn.tp = TcPlanes{};
         }
-        id = prof_begin(PROF_NORM_BWD, (12.0 + 4.0 + (Dn.tp.hi ? pb : 0.0)) * n, st);
+        id = prof_begin(PROF_NORM_BWD, (4.0 + 4.0 + (Dn.tp.hi ? pb : 0.0)) * n, st);   // skip read, fp32 out, planes
         adain_bwd_to(c.x[i], c.st1[i], aff(w.a1[i]), ACT_SNAKE, 0.f, P(w.al1[i]), t, Dn, &D, bsn, daff(w.a1[i]),
-                     G(w.al1[i]), st);
+                     G(w.al1[i]), st, true);
         prof_end(id, st);
     }
 }

@@ -106,9 +106,13 @@ class Engine {
     Opnd operand(bool tc, int L, int C, const Act& fbuf, void* hi, void* lo) const;
     void adain_fwd_to(const Act& x, const double* sums, const Stats& s, const float* gb, int act, float slope,
                       const float* alpha, const Opnd& out, cudaStream_t st);
+    // acc_ready: the reduction pass already ran (recompute_reduce_to with the same x, dy)
     void adain_bwd_to(const Act& x, const Stats& s, const float* gb, int act, float slope, const float* alpha,
                       const Act& dy, const Opnd& out, const Act* skip, double* colsum, float* dgb, float* dalpha,
-                      cudaStream_t st);
+                      cudaStream_t st, bool acc_ready = false);
+    // out = act(AdaIN(x)) again, fused with the backward's reduction over (x, dy)
+    void recompute_reduce_to(const Act& x, const Stats& s, const float* gb, int act, float slope, const float* alpha,
+                             const Act& dy, const Opnd& out, cudaStream_t st);
 
     // Conv wrappers. xp / dyp: the operand's planes when a producer already
     // wrote them. stats: per-(b, co) sums of the output for the next norm

@@ -75,7 +75,14 @@ void adain_act_fwd_v(const Act& x, const double* sums, float eps, float* mean, f
 // (double, nullable, not zeroed here). dgb, dalpha as in adain_act_bwd.
 void adain_act_bwd_v(const Act& x, const float* mean, const float* rstd, const float* gb, int act, float slope,
                      const float* alpha, const Act& dy, const Act* dx, const Act* skip, const PlaneOut* planes,
-                     double* colsum, float* dgb, float* dalpha, double* acc, cudaStream_t st);
+                     double* colsum, float* dgb, float* dalpha, double* acc, cudaStream_t st,
+                     bool acc_ready = false);
+// The backward's reduction pass fused with recomputing the forward output act(AdaIN(x))
+// into y / planes (a weight gradient's operand): acc is zeroed and filled for a
+// following adain_act_bwd_v(..., acc_ready = true) with the same x, dy and affine.
+void adain_recompute_reduce(const Act& x, const float* mean, const float* rstd, const float* gb, int act,
+                            float slope, const float* alpha, const Act* y, const PlaneOut* planes, const Act& dy,
+                            double* acc, cudaStream_t st);
 // out = alpha * src -> dst (nullable), planes (nullable), colsum (nullable, added to)
 void scale_out_v(const Act& src, float alpha, const Act* dst, const PlaneOut* planes, double* colsum,
                  cudaStream_t st);

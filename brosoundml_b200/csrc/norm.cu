@@ -225,7 +225,7 @@ __device__ __forceinline__ float act_b(float z, float g, float slope, float al, 
 
 // acc[(b*C + c)*3 + {0,1,2}] += sum dz, sum dz * xhat, sum dy * d act / d alpha
 template <int ACT>
-__global__ void __launch_bounds__(NT) adain_bwd_reduce_kernel(Act x, int rows, const float* mean, const float* rstd,
+__global__ void __launch_bounds__(NT, 4) adain_bwd_reduce_kernel(Act x, int rows, const float* mean, const float* rstd,
                                                               const float* gb, float slope, const float* alpha, Act dy,
                                                               double* acc) {
     const int b = blockIdx.y;
@@ -276,9 +276,67 @@ __global__ void __launch_bounds__(NT) adain_bwd_reduce_kernel(Act x, int rows, c
     }
 }
 
+// The backward's first pass fused with the recomputation of the forward output:
+// o = act(z) (the weight gradient's operand, recomputed instead of cached) and
+// acc += sum dz, sum dz * xhat, sum dy * d act / d alpha, from one read of x and dy.
+template <int ACT>
+__global__ void __launch_bounds__(NT, 3) adain_recompute_reduce_kernel(Act x, int rows, const float* mean,
+                                                                       const float* rstd, const float* gb,
+                                                                       float slope, const float* alpha, Act dy,
+                                                                       double* acc, Out4 o) {
+    const int b = blockIdx.y;
+    const int l0 = blockIdx.x * rows, l1 = min(x.L, l0 + rows);
+    const int C = x.C, C4 = (C + 3) >> 2;
+    for (int v0 = 0; v0 < C4; v0 += blockDim.x) {
+        const int v = v0 + threadIdx.x;
+        double s[3][4] = {};
+        if (v < C4) {
+            const int c0 = 4 * v, nv = min(4, C - c0);
+            Chan k;
+            load_chan<ACT>(k, b, c0, C, x.L, nullptr, 0.f, nullptr, nullptr, mean, rstd, gb, alpha, false);
+            float f[3][4] = {};
+            const float* xb = x.p + (int64_t)b * x.bstride + c0;
+            const float* gbp = dy.p + (int64_t)b * dy.bstride + c0;
+            auto row = [&](const float4& a, const float4& g, int l) {
+                float r[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const float xh = (get(a, j) - k.m[j]) * k.rs[j];
+                    const float z = fmaf(k.g1[j], xh, k.be[j]);
+                    float dal = 0.f;
+                    r[j] = act_f<ACT>(z, slope, k.al[j], k.ial[j]);
+                    const float dz = act_b<ACT>(z, get(g, j), slope, k.al[j], k.ial[j], dal);
+                    f[0][j] += dz;
+                    f[1][j] = fmaf(dz, xh, f[1][j]);
+                    if (ACT == ACT_SNAKE) f[2][j] += dal;
+                }
+                put(o, b, l, c0, make_float4(r[0], r[1], r[2], r[3]), nv);
+            };
+            const int dl = blockDim.y;
+            int l = l0 + threadIdx.y;
+            for (; l + (UNR - 1) * dl < l1; l += UNR * dl) {
+                float4 a[UNR], g[UNR];
+#pragma unroll
+                for (int u = 0; u < UNR; ++u) {
+                    a[u] = ldg4(xb + (int64_t)(l + u * dl) * x.ld);
+                    g[u] = ldg4(gbp + (int64_t)(l + u * dl) * dy.ld);
+                }
+#pragma unroll
+                for (int u = 0; u < UNR; ++u) row(a[u], g[u], l + u * dl);
+            }
+            for (; l < l1; l += dl) row(ldg4(xb + (int64_t)l * x.ld), ldg4(gbp + (int64_t)l * dy.ld), l);
+#pragma unroll
+            for (int q = 0; q < 3; ++q)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) s[q][j] = f[q][j];
+        }
+        combine_rows<3>(s, v, C4, C, acc + (int64_t)b * C * 3);
+    }
+}
+
 // out = rstd * g1 * (dz - mean(dz) - xhat * mean(dz * xhat)) (+ skip); colsum[c] += sum out
 template <int ACT>
-__global__ void __launch_bounds__(NT) adain_bwd_apply_kernel(Act x, int rows, const float* mean, const float* rstd,
+__global__ void __launch_bounds__(NT, 3) adain_bwd_apply_kernel(Act x, int rows, const float* mean, const float* rstd,
                                                              const float* gb, float slope, const float* alpha, Act dy,
                                                              const double* acc, Out4 o, double* colsum) {
     const int b = blockIdx.y;
@@ -479,24 +537,51 @@ void adain_act_fwd(const Act& x, const float* mean, const float* rstd, const flo
                     nullptr, st);
 }
 
+void adain_recompute_reduce(const Act& x, const float* mean, const float* rstd, const float* gb, int act,
+                            float slope, const float* alpha, const Act* y, const PlaneOut* planes, const Act& dy,
+                            double* acc, cudaStream_t st) {
+    BSML_CUDA(cudaMemsetAsync(acc, 0, sizeof(double) * 3 * (size_t)x.B * x.C, st));
+    if (x.numel() == 0) return;
+    need_vec(x, "adain_recompute_reduce");
+    need_vec(dy, "adain_recompute_reduce");
+    const Out4 o = make_out(y, planes, nullptr, x, "adain_recompute_reduce");
+    const Geo g = geo(x);
+    ::bsml::count_launch();
+    if (act == ACT_SNAKE)
+        adain_recompute_reduce_kernel<ACT_SNAKE><<<g.grid, g.block, 0, st>>>(x, g.rows, mean, rstd, gb, slope, alpha,
+                                                                             dy, acc, o);
+    else if (act == ACT_LEAKY)
+        adain_recompute_reduce_kernel<ACT_LEAKY><<<g.grid, g.block, 0, st>>>(x, g.rows, mean, rstd, gb, slope, alpha,
+                                                                             dy, acc, o);
+    else
+        adain_recompute_reduce_kernel<ACT_NONE><<<g.grid, g.block, 0, st>>>(x, g.rows, mean, rstd, gb, slope, alpha,
+                                                                            dy, acc, o);
+    BSML_LAUNCH("adain_recompute_reduce");
+}
+
 void adain_act_bwd_v(const Act& x, const float* mean, const float* rstd, const float* gb, int act, float slope,
                      const float* alpha, const Act& dy, const Act* dx, const Act* skip, const PlaneOut* planes,
-                     double* colsum, float* dgb, float* dalpha, double* acc, cudaStream_t st) {
+                     double* colsum, float* dgb, float* dalpha, double* acc, cudaStream_t st, bool acc_ready) {
     const int64_t n = (int64_t)x.B * x.C;
-    BSML_CUDA(cudaMemsetAsync(acc, 0, sizeof(double) * 3 * n, st));
+    if (!acc_ready) BSML_CUDA(cudaMemsetAsync(acc, 0, sizeof(double) * 3 * n, st));
     if (x.numel() > 0) {
         need_vec(x, "adain_act_bwd");
         need_vec(dy, "adain_act_bwd");
         const Out4 o = make_out(dx, planes, skip, x, "adain_act_bwd");
         const Geo g = geo(x);
-        ::bsml::count_launch();
-        if (act == ACT_SNAKE)
-            adain_bwd_reduce_kernel<ACT_SNAKE><<<g.grid, g.block, 0, st>>>(x, g.rows, mean, rstd, gb, slope, alpha, dy, acc);
-        else if (act == ACT_LEAKY)
-            adain_bwd_reduce_kernel<ACT_LEAKY><<<g.grid, g.block, 0, st>>>(x, g.rows, mean, rstd, gb, slope, alpha, dy, acc);
-        else
-            adain_bwd_reduce_kernel<ACT_NONE><<<g.grid, g.block, 0, st>>>(x, g.rows, mean, rstd, gb, slope, alpha, dy, acc);
-        BSML_LAUNCH("adain_bwd_reduce");
+        if (!acc_ready) {
+            ::bsml::count_launch();
+            if (act == ACT_SNAKE)
+                adain_bwd_reduce_kernel<ACT_SNAKE><<<g.grid, g.block, 0, st>>>(x, g.rows, mean, rstd, gb, slope, alpha,
+                                                                               dy, acc);
+            else if (act == ACT_LEAKY)
+                adain_bwd_reduce_kernel<ACT_LEAKY><<<g.grid, g.block, 0, st>>>(x, g.rows, mean, rstd, gb, slope, alpha,
+                                                                               dy, acc);
+            else
+                adain_bwd_reduce_kernel<ACT_NONE><<<g.grid, g.block, 0, st>>>(x, g.rows, mean, rstd, gb, slope, alpha,
+                                                                              dy, acc);
+            BSML_LAUNCH("adain_bwd_reduce");
+        }
         ::bsml::count_launch();
         if (act == ACT_SNAKE)
             adain_bwd_apply_kernel<ACT_SNAKE><<<g.grid, g.block, 0, st>>>(x, g.rows, mean, rstd, gb, slope, alpha, dy, acc, o, colsum);
@@ -515,7 +600,8 @@ void adain_act_bwd_v(const Act& x, const float* mean, const float* rstd, const f
 void adain_act_bwd(const Act& x, const float* mean, const float* rstd, const float* gb, int act, float slope,
                    const float* alpha, const Act& dy, const Act& dx, const Act* skip, float* dgb, float* dalpha,
                    double* acc, cudaStream_t st) {
-    adain_act_bwd_v(x, mean, rstd, gb, act, slope, alpha, dy, &dx, skip, nullptr, nullptr, dgb, dalpha, acc, st);
+    adain_act_bwd_v(x, mean, rstd, gb, act, slope, alpha, dy, &dx, skip, nullptr, nullptr, dgb, dalpha, acc, st,
+                    false);
 }
 
 void scale_out_v(const Act& src, float alpha, const Act* dst, const PlaneOut* planes, double* colsum,
