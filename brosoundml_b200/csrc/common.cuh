@@ -55,4 +55,22 @@ struct Act {
 // (a TMA requirement for the tensor-core path).
 inline int pitch(int C) { return (int)round_up(C, 4); }
 
+#ifdef __CUDACC__
+// sum_{q < n} p[q * stride] in double, in order q = 0, 1, ..., with eight loads in
+// flight per thread (split-K partials are latency-bound when read one by one)
+__device__ __forceinline__ double sum_strided(const float* p, int64_t stride, int n) {
+    double s = 0.0;
+    int q = 0;
+    for (; q + 8 <= n; q += 8) {
+        float v[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) v[u] = __ldg(p + (int64_t)(q + u) * stride);
+#pragma unroll
+        for (int u = 0; u < 8; ++u) s += v[u];
+    }
+    for (; q < n; ++q) s += __ldg(p + (int64_t)q * stride);
+    return s;
+}
+#endif
+
 }  // namespace bsml

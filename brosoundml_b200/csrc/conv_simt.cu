@@ -173,8 +173,7 @@ __global__ void __launch_bounds__(256) conv_wgrad_kernel(WgK a) {
 
 __global__ void reduce_splits_kernel(const float* part, int splits, int64_t n, float* out, int accum) {
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
-        double s = 0;
-        for (int q = 0; q < splits; ++q) s += part[(int64_t)q * n + i];
+        const double s = sum_strided(part + i, n, splits);
         out[i] = (float)(accum ? out[i] + s : s);
     }
 }

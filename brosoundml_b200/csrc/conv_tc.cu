@@ -590,37 +590,63 @@ __global__ void act_planes_kernel(Act x, void* hi, void* lo, int ld) {
     }
 }
 
+// Element i of one packed weight: [tap][M][Kp] with zero padding of K to Kp.
+template <bool TF32>
+__device__ __forceinline__ void pack_one(const float* W, int kind, int Co, int Ci, int k, int s, int r, int taps,
+                                         int M, int K, int Kp, void* hi, void* lo, int64_t i) {
+    const int kk = (int)(i % Kp);
+    const int64_t q = i / Kp;
+    const int m = (int)(q % M), t = (int)(q / M);
+    float v = 0.f;
+    if (kk < K) {
+        if (kind == PACK_CONV_FWD) {            // m = co, kk = ci
+            v = W[((int64_t)m * Ci + kk) * k + t];
+        } else if (kind == PACK_CONV_DGRAD) {   // m = ci, kk = co
+            v = W[((int64_t)kk * Ci + m) * k + (k - 1 - t)];
+        } else if (kind == PACK_CONVT_PHASE) {  // convT phase: m = co, kk = ci
+            const int tt = r + (taps - 1 - t) * s;
+            v = W[((int64_t)kk * Co + m) * k + tt];
+        } else {                                // convT dgrad, row-packed: m = ci, kk = j*Co + co
+            const int u_min = -((r + s - 1) / s);
+            const int j = kk / Co, co = kk - j * Co;
+            const int tt = (t + u_min) * s + j + r;
+            if (tt >= 0 && tt < k) v = W[((int64_t)m * Co + co) * k + tt];
+        }
+    }
+    if (TF32) {
+        const float h = tf32_rna(v);
+        static_cast<float*>(hi)[i] = h;
+        static_cast<float*>(lo)[i] = v - h;
+    } else {
+        static_cast<__nv_bfloat16*>(hi)[i] = __float2bfloat16_rn(v);
+    }
+}
+
 template <bool TF32>
 __global__ void pack_w_kernel(const float* W, int kind, int Co, int Ci, int k, int s, int r, int taps, int M, int K,
                               int Kp, void* hi, void* lo) {
     const int64_t n = (int64_t)taps * M * Kp;
-    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
-        const int kk = (int)(i % Kp);
-        const int64_t q = i / Kp;
-        const int m = (int)(q % M), t = (int)(q / M);
-        float v = 0.f;
-        if (kk < K) {
-            if (kind == PACK_CONV_FWD) {            // m = co, kk = ci
-                v = W[((int64_t)m * Ci + kk) * k + t];
-            } else if (kind == PACK_CONV_DGRAD) {   // m = ci, kk = co
-                v = W[((int64_t)kk * Ci + m) * k + (k - 1 - t)];
-            } else if (kind == PACK_CONVT_PHASE) {  // convT phase: m = co, kk = ci
-                const int tt = r + (taps - 1 - t) * s;
-                v = W[((int64_t)kk * Co + m) * k + tt];
-            } else {                                // convT dgrad, row-packed: m = ci, kk = j*Co + co
-                const int u_min = -((r + s - 1) / s);
-                const int j = kk / Co, co = kk - j * Co;
-                const int tt = (t + u_min) * s + j + r;
-                if (tt >= 0 && tt < k) v = W[((int64_t)m * Co + co) * k + tt];
-            }
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        pack_one<TF32>(W, kind, Co, Ci, k, s, r, taps, M, K, Kp, hi, lo, i);
+}
+
+// All jobs of a batch over one flat index space; each thread finds its job by
+// binary search over the jobs' starts (held in shared memory).
+template <bool TF32>
+__global__ void pack_w_batch_kernel(const float* params, const PackJob* jobs, int n_jobs, int64_t total) {
+    __shared__ int64_t start[PACK_MAX_JOBS];
+    for (int j = threadIdx.x; j < n_jobs; j += blockDim.x) start[j] = jobs[j].start;
+    __syncthreads();
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        int lo = 0, hi = n_jobs - 1;
+        while (lo < hi) {   // last job whose start <= i
+            const int mid = (lo + hi + 1) >> 1;
+            if (start[mid] <= i) lo = mid;
+            else hi = mid - 1;
         }
-        if (TF32) {
-            const float h = tf32_rna(v);
-            static_cast<float*>(hi)[i] = h;
-            static_cast<float*>(lo)[i] = v - h;
-        } else {
-            static_cast<__nv_bfloat16*>(hi)[i] = __float2bfloat16_rn(v);
-        }
+        const PackJob& J = jobs[lo];
+        pack_one<TF32>(params + J.w_off, J.kind, J.Co, J.Ci, J.k, J.s, J.r, J.taps, J.M, J.K, J.Kp, J.hi, J.lo,
+                       i - start[lo]);
     }
 }
 
@@ -628,8 +654,7 @@ __global__ void pack_w_kernel(const float* W, int kind, int Co, int Ci, int k, i
 __global__ void wgrad_reduce_kernel(const float* part, int splits, int taps, int Co, int Ci, float* dW, int accum) {
     const int64_t n = (int64_t)Co * Ci * taps;
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
-        double s = 0;
-        for (int sp = 0; sp < splits; ++sp) s += part[sp * n + i];
+        const double s = sum_strided(part + i, n, splits);
         dW[i] = (float)(accum ? dW[i] + s : s);
     }
 }
@@ -648,8 +673,7 @@ __global__ void wgrad_reduce_convT_kernel(const float* part, int splits, int tap
         const int u = tp >= 0 ? tp / s : -((-tp + s - 1) / s);
         const int j = tp - u * s, tau = u - u_min;
         const int64_t src = ((int64_t)m * N + (int64_t)j * CoT + co) * taps + tau;
-        double acc = 0;
-        for (int sp = 0; sp < splits; ++sp) acc += part[sp * stride_split + src];
+        const double acc = sum_strided(part + src, stride_split, splits);
         dW[i] = (float)(accum ? dW[i] + acc : acc);
     }
 }
@@ -853,6 +877,32 @@ void make_act_planes(const Act& x, int mode, void* hi, void* lo, cudaStream_t st
     else
         act_planes_kernel<false><<<grid_for(x.numel()), 256, 0, st>>>(x, hi, lo, ld);
     BSML_LAUNCH("make_act_planes");
+}
+
+PackJob make_pack_job(int64_t w_off, int kind, int Co, int Ci, int k, int s, int r, void* hi, void* lo) {
+    PackJob J;
+    J.w_off = w_off; J.kind = kind; J.Co = Co; J.Ci = Ci; J.k = k; J.s = s; J.r = r; J.hi = hi; J.lo = lo;
+    J.taps = k; J.M = Co; J.K = Ci;
+    if (kind == PACK_CONV_DGRAD) { J.M = Ci; J.K = Co; }
+    if (kind == PACK_CONVT_PHASE) J.taps = (k - r + s - 1) / s;
+    if (kind == PACK_CONVT_DGRAD) {
+        if (r < 0) fail("pack_w_tc", "negative ConvTranspose1d padding");
+        J.M = Ci; J.K = s * Co; J.taps = convT_pack(k, s, r).taps;
+    }
+    J.Kp = (int)round_up(J.K, 8);
+    J.n = (int64_t)J.taps * J.M * J.Kp;
+    return J;
+}
+
+void pack_w_tc_batch(const float* params, const PackJob* jobs, int n_jobs, int64_t total, int mode, cudaStream_t st) {
+    if (n_jobs <= 0 || total <= 0) return;
+    if (n_jobs > PACK_MAX_JOBS) fail("pack_w_tc_batch", "too many jobs in one batch");
+    ::bsml::count_launch();
+    if (mode == TC_TF32X3)
+        pack_w_batch_kernel<true><<<grid_for(total), 256, 0, st>>>(params, jobs, n_jobs, total);
+    else
+        pack_w_batch_kernel<false><<<grid_for(total), 256, 0, st>>>(params, jobs, n_jobs, total);
+    BSML_LAUNCH("pack_w_tc_batch");
 }
 
 void pack_w_tc(const float* W, int kind, int Co, int Ci, int k, int s, int r, int mode, void* hi, void* lo,

@@ -145,6 +145,7 @@ Engine::~Engine() {
     cudaFree(ws_);
     cudaFree(fc_tab_);
     cudaFree(fc_row_entry_);
+    cudaFree(pack_jobs_);
 }
 
 void Engine::set_math(int m) {
@@ -422,39 +423,66 @@ void Engine::ensure_plan(int B, int T, int frames, bool have_har) {
     planned_ = true;
 }
 
-// ── weight packing (every step: the parameters may have changed)
-void Engine::pack_weights(cudaStream_t st) {
-    for (auto* c : lay_.convs) {
-        if (tc_ok(c->cin, c->cout, c->s))
-            pack_w_tc(params_ + c->w, PACK_CONV_FWD, c->cout, c->cin, c->k, 1, 0, tc_mode(), tcw_fwd_hi_[c->id],
-                      tcw_fwd_lo_[c->id], st);
-        else
-            pack_conv_fwd(params_ + c->w, c->cout, c->cin, c->k, wp_fwd_[c->id], st);
-    }
-    for (auto& u : lay_.ups)
-        for (int r = 0; r < u.s; ++r) {
-            if (tc_ok(u.cin, u.cout, 1))
-                pack_w_tc(params_ + u.w, PACK_CONVT_PHASE, u.cout, u.cin, u.k, u.s, r, tc_mode(), tcw_up_hi_[u.id][r],
-                          tcw_up_lo_[u.id][r], st);
-            else
-                pack_convT_phase(params_ + u.w, u.cin, u.cout, u.k, u.s, r, wp_up_[u.id][r], st);
+// ── weight packing (every step: the parameters may have changed). The tensor-core
+// packings of one direction run as one batched launch; the job tables depend only
+// on the math mode and are built on first use.
+void Engine::build_pack_jobs() {
+    std::vector<PackJob> fw, dg;
+    auto add = [](std::vector<PackJob>& v, const PackJob& J) {
+        PackJob j = J;
+        j.start = v.empty() ? 0 : v.back().start + v.back().n;
+        v.push_back(j);
+    };
+    if (math_ != BSML_MATH_FP32_SIMT) {
+        for (auto* c : lay_.convs) {
+            if (tc_ok(c->cin, c->cout, c->s))
+                add(fw, make_pack_job(c->w, PACK_CONV_FWD, c->cout, c->cin, c->k, 1, 0, tcw_fwd_hi_[c->id],
+                                      tcw_fwd_lo_[c->id]));
+            if (c->s == 1 && tc_ok(c->cout, c->cin, 1))
+                add(dg, make_pack_job(c->w, PACK_CONV_DGRAD, c->cout, c->cin, c->k, 1, 0, tcw_dg_hi_[c->id],
+                                      tcw_dg_lo_[c->id]));
         }
+        for (auto& u : lay_.ups) {
+            if (tc_ok(u.cin, u.cout, 1))
+                for (int r = 0; r < u.s; ++r)
+                    add(fw, make_pack_job(u.w, PACK_CONVT_PHASE, u.cout, u.cin, u.k, u.s, r, tcw_up_hi_[u.id][r],
+                                          tcw_up_lo_[u.id][r]));
+            if (convT_tc(u))
+                add(dg, make_pack_job(u.w, PACK_CONVT_DGRAD, u.cout, u.cin, u.k, u.s, u.p, tcw_updg_hi_[u.id],
+                                      tcw_updg_lo_[u.id]));
+        }
+    }
+    if (fw.size() > (size_t)PACK_MAX_JOBS || dg.size() > (size_t)PACK_MAX_JOBS)
+        fail("bsml_decoder", "too many tensor-core weight packings for one batch");
+    if (!pack_jobs_) BSML_CUDA(cudaMalloc(&pack_jobs_, sizeof(PackJob) * 2 * PACK_MAX_JOBS));
+    if (!fw.empty()) BSML_CUDA(cudaMemcpy(pack_jobs_, fw.data(), sizeof(PackJob) * fw.size(), cudaMemcpyHostToDevice));
+    if (!dg.empty())
+        BSML_CUDA(cudaMemcpy(pack_jobs_ + PACK_MAX_JOBS, dg.data(), sizeof(PackJob) * dg.size(),
+                             cudaMemcpyHostToDevice));
+    n_pack_fw_ = (int)fw.size();
+    n_pack_dg_ = (int)dg.size();
+    tot_pack_fw_ = fw.empty() ? 0 : fw.back().start + fw.back().n;
+    tot_pack_dg_ = dg.empty() ? 0 : dg.back().start + dg.back().n;
+    pack_jobs_math_ = math_;
+}
+
+void Engine::pack_weights(cudaStream_t st) {
+    if (pack_jobs_math_ != math_) build_pack_jobs();
+    pack_w_tc_batch(params_, pack_jobs_, n_pack_fw_, tot_pack_fw_, tc_mode(), st);
+    for (auto* c : lay_.convs)
+        if (!tc_ok(c->cin, c->cout, c->s)) pack_conv_fwd(params_ + c->w, c->cout, c->cin, c->k, wp_fwd_[c->id], st);
+    for (auto& u : lay_.ups)
+        if (!tc_ok(u.cin, u.cout, 1))
+            for (int r = 0; r < u.s; ++r) pack_convT_phase(params_ + u.w, u.cin, u.cout, u.k, u.s, r, wp_up_[u.id][r], st);
 }
 void Engine::pack_dgrad_weights(cudaStream_t st) {
-    for (auto* c : lay_.convs) {
-        if (c->s != 1) continue;
-        if (tc_ok(c->cout, c->cin, 1))
-            pack_w_tc(params_ + c->w, PACK_CONV_DGRAD, c->cout, c->cin, c->k, 1, 0, tc_mode(), tcw_dg_hi_[c->id],
-                      tcw_dg_lo_[c->id], st);
-        else
+    if (pack_jobs_math_ != math_) build_pack_jobs();
+    pack_w_tc_batch(params_, pack_jobs_ + PACK_MAX_JOBS, n_pack_dg_, tot_pack_dg_, tc_mode(), st);
+    for (auto* c : lay_.convs)
+        if (c->s == 1 && !tc_ok(c->cout, c->cin, 1))
             pack_conv_dgrad(params_ + c->w, c->cout, c->cin, c->k, wp_dgrad_[c->id], st);
-    }
-    for (auto& u : lay_.ups) {
-        pack_convT_dgrad(params_ + u.w, u.cin, u.cout, u.k, wp_up_dgrad_[u.id], st);
-        if (convT_tc(u))
-            pack_w_tc(params_ + u.w, PACK_CONVT_DGRAD, u.cout, u.cin, u.k, u.s, u.p, tc_mode(), tcw_updg_hi_[u.id],
-                      tcw_updg_lo_[u.id], st);
-    }
+    // the CUDA-core convT input gradient is the fallback when L_u % s != 0
+    for (auto& u : lay_.ups) pack_convT_dgrad(params_ + u.w, u.cin, u.cout, u.k, wp_up_dgrad_[u.id], st);
 }
 
 TcPlanes Engine::tc_planes(const Act& x, cudaStream_t st) {
@@ -704,16 +732,32 @@ void Engine::stats_of(const Act& x, const Stats& s, cudaStream_t st) { in_stats(
 
 // ── AdainResBlk1d (kokoro_decoder_backward.cpp:152-285)
 void Engine::blk_fwd(const BlkP& w, BlkC& c, const Act& y, cudaStream_t st) {
+    // The leaky AdaIN outputs are cached in fp32 (the weight gradients read them)
+    // and, where the next conv runs on the tensor cores, also written as its
+    // operand planes in the same pass; conv1's epilogue returns norm2's statistics.
+    auto planes_in = [&](void* hi, void* lo, int C, TcPlanes& tp, PlaneOut& po) {
+        tp.hi = hi; tp.lo = lo; tp.ld = tc_pitch(C, tc_mode());
+        po.hi = hi; po.lo = lo; po.ld = tp.ld; po.mode = tc_mode();
+    };
     stats_of(c.x, c.s1, st);
-    adain_act_fwd(c.x, c.s1.mean, c.s1.rstd, aff(w.n1), ACT_LEAKY, 0.2f, nullptr, c.r, st);
+    const bool tc1 = !w.up && tc_ok(w.cin, w.cout, 1);
+    TcPlanes rp;
+    PlaneOut ro;
+    if (tc1) planes_in(tc_xh_, tc_xl_, w.cin, rp, ro);
+    adain_act_fwd_v(c.x, nullptr, 1e-5f, c.s1.mean, c.s1.rstd, aff(w.n1), ACT_LEAKY, 0.2f, nullptr, &c.r,
+                    tc1 ? &ro : nullptr, st);
     Act pooled = c.r;
     if (w.up) {
         dwconvT_fwd(c.r, P(w.pool_w), P(w.pool_b), 3, 2, 1, c.pooled, st);
         pooled = c.pooled;
     }
-    conv(w.c1, pooled, c.c1, nullptr, 0, 1.f, false, st);
-    stats_of(c.c1, c.s2, st);
-    adain_act_fwd(c.c1, c.s2.mean, c.s2.rstd, aff(w.n2), ACT_LEAKY, 0.2f, nullptr, c.n2, st);
+    conv(w.c1, pooled, c.c1, nullptr, 0, 1.f, false, st, tc1 ? &rp : nullptr, ssum_);
+    const bool tc2 = tc_ok(w.cout, w.cout, 1);
+    TcPlanes np;
+    PlaneOut no;
+    if (tc2) planes_in(tc_yh_, tc_yl_, w.cout, np, no);
+    adain_act_fwd_v(c.c1, ssum_, 1e-5f, c.s2.mean, c.s2.rstd, aff(w.n2), ACT_LEAKY, 0.2f, nullptr, &c.n2,
+                    tc2 ? &no : nullptr, st);
     // shortcut: a 1x1 conv commutes with nearest-2x, so it runs at L_in and the
     // conv2 epilogue reads it at row >> 1
     const Act* sc = &c.x;
@@ -721,24 +765,43 @@ void Engine::blk_fwd(const BlkP& w, BlkC& c, const Act& y, cudaStream_t st) {
         conv(w.c1x1, c.x, c.sc, nullptr, 0, 1.f, false, st);
         sc = &c.sc;
     }
-    conv(w.c2, c.n2, y, sc, w.up ? 1 : 0, 1.f / std::sqrt(2.f), false, st);
+    conv(w.c2, c.n2, y, sc, w.up ? 1 : 0, 1.f / std::sqrt(2.f), false, st, tc2 ? &np : nullptr);
 }
 
 void Engine::blk_bwd(const BlkP& w, BlkC& c, const Act& dY, const Act& dX, cudaStream_t st) {
     const int Lin = c.Lin, Lout = c.Lout;
-    // d_branch = dY / sqrt(2)  (S_[0])
+    double* bs = grads_ ? bsum_ : nullptr;
+    auto zero_bs = [&](int C) {
+        if (bs) BSML_CUDA(cudaMemsetAsync(bs, 0, sizeof(double) * C, st));
+    };
+    auto planes_in = [&](void* hi, void* lo, int C, TcPlanes& tp, PlaneOut& po) {
+        tp.hi = hi; tp.lo = lo; tp.ld = tc_pitch(C, tc_mode());
+        po.hi = hi; po.lo = lo; po.ld = tp.ld; po.mode = tc_mode();
+    };
+    // d_branch = dY / sqrt(2) (S_[0]), in the same pass its operand planes (tc_dh_)
+    // for conv2's input and weight gradients and its column sums (conv2's bias gradient)
+    const bool tc2 = tc_ok(w.cout, w.cout, 1);
     Act db = view(S_[0], Lout, w.cout);
-    copy_act(dY, db, st);
-    scale_act(db, 1.f / std::sqrt(2.f), st);
+    TcPlanes dbp;
+    PlaneOut dbo;
+    if (tc2) planes_in(tc_dh_, tc_dl_, w.cout, dbp, dbo);
+    zero_bs(w.cout);
+    scale_out_v(dY, 1.f / std::sqrt(2.f), &db, tc2 ? &dbo : nullptr, bs, st);
     Act t1 = view(S_[1], Lout, w.cout);
-    conv_dgrad(w.c2, db, t1, false, st);
-    conv_wgrad(w.c2, db, c.n2, st);
+    conv_dgrad(w.c2, db, t1, false, st, tc2 ? &dbp : nullptr);
+    conv_wgrad(w.c2, db, c.n2, st, tc2 ? &dbp : nullptr, nullptr, bs);
+    // dc1 (S_[2]) with its planes (tc_yh_) and column sums (conv1's bias gradient)
+    const bool tc1 = tc_ok(w.cin, w.cout, 1) && tc_ok(w.cout, w.cin, 1);
     Act dc1 = view(S_[2], Lout, w.cout);
-    adain_act_bwd(c.c1, c.s2.mean, c.s2.rstd, aff(w.n2), ACT_LEAKY, 0.2f, nullptr, t1, dc1, nullptr, daff(w.n2),
-                  nullptr, dacc_, st);
+    TcPlanes dcp;
+    PlaneOut dco;
+    if (tc1) planes_in(tc_yh_, tc_yl_, w.cout, dcp, dco);
+    zero_bs(w.cout);
+    adain_act_bwd_v(c.c1, c.s2.mean, c.s2.rstd, aff(w.n2), ACT_LEAKY, 0.2f, nullptr, t1, &dc1, nullptr,
+                    tc1 ? &dco : nullptr, bs, daff(w.n2), nullptr, dacc_, st);
     Act dpooled = view(S_[1], Lout, w.cin);
-    conv_dgrad(w.c1, dc1, dpooled, false, st);
-    conv_wgrad(w.c1, dc1, w.up ? c.pooled : c.r, st);
+    conv_dgrad(w.c1, dc1, dpooled, false, st, tc1 ? &dcp : nullptr);
+    conv_wgrad(w.c1, dc1, w.up ? c.pooled : c.r, st, tc1 ? &dcp : nullptr, nullptr, bs);
     Act dr = dpooled;
     if (w.up) {
         dr = view(S_[2], Lin, w.cin);
@@ -747,15 +810,22 @@ void Engine::blk_bwd(const BlkP& w, BlkC& c, const Act& dY, const Act& dX, cudaS
     }
     adain_act_bwd(c.x, c.s1.mean, c.s1.rstd, aff(w.n1), ACT_LEAKY, 0.2f, nullptr, dr, dX, nullptr, daff(w.n1),
                   nullptr, dacc_, st);
-    // shortcut branch
+    // shortcut branch: without upsampling dbs = db and its planes are still in tc_dh_
     Act dbs = db;
+    const bool tcs = w.sc && tc_ok(w.cin, w.cout, 1) && tc_ok(w.cout, w.cin, 1);
+    TcPlanes sp = dbp;
     if (w.up) {
         dbs = view(S_[3], Lin, w.cout);
         pair_sum_rows(db, dbs, st);
+        if (tcs) {
+            make_act_planes(dbs, tc_mode(), tc_dh_, tc_dl_, st);
+            sp.hi = tc_dh_; sp.lo = tc_dl_; sp.ld = tc_pitch(w.cout, tc_mode());
+        }
     }
+    const bool have_sp = tcs && (w.up || tc2);
     if (w.sc) {
-        conv_dgrad(w.c1x1, dbs, dX, true, st);
-        conv_wgrad(w.c1x1, dbs, c.x, st);
+        conv_dgrad(w.c1x1, dbs, dX, true, st, have_sp ? &sp : nullptr);
+        conv_wgrad(w.c1x1, dbs, c.x, st, have_sp ? &sp : nullptr);
     } else {
         add_act(dbs, dX, 1.f, st);
     }

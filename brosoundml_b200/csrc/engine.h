@@ -87,6 +87,7 @@ class Engine {
     RB1C plan_rb1(Planner& P, int L, int C);
 
     // ── execution helpers
+    void build_pack_jobs();
     void pack_weights(cudaStream_t st);
     void pack_dgrad_weights(cudaStream_t st);
     const float* aff(const AdaP& a) const { return aff_ + (int64_t)B_ * lay_.aff_base[a.idx]; }
@@ -182,6 +183,9 @@ class Engine {
     void tc_launch(const Act& x, const TcPlanes& xp, const float* whi, const float* wlo, int taps, int M,
                    const Act& y, const float* bias, const Act* r, int r_shift, int p, int d, int No, int o_base,
                    int orow_mul, int orow_off, float alpha, bool accum, double* stats, cudaStream_t st);
+    PackJob* pack_jobs_ = nullptr;                // device: forward jobs, then dgrad jobs at PACK_MAX_JOBS
+    int n_pack_fw_ = 0, n_pack_dg_ = 0, pack_jobs_math_ = -1;
+    int64_t tot_pack_fw_ = 0, tot_pack_dg_ = 0;
     FcRow* fc_tab_ = nullptr;                     // device
     int* fc_row_entry_ = nullptr;                 // device
     int fc_rows_ = 0;

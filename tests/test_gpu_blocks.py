@@ -152,6 +152,15 @@ def test_config1_resblock1_full_size_vs_torch_fp32():
     assert rel_l2(y.cpu().numpy(), yt.detach().cpu().numpy()) < tol
     assert rel_l2(out["dx"].cpu().numpy(), xt.grad.cpu().numpy()) < tol
     assert rel_l2(out["d_style"].cpu().numpy(), st.grad.cpu().numpy()) < tol
-    worst = per_tensor_rel(o.table, out["grads"].cpu().numpy(), td.grads_flat(o.n_params))
+    g, gt = out["grads"].cpu().numpy(), td.grads_flat(o.n_params)
+    # convs1.i feeds only adain2.i's instance norm, which removes any per-channel
+    # constant: the true bias gradient is exactly zero and both sides hold rounding
+    # noise, checked against the global gradient norm instead
+    zero = [e for e in o.table if e["name"].startswith("convs1.") and e["name"].endswith(".bias")]
+    tot = float(np.linalg.norm(gt))
+    for e in zero:
+        sl = slice(e["offset"], e["offset"] + e["numel"])
+        assert float(np.linalg.norm(g[sl])) < 1e-6 * tot and float(np.linalg.norm(gt[sl])) < 1e-6 * tot, e["name"]
+    worst = per_tensor_rel([e for e in o.table if e not in zero], g, gt)
     bad = {k: v for k, v in worst.items() if v > tol}
     assert not bad, bad
