@@ -8,7 +8,11 @@ all-reduce across ranks (N > 1), Adam update. Default workload = BASELINE
 config 2: batch 16 x T=200 asr frames (5 s clips) per GPU (weak scaling).
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-For N > 1 launch with torchrun (one rank per GPU, NCCL over NVLink).
+                  [--workload c2|c0|c3|c3lora|c1] [--eager]
+For N > 1 launch with torchrun (one rank per GPU, NCCL over NVLink). On the
+decoder workloads the forward, loss and backward of a step are recorded once as
+a CUDA graph and replayed (--eager launches every kernel from the host instead);
+the all-reduce and the Adam update run outside the graph.
 """
 
 from __future__ import annotations
@@ -162,19 +166,49 @@ def setup_decoder(args, B, T, dev, rank, math):
     audio = torch.empty((B, dec.audio_len(T)), device=dev)
     lossbuf = torch.empty(1, device=dev)
     dabuf = torch.empty_like(audio)
+    d_asr = torch.empty((B, cfg["asr_dim"], T), device=dev)
+    d_style = torch.empty((B, cfg["style_dim"]), device=dev)
     state = {"step": 0}
 
-    def step(inp):
+    def fwd_bwd(inp):
         dec.forward(params, inp["asr"], inp["F0"], inp["N"], inp["style"], audio=audio)
         l1_loss(audio, inp["target"], lossbuf, dabuf)
-        dec.backward(dabuf, grads=grads)
+        dec.backward(dabuf, grads=grads, d_asr=d_asr, d_style=d_style)   # all weights, asr and style
+
+    def finish():
         dp.average_gradients(grads)   # one NCCL all-reduce of the flat gradient (N > 1)
         state["step"] += 1
         adam_step(params, grads, m, v, 1e-5, state["step"])
 
-    return dict(host=host, dev=d, step=step, result=lossbuf, prof=dec, metric=METRIC, unit=UNIT,
-                units_per_step=audio_seconds(B, T),
-                config={"audio_s_per_step_per_gpu": audio_seconds(B, T),
+    graph = None
+    if args.graph:
+        # forward + loss + backward recorded once (after an eager pass that plans the
+        # workspace) and replayed; the all-reduce and Adam (whose step count is a
+        # launch argument) stay outside the graph
+        from brosoundml_b200.decoder import Graph
+        fwd_bwd(d)
+        torch.cuda.synchronize()
+        graph = Graph(torch.cuda.current_stream())
+        with graph:
+            fwd_bwd(d)
+
+    def step(inp):
+        if graph is None:
+            fwd_bwd(inp)
+        else:
+            if inp is not d:
+                for k in d:
+                    d[k].copy_(inp[k], non_blocking=True)
+            graph.replay()
+        finish()
+
+    def eager_step(inp):
+        fwd_bwd(inp)
+        finish()
+
+    return dict(host=host, dev=d, step=step, eager_step=eager_step, result=lossbuf, prof=dec, metric=METRIC,
+                unit=UNIT, units_per_step=audio_seconds(B, T), graph=graph,
+                config={"audio_s_per_step_per_gpu": audio_seconds(B, T), "cuda_graph": graph is not None,
                         "weights": "random init N(0,0.02), Snake alpha 1", "optimizer": "Adam lr 1e-5"})
 
 
@@ -377,6 +411,9 @@ def main():
     ap.add_argument("--math", default=None, choices=["fp32", "tf32x3", "bf16"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--eager", action="store_true",
+                    help="launch every kernel from the host instead of replaying forward + loss + backward as "
+                         "one CUDA graph (decoder workloads)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -405,6 +442,9 @@ def main():
     math = args.math or Decoder.DEFAULT_MATH
     B, T, desc = WORKLOADS[args.workload]
     dev = torch.device("cuda", local)
+    args.graph = not args.eager and args.workload in ("c0", "c2", "c3")
+    if args.graph:
+        torch.cuda.set_stream(torch.cuda.Stream())   # graph capture needs a non-default stream
     if args.workload == "c1":
         w = setup_block(args, B, T, dev, rank, math)
     elif args.workload == "c3lora":
@@ -442,6 +482,8 @@ def main():
     e1.record(st)
     barrier()
     launches = (_lib.lib().bsml_launch_count() - n0) // max(args.steps, 1)
+    if w.get("graph") is not None:
+        launches += w["graph"].kernels   # kernels a replay issues (not counted on the host)
     ms = max_over_ranks(e0.elapsed_time(e1)) / args.steps
     clk = clocks.stop() if rank == 0 else None
     per_step, unit = w["units_per_step"], w["unit"]
@@ -456,8 +498,13 @@ def main():
         barrier()
         e0.record(st)
         for _ in range(e2e_steps):
-            inp = {k: t.to(dev, non_blocking=True) for k, t in host.items()}
-            train_step(inp)
+            if w.get("graph") is not None:   # the graph reads fixed buffers: copy the step's inputs into them
+                for k, t in host.items():
+                    d[k].copy_(t, non_blocking=True)
+                train_step(d)
+            else:
+                inp = {k: t.to(dev, non_blocking=True) for k, t in host.items()}
+                train_step(inp)
             loss_host.copy_(result, non_blocking=True)
         e1.record(st)
         barrier()
@@ -467,7 +514,7 @@ def main():
 
     # roofline: one profiled step (per-class CUDA events), after the timed region
     prof_src.set_profiling(True)
-    train_step(d)
+    w.get("eager_step", train_step)(d)   # the profile records per-class events: an eager step
     prof = prof_src.read_profile()
     prof_src.set_profiling(False)
     peaks = load_peaks()

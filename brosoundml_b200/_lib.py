@@ -91,6 +91,11 @@ SIGNATURES = {
     "bsml_decoder_backward": ([_P, _P, _P, _P, _P, _P, _P], _I),
     "bsml_decoder_workspace_bytes": ([_P], _L),
     "bsml_selftest_bounded_wait": ([_P], _I),
+    "bsml_graph_begin": ([_P], _I),
+    "bsml_graph_end": ([_P, ctypes.POINTER(_P)], _I),
+    "bsml_graph_launch": ([_P, _P], _I),
+    "bsml_graph_kernel_count": ([_P, ctypes.POINTER(_L)], _I),
+    "bsml_graph_destroy": ([_P], None),
     "bsml_block_create": ([_BS, _I, ctypes.POINTER(_P)], _I),
     "bsml_block_param_count": ([_BS, ctypes.POINTER(_L), ctypes.POINTER(_I), ctypes.POINTER(_I),
                                 ctypes.POINTER(_L)], _I),

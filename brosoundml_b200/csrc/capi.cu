@@ -476,6 +476,66 @@ int bsml_convlora_adam_step(bsml_convlora* l, float lr, float beta1, float beta2
     });
 }
 
+struct bsml_graph {
+    cudaGraph_t g = nullptr;
+    cudaGraphExec_t e = nullptr;
+};
+
+int bsml_graph_begin(void* stream) {
+    return guarded([&] {
+        need(stream != nullptr, "bsml_graph_begin", "capture needs a stream other than the legacy default stream");
+        BSML_CUDA(cudaStreamBeginCapture(S(stream), cudaStreamCaptureModeThreadLocal));
+    });
+}
+
+int bsml_graph_end(void* stream, bsml_graph** out) {
+    return guarded([&] {
+        need(stream != nullptr && out != nullptr, "bsml_graph_end", "null argument");
+        cudaGraph_t g = nullptr;
+        BSML_CUDA(cudaStreamEndCapture(S(stream), &g));
+        auto* G = new bsml_graph;
+        G->g = g;
+        const cudaError_t e = cudaGraphInstantiate(&G->e, g, 0);
+        if (e != cudaSuccess) {
+            cudaGraphDestroy(g);
+            delete G;
+            bsml::check_cuda(e, "cudaGraphInstantiate");
+        }
+        *out = G;
+    });
+}
+
+int bsml_graph_launch(bsml_graph* g, void* stream) {
+    return guarded([&] {
+        need(g != nullptr, "bsml_graph_launch", "null graph");
+        BSML_CUDA(cudaGraphLaunch(g->e, S(stream)));
+    });
+}
+
+int bsml_graph_kernel_count(const bsml_graph* g, int64_t* n) {
+    return guarded([&] {
+        need(g != nullptr && n != nullptr, "bsml_graph_kernel_count", "null argument");
+        size_t nn = 0;
+        BSML_CUDA(cudaGraphGetNodes(g->g, nullptr, &nn));
+        std::vector<cudaGraphNode_t> nodes(nn);
+        if (nn) BSML_CUDA(cudaGraphGetNodes(g->g, nodes.data(), &nn));
+        int64_t k = 0;
+        for (auto node : nodes) {
+            cudaGraphNodeType t;
+            BSML_CUDA(cudaGraphNodeGetType(node, &t));
+            if (t == cudaGraphNodeTypeKernel) ++k;
+        }
+        *n = k;
+    });
+}
+
+void bsml_graph_destroy(bsml_graph* g) {
+    if (!g) return;
+    if (g->e) cudaGraphExecDestroy(g->e);
+    if (g->g) cudaGraphDestroy(g->g);
+    delete g;
+}
+
 int bsml_loss_l1(const float* audio, const float* target, int64_t n, float* loss, float* daudio, void* stream) {
     return guarded([&] {
         need(audio && target && loss && daudio && n > 0, "bsml_loss_l1", "bad argument");

@@ -116,14 +116,19 @@ class Decoder:
             _ptr(aff_in), _ptr(audio), _ptr(aff_out), _stream()))
         return audio
 
-    def backward(self, daudio, grads=None, want_grads=True, want_inputs=True, want_aff=False):
+    def backward(self, daudio, grads=None, want_grads=True, want_inputs=True, want_aff=False, d_asr=None,
+                 d_style=None):
+        """Gradients of the last forward; grads / d_asr / d_style may be given as
+        preallocated outputs (nothing is allocated then, e.g. under graph capture)."""
         B, T = self._last
         daudio = _f32(daudio)
         dev = self.device
         if grads is None and want_grads:
             grads = torch.empty(self.n_params, device=dev, dtype=torch.float32)
-        d_asr = torch.empty((B, self.cfg["asr_dim"], T), device=dev) if want_inputs else None
-        d_style = torch.empty((B, self.cfg["style_dim"]), device=dev) if want_inputs else None
+        if d_asr is None and want_inputs:
+            d_asr = torch.empty((B, self.cfg["asr_dim"], T), device=dev)
+        if d_style is None and want_inputs:
+            d_style = torch.empty((B, self.cfg["style_dim"]), device=dev)
         d_aff = torch.empty(B * self.aff_per_clip, device=dev) if want_aff else None
         _lib.check(_lib.lib().bsml_decoder_backward(self._h, _ptr(daudio), _ptr(grads), _ptr(d_asr),
                                                    _ptr(d_style), _ptr(d_aff), _stream()))
@@ -181,6 +186,48 @@ class Block(Decoder):
         _lib.check(_lib.lib().bsml_block_backward(self._h, _ptr(dy), _ptr(grads), _ptr(dx), _ptr(d_style),
                                                   _ptr(d_aff), _stream()))
         return dict(grads=grads, dx=dx, d_style=d_style, d_aff=d_aff)
+
+
+class Graph:
+    """A CUDA graph of library calls (bsml_graph_*): every call made on the
+    capture stream inside ``with Graph(stream) as g:`` is recorded; ``g.replay()``
+    reruns them with the same buffers. Run the sequence once eagerly before
+    capturing (workspace planning allocates), pre-allocate every output, and keep
+    torch operations out of the captured block."""
+
+    def __init__(self, stream=None):
+        self.stream = stream if stream is not None else torch.cuda.Stream()
+        self._g = None
+
+    def __enter__(self):
+        self._ctx = torch.cuda.stream(self.stream)
+        self._ctx.__enter__()
+        _lib.check(_lib.lib().bsml_graph_begin(ctypes.c_void_p(self.stream.cuda_stream)))
+        return self
+
+    def __exit__(self, et, ev, tb):
+        g = ctypes.c_void_p()
+        rc = _lib.lib().bsml_graph_end(ctypes.c_void_p(self.stream.cuda_stream), ctypes.byref(g))
+        self._ctx.__exit__(et, ev, tb)
+        if et is None:
+            _lib.check(rc)
+            self._g = g
+        return False
+
+    @property
+    def kernels(self) -> int:
+        n = ctypes.c_int64()
+        _lib.check(_lib.lib().bsml_graph_kernel_count(self._g, ctypes.byref(n)))
+        return n.value
+
+    def replay(self, stream=None) -> None:
+        s = stream if stream is not None else torch.cuda.current_stream()
+        _lib.check(_lib.lib().bsml_graph_launch(self._g, ctypes.c_void_p(s.cuda_stream)))
+
+    def __del__(self):
+        if getattr(self, "_g", None) is not None and _lib._lib is not None:
+            _lib.lib().bsml_graph_destroy(self._g)
+            self._g = None
 
 
 def l1_loss(audio, target, loss=None, daudio=None):

@@ -180,6 +180,22 @@ int bsml_block_forward(bsml_decoder* d, int B, int L, const float* params, const
 int bsml_block_backward(bsml_decoder* d, const float* dy, float* grads, float* dx, float* d_style, float* d_aff,
                         void* stream);
 
+/* ── CUDA graphs (no reference counterpart: the reference runs eagerly) ────
+ * Records every library call issued on `stream` between begin and end (a whole
+ * forward, loss and backward, say) into one CUDA graph; launch replays it with
+ * the same pointers and shapes, so new data is written into the same input
+ * buffers between launches. Run the same sequence once eagerly first: the first
+ * call of a shape plans and allocates the engine's workspace, which a capture
+ * cannot do. stream must not be the legacy default stream. Keep an optimiser
+ * step with a step count outside the graph (its count is a launch argument). */
+typedef struct bsml_graph bsml_graph;
+int bsml_graph_begin(void* stream);
+int bsml_graph_end(void* stream, bsml_graph** out);
+int bsml_graph_launch(bsml_graph* g, void* stream);
+/* Kernel nodes in the graph (the launches one replay issues). */
+int bsml_graph_kernel_count(const bsml_graph* g, int64_t* n);
+void bsml_graph_destroy(bsml_graph* g);
+
 /* ── loss and optimiser ─────────────────────────────────────────────────── */
 
 /* L1 loss: loss[0] = mean |audio - target|, daudio = sign(audio - target) / n. */
