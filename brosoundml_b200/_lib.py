@@ -89,8 +89,16 @@ SIGNATURES = {
     "bsml_config_param_table": ([_CFG, _P, _I, _P], _I),
     "bsml_decoder_forward": ([_P, _I, _I, _P, _P, _P, _P, _P, _P, _I, _P, _P, _P, _P], _I),
     "bsml_decoder_backward": ([_P, _P, _P, _P, _P, _P, _P], _I),
+    "bsml_decoder_decode": ([_P, _I, _I, _P, _P, _I, _P, _P, _P, _P, _P], _I),
     "bsml_decoder_workspace_bytes": ([_P], _L),
     "bsml_selftest_bounded_wait": ([_P], _I),
+    "bsml_st_open": ([ctypes.c_char_p, ctypes.POINTER(_P)], _I),
+    "bsml_st_close": ([_P], None),
+    "bsml_st_count": ([_P, ctypes.POINTER(_I)], _I),
+    "bsml_st_info": ([_P, _I, ctypes.c_char_p, _I, ctypes.POINTER(_I), ctypes.POINTER(_I), _P], _I),
+    "bsml_st_read_f32": ([_P, ctypes.c_char_p, _P, _L], _I),
+    "bsml_st_metadata": ([_P, ctypes.c_char_p, ctypes.c_char_p, _I], _I),
+    "bsml_params_from_safetensors": ([_P, _P, _I, ctypes.c_char_p, _P, _L], _I),
     "bsml_graph_begin": ([_P], _I),
     "bsml_graph_end": ([_P, ctypes.POINTER(_P)], _I),
     "bsml_graph_launch": ([_P, _P], _I),
@@ -144,6 +152,10 @@ SIGNATURES = {
     "bsml_convlora_backward": ([_P, _P, _P], _I),
     "bsml_convlora_zero_grad": ([_P, _P], _I),
     "bsml_convlora_adam_step": ([_P, _F, _F, _F, _F, _P], _I),
+    "bsml_convlora_save": ([_P, ctypes.c_char_p], _I),
+    "bsml_convlora_load": ([_P, ctypes.c_char_p], _I),
+    "bsml_lora_save_state": ([_P, ctypes.c_char_p], _I),
+    "bsml_lora_load_state": ([_P, ctypes.c_char_p], _I),
 }
 
 _lib = None

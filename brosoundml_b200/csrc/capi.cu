@@ -12,6 +12,7 @@
 #include "kernels.h"
 #include "convlora.h"
 #include "lora.h"
+#include "safetensors.h"
 
 namespace {
 
@@ -200,6 +201,16 @@ int bsml_decoder_forward(bsml_decoder* d, int B, int T, const float* params, con
     return guarded([&] {
         need(d != nullptr, "bsml_decoder_forward", "null handle");
         d->eng->forward(B, T, params, asr, F0, N, style, har, frames, aff_in, audio, aff_out, S(stream));
+    });
+}
+
+int bsml_decoder_decode(bsml_decoder* d, int B, int T, const float* params, const float* ref_s, int ref_s_stride,
+                        const float* asr, const float* F0, const float* N, float* audio, void* stream) {
+    return guarded([&] {
+        need(d != nullptr, "bsml_decoder_decode", "null handle");
+        need(ref_s != nullptr, "bsml_decoder_decode", "null ref_s");
+        d->eng->forward(B, T, params, asr, F0, N, ref_s, nullptr, 0, nullptr, audio, nullptr, S(stream),
+                        ref_s_stride);
     });
 }
 
@@ -397,6 +408,20 @@ int bsml_lora_load(bsml_lora* l, const char* path) {
     });
 }
 
+int bsml_lora_save_state(const bsml_lora* l, const char* path) {
+    return guarded([&] {
+        need(l != nullptr && path != nullptr, "bsml_lora_save_state", "null argument");
+        l->lora->save(path, true);
+    });
+}
+
+int bsml_lora_load_state(bsml_lora* l, const char* path) {
+    return guarded([&] {
+        need(l != nullptr && path != nullptr, "bsml_lora_load_state", "null argument");
+        l->lora->load(path, true);
+    });
+}
+
 int bsml_lora_state(const bsml_lora* l, float* scale, int* step) {
     return guarded([&] {
         need(l != nullptr, "bsml_lora_state", "null handle");
@@ -469,10 +494,99 @@ int bsml_convlora_zero_grad(bsml_convlora* l, void* stream) {
     });
 }
 
+int bsml_convlora_save(const bsml_convlora* l, const char* path) {
+    return guarded([&] {
+        need(l != nullptr && path != nullptr, "bsml_convlora_save", "null argument");
+        l->lora->save(path);
+    });
+}
+
+int bsml_convlora_load(bsml_convlora* l, const char* path) {
+    return guarded([&] {
+        need(l != nullptr && path != nullptr, "bsml_convlora_load", "null argument");
+        l->lora->load(path);
+    });
+}
+
 int bsml_convlora_adam_step(bsml_convlora* l, float lr, float beta1, float beta2, float eps, void* stream) {
     return guarded([&] {
         need(l != nullptr, "bsml_convlora_adam_step", "null handle");
         l->lora->adam_step(lr, beta1, beta2, eps, S(stream));
+    });
+}
+
+struct bsml_st {
+    std::unique_ptr<bsml::SafeTensors> f;
+};
+
+int bsml_st_open(const char* path, bsml_st** out) {
+    return guarded([&] {
+        need(path && out, "bsml_st_open", "null argument");
+        auto* s = new bsml_st;
+        try {
+            s->f = std::make_unique<bsml::SafeTensors>(path);
+        } catch (...) {
+            delete s;
+            throw;
+        }
+        *out = s;
+    });
+}
+
+void bsml_st_close(bsml_st* f) { delete f; }
+
+int bsml_st_count(const bsml_st* f, int* n) {
+    return guarded([&] {
+        need(f && n, "bsml_st_count", "null argument");
+        *n = (int)f->f->entries().size();
+    });
+}
+
+int bsml_st_info(const bsml_st* f, int i, char* name, int name_cap, int* dtype, int* ndim, int64_t* shape) {
+    return guarded([&] {
+        need(f != nullptr, "bsml_st_info", "null handle");
+        const auto& es = f->f->entries();
+        need(i >= 0 && i < (int)es.size(), "bsml_st_info", "index out of range");
+        const auto& e = es[i];
+        if (name && name_cap > 0) {
+            std::strncpy(name, e.name.c_str(), (size_t)name_cap - 1);
+            name[name_cap - 1] = '\0';
+        }
+        if (dtype) *dtype = e.dtype;
+        if (ndim) *ndim = (int)e.shape.size();
+        if (shape)
+            for (size_t k = 0; k < e.shape.size() && k < 8; ++k) shape[k] = e.shape[k];
+    });
+}
+
+int bsml_st_read_f32(const bsml_st* f, const char* name, float* dst, int64_t n) {
+    return guarded([&] {
+        need(f && name && dst, "bsml_st_read_f32", "null argument");
+        const auto* e = f->f->find(name);
+        if (!e) bsml::fail("bsml_st_read_f32", std::string("missing safetensors key '") + name + "'");
+        if (e->numel != n)
+            bsml::fail("bsml_st_read_f32", std::string("tensor '") + name + "' has " + std::to_string(e->numel) +
+                                               " elements; expected " + std::to_string(n));
+        f->f->read_f32(*e, dst);
+    });
+}
+
+int bsml_st_metadata(const bsml_st* f, const char* key, char* value, int cap) {
+    return guarded([&] {
+        need(f && key && value && cap > 0, "bsml_st_metadata", "null argument");
+        const auto& m = f->f->metadata();
+        auto it = m.find(key);
+        if (it == m.end()) bsml::fail("bsml_st_metadata", std::string("no metadata key '") + key + "'");
+        std::strncpy(value, it->second.c_str(), (size_t)cap - 1);
+        value[cap - 1] = '\0';
+    });
+}
+
+int bsml_params_from_safetensors(const bsml_st* f, const bsml_param_entry* table, int n_entries, const char* prefix,
+                                 float* params, int64_t n_params) {
+    return guarded([&] {
+        need(f && table && params, "bsml_params_from_safetensors", "null argument");
+        f->f->load_params(table, n_entries, prefix ? prefix : "", params, n_params);
     });
 }
 

@@ -3,6 +3,8 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstdio>
+#include <cstring>
 
 #include "kernels.h"
 
@@ -146,6 +148,79 @@ void ConvLora::adam_step(float lr, float b1, float b2, float eps, cudaStream_t s
     BSML_CUDA(cudaSetDevice(device_));
     ++step_;
     adam(P_, G_, M_, V_, n_params_, lr, b1, b2, eps, step_, st);
+}
+
+namespace {
+constexpr char kConvMagic[8] = {'E', 'C', 'L', 'R', '1', 0, 0, 0};
+struct CFile {
+    std::FILE* f;
+    ~CFile() {
+        if (f) std::fclose(f);
+    }
+};
+template <class T>
+void put(std::FILE* f, T v) { std::fwrite(&v, sizeof(T), 1, f); }
+template <class T>
+T get(std::FILE* f) {
+    T v{};
+    if (std::fread(&v, sizeof(T), 1, f) != 1) fail("ConvLora::load", "truncated file");
+    return v;
+}
+}  // namespace
+
+void ConvLora::save(const std::string& path) const {
+    BSML_CUDA(cudaSetDevice(device_));
+    BSML_CUDA(cudaDeviceSynchronize());
+    std::vector<float> p(n_params_), m(n_params_), v(n_params_);
+    BSML_CUDA(cudaMemcpy(p.data(), P_, sizeof(float) * n_params_, cudaMemcpyDeviceToHost));
+    BSML_CUDA(cudaMemcpy(m.data(), M_, sizeof(float) * n_params_, cudaMemcpyDeviceToHost));
+    BSML_CUDA(cudaMemcpy(v.data(), V_, sizeof(float) * n_params_, cudaMemcpyDeviceToHost));
+    CFile fh{std::fopen(path.c_str(), "wb")};
+    if (!fh.f) fail("ConvLora::save", "cannot open " + path);
+    std::fwrite(kConvMagic, 1, 8, fh.f);
+    put<int32_t>(fh.f, rank_);
+    put<float>(fh.f, scale_);
+    put<int32_t>(fh.f, (int32_t)ws_.size());
+    for (const ConvLoraW& w : ws_) {
+        put<int64_t>(fh.f, w.w);
+        put<int32_t>(fh.f, w.rows);
+        put<int32_t>(fh.f, w.cols);
+    }
+    put<int32_t>(fh.f, step_);
+    put<int64_t>(fh.f, n_params_);
+    for (const auto* a : {&p, &m, &v}) std::fwrite(a->data(), sizeof(float), a->size(), fh.f);
+    if (std::ferror(fh.f)) fail("ConvLora::save", "write error on " + path);
+}
+
+void ConvLora::load(const std::string& path) {
+    BSML_CUDA(cudaSetDevice(device_));
+    CFile fh{std::fopen(path.c_str(), "rb")};
+    if (!fh.f) fail("ConvLora::load", "cannot open " + path);
+    char magic[8];
+    if (std::fread(magic, 1, 8, fh.f) != 8 || std::memcmp(magic, kConvMagic, 8) != 0)
+        fail("ConvLora::load", "bad magic in " + path);
+    const int32_t rank = get<int32_t>(fh.f);
+    const float scale = get<float>(fh.f);
+    const int32_t nw = get<int32_t>(fh.f);
+    if (rank != rank_ || nw != (int32_t)ws_.size()) fail("ConvLora::load", "architecture mismatch");
+    for (const ConvLoraW& w : ws_) {
+        const int64_t off = get<int64_t>(fh.f);
+        const int32_t r = get<int32_t>(fh.f), c = get<int32_t>(fh.f);
+        if (off != w.w || r != w.rows || c != w.cols) fail("ConvLora::load", "architecture mismatch");
+    }
+    const int32_t step = get<int32_t>(fh.f);
+    const int64_t n = get<int64_t>(fh.f);
+    if (n != n_params_ || step < 0) fail("ConvLora::load", "architecture mismatch");
+    std::vector<float> p(n_params_), m(n_params_), v(n_params_);
+    for (auto* a : {&p, &m, &v})
+        if (std::fread(a->data(), sizeof(float), a->size(), fh.f) != a->size())
+            fail("ConvLora::load", "truncated data");
+    BSML_CUDA(cudaDeviceSynchronize());
+    BSML_CUDA(cudaMemcpy(P_, p.data(), sizeof(float) * n_params_, cudaMemcpyHostToDevice));
+    BSML_CUDA(cudaMemcpy(M_, m.data(), sizeof(float) * n_params_, cudaMemcpyHostToDevice));
+    BSML_CUDA(cudaMemcpy(V_, v.data(), sizeof(float) * n_params_, cudaMemcpyHostToDevice));
+    step_ = step;
+    scale_ = scale;
 }
 
 }  // namespace bsml

@@ -9,6 +9,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <string>
 #include <vector>
 
 #include "engine.h"
@@ -42,6 +43,9 @@ class ConvLora {
     void backward(const float* daudio, cudaStream_t st);
     void zero_grad(cudaStream_t st);
     void adam_step(float lr, float b1, float b2, float eps, cudaStream_t st);
+    // full training state (ECLR1): parameters, Adam moments and step; synchronous
+    void save(const std::string& path) const;
+    void load(const std::string& path);
 
    private:
     Engine& eng_;

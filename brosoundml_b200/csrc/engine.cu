@@ -938,9 +938,11 @@ void Engine::rb1_bwd(const RB1P& w, RB1C& c, const Act& dOut, float scale, const
 // ── forward
 void Engine::forward(int B, int T, const float* params, const float* asr, const float* F0, const float* N,
                      const float* style, const float* har, int frames, const float* aff_in, float* audio,
-                     float* aff_out, cudaStream_t st) {
+                     float* aff_out, cudaStream_t st, int style_stride) {
     if (lay_.block_kind) fail("bsml_decoder_forward", "the handle holds a single block: use bsml_block_forward");
     if (B < 1 || T < 1) fail("bsml_decoder_forward", "B and T must be positive");
+    if (style_stride != 0 && style_stride < lay_.cfg.style_dim)
+        fail("bsml_decoder_forward", "style row stride below the style width");
     if (!params || !asr || !F0 || !N || !audio) fail("bsml_decoder_forward", "null input");
     if (!aff_in && !style) fail("bsml_decoder_forward", "style is required unless aff_in is given");
     if (!har && lay_.cfg.har_ch != lay_.cfg.n_fft + 2)
@@ -954,7 +956,9 @@ void Engine::forward(int B, int T, const float* params, const float* asr, const 
     BSML_CUDA(cudaMemcpyAsync(F0_copy_, F0, sizeof(float) * B * 2 * T, cudaMemcpyDeviceToDevice, st));
     BSML_CUDA(cudaMemcpyAsync(N_copy_, N, sizeof(float) * B * 2 * T, cudaMemcpyDeviceToDevice, st));
     if (style)
-        BSML_CUDA(cudaMemcpyAsync(style_copy_, style, sizeof(float) * B * cf.style_dim, cudaMemcpyDeviceToDevice, st));
+        BSML_CUDA(cudaMemcpy2DAsync(style_copy_, sizeof(float) * cf.style_dim, style,
+                                    sizeof(float) * (style_stride > 0 ? style_stride : cf.style_dim),
+                                    sizeof(float) * cf.style_dim, B, cudaMemcpyDeviceToDevice, st));
     F0_ = F0_copy_;
     N_ = N_copy_;
     style_ = style ? style_copy_ : nullptr;

@@ -25,9 +25,11 @@ class Engine {
     void set_math(int m);
     int math() const { return math_; }
 
+    // style rows are style_stride floats apart (0 = style_dim; a (B, 2*style_dim)
+    // ref_s passes 2*style_dim and the decoder reads the first style_dim of each row)
     void forward(int B, int T, const float* params, const float* asr, const float* F0, const float* N,
                  const float* style, const float* har, int frames, const float* aff_in, float* audio,
-                 float* aff_out, cudaStream_t st);
+                 float* aff_out, cudaStream_t st, int style_stride = 0);
     void backward(const float* daudio, float* grads, float* d_asr, float* d_style, float* d_aff, cudaStream_t st);
     // one block (a handle made from a bsml_block_spec): x, y, dy, dx NCL
     void forward_block(int B, int L, const float* params, const float* x, const float* style, const float* aff_in,

@@ -348,7 +348,11 @@ void get_tensor(std::FILE* f, float* h, int rows, int cols) {
 }
 }  // namespace
 
-void Lora::save(const std::string& path) const {
+namespace {
+constexpr char kStateMagic[8] = {'E', 'L', 'R', 'S', 'T', 'A', 'T', 'E'};
+}
+
+void Lora::save(const std::string& path, bool full_state) const {
     BSML_CUDA(cudaSetDevice(device_));
     std::vector<float> h(n_params_);
     BSML_CUDA(cudaDeviceSynchronize());
@@ -367,10 +371,24 @@ void Lora::save(const std::string& path) const {
         put_tensor(fh.f, h.data() + a.offA, rank_, S_);
         put_tensor(fh.f, h.data() + a.offB, 2 * a.C, rank_);
     }
+    if (full_state) {
+        // optimiser state after the ELRA1 body (a reader of the plain format stops
+        // before it): magic, step, n, then Adam's first and second moments in the
+        // same order as the parameters above
+        std::vector<float> m(n_params_), v(n_params_);
+        BSML_CUDA(cudaMemcpy(m.data(), M_, sizeof(float) * n_params_, cudaMemcpyDeviceToHost));
+        BSML_CUDA(cudaMemcpy(v.data(), V_, sizeof(float) * n_params_, cudaMemcpyDeviceToHost));
+        std::fwrite(kStateMagic, 1, 8, fh.f);
+        put_i32(fh.f, step_);
+        const int64_t n = n_params_;
+        std::fwrite(&n, sizeof(n), 1, fh.f);
+        std::fwrite(m.data(), sizeof(float), m.size(), fh.f);
+        std::fwrite(v.data(), sizeof(float), v.size(), fh.f);
+    }
     if (std::ferror(fh.f)) fail("DecoderLora::save", "write error on " + path);
 }
 
-void Lora::load(const std::string& path) {
+void Lora::load(const std::string& path, bool full_state) {
     BSML_CUDA(cudaSetDevice(device_));
     File fh{std::fopen(path.c_str(), "rb")};
     if (!fh.f) fail("DecoderLora::load", "cannot open " + path);
@@ -390,8 +408,29 @@ void Lora::load(const std::string& path) {
         get_tensor(fh.f, h.data() + a.offA, rank_, S_);
         get_tensor(fh.f, h.data() + a.offB, 2 * a.C, rank_);
     }
+    std::vector<float> m, v;
+    int32_t step = 0;
+    if (full_state) {
+        char sm[8];
+        if (std::fread(sm, 1, 8, fh.f) != 8 || std::memcmp(sm, kStateMagic, 8) != 0)
+            fail("DecoderLora::load", "no optimiser state in " + path);
+        step = get_i32(fh.f, "state header");
+        int64_t n = 0;
+        if (std::fread(&n, sizeof(n), 1, fh.f) != 1) fail("DecoderLora::load", "truncated state header");
+        if (n != n_params_ || step < 0) fail("DecoderLora::load", "architecture mismatch");
+        m.resize(n_params_);
+        v.resize(n_params_);
+        if (std::fread(m.data(), sizeof(float), m.size(), fh.f) != m.size() ||
+            std::fread(v.data(), sizeof(float), v.size(), fh.f) != v.size())
+            fail("DecoderLora::load", "truncated optimiser state");
+    }
     BSML_CUDA(cudaDeviceSynchronize());
     BSML_CUDA(cudaMemcpy(P_, h.data(), sizeof(float) * n_params_, cudaMemcpyHostToDevice));
+    if (full_state) {
+        BSML_CUDA(cudaMemcpy(M_, m.data(), sizeof(float) * n_params_, cudaMemcpyHostToDevice));
+        BSML_CUDA(cudaMemcpy(V_, v.data(), sizeof(float) * n_params_, cudaMemcpyHostToDevice));
+        step_ = step;
+    }
     scale_ = scale;
 }
 

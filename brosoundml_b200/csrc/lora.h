@@ -57,8 +57,10 @@ class Lora {
     void zero_grad(cudaStream_t st);
     void adam_step(float lr, float b1, float b2, float eps, cudaStream_t st);
     // ELRA1 checkpoint (DecoderLora::save / load, src/decoder_lora.cpp:324-396); synchronous.
-    void save(const std::string& path) const;
-    void load(const std::string& path);
+    // full_state: Adam's moments and step follow the ELRA1 body (a resume point;
+    // the reference format drops them, and its reader stops before them)
+    void save(const std::string& path, bool full_state = false) const;
+    void load(const std::string& path, bool full_state = false);
 
    private:
     void ensure_batch(int B);

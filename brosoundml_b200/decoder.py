@@ -116,6 +116,20 @@ class Decoder:
             _ptr(aff_in), _ptr(audio), _ptr(aff_out), _stream()))
         return audio
 
+    def decode(self, params, ref_s, asr, F0, N, audio=None):
+        """Kokoro::Impl::decode_back_half (src/kokoro.cpp:352-407), batched: the
+        backbone, the harmonic source from F0, the generator and the iSTFT. ref_s
+        (B, 2*style_dim): the decoder reads the first style_dim of each row."""
+        params, ref_s, asr, F0, N = map(_f32, (params, ref_s, asr, F0, N))
+        B, _, T = asr.shape
+        if audio is None:
+            audio = torch.empty((B, self.audio_len(T)), device=self.device, dtype=torch.float32)
+        self._last = (B, T)
+        self._borrowed = params
+        _lib.check(_lib.lib().bsml_decoder_decode(self._h, B, T, _ptr(params), _ptr(ref_s), ref_s.shape[-1],
+                                                  _ptr(asr), _ptr(F0), _ptr(N), _ptr(audio), _stream()))
+        return audio
+
     def backward(self, daudio, grads=None, want_grads=True, want_inputs=True, want_aff=False, d_asr=None,
                  d_style=None):
         """Gradients of the last forward; grads / d_asr / d_style may be given as

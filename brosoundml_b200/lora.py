@@ -94,11 +94,15 @@ class DecoderLora:
     def adam_step(self, lr: float, beta1: float = 0.9, beta2: float = 0.999, eps: float = 1e-8) -> None:
         _lib.check(_lib.lib().bsml_lora_adam_step(self._h, lr, beta1, beta2, eps, _stream()))
 
-    def save(self, path: str) -> None:
-        _lib.check(_lib.lib().bsml_lora_save(self._h, str(path).encode()))
+    def save(self, path: str, full_state: bool = False) -> None:
+        """ELRA1 checkpoint; full_state adds Adam's moments and step after it (the
+        file stays readable by the plain-format readers)."""
+        fn = _lib.lib().bsml_lora_save_state if full_state else _lib.lib().bsml_lora_save
+        _lib.check(fn(self._h, str(path).encode()))
 
-    def load(self, path: str) -> None:
-        _lib.check(_lib.lib().bsml_lora_load(self._h, str(path).encode()))
+    def load(self, path: str, full_state: bool = False) -> None:
+        fn = _lib.lib().bsml_lora_load_state if full_state else _lib.lib().bsml_lora_load
+        _lib.check(fn(self._h, str(path).encode()))
 
 
 class _DeviceBuffer:
@@ -163,3 +167,10 @@ class ConvLora:
 
     def adam_step(self, lr: float, beta1: float = 0.9, beta2: float = 0.999, eps: float = 1e-8) -> None:
         _lib.check(_lib.lib().bsml_convlora_adam_step(self._h, lr, beta1, beta2, eps, _stream()))
+
+    def save(self, path: str) -> None:
+        """Full training state (ECLR1): A, B, Adam moments and step."""
+        _lib.check(_lib.lib().bsml_convlora_save(self._h, str(path).encode()))
+
+    def load(self, path: str) -> None:
+        _lib.check(_lib.lib().bsml_convlora_load(self._h, str(path).encode()))

@@ -110,6 +110,14 @@ int bsml_decoder_forward(bsml_decoder* d, int B, int T, const float* params, con
                          const float* N, const float* style, const float* har, int frames, const float* aff_in,
                          float* audio, float* aff_out, void* stream);
 
+/* Inference: Kokoro::Impl::decode_back_half (src/kokoro.cpp:352-407), batched:
+ * decoder backbone, harmonic source from F0, generator, iSTFT -> audio (B, S).
+ * ref_s rows are ref_s_stride floats apart (2*style_dim for the reference's
+ * (1, 2*style_dim) ref_s); the decoder reads the first style_dim of each row.
+ * A backward may follow (it is the same forward). */
+int bsml_decoder_decode(bsml_decoder* d, int B, int T, const float* params, const float* ref_s, int ref_s_stride,
+                        const float* asr, const float* F0, const float* N, float* audio, void* stream);
+
 /* Backward of the last forward. daudio (B, S). grads (n_params) is
  * OVERWRITTEN with d loss / d params (conv, convT, fc weights and biases,
  * Snake alphas). d_asr (B, asr_dim, T), d_style (B, style_dim), d_aff
@@ -180,6 +188,30 @@ int bsml_block_forward(bsml_decoder* d, int B, int L, const float* params, const
 int bsml_block_backward(bsml_decoder* d, const float* dy, float* grads, float* dx, float* d_style, float* d_aff,
                         void* stream);
 
+/* ── safetensors (host-side IO; the reference's checkpoint format,
+ * src/kokoro_modules.cpp:99-125) ─────────────────────────────────────────── */
+typedef struct bsml_st bsml_st;
+enum { BSML_ST_OTHER = 0, BSML_ST_F32 = 1, BSML_ST_F16 = 2, BSML_ST_BF16 = 3, BSML_ST_F64 = 4 };
+int bsml_st_open(const char* path, bsml_st** out);
+void bsml_st_close(bsml_st* f);
+int bsml_st_count(const bsml_st* f, int* n);
+/* i-th tensor in header order: name (NUL-terminated, truncated to name_cap),
+ * dtype (BSML_ST_*), ndim and up to 8 dimensions. */
+int bsml_st_info(const bsml_st* f, int i, char* name, int name_cap, int* dtype, int* ndim, int64_t* shape);
+/* Reads tensor `name` into host memory as fp32 (F32, F16, BF16 or F64 sources);
+ * n must equal its element count. */
+int bsml_st_read_f32(const bsml_st* f, const char* name, float* dst, int64_t n);
+/* __metadata__ string value of `key` (NUL-terminated, truncated to cap); error if absent. */
+int bsml_st_metadata(const bsml_st* f, const char* key, char* value, int cap);
+/* Fills the host parameter vector laid out by `table` (bsml_*_param_table) with
+ * the tensors named prefix + entry name ("decoder.module." for a Kokoro
+ * checkpoint). A weight held as weight_g / weight_v (PyTorch weight norm, the
+ * unconverted upstream layout) is fused to g * v / ||v|| over all axes but the
+ * first, as the reference's converter does (scripts/convert-kokoro.py:71-110).
+ * Missing keys and size mismatches are errors. */
+int bsml_params_from_safetensors(const bsml_st* f, const bsml_param_entry* table, int n_entries, const char* prefix,
+                                 float* params, int64_t n_params);
+
 /* ── CUDA graphs (no reference counterpart: the reference runs eagerly) ────
  * Records every library call issued on `stream` between begin and end (a whole
  * forward, loss and backward, say) into one CUDA graph; launch replays it with
@@ -244,6 +276,13 @@ int bsml_lora_adam_step(bsml_lora* l, float lr, float beta1, float beta2, float 
  * takes the scale from the file. Synchronous. */
 int bsml_lora_save(const bsml_lora* l, const char* path);
 int bsml_lora_load(bsml_lora* l, const char* path);
+/* Full training state (no reference counterpart; the reference drops the
+ * optimiser state): the ELRA1 file followed by Adam's moments and step, so a
+ * reader of the plain format (bsml_lora_load or the reference's
+ * DecoderLora::load, which stops after the last adapter) still reads it;
+ * load_state restores parameters, moments and step. Synchronous. */
+int bsml_lora_save_state(const bsml_lora* l, const char* path);
+int bsml_lora_load_state(bsml_lora* l, const char* path);
 /* Current LoRA scale and Adam step count. */
 int bsml_lora_state(const bsml_lora* l, float* scale, int* step);
 
@@ -271,6 +310,12 @@ int bsml_convlora_forward(bsml_convlora* l, int B, int T, const float* params, c
 int bsml_convlora_backward(bsml_convlora* l, const float* daudio, void* stream);
 int bsml_convlora_zero_grad(bsml_convlora* l, void* stream);
 int bsml_convlora_adam_step(bsml_convlora* l, float lr, float beta1, float beta2, float eps, void* stream);
+/* Full training state in the ECLR1 format: magic "ECLR1\0\0\0", int32 rank,
+ * float scale, int32 n_weights, per weight (int64 offset, int32 rows, int32 cols),
+ * int32 Adam step, int64 n_params, then parameters, first and second moments
+ * (float32 each). load checks the architecture. Synchronous. */
+int bsml_convlora_save(const bsml_convlora* l, const char* path);
+int bsml_convlora_load(bsml_convlora* l, const char* path);
 
 /* ── atoms (the reference's detail:: functions, batched) ────────────────── */
 

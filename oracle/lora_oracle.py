@@ -146,7 +146,7 @@ def read_elra1(path: str):
     hidden = i32()
     W1, W2 = tensor(), tensor()
     ads = []
-    while pos < len(data):
+    while pos < len(data) and data[pos:pos + 8] != b"ELRSTATE":   # optimiser state may follow
         C = i32()
         A, B = tensor(), tensor()
         ads.append((C, A, B))

@@ -84,3 +84,41 @@ def test_graph_needs_a_stream():
     from brosoundml_b200 import _lib
     assert _lib.lib().bsml_graph_begin(None) != 0
     assert "legacy default stream" in _lib.lib().bsml_last_error().decode()
+
+
+def test_decode_back_half_inference():
+    """bsml_decoder_decode = Kokoro::Impl::decode_back_half batched: ref_s rows of
+    2*style_dim (the decoder reads the first half), the harmonic source from F0;
+    equal to the forward given style = ref_s[:, :style_dim] and replayable as a
+    CUDA graph. (Against the oracle it is compared with har given: the phase
+    channels of har are angles, whose +-pi branch cut turns rounding-level
+    differences of the two harmonic sources into jumps, test_gpu_parity.py.)"""
+    import torch
+
+    from brosoundml_b200.decoder import Decoder, Graph
+
+    cfg, B, T = config.kokoro_82m(), 2, 32
+    S = cfg["style_dim"]
+    dec = Decoder(cfg, 0, math="tf32x3")
+    params = torch.tensor(synth.init_params(dec.table, dec.n_params, 0), device="cuda")
+    x = synth.make_inputs(cfg, B, T, 1)
+    ref_s = np.concatenate([x["style"], np.random.default_rng(5).normal(0, 1, (B, S)).astype(np.float32)], axis=1)
+    dv = {k: torch.tensor(v, device="cuda") for k, v in x.items()}
+    rs = torch.tensor(ref_s, device="cuda")
+    a_dec = dec.decode(params, rs, dv["asr"], dv["F0"], dv["N"]).clone()
+    a_fwd = dec.forward(params, dv["asr"], dv["F0"], dv["N"], rs[:, :S].contiguous()).clone()
+    torch.cuda.synchronize()
+    assert rel_l2(a_dec.cpu().numpy(), a_fwd.cpu().numpy()) < 1e-6
+    # inference as a replayed graph on a side stream
+    s = torch.cuda.Stream()
+    out = torch.empty_like(a_dec)
+    with torch.cuda.stream(s):
+        dec.decode(params, rs, dv["asr"], dv["F0"], dv["N"], audio=out)
+    g = Graph(s)
+    with g:
+        dec.decode(params, rs, dv["asr"], dv["F0"], dv["N"], audio=out)
+    out.zero_()
+    torch.cuda.synchronize()
+    g.replay(s)
+    torch.cuda.synchronize()
+    assert rel_l2(out.cpu().numpy(), a_dec.cpu().numpy()) < 1e-5

@@ -241,3 +241,72 @@ def test_conv_lora_adam_and_grad_accumulation():
     torch.cuda.synchronize()
     expect = p0 - lr * ((1 - b1) * g / (1 - b1)) / (torch.sqrt((1 - b2) * g * g / (1 - b2)) + eps)
     assert torch.allclose(cl.params().double(), expect, rtol=1e-5, atol=1e-7)
+
+
+def _train_steps(obj, fwd, n, lr=1e-3):
+    torch = _torch()
+    for _ in range(n):
+        audio = fwd()
+        obj.zero_grad()
+        obj.backward(torch.sin(audio * 3.0))   # a fixed, data-dependent upstream gradient
+        obj.adam_step(lr)
+
+
+def test_lora_full_state_resume(tmp_path):
+    """save(full_state) then load(full_state) into a fresh object: the next steps
+    match continuing the original (parameters, moments, shared step); the plain
+    readers still read the file."""
+    torch = _torch()
+    cfg, o, p, x, har, ref_s, cond = _case("miniature", 3)
+    dec, a = _make(cfg, "fp32", seed=4)
+    a.params()[a.off_W2:a.off_A[0]].uniform_(-0.3, 0.3)
+    pd = _dev(p)
+    fwd_a = lambda: a.forward(pd, _dev(x["asr"]), _dev(x["F0"]), _dev(x["N"]), _dev(ref_s), _dev(cond),
+                              har=_dev(har))
+    _train_steps(a, fwd_a, 2)
+    path = str(tmp_path / "state.elra")
+    a.save(path, full_state=True)
+    _, b = _make(cfg, "fp32", seed=77)
+    b.load(path, full_state=True)
+    torch.cuda.synchronize()
+    assert b.step == a.step == 2
+    assert torch.equal(a.params(), b.params())
+    fwd_b = lambda: b.forward(pd, _dev(x["asr"]), _dev(x["F0"]), _dev(x["N"]), _dev(ref_s), _dev(cond),
+                              har=_dev(har))
+    _train_steps(a, fwd_a, 2)
+    _train_steps(b, fwd_b, 2)
+    torch.cuda.synchronize()
+    assert b.step == 4
+    assert float((a.params() - b.params()).abs().max()) <= 1e-6 * float(a.params().abs().max())
+    # the plain ELRA1 readers stop before the optimiser state
+    _, c = _make(cfg, "fp32", seed=5)
+    c.load(path)
+    rank, sd, scale, hidden, W1, W2, ads = lo.read_elra1(path)
+    assert len(ads) == c.n_adapters
+    # a plain ELRA1 file has no state to resume from
+    a.save(str(tmp_path / "plain.elra"))
+    from brosoundml_b200._lib import BsmlError
+    with pytest.raises(BsmlError, match="no optimiser state"):
+        c.load(str(tmp_path / "plain.elra"), full_state=True)
+
+
+def test_conv_lora_state_resume(tmp_path):
+    torch = _torch()
+    cfg, o, p, x, har, ref_s, cond = _case("miniature", 4)
+    dec, a = _make_conv(cfg, "fp32", seed=2)
+    pd = _dev(p)
+    fwd_a = lambda: a.forward(pd, _dev(x["asr"]), _dev(x["F0"]), _dev(x["N"]), _dev(x["style"]), har=_dev(har))
+    _train_steps(a, fwd_a, 2)
+    path = str(tmp_path / "conv.eclr")
+    a.save(path)
+    _, b = _make_conv(cfg, "fp32", seed=9)
+    b.load(path)
+    fwd_b = lambda: b.forward(pd, _dev(x["asr"]), _dev(x["F0"]), _dev(x["N"]), _dev(x["style"]), har=_dev(har))
+    _train_steps(a, fwd_a, 2)
+    _train_steps(b, fwd_b, 2)
+    torch.cuda.synchronize()
+    assert float((a.params() - b.params()).abs().max()) <= 1e-6 * float(a.params().abs().max())
+    from brosoundml_b200._lib import BsmlError
+    _, c = _make_conv(cfg, "fp32", rank=4)
+    with pytest.raises(BsmlError, match="architecture mismatch"):
+        c.load(path)
