@@ -128,6 +128,13 @@ class Decoder {
                   float* d_aff = nullptr, void* stream = nullptr) {
         check(bsml_decoder_backward(h_.get(), daudio, grads, d_asr, d_style, d_aff, stream));
     }
+    // Kokoro::Impl::decode_back_half (src/kokoro.cpp:352-407), batched; ref_s rows of
+    // ref_s_stride floats (0 = 2 * style_dim), har from the harmonic source
+    void decode(int B, int T, const float* params, const float* ref_s, const float* asr, const float* F0,
+                const float* N, float* audio, int ref_s_stride = 0, void* stream = nullptr) {
+        check(bsml_decoder_decode(h_.get(), B, T, params, ref_s, ref_s_stride > 0 ? ref_s_stride : 2 * cfg_.style_dim,
+                                  asr, F0, N, audio, stream));
+    }
 
    private:
     impl::Handle h_;
@@ -161,6 +168,52 @@ class Block {
     impl::Handle h_;
     ParamLayout layout_;
     bsml_block_spec spec_{};
+};
+
+// ─── CUDA graph of library calls (capture between begin and end on one stream) ─
+class Graph {
+   public:
+    explicit Graph(void* stream) : stream_(stream) { check(bsml_graph_begin(stream)); }
+    ~Graph() {
+        if (g_) bsml_graph_destroy(g_);
+    }
+    Graph(const Graph&) = delete;
+    Graph& operator=(const Graph&) = delete;
+    void end() { check(bsml_graph_end(stream_, &g_)); }
+    void launch(void* stream) const { check(bsml_graph_launch(g_, stream)); }
+    int64_t kernels() const {
+        int64_t n = 0;
+        check(bsml_graph_kernel_count(g_, &n));
+        return n;
+    }
+
+   private:
+    void* stream_ = nullptr;
+    bsml_graph* g_ = nullptr;
+};
+
+// ─── safetensors checkpoint (host) → flat parameter vector ───────────────────
+class SafeTensors {
+   public:
+    explicit SafeTensors(const std::string& path) { check(bsml_st_open(path.c_str(), &f_)); }
+    ~SafeTensors() { bsml_st_close(f_); }
+    SafeTensors(const SafeTensors&) = delete;
+    SafeTensors& operator=(const SafeTensors&) = delete;
+    // host vector in the layout's order; weight-norm pairs fused
+    std::vector<float> params(const ParamLayout& L, const std::string& prefix = "decoder.module.") const {
+        std::vector<float> p(L.n_params, 0.f);
+        check(bsml_params_from_safetensors(f_, L.table.data(), (int)L.table.size(), prefix.c_str(), p.data(),
+                                           L.n_params));
+        return p;
+    }
+    std::vector<float> read(const std::string& name, int64_t n) const {
+        std::vector<float> v(n);
+        check(bsml_st_read_f32(f_, name.c_str(), v.data(), n));
+        return v;
+    }
+
+   private:
+    bsml_st* f_ = nullptr;
 };
 
 }  // namespace b200
@@ -278,6 +331,9 @@ class DecoderLora {
     }
     void save(const std::string& path) const { b200::check(bsml_lora_save(h_, path.c_str())); }
     void load(const std::string& path) { b200::check(bsml_lora_load(h_, path.c_str())); }
+    // ELRA1 plus Adam's moments and step (a resume point; still readable by load())
+    void save_state(const std::string& path) const { b200::check(bsml_lora_save_state(h_, path.c_str())); }
+    void load_state(const std::string& path) { b200::check(bsml_lora_load_state(h_, path.c_str())); }
 
     int rank() const { return rank_; }
     float scale() const {

@@ -161,6 +161,39 @@ static int gpu_mode(const bsml_decoder_config& cfg, const std::string& dir) {
     std::vector<float> back(lora.n_params());
     cudaMemcpy(back.data(), lora.params(), sizeof(float) * back.size(), cudaMemcpyDeviceToHost);
     EXPECT(std::memcmp(saved.data(), back.data(), sizeof(float) * saved.size()) == 0);
+    // full training state: a fresh object resumes at the same step
+    lora.save_state(dir + "/state.elra");
+    auto resumed = brosoundml::DecoderLora::make(dec, 4, 2.0f, 99);
+    resumed.load_state(dir + "/state.elra");
+    EXPECT(resumed.step() == lora.step());
+    lora.load(dir + "/state.elra");   // the plain reader stops before the optimiser state
+    // decode needs the built-in harmonic source, which this config (har_ch != n_fft + 2) cannot use
+    try {
+        base.decode(B, T, W.p, dR.p, dA.p, dF.p, dN.p, audio.p);
+        return 1;
+    } catch (const std::runtime_error& e) {
+        EXPECT(std::strstr(e.what(), "harmonic source") != nullptr);
+    }
+    // a replayed graph of the base forward reproduces the eager audio
+    cudaStream_t s = nullptr;
+    cudaStreamCreate(&s);
+    base.forward(B, T, W.p, dA.p, dF.p, dN.p, dS.p, dH.p, frames, audio_base.p, nullptr, nullptr, s);
+    cudaStreamSynchronize(s);
+    const auto e0 = audio_base.host();
+    {
+        bb::Graph g(s);
+        base.forward(B, T, W.p, dA.p, dF.p, dN.p, dS.p, dH.p, frames, audio_base.p, nullptr, nullptr, s);
+        g.end();
+        EXPECT(g.kernels() > 10);
+        cudaMemsetAsync(audio_base.p, 0, sizeof(float) * B * S, s);
+        g.launch(s);
+        cudaStreamSynchronize(s);
+    }
+    const auto e1 = audio_base.host();
+    double dn = 0, dd = 0;
+    for (size_t i = 0; i < e0.size(); ++i) { dn += (e1[i] - e0[i]) * (e1[i] - e0[i]); dd += e0[i] * e0[i]; }
+    EXPECT(std::sqrt(dn / dd) < 1e-6);
+    cudaStreamDestroy(s);
     // move-only ownership
     brosoundml::DecoderLora moved = std::move(lora);
     EXPECT(moved.rank() == 4);
