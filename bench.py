@@ -401,6 +401,70 @@ def reference_arm(args):
     print(json.dumps(line), flush=True)
 
 
+SWEEP_B = (1, 4, 16, 64, 256)
+SWEEP_T = (50, 200, 800, 1600)
+SWEEP_MAX_BT = 64 * 400   # B*T of config 3, whose caches (~110 GB) are the largest that fit 180 GB
+
+
+def sweep(args):
+    """BASELINE config 4 on one GPU: full decoder fwd+bwd (CUDA graph) per (B, T),
+    one JSON line each; shapes whose caches exceed one GPU's memory are listed as
+    skipped with the reason."""
+    import gc
+
+    import torch
+
+    from brosoundml_b200.decoder import Decoder
+
+    torch.cuda.set_device(0)
+    torch.cuda.set_stream(torch.cuda.Stream())
+    args.graph = not args.eager
+    dev = torch.device("cuda", 0)
+    math = args.math or Decoder.DEFAULT_MATH
+    peaks = load_peaks()
+    tensor_peak = peaks["bf16_tflops"] if math == "bf16" else peaks["bf16_tflops"] / 2.0
+    for B in SWEEP_B:
+        for T in SWEEP_T:
+            cfgd = {"workload": "BASELINE config 4 sweep: Kokoro-82M decoder fwd+bwd", "global_batch": B,
+                    "seq_len": T, "parallelism": "dp1", "cuda_graph": args.graph}
+            if B * T > SWEEP_MAX_BT:
+                print(json.dumps({"metric": METRIC, "value": None, "unit": UNIT, "n_gpus": 1, "config": cfgd,
+                                  "skipped": f"B*T = {B * T} > {SWEEP_MAX_BT}: the forward caches exceed one "
+                                             "GPU's 180 GB (shard the batch over GPUs)"}), flush=True)
+                continue
+            w = setup_decoder(args, B, T, dev, 0, math)
+            d, step = w["dev"], w["step"]
+            for _ in range(args.warmup):
+                step(d)
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(args.steps):
+                step(d)
+            e1.record()
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1) / args.steps
+            w["prof"].set_profiling(True)
+            w["eager_step"](d)
+            prof = w["prof"].read_profile()
+            w["prof"].set_profiling(False)
+            conv_ms = sum(v[0] for k, v in prof.items() if k.startswith(("conv", "wgrad")))
+            conv_fl = sum(v[1] for k, v in prof.items() if k.startswith(("conv", "wgrad")))
+            tf = conv_fl / (conv_ms / 1e3) / 1e12 if conv_ms > 0 else 0.0
+            nb_ms = prof["norm_bwd"][0]
+            nb_gbs = prof["norm_bwd"][1] / (nb_ms / 1e3) / 1e9 if nb_ms > 0 else 0.0
+            line = {"metric": METRIC, "value": audio_seconds(B, T) / (ms / 1e3), "unit": UNIT, "n_gpus": 1,
+                    "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+                    "dtype": math, "data": "synthetic", "config": cfgd,
+                    "roofline": {"conv_tflops": tf, "conv_frac": tf / tensor_peak,
+                                 "norm_bwd_gbs": nb_gbs, "norm_bwd_frac": nb_gbs / peaks["hbm_gbs"],
+                                 "conv_share": conv_ms / ms, "peak_source": peaks["source"]}}
+            print(json.dumps(line), flush=True)
+            del w, d, step
+            gc.collect()
+            torch.cuda.synchronize()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -411,6 +475,8 @@ def main():
     ap.add_argument("--math", default=None, choices=["fp32", "tf32x3", "bf16"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--sweep", action="store_true",
+                    help="BASELINE config 4: one JSON line per (B, T) of the shape sweep that fits one GPU")
     ap.add_argument("--eager", action="store_true",
                     help="launch every kernel from the host instead of replaying forward + loss + backward as "
                          "one CUDA graph (decoder workloads)")
@@ -419,6 +485,9 @@ def main():
 
     if args.impl == "reference":
         reference_arm(args)
+        return
+    if args.sweep:
+        sweep(args)
         return
 
     import numpy as np
