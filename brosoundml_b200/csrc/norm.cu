@@ -24,6 +24,10 @@ namespace {
 
 constexpr int NT = 256;   // threads per CTA
 constexpr int UNR = 4;    // rows whose loads a thread issues before it stores (memory-level parallelism)
+// the two passes of the AdaIN backward trade occupancy for loads in flight: 2 CTAs
+// per SM with more rows each measured faster on B200 than 3-4 CTAs with fewer
+constexpr int RR_UNR = 6;    // adain_recompute_reduce_kernel: rows of (x, dy) loads in flight
+constexpr int APPLY_ROWS = 4;  // adain_bwd_apply_kernel: rows of (x, dy, skip) loads in flight
 
 struct Out4 {
     float* y = nullptr; int64_t y_bs = 0; int y_ld = 0;                 // fp32 output (nullable)
@@ -280,7 +284,7 @@ __global__ void __launch_bounds__(NT, 4) adain_bwd_reduce_kernel(Act x, int rows
 // o = act(z) (the weight gradient's operand, recomputed instead of cached) and
 // acc += sum dz, sum dz * xhat, sum dy * d act / d alpha, from one read of x and dy.
 template <int ACT>
-__global__ void __launch_bounds__(NT, 3) adain_recompute_reduce_kernel(Act x, int rows, const float* mean,
+__global__ void __launch_bounds__(NT, 2) adain_recompute_reduce_kernel(Act x, int rows, const float* mean,
                                                                        const float* rstd, const float* gb,
                                                                        float slope, const float* alpha, Act dy,
                                                                        double* acc, Out4 o) {
@@ -314,15 +318,15 @@ __global__ void __launch_bounds__(NT, 3) adain_recompute_reduce_kernel(Act x, in
             };
             const int dl = blockDim.y;
             int l = l0 + threadIdx.y;
-            for (; l + (UNR - 1) * dl < l1; l += UNR * dl) {
-                float4 a[UNR], g[UNR];
+            for (; l + (RR_UNR - 1) * dl < l1; l += RR_UNR * dl) {
+                float4 a[RR_UNR], g[RR_UNR];
 #pragma unroll
-                for (int u = 0; u < UNR; ++u) {
+                for (int u = 0; u < RR_UNR; ++u) {
                     a[u] = ldg4(xb + (int64_t)(l + u * dl) * x.ld);
                     g[u] = ldg4(gbp + (int64_t)(l + u * dl) * dy.ld);
                 }
 #pragma unroll
-                for (int u = 0; u < UNR; ++u) row(a[u], g[u], l + u * dl);
+                for (int u = 0; u < RR_UNR; ++u) row(a[u], g[u], l + u * dl);
             }
             for (; l < l1; l += dl) row(ldg4(xb + (int64_t)l * x.ld), ldg4(gbp + (int64_t)l * dy.ld), l);
 #pragma unroll
@@ -336,7 +340,7 @@ __global__ void __launch_bounds__(NT, 3) adain_recompute_reduce_kernel(Act x, in
 
 // out = rstd * g1 * (dz - mean(dz) - xhat * mean(dz * xhat)) (+ skip); colsum[c] += sum out
 template <int ACT>
-__global__ void __launch_bounds__(NT, 3) adain_bwd_apply_kernel(Act x, int rows, const float* mean, const float* rstd,
+__global__ void __launch_bounds__(NT, 2) adain_bwd_apply_kernel(Act x, int rows, const float* mean, const float* rstd,
                                                              const float* gb, float slope, const float* alpha, Act dy,
                                                              const double* acc, Out4 o, double* colsum) {
     const int b = blockIdx.y;
@@ -377,7 +381,7 @@ __global__ void __launch_bounds__(NT, 3) adain_bwd_apply_kernel(Act x, int rows,
                 return o.skip ? ld4(o.skip + (int64_t)b * o.s_bs + (int64_t)l * o.s_ld + c0)
                               : make_float4(0.f, 0.f, 0.f, 0.f);
             };
-            constexpr int U2 = UNR / 2;   // three loads per row
+            constexpr int U2 = APPLY_ROWS;   // up to three loads per row
             const int dl = blockDim.y;
             int l = l0 + threadIdx.y;
             for (; l + (U2 - 1) * dl < l1; l += U2 * dl) {
