@@ -422,7 +422,7 @@ def sweep(args):
     dev = torch.device("cuda", 0)
     math = args.math or Decoder.DEFAULT_MATH
     peaks = load_peaks()
-    tensor_peak = peaks["bf16_tflops"] if math == "bf16" else peaks["bf16_tflops"] / 2.0
+    tensor_peak = peaks["bf16_tflops_sustained"]   # measured dense bf16, sustained
     for B in SWEEP_B:
         for T in SWEEP_T:
             cfgd = {"workload": "BASELINE config 4 sweep: Kokoro-82M decoder fwd+bwd", "global_batch": B,
@@ -597,26 +597,31 @@ def main():
         else:
             rl_all[k] = {"ms": pms, "launches": n, "gbs": work / (pms / 1e3) / 1e9, "share": pms / ms}
     dom = max(rl_all, key=lambda k: rl_all[k]["ms"])
-    tensor_peak = peaks["bf16_tflops"] if math == "bf16" else peaks["bf16_tflops"] / 2.0
+    # the measured dense bf16 figure is the tensor roofline (sustained: these kernels run
+    # inside a long step); TF32 operands run at half that rate on the same pipe
+    bf16_peak = peaks["bf16_tflops_sustained"]
     if dom.startswith(("conv", "wgrad")):
         ach = rl_all[dom]["tflops"]
         traffic = None
-        note = f"dominant kernel class '{dom}'; achieved = useful conv FLOPs / CUDA-event time; "
+        note = (f"dominant kernel class '{dom}'; achieved = useful conv FLOPs / CUDA-event time; peak = "
+                f"{peaks['source']} dense bf16 (sustained)")
+        extra = {}
         if dom.endswith("_simt"):
-            note += f"runs on fp32 CUDA cores; peak = tf32 dense (half the {peaks['source']} bf16 cuBLAS figure)"
-        elif math == "bf16":
-            note += f"peak = {peaks['source']} bf16 dense"
-        else:
-            note += (f"peak = {peaks['source']} tf32 dense (bf16/2); TF32x3 issues 3 tensor products per useful "
-                     f"one, so the tensor pipe runs {3 * ach / tensor_peak:.0%} busy at this rate")
+            note += "; this class runs on fp32 CUDA cores"
+        elif math != "bf16":
+            tf32_peak = bf16_peak / 2.0
+            extra = {"tf32_peak": tf32_peak, "frac_of_tf32_peak": ach / tf32_peak,
+                     "tensor_pipe_frac_issued": 3.0 * ach / tf32_peak}
+            note += (f"; TF32x3 (fp32-grade) runs tf32 operands, whose dense rate is half of bf16, and issues "
+                     f"3 tensor products per useful one: {3 * ach / tf32_peak:.0%} of the tf32 rate is issued")
             if dom == "conv_tc":
                 # DRAM bytes per FLOP of conv_fwd_tc_kernel from one ncu capture of the probe case
                 # (python -m brosoundml_b200.kernel_probe --B 16 --C 128 --L 24001 --k 7 --d 3 --math tf32x3),
                 # scaled to this class's average launch by its FLOPs
                 traffic = NCU_CONV_FWD_TC["dram_bytes"] / NCU_CONV_FWD_TC["flops"] * rl_all[dom]["flops_per_launch"]
                 note += "; traffic scaled from the ncu capture of the probe case by FLOPs"
-        roofline = {"bound": "tensor", "achieved": ach, "peak": tensor_peak, "unit": "TFLOP/s",
-                    "frac": ach / tensor_peak, "traffic": traffic, "note": note}
+        roofline = dict({"bound": "tensor", "achieved": ach, "peak": bf16_peak, "unit": "TFLOP/s",
+                         "frac": ach / bf16_peak, "traffic": traffic, "note": note}, **extra)
     else:
         ach = rl_all[dom]["gbs"]
         roofline = {"bound": "hbm", "achieved": ach, "peak": peaks["hbm_gbs"], "unit": "GB/s",
