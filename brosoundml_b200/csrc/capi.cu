@@ -77,7 +77,10 @@ bool atom_tc(int K, int M, int s) { return g_atom_math.load() != BSML_MATH_FP32_
 bool atom_convT_tc(int Ci, int Co, int s, int Lu) {
     return g_atom_math.load() != BSML_MATH_FP32_SIMT && Ci >= 64 && s * Co >= 32 && Co % 8 == 0 && Lu % s == 0;
 }
-int atom_tc_mode() { return g_atom_math.load() == BSML_MATH_BF16 ? bsml::TC_BF16 : bsml::TC_TF32X3; }
+int atom_tc_mode() {
+    const int m = g_atom_math.load();
+    return m == BSML_MATH_BF16 ? bsml::TC_BF16 : m == BSML_MATH_BF16X3 ? bsml::TC_BF16X3 : bsml::TC_TF32X3;
+}
 
 // Tensor-core forward-like conv for the atoms: planes of x, packed weight planes, launch.
 void atom_tc_conv(Scratch& sc, const bsml::Act& xa, const float* W, int kind, int Co_w, int Ci_w, int k, int s_ph,
@@ -283,7 +286,8 @@ int64_t bsml_launch_count(void) { return bsml::launch_count(); }
 
 int bsml_set_atom_math(int math_mode) {
     return guarded([&] {
-        need(math_mode == BSML_MATH_FP32_SIMT || math_mode == BSML_MATH_TF32X3 || math_mode == BSML_MATH_BF16,
+        need(math_mode == BSML_MATH_FP32_SIMT || math_mode == BSML_MATH_TF32X3 || math_mode == BSML_MATH_BF16 ||
+                 math_mode == BSML_MATH_BF16X3,
              "bsml_set_atom_math", "unknown math mode");
         g_atom_math.store(math_mode);
     });

@@ -54,10 +54,22 @@ __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
 }
 
 // ── forward-like kernel ──────────────────────────────────────────────────────
-template <bool TF32, int NP>
+// Operand format of a mode: fp32 containers read by tf32 MMAs (TF32X3, planes hi +
+// lo) or bf16 (BF16: one plane; BF16X3: hi + lo planes). Two planes issue the three
+// products hi*hi + hi*lo + lo*hi per K step.
+template <int MODE>
+struct Fmt {
+    static constexpr bool F32 = MODE == TC_TF32X3;
+    static constexpr bool LO = MODE != TC_BF16;
+    static constexpr int PLANES = LO ? 2 : 1;
+    static constexpr int BKE = F32 ? 32 : 64;             // elements per 128-byte row
+    static constexpr uint32_t KIND = F32 ? 2u : 1u;       // instruction-descriptor A/B format
+};
+
+template <int MODE, int NP>
 struct FCfg {
-    static constexpr int BKE = TF32 ? 32 : 64;            // channels per 128-byte row
-    static constexpr int PLANES = TF32 ? 2 : 1;
+    static constexpr int BKE = Fmt<MODE>::BKE;            // channels per 128-byte row
+    static constexpr int PLANES = Fmt<MODE>::PLANES;
     static constexpr int NPOS = NP;                        // positions per tile (MMA N): 256, 224 or 192
     static constexpr int HALF = NP / 2;                    // columns per epilogue warp (multiple of 16)
     static constexpr int WT_BYTES = PLANES * TILE_BYTES;   // one weight stage: 128 co x 128 B per plane
@@ -81,12 +93,13 @@ struct FArgs {
 
 // 320 threads = 10 warps, so one SM sub-partition holds 3 of them: 168
 // registers per thread at most (3 x 32 x 168 <= 16384).
-template <bool TF32, int NPT>
-__global__ void __launch_bounds__(FCfg<TF32, NPT>::THREADS, 1)
+template <int MODE, int NPT>
+__global__ void __launch_bounds__(FCfg<MODE, NPT>::THREADS, 1)
     conv_fwd_tc_kernel(const __grid_constant__ CUtensorMap mWh, const __grid_constant__ CUtensorMap mWl,
                        const __grid_constant__ CUtensorMap mXh, const __grid_constant__ CUtensorMap mXl,
                        const FArgs a) {
-    using F = FCfg<TF32, NPT>;
+    using F = FCfg<MODE, NPT>;
+    constexpr bool LO = Fmt<MODE>::LO, F32E = Fmt<MODE>::F32;
     constexpr int NP = F::NPOS, HC = F::HALF;
     constexpr uint32_t TCOLS = 512;   // two promotion buffers of NP fp32 columns (allocation: a power of 2)
     extern __shared__ uint8_t smem_raw[];
@@ -124,7 +137,7 @@ __global__ void __launch_bounds__(FCfg<TF32, NPT>::THREADS, 1)
         tc::fence_barrier_init();
         tc::prefetch_tmap(&mWh);
         tc::prefetch_tmap(&mXh);
-        if (TF32) {
+        if (LO) {
             tc::prefetch_tmap(&mWl);
             tc::prefetch_tmap(&mXl);
         }
@@ -158,7 +171,7 @@ __global__ void __launch_bounds__(FCfg<TF32, NPT>::THREADS, 1)
                     tc::mbar_arrive_expect_tx(&xfull[xs], a.win_bytes);
                     tc::tma_load_3d(wb, &mXh, &xfull[xs], kx, row0, b);
                     tc::tma_load_3d(wb + a.wbox * 128, &mXh, &xfull[xs], kx, row0 + a.wbox, b);
-                    if (TF32) {
+                    if (LO) {
                         tc::tma_load_3d(wb + plane_bytes, &mXl, &xfull[xs], kx, row0, b);
                         tc::tma_load_3d(wb + plane_bytes + a.wbox * 128, &mXl, &xfull[xs], kx, row0 + a.wbox, b);
                     }
@@ -172,7 +185,7 @@ __global__ void __launch_bounds__(FCfg<TF32, NPT>::THREADS, 1)
                         uint8_t* ws = wst + s * F::WT_BYTES;
                         tc::mbar_arrive_expect_tx(&wfull[s], F::WT_BYTES);
                         tc::tma_load_3d(ws, &mWh, &wfull[s], kx, m0, t);
-                        if (TF32) tc::tma_load_3d(ws + TILE_BYTES, &mWl, &wfull[s], kx, m0, t);
+                        if (LO) tc::tma_load_3d(ws + TILE_BYTES, &mWl, &wfull[s], kx, m0, t);
                         ++kit;
                     }
                 }
@@ -187,7 +200,7 @@ __global__ void __launch_bounds__(FCfg<TF32, NPT>::THREADS, 1)
     } else if (warp == 1) {
         if (lane == 0) {
             // ── MMA issuer
-            constexpr uint32_t idesc = tc::make_idesc(TF32 ? 2u : 1u, 0u, 0u, 128, NP);
+            constexpr uint32_t idesc = tc::make_idesc(Fmt<MODE>::KIND, 0u, 0u, 128, NP);
             int kit = 0, cw = 0, G = 0;
             bool ok = true;
             for (int tile = blockIdx.x; ok && tile < a.n_tiles; tile += gridDim.x) {
@@ -225,12 +238,12 @@ __global__ void __launch_bounds__(FCfg<TF32, NPT>::THREADS, 1)
                             const uint64_t dAh = tc::desc_kmajor_sw128(wa + kk * 32);
                             const uint64_t dBh = tc::desc_kmajor_sw128(xh + roff + kk * 32);
                             const uint32_t acc = (g_first && kk == 0) ? 0u : 1u;
-                            tc::umma<TF32>(d_tmem, dAh, dBh, idesc, acc);
-                            if (TF32) {
+                            tc::umma<F32E>(d_tmem, dAh, dBh, idesc, acc);
+                            if (LO) {
                                 const uint64_t dAl = tc::desc_kmajor_sw128(wa + TILE_BYTES + kk * 32);
                                 const uint64_t dBl = tc::desc_kmajor_sw128(xl + roff + kk * 32);
-                                tc::umma<TF32>(d_tmem, dAh, dBl, idesc, 1u);
-                                tc::umma<TF32>(d_tmem, dAl, dBh, idesc, 1u);
+                                tc::umma<F32E>(d_tmem, dAh, dBl, idesc, 1u);
+                                tc::umma<F32E>(d_tmem, dAl, dBh, idesc, 1u);
                             }
                         }
                         tc::umma_commit(&wempty[s]);   // frees the weight stage once these MMAs have read it
@@ -358,13 +371,13 @@ __global__ void __launch_bounds__(FCfg<TF32, NPT>::THREADS, 1)
 // (a descriptor offset), so the dY chunk and the X rows serve both taps.
 constexpr int BM = 128, BN = 128;
 
-template <bool TF32>
+template <int MODE>
 struct WCfg {
-    static constexpr int PLANES = TF32 ? 2 : 1;
-    static constexpr int BKE = TF32 ? 32 : 64;        // elements per 128-byte row
+    static constexpr int PLANES = Fmt<MODE>::PLANES;
+    static constexpr int BKE = Fmt<MODE>::BKE;        // elements per 128-byte row
     // positions (K rows) per stage; one MMA consumes 32 bytes of K = 8 (tf32)
     // or 16 (bf16) rows; 128-byte column blocks per 128-wide operand
-    static constexpr int KROWS = TF32 ? 32 : 64;
+    static constexpr int KROWS = Fmt<MODE>::F32 ? 32 : 64;
     static constexpr int MN_BLOCKS = 128 / BKE;
     static constexpr int A_BYTES = PLANES * MN_BLOCKS * KROWS * 128;   // dY chunk, all planes
     static constexpr int NEPI = 8;                                      // 4 lane quarters x 2 taps
@@ -382,12 +395,13 @@ struct WArgs {
     float* part;      // [split][Co][Ci][tap]
 };
 
-template <bool TF32>
-__global__ void __launch_bounds__(WCfg<TF32>::THREADS, 1)
+template <int MODE>
+__global__ void __launch_bounds__(WCfg<MODE>::THREADS, 1)
     conv_wgrad_tc_kernel(const __grid_constant__ CUtensorMap mAh, const __grid_constant__ CUtensorMap mAl,
                          const __grid_constant__ CUtensorMap mBh, const __grid_constant__ CUtensorMap mBl,
                          const WArgs a) {
-    using C = WCfg<TF32>;
+    using C = WCfg<MODE>;
+    constexpr bool LO = Fmt<MODE>::LO, F32E = Fmt<MODE>::F32;
     constexpr uint32_t TCOLS = 4 * BN;   // 2 taps x 2 promotion buffers
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = align1024(smem_raw);
@@ -427,7 +441,7 @@ __global__ void __launch_bounds__(WCfg<TF32>::THREADS, 1)
         tc::fence_barrier_init();
         tc::prefetch_tmap(&mAh);
         tc::prefetch_tmap(&mBh);
-        if (TF32) {
+        if (LO) {
             tc::prefetch_tmap(&mAl);
             tc::prefetch_tmap(&mBl);
         }
@@ -461,7 +475,7 @@ __global__ void __launch_bounds__(WCfg<TF32>::THREADS, 1)
                 for (int j = 0; j < C::MN_BLOCKS; ++j) {
                     tc::tma_load_3d(st + j * C::KROWS * 128, &mAh, &full[s], m0 + j * C::BKE, orow, bb);
                     tc::tma_load_3d(sB + j * a.wrows * 128, &mBh, &full[s], n0 + j * C::BKE, xrow, bb);
-                    if (TF32) {
+                    if (LO) {
                         tc::tma_load_3d(st + C::A_BYTES / 2 + j * C::KROWS * 128, &mAl, &full[s], m0 + j * C::BKE,
                                         orow, bb);
                         tc::tma_load_3d(sB + xplane + j * a.wrows * 128, &mBl, &full[s], n0 + j * C::BKE, xrow, bb);
@@ -477,7 +491,7 @@ __global__ void __launch_bounds__(WCfg<TF32>::THREADS, 1)
     } else if (warp == 1) {
         if (lane == 0) {
             // ── MMA issuer
-            constexpr uint32_t idesc = tc::make_idesc(TF32 ? 2u : 1u, 1u, 1u, BM, BN);
+            constexpr uint32_t idesc = tc::make_idesc(Fmt<MODE>::KIND, 1u, 1u, BM, BN);
             const uint32_t lbo_a = C::KROWS * 128, lbo_b = (uint32_t)a.wrows * 128;
             for (int it = 0; it < n_iters; ++it) {
                 const int s = it % a.stages;
@@ -500,16 +514,16 @@ __global__ void __launch_bounds__(WCfg<TF32>::THREADS, 1)
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk) {
                         // +32 bytes of K = 8 rows (tf32) or 16 rows (bf16) = 1024 / 2048 B
-                        const uint32_t off = kk * (TF32 ? 1024 : 2048);
-                        const uint64_t dAh = tc::desc_mnmajor(aH + off, lbo_a, TF32);
-                        const uint64_t dBh = tc::desc_mnmajor(bH + bshift + off, lbo_b, TF32);
+                        const uint32_t off = kk * (F32E ? 1024 : 2048);
+                        const uint64_t dAh = tc::desc_mnmajor(aH + off, lbo_a, F32E);
+                        const uint64_t dBh = tc::desc_mnmajor(bH + bshift + off, lbo_b, F32E);
                         const uint32_t acc = (g_first && kk == 0) ? 0u : 1u;
-                        tc::umma<TF32>(d_tmem, dAh, dBh, idesc, acc);
-                        if (TF32) {
-                            const uint64_t dAl = tc::desc_mnmajor(aL + off, lbo_a, TF32);
-                            const uint64_t dBl = tc::desc_mnmajor(bL + bshift + off, lbo_b, TF32);
-                            tc::umma<TF32>(d_tmem, dAh, dBl, idesc, 1u);
-                            tc::umma<TF32>(d_tmem, dAl, dBh, idesc, 1u);
+                        tc::umma<F32E>(d_tmem, dAh, dBh, idesc, acc);
+                        if (LO) {
+                            const uint64_t dAl = tc::desc_mnmajor(aL + off, lbo_a, F32E);
+                            const uint64_t dBl = tc::desc_mnmajor(bL + bshift + off, lbo_b, F32E);
+                            tc::umma<F32E>(d_tmem, dAh, dBl, idesc, 1u);
+                            tc::umma<F32E>(d_tmem, dAl, dBh, idesc, 1u);
                         }
                     }
                 }
@@ -571,7 +585,23 @@ __global__ void __launch_bounds__(WCfg<TF32>::THREADS, 1)
 
 // ── operand planes
 
-template <bool TF32>
+// v as the operand planes of MODE at element o
+template <int MODE>
+__device__ __forceinline__ void put_planes(void* hi, void* lo, int64_t o, float v) {
+    if (MODE == TC_TF32X3) {
+        const float h = tf32_rna(v);
+        static_cast<float*>(hi)[o] = h;
+        static_cast<float*>(lo)[o] = v - h;
+    } else if (MODE == TC_BF16X3) {
+        const __nv_bfloat16 h = __float2bfloat16_rn(v);
+        static_cast<__nv_bfloat16*>(hi)[o] = h;
+        static_cast<__nv_bfloat16*>(lo)[o] = __float2bfloat16_rn(v - __bfloat162float(h));
+    } else {
+        static_cast<__nv_bfloat16*>(hi)[o] = __float2bfloat16_rn(v);
+    }
+}
+
+template <int MODE>
 __global__ void act_planes_kernel(Act x, void* hi, void* lo, int ld) {
     const int64_t n = x.numel();
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
@@ -580,18 +610,12 @@ __global__ void act_planes_kernel(Act x, void* hi, void* lo, int ld) {
         const int l = (int)(r % x.L), b = (int)(r / x.L);
         const float v = x.row(b, l)[c];
         const int64_t o = ((int64_t)b * x.L + l) * ld + c;
-        if (TF32) {
-            const float h = tf32_rna(v);
-            static_cast<float*>(hi)[o] = h;
-            static_cast<float*>(lo)[o] = v - h;
-        } else {
-            static_cast<__nv_bfloat16*>(hi)[o] = __float2bfloat16_rn(v);
-        }
+        put_planes<MODE>(hi, lo, o, v);
     }
 }
 
 // Element i of one packed weight: [tap][M][Kp] with zero padding of K to Kp.
-template <bool TF32>
+template <int MODE>
 __device__ __forceinline__ void pack_one(const float* W, int kind, int Co, int Ci, int k, int s, int r, int taps,
                                          int M, int K, int Kp, void* hi, void* lo, int64_t i) {
     const int kk = (int)(i % Kp);
@@ -613,26 +637,20 @@ __device__ __forceinline__ void pack_one(const float* W, int kind, int Co, int C
             if (tt >= 0 && tt < k) v = W[((int64_t)m * Co + co) * k + tt];
         }
     }
-    if (TF32) {
-        const float h = tf32_rna(v);
-        static_cast<float*>(hi)[i] = h;
-        static_cast<float*>(lo)[i] = v - h;
-    } else {
-        static_cast<__nv_bfloat16*>(hi)[i] = __float2bfloat16_rn(v);
-    }
+    put_planes<MODE>(hi, lo, i, v);
 }
 
-template <bool TF32>
+template <int MODE>
 __global__ void pack_w_kernel(const float* W, int kind, int Co, int Ci, int k, int s, int r, int taps, int M, int K,
                               int Kp, void* hi, void* lo) {
     const int64_t n = (int64_t)taps * M * Kp;
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
-        pack_one<TF32>(W, kind, Co, Ci, k, s, r, taps, M, K, Kp, hi, lo, i);
+        pack_one<MODE>(W, kind, Co, Ci, k, s, r, taps, M, K, Kp, hi, lo, i);
 }
 
 // All jobs of a batch over one flat index space; each thread finds its job by
 // binary search over the jobs' starts (held in shared memory).
-template <bool TF32>
+template <int MODE>
 __global__ void pack_w_batch_kernel(const float* params, const PackJob* jobs, int n_jobs, int64_t total) {
     __shared__ int64_t start[PACK_MAX_JOBS];
     for (int j = threadIdx.x; j < n_jobs; j += blockDim.x) start[j] = jobs[j].start;
@@ -645,7 +663,7 @@ __global__ void pack_w_batch_kernel(const float* params, const PackJob* jobs, in
             else hi = mid - 1;
         }
         const PackJob& J = jobs[lo];
-        pack_one<TF32>(params + J.w_off, J.kind, J.Co, J.Ci, J.k, J.s, J.r, J.taps, J.M, J.K, J.Kp, J.hi, J.lo,
+        pack_one<MODE>(params + J.w_off, J.kind, J.Co, J.Ci, J.k, J.s, J.r, J.taps, J.M, J.K, J.Kp, J.hi, J.lo,
                        i - start[lo]);
     }
 }
@@ -710,7 +728,7 @@ CUtensorMap make_map(const void* base, int mode, uint64_t d0, uint64_t d1, uint6
     cuuint32_t box[3] = {box0, box1, 1};
     cuuint32_t estr[3] = {1, 1, 1};
     const CUtensorMapDataType dt =
-        mode == TC_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+        mode == TC_TF32X3 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
     if ((reinterpret_cast<uintptr_t>(base) & 15) != 0) fail("conv_tc", "operand base not 16-byte aligned");
     if (box0 * es != 128) fail("conv_tc", "box inner extent must be 128 bytes");
     const CUresult rc = get_encode()(&m, dt, 3, const_cast<void*>(base), dims, strides, box, estr,
@@ -736,8 +754,8 @@ int sm_count() {
 struct FwdGeom {
     int np, wbox, win_bytes, sw, smem;
 };
-FwdGeom fwd_geom(bool tf32, int halo) {
-    const int planes = tf32 ? 2 : 1, wt = planes * TILE_BYTES, fixed = 1024 + 256;
+FwdGeom fwd_geom(int planes, int halo) {
+    const int wt = planes * TILE_BYTES, fixed = 1024 + 256;
     FwdGeom g{};
     for (int np : {256, 224, 192}) {
         g.np = np;
@@ -752,12 +770,13 @@ FwdGeom fwd_geom(bool tf32, int halo) {
     return g;
 }
 
-template <bool TF32, int NPT>
+template <int MODE, int NPT>
 void launch_fwd_np(const TcConvFwd& c, int mode, const FwdGeom& g, cudaStream_t st) {
-    using F = FCfg<TF32, NPT>;
+    using F = FCfg<MODE, NPT>;
+    constexpr bool LO = Fmt<MODE>::LO;
     static bool attr = false;
     if (!attr) {
-        BSML_CUDA(cudaFuncSetAttribute(conv_fwd_tc_kernel<TF32, NPT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        BSML_CUDA(cudaFuncSetAttribute(conv_fwd_tc_kernel<MODE, NPT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        SMEM_OPTIN));
         attr = true;
     }
@@ -767,9 +786,9 @@ void launch_fwd_np(const TcConvFwd& c, int mode, const FwdGeom& g, cudaStream_t 
     a.sw = g.sw;
     const uint32_t bke = F::BKE;
     const CUtensorMap mWh = make_map(c.w.hi, mode, c.Ci, c.Co, c.taps, c.w.ld, c.Co, bke, 128);
-    const CUtensorMap mWl = TF32 ? make_map(c.w.lo, mode, c.Ci, c.Co, c.taps, c.w.ld, c.Co, bke, 128) : mWh;
+    const CUtensorMap mWl = LO ? make_map(c.w.lo, mode, c.Ci, c.Co, c.taps, c.w.ld, c.Co, bke, 128) : mWh;
     const CUtensorMap mXh = make_map(c.x.hi, mode, c.Ci, c.L_in, c.B, c.x.ld, c.L_in, bke, a.wbox);
-    const CUtensorMap mXl = TF32 ? make_map(c.x.lo, mode, c.Ci, c.L_in, c.B, c.x.ld, c.L_in, bke, a.wbox) : mXh;
+    const CUtensorMap mXl = LO ? make_map(c.x.lo, mode, c.Ci, c.L_in, c.B, c.x.ld, c.L_in, bke, a.wbox) : mXh;
     a.No = c.No; a.o_base = c.o_base; a.p = c.p; a.d = c.d; a.taps = c.taps;
     a.kchunks = (int)ceil_div(c.Ci, F::BKE);
     a.Co = c.Co;
@@ -790,27 +809,28 @@ void launch_fwd_np(const TcConvFwd& c, int mode, const FwdGeom& g, cudaStream_t 
         fail("conv_fwd_tc", "clip too long for 32-bit row offsets");
     const int grid = (int)std::min<int64_t>(tiles, sm_count());
     ::bsml::count_launch();
-    conv_fwd_tc_kernel<TF32, NPT><<<grid, F::THREADS, g.smem, st>>>(mWh, mWl, mXh, mXl, a);
+    conv_fwd_tc_kernel<MODE, NPT><<<grid, F::THREADS, g.smem, st>>>(mWh, mWl, mXh, mXl, a);
     BSML_LAUNCH("conv_fwd_tc");
 }
 
-template <bool TF32>
+template <int MODE>
 void launch_fwd(const TcConvFwd& c, int mode, cudaStream_t st) {
-    const FwdGeom g = fwd_geom(TF32, (c.taps - 1) * c.d);
+    const FwdGeom g = fwd_geom(Fmt<MODE>::PLANES, (c.taps - 1) * c.d);
     if (g.np == 256)
-        launch_fwd_np<TF32, 256>(c, mode, g, st);
+        launch_fwd_np<MODE, 256>(c, mode, g, st);
     else if (g.np == 224)
-        launch_fwd_np<TF32, 224>(c, mode, g, st);
+        launch_fwd_np<MODE, 224>(c, mode, g, st);
     else
-        launch_fwd_np<TF32, 192>(c, mode, g, st);
+        launch_fwd_np<MODE, 192>(c, mode, g, st);
 }
 
-template <bool TF32>
+template <int MODE>
 void launch_wgrad(const TcConvWgrad& c, int mode, float* part, int64_t part_cap, cudaStream_t st) {
-    using CF = WCfg<TF32>;
+    using CF = WCfg<MODE>;
+    constexpr bool LO = Fmt<MODE>::LO, F32E = Fmt<MODE>::F32;
     static bool attr = false;
     if (!attr) {
-        BSML_CUDA(cudaFuncSetAttribute(conv_wgrad_tc_kernel<TF32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        BSML_CUDA(cudaFuncSetAttribute(conv_wgrad_tc_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        SMEM_OPTIN));
         attr = true;
     }
@@ -826,11 +846,11 @@ void launch_wgrad(const TcConvWgrad& c, int mode, float* part, int64_t part_cap,
     const int smem = a.stages * a.stage_bytes + fixed;
     const uint32_t bke = CF::BKE, kr = CF::KROWS;
     // A: dY planes [B][Lo][ld] (M = Co along the contiguous dim); B: X planes (N = Ci)
-    const CUtensorMap mAh = make_map(c.dy.hi, mode, c.Co, c.Lo, c.B, c.dy.ld, c.Lo, bke, kr, TF32);
-    const CUtensorMap mAl = TF32 ? make_map(c.dy.lo, mode, c.Co, c.Lo, c.B, c.dy.ld, c.Lo, bke, kr, TF32) : mAh;
-    const CUtensorMap mBh = make_map(c.x.hi, mode, c.Ci, c.L_in, c.B, c.x.ld, c.L_in, bke, a.wrows, TF32);
+    const CUtensorMap mAh = make_map(c.dy.hi, mode, c.Co, c.Lo, c.B, c.dy.ld, c.Lo, bke, kr, F32E);
+    const CUtensorMap mAl = LO ? make_map(c.dy.lo, mode, c.Co, c.Lo, c.B, c.dy.ld, c.Lo, bke, kr, F32E) : mAh;
+    const CUtensorMap mBh = make_map(c.x.hi, mode, c.Ci, c.L_in, c.B, c.x.ld, c.L_in, bke, a.wrows, F32E);
     const CUtensorMap mBl =
-        TF32 ? make_map(c.x.lo, mode, c.Ci, c.L_in, c.B, c.x.ld, c.L_in, bke, a.wrows, TF32) : mBh;
+        LO ? make_map(c.x.lo, mode, c.Ci, c.L_in, c.B, c.x.ld, c.L_in, bke, a.wrows, F32E) : mBh;
     a.n_ci_tiles = (int)ceil_div(c.Ci, BN);
     a.n_pairs = (int)ceil_div(c.taps, 2);
     a.chunks_pc = (int)ceil_div(c.Lo, CF::KROWS);
@@ -846,7 +866,7 @@ void launch_wgrad(const TcConvWgrad& c, int mode, float* part, int64_t part_cap,
     a.part = part;
     dim3 grid((unsigned)ceil_div(c.Co, BM), (unsigned)(a.n_ci_tiles * a.n_pairs), (unsigned)splits);
     ::bsml::count_launch();
-    conv_wgrad_tc_kernel<TF32><<<grid, CF::THREADS, smem, st>>>(mAh, mAl, mBh, mBl, a);
+    conv_wgrad_tc_kernel<MODE><<<grid, CF::THREADS, smem, st>>>(mAh, mAl, mBh, mBl, a);
     BSML_LAUNCH("conv_wgrad_tc");
     ::bsml::count_launch();
     if (c.ct_s > 0) {
@@ -873,9 +893,11 @@ void make_act_planes(const Act& x, int mode, void* hi, void* lo, cudaStream_t st
     }
     ::bsml::count_launch();
     if (mode == TC_TF32X3)
-        act_planes_kernel<true><<<grid_for(x.numel()), 256, 0, st>>>(x, hi, lo, ld);
+        act_planes_kernel<TC_TF32X3><<<grid_for(x.numel()), 256, 0, st>>>(x, hi, lo, ld);
+    else if (mode == TC_BF16X3)
+        act_planes_kernel<TC_BF16X3><<<grid_for(x.numel()), 256, 0, st>>>(x, hi, lo, ld);
     else
-        act_planes_kernel<false><<<grid_for(x.numel()), 256, 0, st>>>(x, hi, lo, ld);
+        act_planes_kernel<TC_BF16><<<grid_for(x.numel()), 256, 0, st>>>(x, hi, lo, ld);
     BSML_LAUNCH("make_act_planes");
 }
 
@@ -899,9 +921,11 @@ void pack_w_tc_batch(const float* params, const PackJob* jobs, int n_jobs, int64
     if (n_jobs > PACK_MAX_JOBS) fail("pack_w_tc_batch", "too many jobs in one batch");
     ::bsml::count_launch();
     if (mode == TC_TF32X3)
-        pack_w_batch_kernel<true><<<grid_for(total), 256, 0, st>>>(params, jobs, n_jobs, total);
+        pack_w_batch_kernel<TC_TF32X3><<<grid_for(total), 256, 0, st>>>(params, jobs, n_jobs, total);
+    else if (mode == TC_BF16X3)
+        pack_w_batch_kernel<TC_BF16X3><<<grid_for(total), 256, 0, st>>>(params, jobs, n_jobs, total);
     else
-        pack_w_batch_kernel<false><<<grid_for(total), 256, 0, st>>>(params, jobs, n_jobs, total);
+        pack_w_batch_kernel<TC_BF16><<<grid_for(total), 256, 0, st>>>(params, jobs, n_jobs, total);
     BSML_LAUNCH("pack_w_tc_batch");
 }
 
@@ -918,26 +942,32 @@ void pack_w_tc(const float* W, int kind, int Co, int Ci, int k, int s, int r, in
     const int64_t n = (int64_t)taps * M * Kp;
     ::bsml::count_launch();
     if (mode == TC_TF32X3)
-        pack_w_kernel<true><<<grid_for(n), 256, 0, st>>>(W, kind, Co, Ci, k, s, r, taps, M, K, Kp, hi, lo);
+        pack_w_kernel<TC_TF32X3><<<grid_for(n), 256, 0, st>>>(W, kind, Co, Ci, k, s, r, taps, M, K, Kp, hi, lo);
+    else if (mode == TC_BF16X3)
+        pack_w_kernel<TC_BF16X3><<<grid_for(n), 256, 0, st>>>(W, kind, Co, Ci, k, s, r, taps, M, K, Kp, hi, lo);
     else
-        pack_w_kernel<false><<<grid_for(n), 256, 0, st>>>(W, kind, Co, Ci, k, s, r, taps, M, K, Kp, hi, lo);
+        pack_w_kernel<TC_BF16><<<grid_for(n), 256, 0, st>>>(W, kind, Co, Ci, k, s, r, taps, M, K, Kp, hi, lo);
     BSML_LAUNCH("pack_w_tc");
 }
 
 void conv_fwd_tc(const TcConvFwd& c, int mode, cudaStream_t st) {
     if (c.No <= 0) return;
     if (mode == TC_TF32X3)
-        launch_fwd<true>(c, mode, st);
+        launch_fwd<TC_TF32X3>(c, mode, st);
+    else if (mode == TC_BF16X3)
+        launch_fwd<TC_BF16X3>(c, mode, st);
     else
-        launch_fwd<false>(c, mode, st);
+        launch_fwd<TC_BF16>(c, mode, st);
 }
 
 void conv_wgrad_tc(const TcConvWgrad& c, int mode, float* part, int64_t part_cap, cudaStream_t st) {
     if (c.Lo <= 0) return;
     if (mode == TC_TF32X3)
-        launch_wgrad<true>(c, mode, part, part_cap, st);
+        launch_wgrad<TC_TF32X3>(c, mode, part, part_cap, st);
+    else if (mode == TC_BF16X3)
+        launch_wgrad<TC_BF16X3>(c, mode, part, part_cap, st);
     else
-        launch_wgrad<false>(c, mode, part, part_cap, st);
+        launch_wgrad<TC_BF16>(c, mode, part, part_cap, st);
 }
 
 // One thread waits, through the same bounded wait every tensor-core kernel uses,

@@ -12,18 +12,20 @@ namespace bsml {
 //   TC_TF32X3: each fp32 operand is split hi + lo (hi = tf32-rounded value,
 //              lo = exact fp32 remainder) and D += Ahi*Bhi + Ahi*Blo + Alo*Bhi.
 //   TC_BF16:   bf16 operands, one product, fp32 accumulation.
-enum TcMode { TC_BF16 = 0, TC_TF32X3 = 1 };
+//   TC_BF16X3: each fp32 operand split into bf16 hi + bf16 lo (lo = v - hi rounded),
+//              three products as in TF32X3, at the bf16 rate.
+enum TcMode { TC_BF16 = 0, TC_TF32X3 = 1, TC_BF16X3 = 2 };
 
 // Operand planes in global memory: fp32 (tf32 hi/lo) or bf16, row pitch `ld`
 // elements (16-byte multiple).
 struct TcPlanes {
     const void* hi = nullptr;
-    const void* lo = nullptr;   // TC_TF32X3 only
+    const void* lo = nullptr;   // TC_TF32X3 / TC_BF16X3 only
     int ld = 0;
 };
 
-inline int tc_pitch(int C, int mode) { return (int)round_up(C, mode == TC_BF16 ? 8 : 4); }
-inline int tc_esize(int mode) { return mode == TC_BF16 ? 2 : 4; }
+inline int tc_pitch(int C, int mode) { return (int)round_up(C, mode == TC_TF32X3 ? 4 : 8); }
+inline int tc_esize(int mode) { return mode == TC_TF32X3 ? 4 : 2; }
 
 // Activation x (B, L, C) -> planes (same geometry, pitch tc_pitch(C)).
 void make_act_planes(const Act& x, int mode, void* hi, void* lo, cudaStream_t st);

@@ -149,7 +149,7 @@ Engine::~Engine() {
 }
 
 void Engine::set_math(int m) {
-    if (m != BSML_MATH_FP32_SIMT && m != BSML_MATH_TF32X3 && m != BSML_MATH_BF16)
+    if (m != BSML_MATH_FP32_SIMT && m != BSML_MATH_TF32X3 && m != BSML_MATH_BF16 && m != BSML_MATH_BF16X3)
         fail("bsml_decoder_set_math", "unknown math mode " + std::to_string(m));
     math_ = m;
 }
@@ -841,7 +841,7 @@ void Engine::rb1_fwd(const RB1P& w, RB1C& c, const Act& x0, bool x0_stats, const
     const int L = c.L, C = w.C;
     const bool tc = tc_ok(C, C, 1);   // every conv of the block is C -> C, stride 1
     // bytes of one AdaIN+Snake forward: read x, write the conv operand
-    const double out_b = !tc ? 4.0 : tc_mode() == TC_BF16 ? 2.0 : 8.0;
+    const double out_b = !tc ? 4.0 : plane_bytes();
     const double nb = (4.0 + out_b) * (double)x0.numel();
     for (int i = 0; i < 3; ++i) {
         int id = prof_begin(PROF_NORM_FWD, nb, st);
@@ -876,7 +876,7 @@ void Engine::rb1_fwd(const RB1P& w, RB1C& c, const Act& x0, bool x0_stats, const
 void Engine::rb1_bwd(const RB1P& w, RB1C& c, const Act& dOut, float scale, const Act& D, cudaStream_t st) {
     const int L = c.L, C = w.C;
     const bool tc = tc_ok(C, C, 1);
-    const double pb = !tc ? 4.0 : tc_mode() == TC_BF16 ? 2.0 : 8.0;
+    const double pb = !tc ? 4.0 : plane_bytes();
     const double n = (double)D.numel();
     Act t = view(S_[4], L, C);
     double* bs = grads_ ? bsum_ : nullptr;

@@ -177,7 +177,11 @@ class Engine {
     float* tc_yl_ = nullptr;
     float* tc_dh_ = nullptr;          // planes of the running resblock input gradient
     float* tc_dl_ = nullptr;
-    int tc_mode() const { return math_ == BSML_MATH_BF16 ? TC_BF16 : TC_TF32X3; }
+    int tc_mode() const {
+        return math_ == BSML_MATH_BF16 ? TC_BF16 : math_ == BSML_MATH_BF16X3 ? TC_BF16X3 : TC_TF32X3;
+    }
+    // bytes per element of a conv operand in planes (all planes)
+    double plane_bytes() const { return tc_mode() == TC_BF16 ? 2.0 : tc_mode() == TC_BF16X3 ? 4.0 : 8.0; }
     // stride-1 convs run on the tensor cores; narrow channel counts (conv_post's 22
     // outputs, the 22 harmonic channels) are zero-padded to the tile by TMA
     bool tc_ok(int K, int M, int s) const { return math_ != BSML_MATH_FP32_SIMT && s == 1 && K >= 8 && M >= 16; }

@@ -10,9 +10,11 @@
 
 namespace bsml {
 
-// TcMode values (conv_tc.h): 0 = bf16 plane, 1 = tf32 hi + fp32 lo planes.
+// TcMode values (conv_tc.h): 0 = bf16 plane, 1 = tf32 hi + fp32 lo planes,
+// 2 = bf16 hi + bf16 lo planes.
 constexpr int PLANES_BF16 = 0;
 constexpr int PLANES_TF32X3 = 1;
+constexpr int PLANES_BF16X3 = 2;
 
 __device__ __forceinline__ float tf32_rna(float x) {
     uint32_t r;
@@ -44,6 +46,28 @@ __device__ __forceinline__ void st_planes4(void* hi, void* lo, int mode, int64_t
         const float4 l = make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w);
         st4(static_cast<float*>(hi) + off, h, nv);
         st4(static_cast<float*>(lo) + off, l, nv);
+    } else if (mode == PLANES_BF16X3) {
+        __nv_bfloat16* ph = static_cast<__nv_bfloat16*>(hi) + off;
+        __nv_bfloat16* pl = static_cast<__nv_bfloat16*>(lo) + off;
+        const __nv_bfloat162 a = __floats2bfloat162_rn(v.x, v.y), b = __floats2bfloat162_rn(v.z, v.w);
+        const float2 fa = __bfloat1622float2(a), fb = __bfloat1622float2(b);
+        const __nv_bfloat162 c = __floats2bfloat162_rn(v.x - fa.x, v.y - fa.y);
+        const __nv_bfloat162 d = __floats2bfloat162_rn(v.z - fb.x, v.w - fb.y);
+        if (nv == 4) {
+            uint2 u, w;
+            u.x = *reinterpret_cast<const uint32_t*>(&a);
+            u.y = *reinterpret_cast<const uint32_t*>(&b);
+            w.x = *reinterpret_cast<const uint32_t*>(&c);
+            w.y = *reinterpret_cast<const uint32_t*>(&d);
+            *reinterpret_cast<uint2*>(ph) = u;
+            *reinterpret_cast<uint2*>(pl) = w;
+        } else {
+            const __nv_bfloat16 hs[4] = {a.x, a.y, b.x, b.y}, ls[4] = {c.x, c.y, d.x, d.y};
+            for (int j = 0; j < nv; ++j) {
+                ph[j] = hs[j];
+                pl[j] = ls[j];
+            }
+        }
     } else {
         __nv_bfloat16* p = static_cast<__nv_bfloat16*>(hi) + off;
         if (nv == 4) {

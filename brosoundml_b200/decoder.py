@@ -14,7 +14,7 @@ import torch
 
 from . import _lib
 
-MATH = {"fp32": 0, "tf32x3": 1, "bf16": 2}
+MATH = {"fp32": 0, "tf32x3": 1, "bf16": 2, "bf16x3": 3}
 
 
 def _ptr(t):

@@ -69,8 +69,10 @@ typedef struct bsml_decoder bsml_decoder;
 /* Arithmetic used for the conv / convT contractions. FP32_SIMT: fp32 CUDA-core
  * kernels. TF32X3: tcgen05 tensor cores, each fp32 operand split hi+lo, three
  * products (fp32-equivalent accuracy). BF16: tcgen05 with bf16 operands, fp32
- * accumulation. Elementwise, normalisation and spectral work is fp32 in all modes. */
-enum { BSML_MATH_FP32_SIMT = 0, BSML_MATH_TF32X3 = 1, BSML_MATH_BF16 = 2 };
+ * accumulation. BF16X3: each operand split into bf16 hi + bf16 lo, three products
+ * at the bf16 rate (about 16 bits of operand precision). Elementwise,
+ * normalisation and spectral work is fp32 in all modes. */
+enum { BSML_MATH_FP32_SIMT = 0, BSML_MATH_TF32X3 = 1, BSML_MATH_BF16 = 2, BSML_MATH_BF16X3 = 3 };
 
 const char* bsml_last_error(void);
 int bsml_version(void);
