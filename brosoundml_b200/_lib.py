@@ -99,6 +99,10 @@ SIGNATURES = {
     "bsml_st_read_f32": ([_P, ctypes.c_char_p, _P, _L], _I),
     "bsml_st_metadata": ([_P, ctypes.c_char_p, ctypes.c_char_p, _I], _I),
     "bsml_params_from_safetensors": ([_P, _P, _I, ctypes.c_char_p, _P, _L], _I),
+    "bsml_nccl_unique_id": ([_P], _I),
+    "bsml_nccl_comm_init": ([_I, _P, _I, _I, ctypes.POINTER(_P)], _I),
+    "bsml_nccl_comm_destroy": ([_P], _I),
+    "bsml_allreduce_grads": ([_P, _P, _L, _I, _P], _I),
     "bsml_graph_begin": ([_P], _I),
     "bsml_graph_end": ([_P, ctypes.POINTER(_P)], _I),
     "bsml_graph_launch": ([_P, _P], _I),

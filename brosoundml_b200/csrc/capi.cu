@@ -12,6 +12,7 @@
 #include "kernels.h"
 #include "convlora.h"
 #include "lora.h"
+#include "nccl_dl.h"
 #include "safetensors.h"
 
 namespace {
@@ -592,6 +593,28 @@ int bsml_params_from_safetensors(const bsml_st* f, const bsml_param_entry* table
         need(f && table && params, "bsml_params_from_safetensors", "null argument");
         f->f->load_params(table, n_entries, prefix ? prefix : "", params, n_params);
     });
+}
+
+int bsml_nccl_unique_id(void* id) {
+    return guarded([&] {
+        need(id != nullptr, "bsml_nccl_unique_id", "null argument");
+        bsml::nccl_unique_id(id);
+    });
+}
+
+int bsml_nccl_comm_init(int nranks, const void* id, int rank, int device, void** comm) {
+    return guarded([&] {
+        need(id != nullptr && comm != nullptr, "bsml_nccl_comm_init", "null argument");
+        *comm = bsml::nccl_comm_init(nranks, id, rank, device);
+    });
+}
+
+int bsml_nccl_comm_destroy(void* comm) {
+    return guarded([&] { bsml::nccl_comm_destroy(comm); });
+}
+
+int bsml_allreduce_grads(void* comm, float* grads, int64_t n, int average, void* stream) {
+    return guarded([&] { bsml::nccl_allreduce(comm, grads, n, average != 0, S(stream)); });
 }
 
 struct bsml_graph {

@@ -35,7 +35,7 @@ def _f32(t):
 
 class Decoder:
     # math modes smoke() exercises (the tensor-core modes join once built)
-    SMOKE_MATH = ("fp32", "tf32x3")
+    SMOKE_MATH = ("fp32", "tf32x3", "bf16x3")
     # math mode bench.py uses by default (fp32-grade accuracy on the tensor cores)
     DEFAULT_MATH = "tf32x3"
 

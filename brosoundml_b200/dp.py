@@ -33,3 +33,56 @@ def average_gradients(grads, group=None) -> None:
         grads /= dist.get_world_size(group)
     else:
         dist.all_reduce(grads, op=dist.ReduceOp.AVG, group=group)
+
+
+class NcclComm:
+    """A communicator of the library's own NCCL path (``bsml_nccl_*``), for callers
+    without torch.distributed: rank 0 makes :meth:`unique_id` and passes the 128
+    bytes to the other ranks by any channel; every rank then builds its
+    communicator and all-reduces its flat gradient once per step."""
+
+    @staticmethod
+    def unique_id() -> bytes:
+        import ctypes
+
+        from . import _lib
+
+        buf = ctypes.create_string_buffer(128)
+        _lib.check(_lib.lib().bsml_nccl_unique_id(ctypes.cast(buf, ctypes.c_void_p)))
+        return buf.raw
+
+    def __init__(self, nranks: int, uid: bytes, rank: int, device: int):
+        import ctypes
+
+        from . import _lib
+
+        if len(uid) != 128:
+            raise ValueError("brosoundml: NcclComm: the unique id has 128 bytes")
+        buf = ctypes.create_string_buffer(uid, 128)
+        c = ctypes.c_void_p()
+        _lib.check(_lib.lib().bsml_nccl_comm_init(nranks, ctypes.cast(buf, ctypes.c_void_p), rank, device,
+                                                  ctypes.byref(c)))
+        self._c = c
+
+    def allreduce(self, grads, average: bool = True) -> None:
+        """In place over a float32 CUDA tensor, on the current stream."""
+        import ctypes
+
+        import torch
+
+        from . import _lib
+
+        if not (grads.is_cuda and grads.dtype == torch.float32 and grads.is_contiguous()):
+            raise TypeError("brosoundml: NcclComm.allreduce needs a contiguous float32 CUDA tensor")
+        _lib.check(_lib.lib().bsml_allreduce_grads(self._c, ctypes.c_void_p(grads.data_ptr()), grads.numel(),
+                                                   1 if average else 0,
+                                                   ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)))
+
+    def close(self) -> None:
+        from . import _lib
+
+        if getattr(self, "_c", None) is not None and _lib._lib is not None:
+            _lib.lib().bsml_nccl_comm_destroy(self._c)
+            self._c = None
+
+    __del__ = close

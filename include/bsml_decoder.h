@@ -214,6 +214,17 @@ int bsml_st_metadata(const bsml_st* f, const char* key, char* value, int cap);
 int bsml_params_from_safetensors(const bsml_st* f, const bsml_param_entry* table, int n_entries, const char* prefix,
                                  float* params, int64_t n_params);
 
+/* ── data-parallel gradient averaging without torch ──────────────────────
+ * One process per GPU. Rank 0 makes a 128-byte NCCL unique id and hands it to
+ * the other ranks by any channel (a file, a socket, MPI); every rank then makes
+ * its communicator and, each step, all-reduces its flat gradient buffer once
+ * before the optimiser step. NCCL is loaded at run time (libnccl.so.2). */
+int bsml_nccl_unique_id(void* id /* 128 bytes */);
+int bsml_nccl_comm_init(int nranks, const void* id, int rank, int device, void** comm);
+int bsml_nccl_comm_destroy(void* comm);
+/* grads (n floats, device) summed over the ranks, or averaged when average != 0. */
+int bsml_allreduce_grads(void* comm, float* grads, int64_t n, int average, void* stream);
+
 /* ── CUDA graphs (no reference counterpart: the reference runs eagerly) ────
  * Records every library call issued on `stream` between begin and end (a whole
  * forward, loss and backward, say) into one CUDA graph; launch replays it with
