@@ -1,4 +1,4 @@
-// Conv-weight LoRA (no counterpart in the reference): a rank-r
+// Conv-weight LoRA (the fine-tune of every conv weight; no counterpart in the reference): a rank-r
 // adapter on every Conv1d / ConvTranspose1d weight of the decoder, base weights
 // frozen. A weight stored as (d0, d1, k) is viewed as the matrix [d0][d1*k] and
 // adapted as W + scale * B A, with A [rank][d1*k] and B [d0][rank]. Each forward

@@ -115,7 +115,7 @@ def _device_view(ptr: int, n: int, device) -> torch.Tensor:
 
 
 class ConvLora:
-    """Conv-weight LoRA (no counterpart in the reference): a rank-r
+    """Conv-weight LoRA (the fine-tune of every conv weight; no counterpart in the reference): a rank-r
     adapter W + scale * B A on every Conv1d / ConvTranspose1d weight of ``decoder``,
     base weights frozen. A weight stored (d0, d1, k) is viewed as [d0][d1*k];
     A [rank][d1*k] starts N(0, 0.01), B [d0][rank] starts at zero."""

@@ -160,7 +160,7 @@ int bsml_decoder_read_profile_records(bsml_decoder* d, double* out, int max_reco
  *                         nearest-2x shortcut), learned 1x1 shortcut when cin != cout
  *   BSML_BLOCK_RESBLOCK1  detail::adain_resblock1_forward_train / _backward
  *                         (:125-144): AdaINResBlock1 with Snake, C channels, kernel,
- *                         convs1 dilations dil[3] (BASELINE config 1)
+ *                         convs1 dilations dil[3]
  * The handle is a bsml_decoder: param_count / param_table, set_math, profiling
  * and destroy apply; parameter keys are block-relative ("norm1.fc.weight",
  * "convs1.0.weight", "alpha2.1", ...). The whole-decoder entry points reject a
@@ -299,7 +299,7 @@ int bsml_lora_load_state(bsml_lora* l, const char* path);
 /* Current LoRA scale and Adam step count. */
 int bsml_lora_state(const bsml_lora* l, float* scale, int* step);
 
-/* ── conv-weight LoRA (no counterpart in the reference) ──
+/* ── conv-weight LoRA (no counterpart in the reference) ─────────────────────
  * A rank-r adapter on every Conv1d / ConvTranspose1d weight, base weights frozen.
  * A weight stored (d0, d1, k) is viewed as [d0][d1*k] and adapted to
  * W + scale * B A, A [rank][d1*k] ~ N(0, 0.01) at creation, B [d0][rank] = 0.

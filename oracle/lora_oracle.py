@@ -153,7 +153,7 @@ def read_elra1(path: str):
     return rank, sd, scale, hidden, W1, W2, ads
 
 
-# ── conv-weight LoRA (no reference counterpart) ──────────────
+# ── conv-weight LoRA (no reference counterpart) ───────────────────────────────
 class ConvLoraLayout:
     """Every 3-d ``*.weight`` of the decoder (Conv1d / ConvTranspose1d), viewed [d0][d1*k];
     flat LoRA vector: per weight A [rank][d1*k] then B [d0][rank]."""
