@@ -327,6 +327,26 @@ __global__ void __launch_bounds__(128) colsum_chunk_kernel(const float* dy, int6
     if (c < C) part[(int64_t)blockIdx.x * C + c] = red[0][threadIdx.x] + red[1][threadIdx.x] + red[2][threadIdx.x] +
                                                    red[3][threadIdx.x];
 }
+// out[c] (+)= sum over the chunk partials part[q][c]: 32 channels per CTA, 32 rows of
+// threads taking every 32nd chunk (a fixed order), then a tree over the rows in
+// shared memory; double throughout
+__global__ void __launch_bounds__(1024) colsum_reduce_kernel(const float* part, int chunks, int C, float* out,
+                                                            int accum) {
+    __shared__ double red[32][33];
+    const int c = blockIdx.x * 32 + threadIdx.x;
+    double s = 0.0;
+    if (c < C) {
+        const int n = chunks > (int)threadIdx.y ? (chunks - (int)threadIdx.y + 31) / 32 : 0;
+        s = sum_strided(part + (int64_t)threadIdx.y * C + c, 32ll * C, n);
+    }
+    red[threadIdx.y][threadIdx.x] = s;
+    __syncthreads();
+    for (int h = 16; h > 0; h >>= 1) {
+        if ((int)threadIdx.y < h) red[threadIdx.y][threadIdx.x] += red[threadIdx.y + h][threadIdx.x];
+        __syncthreads();
+    }
+    if (threadIdx.y == 0 && c < C) out[c] = (float)(accum ? out[c] + red[0][threadIdx.x] : red[0][threadIdx.x]);
+}
 }  // namespace
 
 void colsum(const Act& dy, float* db, bool accum, float* part, cudaStream_t st) {
@@ -337,7 +357,7 @@ void colsum(const Act& dy, float* db, bool accum, float* part, cudaStream_t st) 
     colsum_chunk_kernel<<<grid, 128, 0, st>>>(dy.p, dy.bstride, dy.ld, dy.L, dy.C, rows, part);
     BSML_LAUNCH("colsum");
     ::bsml::count_launch();
-    reduce_splits_kernel<<<grid_for(dy.C), 256, 0, st>>>(part, chunks, dy.C, db, accum ? 1 : 0);
+    colsum_reduce_kernel<<<(unsigned)ceil_div(dy.C, 32), dim3(32, 32), 0, st>>>(part, chunks, dy.C, db, accum ? 1 : 0);
     BSML_LAUNCH("colsum_reduce");
 }
 
