@@ -90,3 +90,43 @@ def test_decode_prep_roundtrip_and_stack(tmp_path):
     weights.save_safetensors(str(tmp_path / "other.safetensors"), {"x": np.zeros(2, np.float32)}, {"format": "x"})
     with pytest.raises(ValueError, match="not a KokoroDecodePrep"):
         weights.load_decode_prep(str(tmp_path / "other.safetensors"))
+
+
+@pytest.mark.gpu
+def test_loaded_checkpoint_drives_the_decoder(tmp_path):
+    """A checkpoint written with the upstream keys (weight-norm pairs on the convs)
+    loads into the parameter vector the engine runs on: same audio as the vector it
+    was written from."""
+    from tests.conftest import cuda_available
+    if not cuda_available():
+        pytest.skip("needs a CUDA device")
+    import torch
+
+    from brosoundml_b200 import synth
+    from brosoundml_b200.decoder import Decoder
+    cfg = config.miniature()
+    dec = Decoder(cfg, 0, math="tf32x3")
+    p = synth.init_params(dec.table, dec.n_params, 0)
+    tensors = {}
+    rng = np.random.default_rng(2)
+    for e in dec.table:
+        w = p[e["offset"]:e["offset"] + e["numel"]].reshape(e["shape"]).astype(np.float64)
+        key = "decoder.module." + e["name"]
+        if e["name"].endswith(".weight") and len(e["shape"]) == 3:
+            g = np.sqrt((w ** 2).reshape(w.shape[0], -1).sum(1)).reshape(-1, 1, 1)
+            v = w * rng.uniform(0.5, 2.0, (w.shape[0], 1, 1))    # any positive per-row rescaling of w
+            tensors[key + "_g"], tensors[key + "_v"] = g.astype(np.float32), v.astype(np.float32)
+        else:
+            tensors[key] = w.astype(np.float32)
+    path = str(tmp_path / "model.safetensors")
+    weights.save_safetensors(path, tensors)
+    q = weights.load_params(dec, path)
+    assert np.allclose(q, p, rtol=1e-5, atol=1e-7)
+    B, T, frames = 2, 4, 33
+    x = synth.make_inputs(cfg, B, T, 1)
+    har = np.random.default_rng(3).uniform(-0.4, 0.4, (B, cfg["har_ch"], frames)).astype(np.float32)
+    dv = {k: torch.tensor(v, device="cuda") for k, v in dict(x, har=har).items()}
+    a = dec.forward(torch.tensor(p, device="cuda"), dv["asr"], dv["F0"], dv["N"], dv["style"], har=dv["har"]).clone()
+    b = dec.forward(torch.tensor(q, device="cuda"), dv["asr"], dv["F0"], dv["N"], dv["style"], har=dv["har"]).clone()
+    torch.cuda.synchronize()
+    assert float((a - b).norm() / a.norm()) < 1e-5
