@@ -226,6 +226,8 @@ class Graph:
         if et is None:
             _lib.check(rc)
             self._g = g
+        elif rc == 0 and g.value:
+            _lib.lib().bsml_graph_destroy(g)   # the block raised: the partial graph is not kept
         return False
 
     @property

@@ -58,7 +58,8 @@ def _make(cfg, math, seed=5, rank=RANK):
     return dec, DecoderLora(dec, rank=rank, scale=SCALE, seed=seed)
 
 
-@pytest.mark.parametrize("which,math", [("miniature", "fp32"), ("miniature", "tf32x3"), ("kokoro", "tf32x3")])
+@pytest.mark.parametrize("which,math", [("miniature", "fp32"), ("miniature", "tf32x3"), ("kokoro", "tf32x3"),
+                                        ("kokoro", "bf16x3")])
 def test_lora_forward_backward_vs_oracle(which, math):
     torch = _torch()
     cfg, o, p, x, har, ref_s, cond = _case(which)
@@ -76,7 +77,7 @@ def test_lora_forward_backward_vs_oracle(which, math):
     S = cfg["style_dim"]
     r = lo.run(o, lay, p.astype(np.float64), lp.astype(np.float64), x["asr"], x["F0"], x["N"], ref_s[:, :S], cond,
                SCALE, har=har, daudio=da.astype(np.float64))
-    tol = 1e-4   # fp32 / TF32x3 against the float64 oracle (BASELINE's 3xTF32 bar)
+    tol = 2e-2 if math == "bf16x3" else 1e-4   # the BF16 and 3xTF32 bars against float64
     assert rel_l2(audio.cpu().numpy(), r["audio"]) < tol
     g = lora.grads().cpu().numpy()
     assert rel_l2(g, r["grads"]) < tol
