@@ -101,6 +101,8 @@ void atom_tc_conv(Scratch& sc, const bsml::Act& xa, const float* W, int kind, in
     a.w.hi = wh; a.w.lo = wl; a.w.ld = (int)bsml::round_up(xa.C, 8);
     a.taps = taps; a.Co = M; a.p = p; a.d = d; a.No = No; a.o_base = o_base;
     a.y = ya; a.bias = bias; a.orow_mul = orow_mul; a.orow_off = orow_off;
+    a.part_cap = bsml::conv_fwd_tc_part_floats(a, mode);
+    if (a.part_cap > 0) a.part = sc.f(a.part_cap);
     bsml::conv_fwd_tc(a, mode, st);
 }
 
@@ -834,6 +836,8 @@ int bsml_conv_transpose1d_backward_input(const float* dy, int B, int Ci, int L, 
             a.w.hi = wh; a.w.lo = wl; a.w.ld = (int)bsml::round_up(K, 8);
             a.taps = pk.taps; a.Co = Ci; a.p = -pk.u_min; a.d = 1; a.No = L;
             a.y = xa;
+            a.part_cap = bsml::conv_fwd_tc_part_floats(a, mode);
+            if (a.part_cap > 0) a.part = sc.f(a.part_cap);
             bsml::conv_fwd_tc(a, mode, st);
             bsml::cl_to_ncl(xa, dx, st);
             return;

@@ -8,6 +8,9 @@
 // activation window of NP + (taps-1)*d rows and reuses it for every tap: tap
 // t's operand is the same window shifted by t*d rows (a descriptor offset, not
 // a new load). Only the per-tap weight tiles stream through their own ring.
+// A launch with fewer tiles than half the SMs also splits each tile's K loop
+// (chunk ranges) over the idle SMs; the partial tiles are summed in a fixed
+// order by a reduce pass that applies the epilogue.
 //
 // Weight-gradient form (stride-1 convs):
 //   D[co, ci] (tap t) = sum_{b, o} dY[b, o, co] * X[b, o + t*d - p, ci]
@@ -32,6 +35,7 @@
 
 #include <algorithm>
 #include <mutex>
+#include <type_traits>
 
 #include "conv_tc.h"
 #include "kernels.h"
@@ -89,7 +93,14 @@ struct FArgs {
     const float* r; int64_t r_bs; int r_ld; int r_shift;
     float alpha; int accum;
     double* stats;   // per-(b, co) sum and sum of squares of the stored outputs (nullable)
+    // split-K: work item i = tile (i % n_tiles) over chunk range (i / n_tiles) of ksplit;
+    // with ksplit > 1 the epilogue stores raw fp32 partials part[split][b][o][co]
+    int ksplit, nb;
+    float* part;
 };
+
+// Input-channel chunks [lo, hi) of split `s` of `ks` (near-equal ranges).
+__device__ __forceinline__ int split_lo(int s, int ks, int kchunks) { return (int)((int64_t)s * kchunks / ks); }
 
 // 320 threads = 10 warps, so one SM sub-partition holds 3 of them: 168
 // registers per thread at most (3 x 32 x 168 <= 16384).
@@ -118,8 +129,7 @@ __global__ void __launch_bounds__(FCfg<MODE, NPT>::THREADS, 1)
     int* err = &g_tc_err;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int n_iters = a.taps * a.kchunks;          // K steps per tile
-    const int n_groups = (n_iters + PG - 1) / PG;    // promotion groups per tile
+    const int n_items = a.n_tiles * a.ksplit;
     const int plane_bytes = 2 * a.wbox * 128;
 
     if (threadIdx.x == 0) {
@@ -156,11 +166,13 @@ __global__ void __launch_bounds__(FCfg<MODE, NPT>::THREADS, 1)
             // ── TMA producer: per chunk one window, then one weight tile per tap
             int kit = 0, cw = 0;
             bool ok = true;
-            for (int tile = blockIdx.x; ok && tile < a.n_tiles; tile += gridDim.x) {
+            for (int it = blockIdx.x; ok && it < n_items; it += gridDim.x) {
+                const int tile = it % a.n_tiles, ks = it / a.n_tiles;
                 const int ct = tile % a.n_co, rest = tile / a.n_co;
                 const int pt = rest % a.n_pt, b = rest / a.n_pt;
                 const int m0 = ct * 128, row0 = pt * NP + a.o_base - a.p;
-                for (int c = 0; ok && c < a.kchunks; ++c) {
+                const int c_hi = split_lo(ks + 1, a.ksplit, a.kchunks);
+                for (int c = split_lo(ks, a.ksplit, a.kchunks); ok && c < c_hi; ++c) {
                     const int kx = c * F::BKE;
                     const int xs = cw & 1;
                     if (!tc::mbar_wait(&xempty[xs], ((cw >> 1) & 1) ^ 1, err, tc::TC_ERR_WAIT_EMPTY)) {
@@ -203,8 +215,12 @@ __global__ void __launch_bounds__(FCfg<MODE, NPT>::THREADS, 1)
             constexpr uint32_t idesc = tc::make_idesc(Fmt<MODE>::KIND, 0u, 0u, 128, NP);
             int kit = 0, cw = 0, G = 0;
             bool ok = true;
-            for (int tile = blockIdx.x; ok && tile < a.n_tiles; tile += gridDim.x) {
-                for (int c = 0; ok && c < a.kchunks; ++c) {
+            for (int it = blockIdx.x; ok && it < n_items; it += gridDim.x) {
+                const int ks = it / a.n_tiles;
+                const int c_lo = split_lo(ks, a.ksplit, a.kchunks), c_hi = split_lo(ks + 1, a.ksplit, a.kchunks);
+                const int n_iters = a.taps * (c_hi - c_lo);        // K steps of this item
+                const int n_groups = (n_iters + PG - 1) / PG;      // its promotion groups
+                for (int c = c_lo; ok && c < c_hi; ++c) {
                     const int xs = cw & 1;
                     if (!tc::mbar_wait(&xfull[xs], (cw >> 1) & 1, err, tc::TC_ERR_WAIT_FULL)) {
                         ok = false;
@@ -214,7 +230,7 @@ __global__ void __launch_bounds__(FCfg<MODE, NPT>::THREADS, 1)
                     const uint32_t xh = tc::smem_u32(win + xs * a.win_bytes);
                     const uint32_t xl = xh + plane_bytes;
                     for (int t = 0; t < a.taps; ++t) {
-                        const int li = c * a.taps + t;
+                        const int li = (c - c_lo) * a.taps + t;
                         const bool g_first = (li % PG) == 0;
                         const bool g_last = (li % PG) == PG - 1 || li == n_iters - 1;
                         const int g = G + li / PG;
@@ -268,7 +284,10 @@ __global__ void __launch_bounds__(FCfg<MODE, NPT>::THREADS, 1)
         const uint32_t trow = tbase + ((uint32_t)(q * 32) << 16) + (uint32_t)(h * HC);
         int G = 0;
         bool ok = true;
-        for (int tile = blockIdx.x; ok && tile < a.n_tiles; tile += gridDim.x) {
+        for (int it = blockIdx.x; ok && it < n_items; it += gridDim.x) {
+            const int tile = it % a.n_tiles, ks = it / a.n_tiles;
+            const int n_iters = a.taps * (split_lo(ks + 1, a.ksplit, a.kchunks) - split_lo(ks, a.ksplit, a.kchunks));
+            const int n_groups = (n_iters + PG - 1) / PG;
             const int ct = tile % a.n_co, rest = tile / a.n_co;
             const int pt = rest % a.n_pt, b = rest / a.n_pt;
             const int mrow = ct * 128 + q * 32 + lane;   // co
@@ -279,19 +298,18 @@ __global__ void __launch_bounds__(FCfg<MODE, NPT>::THREADS, 1)
             int jhi = min(HC, a.No - o0);
             jhi = a.y_rows > row0 ? min(jhi, (a.y_rows - row0 + a.orow_mul - 1) / a.orow_mul) : 0;
             if (mrow >= a.Co) jhi = 0;
-            const float* rb = a.r ? a.r + (int64_t)b * a.r_bs + mrow : nullptr;
+            const float* rb = (a.r && a.ksplit == 1) ? a.r + (int64_t)b * a.r_bs + mrow : nullptr;
             float* yb = a.y + (int64_t)b * a.y_bs + mrow;
-            // the residual / prior-output rows this tile reads at its end go to L2 now,
+            // the prior-output rows an accumulating tile reads at its end go to L2 now,
             // while its MMAs run (a warp's 32 lanes share each 128-byte line)
-            if (rb || a.accum) {
-                for (int j = jlo; j < jhi; ++j) {
-                    if (rb) tc::prefetch_l2(rb + ((row0 + j * a.orow_mul) >> a.r_shift) * a.r_ld);
-                    if (a.accum) tc::prefetch_l2(yb + (row0 + j * a.orow_mul) * a.y_ld);
-                }
-            }
+            if (a.accum && a.ksplit == 1)
+                for (int j = jlo; j < jhi; ++j) tc::prefetch_l2(yb + (row0 + j * a.orow_mul) * a.y_ld);
+            // the residual starts the sum: its loads complete under the tile's first
+            // MMAs instead of stalling the tile-end stores
             float R[HC];
 #pragma unroll
-            for (int j = 0; j < HC; ++j) R[j] = 0.f;
+            for (int j = 0; j < HC; ++j)
+                R[j] = (rb && j >= jlo && j < jhi) ? rb[((row0 + j * a.orow_mul) >> a.r_shift) * a.r_ld] : 0.f;
             for (int gi = 0; gi < n_groups; ++gi) {
                 const int g = G + gi, buf = g & 1;
                 bool w = true;
@@ -313,45 +331,74 @@ __global__ void __launch_bounds__(FCfg<MODE, NPT>::THREADS, 1)
             }
             G += n_groups;
             if (!ok || *(volatile int*)err != tc::TC_OK) break;
+            if (a.ksplit > 1) {   // raw partial sums; the reduce pass applies the epilogue
+                if (mrow < a.Co) {
+                    const int nrow = min(HC, a.No - o0);
+                    float* pp = a.part + (((int64_t)ks * a.nb + b) * a.No + o0) * a.Co + mrow;
+#pragma unroll
+                    for (int jj = 0; jj < HC; ++jj)
+                        if (jj < nrow) pp[(int64_t)jj * a.Co] = R[jj];
+                }
+                continue;
+            }
             if (mrow < a.Co) {
                 const float bv = a.bias ? a.bias[mrow] : 0.f;
-                double s1 = 0.0, s2 = 0.0;
-                if (!rb && !a.accum) {
-#pragma unroll
-                    for (int jj = 0; jj < HC; ++jj) {
-                        if (jj < jlo || jj >= jhi) continue;
-                        const float val = (R[jj] + bv) * a.alpha;
+                // ST: also the output statistics: fp32 sums over groups of four columns,
+                // each group's sums added in double (one conversion per four outputs);
+                // without statistics no double-precision work is issued at all
+                auto store = [&](auto st_tag) {
+                    constexpr bool ST = decltype(st_tag)::value;
+                    double s1 = 0.0, s2 = 0.0;
+                    float g1 = 0.f, g2 = 0.f;
+                    auto emit = [&](int jj, float val) {
                         yb[(row0 + jj * a.orow_mul) * a.y_ld] = val;
-                        s1 += val;
-                        s2 = fma((double)val, (double)val, s2);
-                    }
-                }
-                // EB columns at a time: their reads are all issued before their stores
-                constexpr int EB = 8;
+                        if (ST) {
+                            g1 += val;
+                            g2 = fmaf(val, val, g2);
+                        }
+                    };
+                    auto flush = [&](int jj) {
+                        if (ST && (jj & 3) == 3) {
+                            s1 += (double)g1;
+                            s2 += (double)g2;
+                            g1 = 0.f;
+                            g2 = 0.f;
+                        }
+                    };
+                    if (!a.accum) {
 #pragma unroll
-                for (int c16 = 0; (rb || a.accum) && c16 < HC; c16 += EB) {
-                    float t[EB], u[EB];
+                        for (int jj = 0; jj < HC; ++jj) {
+                            if (jj >= jlo && jj < jhi) emit(jj, (R[jj] + bv) * a.alpha);
+                            flush(jj);
+                        }
+                    } else {
+                        // EB columns at a time: their reads are all issued before their stores
+                        constexpr int EB = 8;
 #pragma unroll
-                    for (int j = 0; j < EB; ++j) {
-                        const int jj = c16 + j, row = row0 + jj * a.orow_mul;
-                        const bool in = jj >= jlo && jj < jhi;
-                        t[j] = (rb && in) ? rb[(row >> a.r_shift) * a.r_ld] : 0.f;
-                        u[j] = (a.accum && in) ? yb[row * a.y_ld] : 0.f;
-                    }
+                        for (int c16 = 0; c16 < HC; c16 += EB) {
+                            float u[EB];
 #pragma unroll
-                    for (int j = 0; j < EB; ++j) {
-                        const int jj = c16 + j;
-                        if (jj < jlo || jj >= jhi) continue;
-                        const float val = (R[jj] + bv + t[j]) * a.alpha + u[j];
-                        yb[(row0 + jj * a.orow_mul) * a.y_ld] = val;
-                        s1 += val;
-                        s2 = fma((double)val, (double)val, s2);
+                            for (int j = 0; j < EB; ++j) {
+                                const int jj = c16 + j;
+                                u[j] = (jj >= jlo && jj < jhi) ? yb[(row0 + jj * a.orow_mul) * a.y_ld] : 0.f;
+                            }
+#pragma unroll
+                            for (int j = 0; j < EB; ++j) {
+                                const int jj = c16 + j;
+                                if (jj >= jlo && jj < jhi) emit(jj, (R[jj] + bv) * a.alpha + u[j]);
+                                flush(jj);
+                            }
+                        }
                     }
-                }
-                if (a.stats) {
-                    atomicAdd(&a.stats[((int64_t)b * a.Co + mrow) * 2], s1);
-                    atomicAdd(&a.stats[((int64_t)b * a.Co + mrow) * 2 + 1], s2);
-                }
+                    if (ST) {
+                        atomicAdd(&a.stats[((int64_t)b * a.Co + mrow) * 2], s1);
+                        atomicAdd(&a.stats[((int64_t)b * a.Co + mrow) * 2 + 1], s2);
+                    }
+                };
+                if (a.stats)
+                    store(std::true_type{});
+                else
+                    store(std::false_type{});
             }
         }
     }
@@ -361,6 +408,39 @@ __global__ void __launch_bounds__(FCfg<MODE, NPT>::THREADS, 1)
         __syncwarp();
         tc::tc_fence_after();
         tc::tmem_dealloc(tbase, TCOLS);
+    }
+}
+
+// Split-K epilogue: sums the ksplit partial tiles of each output element in a
+// fixed order and applies the forward kernel's epilogue (bias, residual, scale,
+// accumulation, output statistics). One thread per output channel, a strip of
+// FR_ROWS positions per CTA.
+constexpr int FR_ROWS = 16;
+__global__ void __launch_bounds__(128) fwd_split_reduce_kernel(const FArgs a) {
+    const int co = blockIdx.y * 128 + threadIdx.x, b = blockIdx.z;
+    if (co >= a.Co) return;
+    const int o0 = blockIdx.x * FR_ROWS, o1 = min(a.No, o0 + FR_ROWS);
+    const int64_t sstride = (int64_t)a.nb * a.No * a.Co;
+    const float* pb = a.part + ((int64_t)b * a.No) * a.Co + co;
+    const float bv = a.bias ? a.bias[co] : 0.f;
+    const float* rb = a.r ? a.r + (int64_t)b * a.r_bs + co : nullptr;
+    float* yb = a.y + (int64_t)b * a.y_bs + co;
+    double s1 = 0.0, s2 = 0.0;
+    for (int o = o0; o < o1; ++o) {
+        const int row = (o + a.o_base) * a.orow_mul + a.orow_off;
+        if (row < 0 || row >= a.y_rows) continue;
+        float acc = 0.f;
+        for (int k = 0; k < a.ksplit; ++k) acc += pb[k * sstride + (int64_t)o * a.Co];
+        const float t = rb ? rb[(int64_t)(row >> a.r_shift) * a.r_ld] : 0.f;
+        const float u = a.accum ? yb[(int64_t)row * a.y_ld] : 0.f;
+        const float val = (acc + bv + t) * a.alpha + u;
+        yb[(int64_t)row * a.y_ld] = val;
+        s1 += val;
+        s2 = fma((double)val, (double)val, s2);
+    }
+    if (a.stats) {
+        atomicAdd(&a.stats[((int64_t)b * a.Co + co) * 2], s1);
+        atomicAdd(&a.stats[((int64_t)b * a.Co + co) * 2 + 1], s2);
     }
 }
 
@@ -770,6 +850,20 @@ FwdGeom fwd_geom(int planes, int halo) {
     return g;
 }
 
+// K splits of a forward-like launch: only when its output tiles fill less than half
+// of the SMs, at most one input-channel chunk range per idle SM, and within the
+// caller's scratch (`cap` floats for ksplit x B x No x Co partials).
+int fwd_ksplit(const TcConvFwd& c, int mode, int np, int64_t cap) {
+    const int kchunks = (int)ceil_div(c.Ci, mode == TC_TF32X3 ? 32 : 64);
+    const int64_t tiles = ceil_div(c.Co, 128) * ceil_div(c.No, np) * (int64_t)c.B;
+    const int sms = sm_count();
+    if (tiles * 2 > sms || kchunks < 2) return 1;
+    int64_t ks = std::min<int64_t>(kchunks, sms / tiles);
+    const int64_t per = (int64_t)c.B * c.No * c.Co;
+    ks = std::min<int64_t>(ks, cap / std::max<int64_t>(per, 1));
+    return ks >= 2 ? (int)ks : 1;
+}
+
 template <int MODE, int NPT>
 void launch_fwd_np(const TcConvFwd& c, int mode, const FwdGeom& g, cudaStream_t st) {
     using F = FCfg<MODE, NPT>;
@@ -803,14 +897,23 @@ void launch_fwd_np(const TcConvFwd& c, int mode, const FwdGeom& g, cudaStream_t 
     a.r = c.r ? c.r->p : nullptr; a.r_bs = c.r ? c.r->bstride : 0; a.r_ld = c.r ? c.r->ld : 0; a.r_shift = c.r_shift;
     a.alpha = c.alpha; a.accum = c.accum ? 1 : 0;
     a.stats = c.stats;
+    a.nb = c.B;
+    a.part = c.part;
+    a.ksplit = c.part ? fwd_ksplit(c, mode, F::NPOS, c.part_cap) : 1;
     if (c.stats && c.accum) fail("conv_fwd_tc", "output statistics need a non-accumulating output");
     // the epilogue forms in-clip offsets (row * ld) in 32 bits
     if ((int64_t)c.y.L * c.y.ld >= (1ll << 31) || (c.r && (int64_t)c.r->L * c.r->ld >= (1ll << 31)))
         fail("conv_fwd_tc", "clip too long for 32-bit row offsets");
-    const int grid = (int)std::min<int64_t>(tiles, sm_count());
+    const int grid = (int)std::min<int64_t>(tiles * a.ksplit, sm_count());
     ::bsml::count_launch();
     conv_fwd_tc_kernel<MODE, NPT><<<grid, F::THREADS, g.smem, st>>>(mWh, mWl, mXh, mXl, a);
     BSML_LAUNCH("conv_fwd_tc");
+    if (a.ksplit > 1) {
+        ::bsml::count_launch();
+        fwd_split_reduce_kernel<<<dim3((unsigned)ceil_div(c.No, FR_ROWS), (unsigned)ceil_div(c.Co, 128), (unsigned)c.B),
+                                  128, 0, st>>>(a);
+        BSML_LAUNCH("fwd_split_reduce");
+    }
 }
 
 template <int MODE>
@@ -948,6 +1051,13 @@ void pack_w_tc(const float* W, int kind, int Co, int Ci, int k, int s, int r, in
     else
         pack_w_kernel<TC_BF16><<<grid_for(n), 256, 0, st>>>(W, kind, Co, Ci, k, s, r, taps, M, K, Kp, hi, lo);
     BSML_LAUNCH("pack_w_tc");
+}
+
+int64_t conv_fwd_tc_part_floats(const TcConvFwd& c, int mode) {
+    const int planes = mode == TC_BF16 ? 1 : 2;
+    const int np = fwd_geom(planes, (c.taps - 1) * c.d).np;
+    const int ks = fwd_ksplit(c, mode, np, INT64_MAX);
+    return ks > 1 ? (int64_t)ks * c.B * c.No * c.Co : 0;
 }
 
 void conv_fwd_tc(const TcConvFwd& c, int mode, cudaStream_t st) {

@@ -87,8 +87,15 @@ struct TcConvFwd {
     // optional: stats[(b*Co + co)*2 + {0,1}] += sum, sum of squares of the
     // stored outputs over the rows this call writes (accum must be false)
     double* stats = nullptr;
+    // optional split-K scratch (floats): a call with fewer output tiles than half
+    // the SMs splits its K loop (input-channel chunks) over otherwise idle SMs,
+    // writes fp32 partial tiles here and applies the epilogue in a reduce pass
+    float* part = nullptr;
+    int64_t part_cap = 0;
 };
 void conv_fwd_tc(const TcConvFwd& a, int mode, cudaStream_t st);
+// scratch floats conv_fwd_tc would use for a split-K launch of `a` (0: no split)
+int64_t conv_fwd_tc_part_floats(const TcConvFwd& a, int mode);
 
 // Weight gradient of a stride-1 conv: dW[(co*Ci + ci)*taps + t] (+)=
 //   sum_{b,o} dY[b, o, co] * X[b, o + t*d - p, ci]

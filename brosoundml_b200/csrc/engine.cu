@@ -540,6 +540,7 @@ void Engine::tc_launch(const Act& x, const TcPlanes& xp, const float* whi, const
     a.y = y; a.bias = bias; a.r = r; a.r_shift = r_shift; a.orow_mul = orow_mul; a.orow_off = orow_off;
     a.alpha = alpha; a.accum = accum;
     a.stats = stats;
+    a.part = part_; a.part_cap = part_floats_;   // split-K scratch, shared with the weight gradients
     conv_fwd_tc(a, tc_mode(), st);
 }
 
@@ -672,6 +673,7 @@ void Engine::convT_dgrad(const UpP& u, const Act& dy, const Act& dx, cudaStream_
         a.taps = pk.taps; a.Co = u.cin;
         a.p = -pk.u_min; a.d = 1; a.No = dx.L; a.o_base = 0;
         a.y = dx;
+        a.part = part_; a.part_cap = part_floats_;
         const int id = prof_begin(PROF_CONV_TC, 2.0 * u.cin * u.cout * u.k * (double)dx.L * dx.B, st);
         conv_fwd_tc(a, tc_mode(), st);
         prof_end(id, st);

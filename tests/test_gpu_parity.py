@@ -102,6 +102,7 @@ TC_CONV_CASES = [  # (B, Ci, L, Co, k, pad, dil): stride-1 shapes the tensor-cor
     (2, 64, 129, 96, 1, 0, 1),         # 1x1, partial M tile
     (8, 128, 24000, 128, 7, 9, 3),     # several 256-position tiles per persistent CTA
     (16, 96, 3000, 128, 3, 1, 1),      # odd promotion-group count per tile, two tiles on some CTAs
+    (1, 1024, 64, 1024, 3, 1, 1),      # config-0 backbone: 8 output tiles, K split over idle SMs
 ]
 # tf32x3 with promoted accumulation is fp32-grade; bf16 is one bf16 product
 TC_TOL = {"tf32x3": 1e-5, "bf16x3": 1e-4, "bf16": 1e-2}
