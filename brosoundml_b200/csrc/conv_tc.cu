@@ -413,28 +413,42 @@ __global__ void __launch_bounds__(FCfg<MODE, NPT>::THREADS, 1)
 
 // Split-K epilogue: sums the ksplit partial tiles of each output element in a
 // fixed order and applies the forward kernel's epilogue (bias, residual, scale,
-// accumulation, output statistics). One thread per output channel, a strip of
-// FR_ROWS positions per CTA.
-constexpr int FR_ROWS = 16;
+// accumulation, output statistics). One thread per output channel over a strip
+// of FR_ROWS positions, whose loads are all issued before the first store.
+constexpr int FR_ROWS = 8;
 __global__ void __launch_bounds__(128) fwd_split_reduce_kernel(const FArgs a) {
     const int co = blockIdx.y * 128 + threadIdx.x, b = blockIdx.z;
     if (co >= a.Co) return;
-    const int o0 = blockIdx.x * FR_ROWS, o1 = min(a.No, o0 + FR_ROWS);
+    const int o0 = blockIdx.x * FR_ROWS;
     const int64_t sstride = (int64_t)a.nb * a.No * a.Co;
-    const float* pb = a.part + ((int64_t)b * a.No) * a.Co + co;
+    const float* __restrict__ pb = a.part + ((int64_t)b * a.No + o0) * a.Co + co;
+    float acc[FR_ROWS], t[FR_ROWS], u[FR_ROWS];
+    int row[FR_ROWS];
+    bool in[FR_ROWS];
+#pragma unroll
+    for (int r = 0; r < FR_ROWS; ++r) {
+        row[r] = (o0 + r + a.o_base) * a.orow_mul + a.orow_off;
+        in[r] = o0 + r < a.No && row[r] >= 0 && row[r] < a.y_rows;
+        acc[r] = 0.f;
+    }
+    for (int k = 0; k < a.ksplit; ++k)
+#pragma unroll
+        for (int r = 0; r < FR_ROWS; ++r)
+            if (in[r]) acc[r] += pb[k * sstride + (int64_t)r * a.Co];
     const float bv = a.bias ? a.bias[co] : 0.f;
     const float* rb = a.r ? a.r + (int64_t)b * a.r_bs + co : nullptr;
     float* yb = a.y + (int64_t)b * a.y_bs + co;
+#pragma unroll
+    for (int r = 0; r < FR_ROWS; ++r) {
+        t[r] = (rb && in[r]) ? rb[(int64_t)(row[r] >> a.r_shift) * a.r_ld] : 0.f;
+        u[r] = (a.accum && in[r]) ? yb[(int64_t)row[r] * a.y_ld] : 0.f;
+    }
     double s1 = 0.0, s2 = 0.0;
-    for (int o = o0; o < o1; ++o) {
-        const int row = (o + a.o_base) * a.orow_mul + a.orow_off;
-        if (row < 0 || row >= a.y_rows) continue;
-        float acc = 0.f;
-        for (int k = 0; k < a.ksplit; ++k) acc += pb[k * sstride + (int64_t)o * a.Co];
-        const float t = rb ? rb[(int64_t)(row >> a.r_shift) * a.r_ld] : 0.f;
-        const float u = a.accum ? yb[(int64_t)row * a.y_ld] : 0.f;
-        const float val = (acc + bv + t) * a.alpha + u;
-        yb[(int64_t)row * a.y_ld] = val;
+#pragma unroll
+    for (int r = 0; r < FR_ROWS; ++r) {
+        if (!in[r]) continue;
+        const float val = (acc[r] + bv + t[r]) * a.alpha + u[r];
+        yb[(int64_t)row[r] * a.y_ld] = val;
         s1 += val;
         s2 = fma((double)val, (double)val, s2);
     }
