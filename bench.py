@@ -31,8 +31,8 @@ sys.path.insert(0, ROOT)
 
 METRIC = "Kokoro decoder fwd+bwd audio-seconds/sec at 1/2/4/8 B200; % tensor/HBM roofline"
 # ncu capture (gpu__time_duration, dram__bytes_read/write) of conv_fwd_tc_kernel<tf32x3> on the probe
-# case B=16, Ci=Co=128, L=24001, k=7, d=3: 452.3 us, 394.8 MB read + 163.0 MB written
-NCU_CONV_FWD_TC = {"dram_bytes": 394.8e6 + 163.0e6, "flops": 2.0 * 16 * 128 * 128 * 7 * 24001}
+# case B=16, Ci=Co=128, L=24001, k=7, d=3: 443.7 us, 395.0 MB read + 162.7 MB written
+NCU_CONV_FWD_TC = {"dram_bytes": 395.0e6 + 162.7e6, "flops": 2.0 * 16 * 128 * 128 * 7 * 24001}
 UNIT = "audio-s/s"
 WORKLOADS = {
     # name: (B per GPU, T asr frames (c1: samples L), description)

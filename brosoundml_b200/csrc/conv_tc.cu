@@ -70,14 +70,15 @@ struct Fmt {
     static constexpr uint32_t KIND = F32 ? 2u : 1u;       // instruction-descriptor A/B format
 };
 
-template <int MODE, int NP>
+template <int MODE, int NP, int NH_>
 struct FCfg {
     static constexpr int BKE = Fmt<MODE>::BKE;            // channels per 128-byte row
     static constexpr int PLANES = Fmt<MODE>::PLANES;
     static constexpr int NPOS = NP;                        // positions per tile (MMA N): 256, 224 or 192
-    static constexpr int HALF = NP / 2;                    // columns per epilogue warp (multiple of 16)
+    static constexpr int NH = NH_;                         // column groups per TMEM lane quarter (2 or 4)
+    static constexpr int HALF = NP / NH;                   // columns per epilogue warp (multiple of 8)
     static constexpr int WT_BYTES = PLANES * TILE_BYTES;   // one weight stage: 128 co x 128 B per plane
-    static constexpr int NEPI = 8;                         // epilogue warps: 4 lane quarters x 2 column halves
+    static constexpr int NEPI = 4 * NH;                    // epilogue warps: 4 lane quarters x NH column groups
     static constexpr int THREADS = 64 + NEPI * 32;
     static constexpr int MAX_SW = 8;
 };
@@ -102,14 +103,17 @@ struct FArgs {
 // Input-channel chunks [lo, hi) of split `s` of `ks` (near-equal ranges).
 __device__ __forceinline__ int split_lo(int s, int ks, int kchunks) { return (int)((int64_t)s * kchunks / ks); }
 
-// 320 threads = 10 warps, so one SM sub-partition holds 3 of them: 168
-// registers per thread at most (3 x 32 x 168 <= 16384).
-template <int MODE, int NPT>
-__global__ void __launch_bounds__(FCfg<MODE, NPT>::THREADS, 1)
+// 2 + 4*NH warps. NH = 2: 320 threads, 168 registers per thread at most (3 warps
+// per SM sub-partition); NH = 4: 576 threads, 96 registers (5 warps per
+// sub-partition). More epilogue warps shorten each warp's share of the tile-end
+// stores, which must finish before the MMAs, two promotion groups ahead, need its
+// buffer; fewer, with more registers, fold faster when a tile has many K steps.
+template <int MODE, int NPT, int NH>
+__global__ void __launch_bounds__(FCfg<MODE, NPT, NH>::THREADS, 1)
     conv_fwd_tc_kernel(const __grid_constant__ CUtensorMap mWh, const __grid_constant__ CUtensorMap mWl,
                        const __grid_constant__ CUtensorMap mXh, const __grid_constant__ CUtensorMap mXl,
                        const FArgs a) {
-    using F = FCfg<MODE, NPT>;
+    using F = FCfg<MODE, NPT, NH>;
     constexpr bool LO = Fmt<MODE>::LO, F32E = Fmt<MODE>::F32;
     constexpr int NP = F::NPOS, HC = F::HALF;
     constexpr uint32_t TCOLS = 512;   // two promotion buffers of NP fp32 columns (allocation: a power of 2)
@@ -318,12 +322,20 @@ __global__ void __launch_bounds__(FCfg<MODE, NPT>::THREADS, 1)
                 if (!ok) break;
                 tc::tc_fence_after();
 #pragma unroll
-                for (int c16 = 0; c16 < HC; c16 += 16) {
+                for (int c16 = 0; c16 + 16 <= HC; c16 += 16) {
                     uint32_t v[16];
                     tc::tmem_ld16_nowait(trow + (uint32_t)(buf * NP + c16), v);
                     tc::tmem_wait_ld();
 #pragma unroll
                     for (int j = 0; j < 16; ++j) R[c16 + j] += __uint_as_float(v[j]);
+                }
+                if (HC % 16 == 8) {
+                    constexpr int c8 = HC - 8;
+                    uint32_t v[8];
+                    tc::tmem_ld8_nowait(trow + (uint32_t)(buf * NP + c8), v);
+                    tc::tmem_wait_ld();
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) R[c8 + j] += __uint_as_float(v[j]);
                 }
                 tc::tc_fence_before();
                 __syncwarp();
@@ -878,13 +890,13 @@ int fwd_ksplit(const TcConvFwd& c, int mode, int np, int64_t cap) {
     return ks >= 2 ? (int)ks : 1;
 }
 
-template <int MODE, int NPT>
+template <int MODE, int NPT, int NH>
 void launch_fwd_np(const TcConvFwd& c, int mode, const FwdGeom& g, cudaStream_t st) {
-    using F = FCfg<MODE, NPT>;
+    using F = FCfg<MODE, NPT, NH>;
     constexpr bool LO = Fmt<MODE>::LO;
     static bool attr = false;
     if (!attr) {
-        BSML_CUDA(cudaFuncSetAttribute(conv_fwd_tc_kernel<MODE, NPT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        BSML_CUDA(cudaFuncSetAttribute(conv_fwd_tc_kernel<MODE, NPT, NH>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        SMEM_OPTIN));
         attr = true;
     }
@@ -920,7 +932,7 @@ void launch_fwd_np(const TcConvFwd& c, int mode, const FwdGeom& g, cudaStream_t 
         fail("conv_fwd_tc", "clip too long for 32-bit row offsets");
     const int grid = (int)std::min<int64_t>(tiles * a.ksplit, sm_count());
     ::bsml::count_launch();
-    conv_fwd_tc_kernel<MODE, NPT><<<grid, F::THREADS, g.smem, st>>>(mWh, mWl, mXh, mXl, a);
+    conv_fwd_tc_kernel<MODE, NPT, NH><<<grid, F::THREADS, g.smem, st>>>(mWh, mWl, mXh, mXl, a);
     BSML_LAUNCH("conv_fwd_tc");
     if (a.ksplit > 1) {
         ::bsml::count_launch();
@@ -930,15 +942,33 @@ void launch_fwd_np(const TcConvFwd& c, int mode, const FwdGeom& g, cudaStream_t 
     }
 }
 
+template <int MODE, int NH>
+void launch_fwd_nh(const TcConvFwd& c, int mode, const FwdGeom& g, cudaStream_t st) {
+    if (g.np == 256)
+        launch_fwd_np<MODE, 256, NH>(c, mode, g, st);
+    else if (g.np == 224)
+        launch_fwd_np<MODE, 224, NH>(c, mode, g, st);
+    else
+        launch_fwd_np<MODE, 192, NH>(c, mode, g, st);
+}
+
+// Epilogue width by the K steps of a work item (taps x input-channel chunks, after
+// any split): up to 32 steps the tile-end stores recur often enough to stall the
+// MMAs and 16 epilogue warps win (measured: C128 k3 -8 %, k7 -2 %, BF16x3 k7 -8 %);
+// longer K loops keep 8 warps with more registers (C128 k11 d5 and C1024 k3 lose
+// 1-4 % with 16).
+constexpr int NH4_MAX_KSTEPS = 32;
+
 template <int MODE>
 void launch_fwd(const TcConvFwd& c, int mode, cudaStream_t st) {
     const FwdGeom g = fwd_geom(Fmt<MODE>::PLANES, (c.taps - 1) * c.d);
-    if (g.np == 256)
-        launch_fwd_np<MODE, 256>(c, mode, g, st);
-    else if (g.np == 224)
-        launch_fwd_np<MODE, 224>(c, mode, g, st);
+    const int kchunks = (int)ceil_div(c.Ci, Fmt<MODE>::BKE);
+    const int ks = c.part ? fwd_ksplit(c, mode, g.np, c.part_cap) : 1;
+    const int64_t ksteps = (int64_t)c.taps * ceil_div(kchunks, ks);
+    if (ksteps <= NH4_MAX_KSTEPS)
+        launch_fwd_nh<MODE, 4>(c, mode, g, st);
     else
-        launch_fwd_np<MODE, 192>(c, mode, g, st);
+        launch_fwd_nh<MODE, 2>(c, mode, g, st);
 }
 
 template <int MODE>
