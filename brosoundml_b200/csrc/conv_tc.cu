@@ -355,34 +355,28 @@ __global__ void __launch_bounds__(FCfg<MODE, NPT, NH>::THREADS, 1)
             }
             if (mrow < a.Co) {
                 const float bv = a.bias ? a.bias[mrow] : 0.f;
-                // ST: also the output statistics: fp32 sums over groups of four columns,
-                // each group's sums added in double (one conversion per four outputs);
-                // without statistics no double-precision work is issued at all
+                // ST: also the output statistics. They are summed in fp32 about a shift c
+                // (this thread's first column), so the sums stay at the scale of the
+                // spread rather than of the mean, and moved to double once per tile: per
+                // output one subtract and two fp32 adds, no float-to-double conversion
+                // (those run on the narrow XU pipe and throttled the epilogue). Without
+                // statistics no such work is issued at all.
                 auto store = [&](auto st_tag) {
                     constexpr bool ST = decltype(st_tag)::value;
-                    double s1 = 0.0, s2 = 0.0;
+                    const float c = (R[0] + bv) * a.alpha;
                     float g1 = 0.f, g2 = 0.f;
                     auto emit = [&](int jj, float val) {
                         yb[(row0 + jj * a.orow_mul) * a.y_ld] = val;
                         if (ST) {
-                            g1 += val;
-                            g2 = fmaf(val, val, g2);
-                        }
-                    };
-                    auto flush = [&](int jj) {
-                        if (ST && (jj & 3) == 3) {
-                            s1 += (double)g1;
-                            s2 += (double)g2;
-                            g1 = 0.f;
-                            g2 = 0.f;
+                            const float dv = val - c;
+                            g1 += dv;
+                            g2 = fmaf(dv, dv, g2);
                         }
                     };
                     if (!a.accum) {
 #pragma unroll
-                        for (int jj = 0; jj < HC; ++jj) {
+                        for (int jj = 0; jj < HC; ++jj)
                             if (jj >= jlo && jj < jhi) emit(jj, (R[jj] + bv) * a.alpha);
-                            flush(jj);
-                        }
                     } else {
                         // EB columns at a time: their reads are all issued before their stores
                         constexpr int EB = 8;
@@ -398,13 +392,14 @@ __global__ void __launch_bounds__(FCfg<MODE, NPT, NH>::THREADS, 1)
                             for (int j = 0; j < EB; ++j) {
                                 const int jj = c16 + j;
                                 if (jj >= jlo && jj < jhi) emit(jj, (R[jj] + bv) * a.alpha + u[j]);
-                                flush(jj);
                             }
                         }
                     }
                     if (ST) {
-                        atomicAdd(&a.stats[((int64_t)b * a.Co + mrow) * 2], s1);
-                        atomicAdd(&a.stats[((int64_t)b * a.Co + mrow) * 2 + 1], s2);
+                        // sum (v) = sum (v - c) + n c;  sum (v^2) = sum (v - c)^2 + 2 c sum (v - c) + n c^2
+                        const double n = (double)max(jhi - jlo, 0), cd = c, d1 = g1;
+                        atomicAdd(&a.stats[((int64_t)b * a.Co + mrow) * 2], d1 + n * cd);
+                        atomicAdd(&a.stats[((int64_t)b * a.Co + mrow) * 2 + 1], (double)g2 + cd * (2.0 * d1 + n * cd));
                     }
                 };
                 if (a.stats)
