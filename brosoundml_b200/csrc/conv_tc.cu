@@ -493,7 +493,7 @@ struct WArgs {
     int wrows;        // X window rows per column block (KROWS + d, rounded up to 8)
     int stage_bytes;  // A_BYTES + X window (all planes)
     int stages;
-    float* part;      // [split][Co][Ci][tap]
+    float* part;      // [split][tap][Ci][Co]
 };
 
 template <int MODE>
@@ -668,11 +668,12 @@ __global__ void __launch_bounds__(WCfg<MODE>::THREADS, 1)
         }
         const bool valid = ok && *(volatile int*)err == tc::TC_OK;
         if (valid && u < ntap && mrow < a.Co) {
-            // partials [split][co][ci][tap]: the reduce then reads them in dW order
-            float* pp = a.part + (((int64_t)blockIdx.z * a.Co + mrow) * a.Ci + n0) * a.taps + t0 + u;
+            // partials [split][tap][ci][co]: a warp's 32 lanes (consecutive co) store
+            // one 128-byte line per column; the reduce reorders into dW
+            float* pp = a.part + (((int64_t)blockIdx.z * a.taps + t0 + u) * a.Ci + n0) * a.Co + mrow;
 #pragma unroll
             for (int j = 0; j < BN; ++j)
-                if (n0 + j < a.Ci) pp[(int64_t)j * a.taps] = R[j];
+                if (n0 + j < a.Ci) pp[(int64_t)j * a.Co] = R[j];
         }
     }
     tc::tc_fence_before();
@@ -769,31 +770,36 @@ __global__ void pack_w_batch_kernel(const float* params, const PackJob* jobs, in
     }
 }
 
-// dW[(co*Ci + ci)*k + t] (+)= sum_split part[split][co][ci][t]
+// dW[(co*Ci + ci)*k + t] (+)= sum_split part[split][t][ci][co]; threads run in
+// partial order (coalesced reads of the large partials, scattered writes of dW)
 __global__ void wgrad_reduce_kernel(const float* part, int splits, int taps, int Co, int Ci, float* dW, int accum) {
     const int64_t n = (int64_t)Co * Ci * taps;
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const int co = (int)(i % Co);
+        const int64_t q = i / Co;
+        const int ci = (int)(q % Ci), t = (int)(q / Ci);
         const double s = sum_strided(part + i, n, splits);
-        dW[i] = (float)(accum ? dW[i] + s : s);
+        const int64_t o = ((int64_t)co * Ci + ci) * taps + t;
+        dW[o] = (float)(accum ? dW[o] + s : s);
     }
 }
 
 // ConvTranspose1d weight gradient from the row-packed partials:
-// dW[(ci*CoT + co)*k + t] (+)= sum_split part[split][ci][j*CoT + co][tau], t - p = (tau + u_min)*s + j
+// dW[(ci*CoT + co)*k + t] (+)= sum_split part[split][tau][j*CoT + co][ci], t - p = (tau + u_min)*s + j.
+// Threads run in partial order; (tau, j) pairs whose t falls outside [0, k) carry no weight.
 __global__ void wgrad_reduce_convT_kernel(const float* part, int splits, int taps, int M, int N, int CoT, int k, int s,
                                           int p, int u_min, float* dW, int accum) {
-    const int64_t n = (int64_t)M * CoT * k;
-    const int64_t stride_split = (int64_t)taps * M * N;
+    const int64_t n = (int64_t)taps * N * M;
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
-        const int t = (int)(i % k);
-        const int64_t q = i / k;
-        const int co = (int)(q % CoT), m = (int)(q / CoT);
-        const int tp = t - p;
-        const int u = tp >= 0 ? tp / s : -((-tp + s - 1) / s);
-        const int j = tp - u * s, tau = u - u_min;
-        const int64_t src = ((int64_t)m * N + (int64_t)j * CoT + co) * taps + tau;
-        const double acc = sum_strided(part + src, stride_split, splits);
-        dW[i] = (float)(accum ? dW[i] + acc : acc);
+        const int m = (int)(i % M);
+        const int64_t q = i / M;
+        const int nn = (int)(q % N), tau = (int)(q / N);
+        const int j = nn / CoT, co = nn - j * CoT;
+        const int t = (tau + u_min) * s + j + p;
+        if (t < 0 || t >= k) continue;
+        const double acc = sum_strided(part + i, n, splits);
+        const int64_t o = ((int64_t)m * CoT + co) * k + t;
+        dW[o] = (float)(accum ? dW[o] + acc : acc);
     }
 }
 
@@ -997,9 +1003,11 @@ void launch_wgrad(const TcConvWgrad& c, int mode, float* part, int64_t part_cap,
     a.n_pairs = (int)ceil_div(c.taps, 2);
     a.chunks_pc = (int)ceil_div(c.Lo, CF::KROWS);
     a.chunks_total = a.chunks_pc * c.B;
-    // ~2 full waves of equal CTAs, each with >= 8 chunks of K, within the partial budget
+    // one full wave of equal CTAs (one per SM: a second wave repeats each CTA's pipeline
+    // fill and epilogue, measured 2-9 % slower), each with >= 8 chunks of K, within the
+    // partial budget
     const int64_t tiles = ceil_div(c.Co, BM) * a.n_ci_tiles * a.n_pairs;
-    int64_t splits = std::max<int64_t>(1, 2 * sm_count() / tiles);
+    int64_t splits = std::max<int64_t>(1, sm_count() / tiles);
     splits = std::min<int64_t>(splits, ceil_div(a.chunks_total, 8));
     splits = std::min<int64_t>(splits, part_cap / ((int64_t)c.taps * c.Co * c.Ci));
     if (splits < 1) fail("conv_wgrad_tc", "split-K partial buffer too small");
@@ -1014,7 +1022,7 @@ void launch_wgrad(const TcConvWgrad& c, int mode, float* part, int64_t part_cap,
     if (c.ct_s > 0) {
         const ConvTPack pk = convT_pack(c.ct_k, c.ct_s, c.ct_p);
         if (pk.taps != c.taps || c.Ci != c.ct_s * c.ct_Co) fail("conv_wgrad_tc", "inconsistent ConvTranspose1d packing");
-        wgrad_reduce_convT_kernel<<<grid_for((int64_t)c.Co * c.ct_Co * c.ct_k), 256, 0, st>>>(
+        wgrad_reduce_convT_kernel<<<grid_for((int64_t)c.taps * c.Ci * c.Co), 256, 0, st>>>(
             part, (int)splits, c.taps, c.Co, c.Ci, c.ct_Co, c.ct_k, c.ct_s, c.ct_p, pk.u_min, c.dW, c.accum ? 1 : 0);
     } else {
         wgrad_reduce_kernel<<<grid_for((int64_t)c.Co * c.Ci * c.taps), 256, 0, st>>>(part, (int)splits, c.taps, c.Co,
