@@ -100,9 +100,12 @@ SIGNATURES = {
     "bsml_st_metadata": ([_P, ctypes.c_char_p, ctypes.c_char_p, _I], _I),
     "bsml_params_from_safetensors": ([_P, _P, _I, ctypes.c_char_p, _P, _L], _I),
     "bsml_nccl_unique_id": ([_P], _I),
+    "bsml_nccl_version": ([ctypes.POINTER(_I)], _I),
     "bsml_nccl_comm_init": ([_I, _P, _I, _I, ctypes.POINTER(_P)], _I),
+    "bsml_nccl_comm_init_timeout": ([_I, _P, _I, _I, _I, ctypes.POINTER(_P)], _I),
     "bsml_nccl_comm_destroy": ([_P], _I),
     "bsml_allreduce_grads": ([_P, _P, _L, _I, _P], _I),
+    "bsml_nccl_sync": ([_P, _P], _I),
     "bsml_graph_begin": ([_P], _I),
     "bsml_graph_end": ([_P, ctypes.POINTER(_P)], _I),
     "bsml_graph_launch": ([_P, _P], _I),
@@ -136,6 +139,8 @@ SIGNATURES = {
     "bsml_istft_forward": ([_P, _P, _I, _I, _I, _I, _P, _P], _I),
     "bsml_istft_backward": ([_P, _I, _I, _I, _I, _P, _P, _P], _I),
     "bsml_harmonic_source": ([_CFG, _P, _I, _I, _P, _P, _P, _P], _I),
+    "bsml_harmonic_source_mode": ([_CFG, _P, _I, _I, _P, _P, _P, _I, _P], _I),
+    "bsml_decoder_set_phase_mode": ([_P, _I], _I),
     "bsml_lora_create": ([_P, _I, _F, ctypes.c_uint64, ctypes.POINTER(_P)], _I),
     "bsml_lora_destroy": ([_P], None),
     "bsml_lora_layout": ([_P, ctypes.POINTER(_L), ctypes.POINTER(_I), ctypes.POINTER(_I), ctypes.POINTER(_I),

@@ -69,7 +69,12 @@ void need(bool ok, const char* where, const char* why) {
     if (!ok) bsml::fail(where, why);
 }
 
-int conv_out(int L, int k, int s, int p, int d) { return (L + 2 * p - d * (k - 1) - 1) / s + 1; }
+// output length of a conv; 0 (rejected by the callers) when the padded input is
+// shorter than the dilated kernel (a negative numerator must not truncate to 0)
+int conv_out(int L, int k, int s, int p, int d) {
+    const int64_t num = (int64_t)L + 2 * (int64_t)p - (int64_t)d * (k - 1) - 1;
+    return (num < 0 || s <= 0) ? 0 : (int)(num / s + 1);
+}
 
 std::atomic<int> g_atom_math{BSML_MATH_FP32_SIMT};
 
@@ -604,11 +609,16 @@ int bsml_nccl_unique_id(void* id) {
     });
 }
 
-int bsml_nccl_comm_init(int nranks, const void* id, int rank, int device, void** comm) {
+int bsml_nccl_comm_init_timeout(int nranks, const void* id, int rank, int device, int timeout_ms, void** comm) {
     return guarded([&] {
         need(id != nullptr && comm != nullptr, "bsml_nccl_comm_init", "null argument");
-        *comm = bsml::nccl_comm_init(nranks, id, rank, device);
+        *comm = nullptr;
+        *comm = bsml::nccl_comm_init(nranks, id, rank, device, timeout_ms);
     });
+}
+
+int bsml_nccl_comm_init(int nranks, const void* id, int rank, int device, void** comm) {
+    return bsml_nccl_comm_init_timeout(nranks, id, rank, device, BSML_NCCL_DEFAULT_TIMEOUT_MS, comm);
 }
 
 int bsml_nccl_comm_destroy(void* comm) {
@@ -617,6 +627,17 @@ int bsml_nccl_comm_destroy(void* comm) {
 
 int bsml_allreduce_grads(void* comm, float* grads, int64_t n, int average, void* stream) {
     return guarded([&] { bsml::nccl_allreduce(comm, grads, n, average != 0, S(stream)); });
+}
+
+int bsml_nccl_sync(void* comm, void* stream) {
+    return guarded([&] { bsml::nccl_sync(comm, S(stream)); });
+}
+
+int bsml_nccl_version(int* version) {
+    return guarded([&] {
+        need(version != nullptr, "bsml_nccl_version", "null argument");
+        *version = bsml::nccl_version();
+    });
 }
 
 struct bsml_graph {
@@ -969,10 +990,12 @@ int bsml_istft_backward(const float* daudio, int B, int n_fft, int hop, int L, f
     });
 }
 
-int bsml_harmonic_source(const bsml_decoder_config* cfg, const float* F0, int B, int F, const float* l_weight,
-                         const float* l_bias, float* har, void* stream) {
+int bsml_harmonic_source_mode(const bsml_decoder_config* cfg, const float* F0, int B, int F, const float* l_weight,
+                              const float* l_bias, float* har, int phase_mode, void* stream) {
     return guarded([&] {
         need(cfg && F0 && l_weight && l_bias && har && B > 0 && F > 0, "bsml_harmonic_source", "bad argument");
+        need(phase_mode == BSML_PHASE_FP32_RUNNING || phase_mode == BSML_PHASE_EXACT, "bsml_harmonic_source",
+             "unknown phase mode");
         cudaStream_t st = S(stream);
         Scratch sc(st);
         const int S_len = F * cfg->upsample_scale;
@@ -980,8 +1003,20 @@ int bsml_harmonic_source(const bsml_decoder_config* cfg, const float* F0, int B,
         bsml::Act ha = sc.act(B, frames, cfg->n_fft + 2);
         bsml::harmonic_source(F0, B, F, cfg->upsample_scale, cfg->harmonic_num, cfg->sample_rate, cfg->n_fft, cfg->hop,
                               l_weight, l_bias, sc.d((int64_t)B * (cfg->harmonic_num + 1) * F), sc.f((int64_t)B * S_len),
-                              ha, st);
+                              ha, st, phase_mode);
         bsml::cl_to_ncl(ha, har, st);
+    });
+}
+
+int bsml_harmonic_source(const bsml_decoder_config* cfg, const float* F0, int B, int F, const float* l_weight,
+                         const float* l_bias, float* har, void* stream) {
+    return bsml_harmonic_source_mode(cfg, F0, B, F, l_weight, l_bias, har, BSML_PHASE_FP32_RUNNING, stream);
+}
+
+int bsml_decoder_set_phase_mode(bsml_decoder* d, int phase_mode) {
+    return guarded([&] {
+        need(d != nullptr, "bsml_decoder_set_phase_mode", "null handle");
+        d->eng->set_phase_mode(phase_mode);
     });
 }
 

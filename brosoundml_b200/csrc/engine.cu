@@ -38,7 +38,10 @@ Act flat_input(const float* p, int B, int L) {   // (B, L) as channels-last with
     return a;
 }
 
-int conv_out(int L, const ConvP& c) { return (L + 2 * c.p - c.d * (c.k - 1) - 1) / c.s + 1; }
+int conv_out(int L, const ConvP& c) {
+    const int64_t num = (int64_t)L + 2 * (int64_t)c.p - (int64_t)c.d * (c.k - 1) - 1;
+    return num < 0 ? 0 : (int)(num / c.s + 1);
+}
 
 }  // namespace
 
@@ -135,11 +138,18 @@ void Engine::init() {
     for (size_t a = 0; a < lay_.aff_C.size(); ++a)
         for (int o = 0; o < 2 * lay_.aff_C[a]; ++o) re[q++] = (int)a;
     BSML_CUDA(cudaMemcpy(fc_row_entry_, re.data(), sizeof(int) * fc_rows_, cudaMemcpyHostToDevice));
+    // the harmonic source depends only on F0: it runs on a second stream beside the backbone
+    BSML_CUDA(cudaStreamCreateWithFlags(&side_, cudaStreamNonBlocking));
+    BSML_CUDA(cudaEventCreateWithFlags(&ev_fork_, cudaEventDisableTiming));
+    BSML_CUDA(cudaEventCreateWithFlags(&ev_join_, cudaEventDisableTiming));
 }
 
 Engine::~Engine() {
     cudaSetDevice(device_);
     for (auto ev : ev_pool_) cudaEventDestroy(ev);
+    if (ev_fork_) cudaEventDestroy(ev_fork_);
+    if (ev_join_) cudaEventDestroy(ev_join_);
+    if (side_) cudaStreamDestroy(side_);
     cudaFree(wp_mem_);
     cudaFree(tcw_mem_);
     cudaFree(ws_);
@@ -155,6 +165,12 @@ void Engine::set_math(int m) {
 }
 
 void Engine::set_profiling(bool on) { prof_on_ = on; }
+
+void Engine::set_phase_mode(int m) {
+    if (m != PHASE_FP32_RUNNING && m != PHASE_EXACT)
+        fail("bsml_decoder_set_phase_mode", "unknown phase mode " + std::to_string(m));
+    phase_mode_ = m;
+}
 
 int Engine::prof_begin(int cls, double work, cudaStream_t st) {
     if (!prof_on_) return -1;
@@ -964,6 +980,14 @@ void Engine::forward(int B, int T, const float* params, const float* asr, const 
     F0_ = F0_copy_;
     N_ = N_copy_;
     style_ = style ? style_copy_ : nullptr;
+    if (!have_har_) {
+        // har is first read by the generator; the source runs on the side stream meanwhile
+        BSML_CUDA(cudaEventRecord(ev_fork_, st));
+        BSML_CUDA(cudaStreamWaitEvent(side_, ev_fork_, 0));
+        harmonic_source(F0_copy_, B, 2 * T, cf.upsample_scale, cf.harmonic_num, cf.sample_rate, cf.n_fft, cf.hop,
+                        params_ + lay_.llin_w, params_ + lay_.llin_b, hs_phase_, hs_src_, har_, side_, phase_mode_);
+        BSML_CUDA(cudaEventRecord(ev_join_, side_));
+    }
     ref_mode_ = aff_in != nullptr;
     fwd_done_ = false;
     pack_weights(st);
@@ -1003,12 +1027,10 @@ void Engine::forward(int B, int T, const float* params, const float* asr, const 
         }
     }
     // har
-    if (have_har_) {
+    if (have_har_)
         ncl_to_cl(har, har_, st);
-    } else {
-        harmonic_source(F0, B, 2 * T, cf.upsample_scale, cf.harmonic_num, cf.sample_rate, cf.n_fft, cf.hop,
-                        params_ + lay_.llin_w, params_ + lay_.llin_b, hs_phase_, hs_src_, har_, st);
-    }
+    else
+        BSML_CUDA(cudaStreamWaitEvent(st, ev_join_, 0));
     // generator (kokoro_decoder_backward.cpp:592-667)
     const int U = cf.n_ups, K = cf.n_kernels;
     for (int i = 0; i < U; ++i) {

@@ -46,6 +46,8 @@ class Engine {
         PROF_NORM_BWD = BSML_PROF_NORM_BWD, PROF_N = BSML_PROF_CLASSES
     };
     void set_profiling(bool on);
+    // harmonic-source phase arithmetic: PHASE_FP32_RUNNING (the reference's, default) or PHASE_EXACT
+    void set_phase_mode(int m);
     void read_profile(double* out);   // PROF_N * 3 doubles, then clears
     // per launch in issue order: (class, work, ms), at most max_records; then clears
     void read_profile_records(double* out, int max_records, int* n_records);
@@ -157,6 +159,9 @@ class Engine {
 
     Layout lay_;
     int device_ = 0;
+    int phase_mode_ = PHASE_FP32_RUNNING;
+    cudaStream_t side_ = nullptr;     // harmonic source, forked from and joined to the caller's stream
+    cudaEvent_t ev_fork_ = nullptr, ev_join_ = nullptr;
     int math_ = BSML_MATH_FP32_SIMT;
 
     // packed weights (persistent, independent of B/T)

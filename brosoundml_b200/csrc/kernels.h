@@ -143,10 +143,12 @@ void istft_polar_bwd(const float* daudio, const Act& post, int n_fft, int hop, c
 void istft_bwd_ncl(const float* daudio, int B, int L, int n_fft, int hop, float* dre, float* dim, cudaStream_t st);
 void istft_fwd_ncl(const float* re, const float* im, int B, int L, int n_fft, int hop, float* audio,
                    float* spec_scratch, cudaStream_t st);
-// F0 (B, F) -> har Act (B, frames, 2*nf); scratch: B*(harmonic_num+1)*F doubles + B*F*scale floats
+// F0 (B, F) -> har Act (B, frames, 2*nf); scratch: B*(harmonic_num+1)*F doubles + B*F*scale floats.
+// phase_mode: PHASE_FP32_RUNNING (the reference's fp32 per-sample accumulator) or PHASE_EXACT.
+enum { PHASE_FP32_RUNNING = 0, PHASE_EXACT = 1 };
 void harmonic_source(const float* F0, int B, int F, int scale, int harmonic_num, int sample_rate, int n_fft, int hop,
                      const float* lw, const float* lb, double* phase_start, float* src, const Act& har,
-                     cudaStream_t st);
+                     cudaStream_t st, int phase_mode = PHASE_FP32_RUNNING);
 
 // ── loss and optimiser ───────────────────────────────────────────────────────
 void l1_loss(const float* a, const float* t, int64_t n, float* loss, float* da, double* acc, cudaStream_t st);

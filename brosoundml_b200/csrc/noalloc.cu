@@ -48,7 +48,10 @@ extern "C" int bsml_conv1d_backward_weight_noalloc(const float* dy, const float*
                                                     void* stream) {
     try {
         const char* where = "bsml_conv1d_backward_weight_noalloc";
-        const int Lo = (L + 2 * pad - dil * (k - 1) - 1) / stride + 1;
+        // a padded input shorter than the dilated kernel has no output (the numerator
+        // is negative; C division would truncate it to an output of length 1)
+        const int64_t num = (int64_t)L + 2 * (int64_t)pad - (int64_t)dil * (k - 1) - 1;
+        const int Lo = (num < 0 || stride <= 0) ? 0 : (int)(num / stride + 1);
         if (!dy || !x || !dW || B <= 0 || Ci <= 0 || Co <= 0 || k <= 0 || stride <= 0 || dil <= 0 || Lo <= 0)
             bsml::fail(where, "bad argument");
         bsml::Act ga, xa;

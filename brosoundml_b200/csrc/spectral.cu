@@ -153,8 +153,82 @@ __global__ void ncl_pair_to_spec_kernel(const float* re, const float* im, int B,
 }
 
 // ── harmonic source (kokoro_modules.cpp:1574-1665)
-// Phase at the start of every F0 frame, per (clip, harmonic): exact running sum
-// of the per-sample float increments, reduced mod 2*pi, in double.
+//
+// Two phase modes. PHASE_FP32_RUNNING (default) is the reference's own
+// arithmetic (kokoro_modules.cpp:1601-1616): per harmonic an fp32 accumulator,
+// per sample phase = fl(phase + omega) and, when it exceeds 2*pi (the float
+// constant), one fp32 subtraction of it; omega = fl(fl(fl(2pi * (h+1)) * f0) / sr).
+// Every rounding is pinned with the _rn intrinsics, so the phase sequence is the
+// reference's bit for bit. The recurrence is serial: hs_phase32_kernel runs one
+// thread per (clip, harmonic) through all samples and records the accumulator at
+// each F0 frame start; hs_source32_kernel then replays one frame per thread from
+// those starts (the same fp32 steps, so the same values) and forms the sines.
+// PHASE_EXACT forms each frame's start phase exactly in double instead (an
+// accurate sine source whose phase does not drift with clip length).
+constexpr float kTwoPiF = 6.28318530717958647692f;
+constexpr int MAX_HARM = 16;
+
+__device__ __forceinline__ float hs_omega(int h, float f0, float sr) {
+    return __fdiv_rn(__fmul_rn(__fmul_rn(kTwoPiF, (float)(h + 1)), f0), sr);
+}
+__device__ __forceinline__ float hs_step(float p, float om) {
+    p = __fadd_rn(p, om);
+    return p > kTwoPiF ? __fsub_rn(p, kTwoPiF) : p;
+}
+
+__global__ void hs_phase32_kernel(const float* F0, int B, int F, int scale, int H, float sr, float* start) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= B * H) return;
+    const int b = i / H, h = i % H;
+    float p = 0.f;
+    for (int f = 0; f < F; ++f) {
+        start[(int64_t)i * F + f] = p;
+        const float om = hs_omega(h, F0[(int64_t)b * F + f], sr);
+        int j = 0;
+        for (; j + 4 <= scale; j += 4) {
+            p = hs_step(p, om);
+            p = hs_step(p, om);
+            p = hs_step(p, om);
+            p = hs_step(p, om);
+        }
+        for (; j < scale; ++j) p = hs_step(p, om);
+    }
+}
+
+// one thread per (clip, frame): H running phases from the frame start, sine
+// mixture -> l_linear -> tanh for the frame's samples
+__global__ void hs_source32_kernel(const float* F0, int B, int F, int scale, int H, float sr, const float* start,
+                                   const float* lw, const float* lb, float* src) {
+    const int64_t n = (int64_t)B * F;
+    const int64_t S = (int64_t)F * scale;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const int b = (int)(i / F), f = (int)(i % F);
+        const float f0 = F0[i];
+        const float uv = f0 > 0.f ? 1.f : 0.f;
+        float p[MAX_HARM], om[MAX_HARM], w[MAX_HARM];
+#pragma unroll
+        for (int h = 0; h < MAX_HARM; ++h) {
+            p[h] = h < H ? start[((int64_t)b * H + h) * F + f] : 0.f;
+            om[h] = h < H ? hs_omega(h, f0, sr) : 0.f;
+            w[h] = h < H ? lw[h] : 0.f;
+        }
+        const float bias = lb[0];
+        float* out = src + (int64_t)b * S + (int64_t)f * scale;
+        for (int j = 0; j < scale; ++j) {
+            float mf = 0.f;
+#pragma unroll
+            for (int h = 0; h < MAX_HARM; ++h)
+                if (h < H) {
+                    p[h] = hs_step(p[h], om[h]);
+                    mf += w[h] * (sinf(p[h]) * 0.1f * uv);
+                }
+            out[j] = tanhf(mf + bias);
+        }
+    }
+}
+
+// PHASE_EXACT: phase at the start of every F0 frame, per (clip, harmonic), as the
+// exact running sum of the per-sample float increments, reduced mod 2*pi in double.
 __global__ void hs_phase_kernel(const float* F0, int B, int F, int scale, int H, float sr, double* start) {
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= B * H) return;
@@ -163,12 +237,12 @@ __global__ void hs_phase_kernel(const float* F0, int B, int F, int scale, int H,
     double acc = 0.0;
     for (int f = 0; f < F; ++f) {
         start[(int64_t)i * F + f] = acc;
-        const float omega = 6.28318530717958647692f * (float)(h + 1) * F0[(int64_t)b * F + f] / sr;
+        const float omega = hs_omega(h, F0[(int64_t)b * F + f], sr);
         acc = fmod(acc + (double)scale * (double)omega, two_pi);
     }
 }
 
-// sine mixture -> l_linear -> tanh, one thread per sample
+// PHASE_EXACT: sine mixture -> l_linear -> tanh, one thread per sample
 __global__ void hs_source_kernel(const float* F0, int B, int F, int scale, int H, float sr, const double* start,
                                  const float* lw, const float* lb, float* src) {
     const int64_t S = (int64_t)F * scale;
@@ -183,7 +257,7 @@ __global__ void hs_source_kernel(const float* F0, int B, int F, int scale, int H
         const float uv = f0 > 0.f ? 1.f : 0.f;
         float mf = 0.f;
         for (int h = 0; h < H; ++h) {
-            const float omega = 6.28318530717958647692f * (float)(h + 1) * f0 / sr;
+            const float omega = hs_omega(h, f0, sr);
             const double ph = fmod(start[((int64_t)b * H + h) * F + f] + (double)(j + 1) * (double)omega, two_pi);
             mf += lw[h] * (sinf((float)ph) * 0.1f * uv);
         }
@@ -293,14 +367,28 @@ void istft_fwd_ncl(const float* re, const float* im, int B, int L, int n_fft, in
 
 void harmonic_source(const float* F0, int B, int F, int scale, int harmonic_num, int sample_rate, int n_fft, int hop,
                      const float* lw, const float* lb, double* phase_start, float* src, const Act& har,
-                     cudaStream_t st) {
+                     cudaStream_t st, int phase_mode) {
     if (n_fft > MAX_NFFT) fail("harmonic_source", "n_fft above 64 is not supported");
     const int H = harmonic_num + 1;
-    ::bsml::count_launch();
-    hs_phase_kernel<<<(unsigned)ceil_div(B * H, 64), 64, 0, st>>>(F0, B, F, scale, H, (float)sample_rate, phase_start);
+    if (H > MAX_HARM) fail("harmonic_source", "harmonic_num above 15 is not supported");
     const int64_t S = (int64_t)F * scale;
-    ::bsml::count_launch();
-    hs_source_kernel<<<grid_for(B * S), 256, 0, st>>>(F0, B, F, scale, H, (float)sample_rate, phase_start, lw, lb, src);
+    if (phase_mode == PHASE_EXACT) {
+        ::bsml::count_launch();
+        hs_phase_kernel<<<(unsigned)ceil_div(B * H, 64), 64, 0, st>>>(F0, B, F, scale, H, (float)sample_rate,
+                                                                      phase_start);
+        ::bsml::count_launch();
+        hs_source_kernel<<<grid_for(B * S), 256, 0, st>>>(F0, B, F, scale, H, (float)sample_rate, phase_start, lw,
+                                                          lb, src);
+    } else {
+        // the fp32 starts fit in the B*H*F doubles reserved for them
+        float* start = reinterpret_cast<float*>(phase_start);
+        ::bsml::count_launch();
+        hs_phase32_kernel<<<(unsigned)ceil_div(B * H, 32), 32, 0, st>>>(F0, B, F, scale, H, (float)sample_rate,
+                                                                        start);
+        ::bsml::count_launch();
+        hs_source32_kernel<<<grid_for((int64_t)B * F, 64), 64, 0, st>>>(F0, B, F, scale, H, (float)sample_rate,
+                                                                        start, lw, lb, src);
+    }
     ::bsml::count_launch();
     hs_stft_kernel<<<grid_for((int64_t)B * har.L, 128), 128, 0, st>>>(src, B, (int)S, n_fft, hop, har);
     BSML_LAUNCH("harmonic_source");

@@ -15,6 +15,7 @@ import torch
 from . import _lib
 
 MATH = {"fp32": 0, "tf32x3": 1, "bf16": 2, "bf16x3": 3}
+PHASE = {"fp32": 0, "exact": 1}
 
 
 def _ptr(t):
@@ -70,6 +71,11 @@ class Decoder:
     def set_math(self, math: str) -> None:
         _lib.check(_lib.lib().bsml_decoder_set_math(self._h, MATH[math]))
         self.math = math
+
+    def set_phase_mode(self, mode: str) -> None:
+        """Harmonic-source phase arithmetic: "fp32" (the reference's running
+        accumulator, default) or "exact" (double-precision frame phases)."""
+        _lib.check(_lib.lib().bsml_decoder_set_phase_mode(self._h, PHASE[mode]))
 
     def audio_len(self, T: int, frames: int | None = None) -> int:
         c = self.cfg

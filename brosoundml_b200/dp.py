@@ -51,7 +51,7 @@ class NcclComm:
         _lib.check(_lib.lib().bsml_nccl_unique_id(ctypes.cast(buf, ctypes.c_void_p)))
         return buf.raw
 
-    def __init__(self, nranks: int, uid: bytes, rank: int, device: int):
+    def __init__(self, nranks: int, uid: bytes, rank: int, device: int, timeout_ms: int = 120000):
         import ctypes
 
         from . import _lib
@@ -60,9 +60,22 @@ class NcclComm:
             raise ValueError("brosoundml: NcclComm: the unique id has 128 bytes")
         buf = ctypes.create_string_buffer(uid, 128)
         c = ctypes.c_void_p()
-        _lib.check(_lib.lib().bsml_nccl_comm_init(nranks, ctypes.cast(buf, ctypes.c_void_p), rank, device,
-                                                  ctypes.byref(c)))
+        self._c = None
+        _lib.check(_lib.lib().bsml_nccl_comm_init_timeout(nranks, ctypes.cast(buf, ctypes.c_void_p), rank, device,
+                                                          timeout_ms, ctypes.byref(c)))
         self._c = c
+
+    def sync(self) -> None:
+        """Waits for the current stream's work, bounded by the communicator's
+        timeout; raises (and aborts the communicator) when a peer has left or
+        NCCL reports an error."""
+        import ctypes
+
+        import torch
+
+        from . import _lib
+
+        _lib.check(_lib.lib().bsml_nccl_sync(self._c, ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)))
 
     def allreduce(self, grads, average: bool = True) -> None:
         """In place over a float32 CUDA tensor, on the current stream."""

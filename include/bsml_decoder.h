@@ -218,12 +218,26 @@ int bsml_params_from_safetensors(const bsml_st* f, const bsml_param_entry* table
  * One process per GPU. Rank 0 makes a 128-byte NCCL unique id and hands it to
  * the other ranks by any channel (a file, a socket, MPI); every rank then makes
  * its communicator and, each step, all-reduces its flat gradient buffer once
- * before the optimiser step. NCCL is loaded at run time (libnccl.so.2). */
+ * before the optimiser step. NCCL (2.14 or later) is loaded at run time
+ * (libnccl.so.2). No reference counterpart: the reference has no multi-GPU path.
+ *
+ * Failure handling: the communicator is non-blocking and carries a timeout.
+ * Set-up returns an error when the other ranks do not join within it;
+ * bsml_nccl_sync waits for a step's collectives and, when they do not finish
+ * within it (a peer left between steps) or NCCL reports an error, aborts the
+ * communicator (ending its kernels still waiting on the GPU) and returns an
+ * error. An aborted communicator rejects further use; destroy it. */
+#define BSML_NCCL_DEFAULT_TIMEOUT_MS 120000
 int bsml_nccl_unique_id(void* id /* 128 bytes */);
+int bsml_nccl_version(int* version);
 int bsml_nccl_comm_init(int nranks, const void* id, int rank, int device, void** comm);
+int bsml_nccl_comm_init_timeout(int nranks, const void* id, int rank, int device, int timeout_ms, void** comm);
 int bsml_nccl_comm_destroy(void* comm);
-/* grads (n floats, device) summed over the ranks, or averaged when average != 0. */
+/* grads (n floats, device) summed over the ranks, or averaged when average != 0.
+ * Asynchronous on stream. */
 int bsml_allreduce_grads(void* comm, float* grads, int64_t n, int average, void* stream);
+/* Blocks the host until stream is idle, bounded by the communicator's timeout. */
+int bsml_nccl_sync(void* comm, void* stream);
 
 /* ── CUDA graphs (no reference counterpart: the reference runs eagerly) ────
  * Records every library call issued on `stream` between begin and end (a whole
@@ -393,9 +407,19 @@ int bsml_istft_forward(const float* re, const float* im, int B, int n_fft, int h
                        void* stream);
 int bsml_istft_backward(const float* daudio, int B, int n_fft, int hop, int L, float* dre, float* dim,
                         void* stream);
-/* HarmonicSource::forward (kokoro_modules.cpp:1574-1665): F0 (B, F) -> har (B, n_fft+2, F*scale/hop+1). */
+/* HarmonicSource::forward (kokoro_modules.cpp:1574-1665): F0 (B, F) -> har (B, n_fft+2, F*scale/hop+1).
+ * Phase arithmetic: BSML_PHASE_FP32_RUNNING is the reference's own (one fp32
+ * accumulator per harmonic, per-sample add and a single 2*pi subtraction,
+ * kokoro_modules.cpp:1601-1616), reproduced bit for bit; the default.
+ * BSML_PHASE_EXACT forms every frame's start phase exactly (double), a sine
+ * source whose phase does not drift over long clips (not the reference's). */
+enum { BSML_PHASE_FP32_RUNNING = 0, BSML_PHASE_EXACT = 1 };
 int bsml_harmonic_source(const bsml_decoder_config* cfg, const float* F0, int B, int F, const float* l_weight,
                          const float* l_bias, float* har, void* stream);
+int bsml_harmonic_source_mode(const bsml_decoder_config* cfg, const float* F0, int B, int F, const float* l_weight,
+                              const float* l_bias, float* har, int phase_mode, void* stream);
+/* The phase mode of the harmonic source a decoder runs when no har is passed. */
+int bsml_decoder_set_phase_mode(bsml_decoder* d, int phase_mode);
 
 #ifdef __cplusplus
 }

@@ -63,3 +63,18 @@ def test_create_without_gpu_fails_loudly():
     rc = L.bsml_decoder_create(ctypes.byref(c), 0, ctypes.byref(h))
     assert rc != 0
     assert L.bsml_last_error().decode().startswith("brosoundml: ")
+
+
+@pytest.mark.parametrize("fn", ["bsml_conv1d_backward_weight", "bsml_conv1d_backward_weight_noalloc",
+                                "bsml_conv1d_forward"])
+def test_conv_shorter_than_kernel_is_rejected(fn):
+    """L + 2p - d(k-1) - 1 < 0 (L=2, k=7, p=0, stride 6) has no output. The shape
+    check runs before any device work, so this holds with or without a GPU."""
+    L = _lib.lib()
+    z = ctypes.c_void_p(16)   # never dereferenced: the arguments are rejected first
+    if fn == "bsml_conv1d_forward":
+        rc = L.bsml_conv1d_forward(z, 1, 4, 2, z, None, 4, 7, 6, 0, 1, z, None)
+    else:
+        rc = getattr(L, fn)(z, z, 1, 4, 2, 4, 7, 6, 0, 1, z, None, None)
+    assert rc != 0
+    assert "bad argument" in L.bsml_last_error().decode()

@@ -274,27 +274,59 @@ def test_istft_atoms(orc, n_fft, hop, L):
     assert rel_l2(host(dim), rim) < 1e-5
 
 
-def test_harmonic_source():
+def _har_gpu(cfg, o, p, F0, mode):
+    lw = next(e for e in o.table if e["name"] == "generator.m_source.l_linear.weight")["offset"]
+    lb = next(e for e in o.table if e["name"] == "generator.m_source.l_linear.bias")["offset"]
+    B, F = F0.shape
+    pd, f0d = dev(p), dev(F0)
+    har = torch.empty((B, cfg["har_ch"], config.har_frames(cfg, F // 2)), device="cuda")
+    c = _lib.make_config(cfg)
+    _lib.check(_lib.lib().bsml_harmonic_source_mode(ctypes.byref(c), P(f0d), B, F,
+                                                    ctypes.c_void_p(pd.data_ptr() + 4 * lw),
+                                                    ctypes.c_void_p(pd.data_ptr() + 4 * lb), P(har),
+                                                    {"fp32": 0, "exact": 1}[mode], stream()))
+    return host(har)
+
+
+def _spectrum(h, nf):
+    return h[:, :nf] * np.exp(1j * h[:, nf:].astype(np.float64))
+
+
+# The reference's phase is an fp32 running sum (kokoro_modules.cpp:1601-1616); the
+# default GPU mode reproduces its every rounding, so only the sines, the mixture and
+# the STFT sums differ (a few fp32 ulps). Compared on the complex spectrum |X| e^{i angle X}:
+# the angle channels alone are atan2 of bins that are exactly zero in unvoiced
+# stretches (a constant source under a periodic Hann window), i.e. rounding noise in
+# any implementation. T=200 is config 2's clip length, T=1600 config 4's longest.
+HAR_BAR = 1e-5
+
+
+@pytest.mark.parametrize("T", [16, 200, 1600])
+def test_harmonic_source(T):
+    cfg = config.kokoro_82m()
+    o = Oracle(cfg)
+    p = synth.init_params(o.table, o.n_params, 0)
+    x = synth.make_inputs(cfg, 2, T, 1)
+    ref = o.harmonic_source(p, x["F0"])
+    h = _har_gpu(cfg, o, p, x["F0"], "fp32")
+    nf = cfg["n_fft"] // 2 + 1
+    c1, c2 = _spectrum(h, nf), _spectrum(ref, nf)
+    assert np.linalg.norm(c1 - c2) / np.linalg.norm(c2) < HAR_BAR
+    assert rel_l2(h[:, :nf], ref[:, :nf]) < HAR_BAR
+
+
+def test_harmonic_source_exact_phase_mode():
+    """The double-precision phase mode is an accurate sine source, close to the
+    reference's on short clips (its fp32 phase has drifted little by then)."""
     cfg = config.kokoro_82m()
     o = Oracle(cfg)
     p = synth.init_params(o.table, o.n_params, 0)
     x = synth.make_inputs(cfg, 2, 16, 1)
     ref = o.harmonic_source(p, x["F0"])
-    lw = next(e for e in o.table if e["name"] == "generator.m_source.l_linear.weight")["offset"]
-    lb = next(e for e in o.table if e["name"] == "generator.m_source.l_linear.bias")["offset"]
-    pd, f0d = dev(p), dev(x["F0"])
-    har = torch.empty(ref.shape, device="cuda")
-    c = _lib.make_config(cfg)
-    _lib.check(_lib.lib().bsml_harmonic_source(ctypes.byref(c), P(f0d), 2, 32,
-                                               ctypes.c_void_p(pd.data_ptr() + 4 * lw),
-                                               ctypes.c_void_p(pd.data_ptr() + 4 * lb), P(har), stream()))
-    h = host(har)
-    nf = 11
-    c1 = h[:, :nf] * np.exp(1j * h[:, nf:])
-    c2 = ref[:, :nf] * np.exp(1j * ref[:, nf:])
-    # the reference's fp32 running phase vs the GPU's exact per-frame phase
+    h = _har_gpu(cfg, o, p, x["F0"], "exact")
+    nf = cfg["n_fft"] // 2 + 1
+    c1, c2 = _spectrum(h, nf), _spectrum(ref, nf)
     assert np.linalg.norm(c1 - c2) / np.linalg.norm(c2) < 1e-4
-    assert rel_l2(h[:, :nf], ref[:, :nf]) < 1e-4
 
 
 def test_l1_and_adam():
