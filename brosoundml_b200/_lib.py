@@ -138,6 +138,21 @@ SIGNATURES = {
     "bsml_snake_backward": ([_P, _P, _P, _I, _I, _I, _P, _P, _P], _I),
     "bsml_istft_forward": ([_P, _P, _I, _I, _I, _I, _P, _P], _I),
     "bsml_istft_backward": ([_P, _I, _I, _I, _I, _P, _P, _P], _I),
+    "bsml_backbone_out_len": ([_P, _I, ctypes.POINTER(_I)], _I),
+    "bsml_backbone_forward": ([_P, _I, _I, _P, _P, _P, _P, _P, _I, _P, _P, _P, _P], _I),
+    "bsml_backbone_backward": ([_P, _P, _P, _P, _P, _P, _P], _I),
+    "bsml_generator_forward": ([_P, _I, _I, _P, _P, _P, _I, _P, _I, _P, _P, _P, _P], _I),
+    "bsml_generator_backward": ([_P, _P, _P, _P, _P, _P, _P], _I),
+    "bsml_spectral_head_forward": ([_P, _I, _I, _I, _P, _P, _I, _I, _I, _P, _P, _P], _I),
+    "bsml_spectral_head_backward": ([_P, _P, _P, _I, _I, _I, _P, _I, _I, _I, _P, _P], _I),
+    "bsml_transpose": ([_P, _L, _I, _I, _P, _P], _I),
+    "bsml_managed_alloc": ([_L, ctypes.POINTER(_P)], _I),
+    "bsml_managed_free": ([_P], _I),
+    "bsml_synchronize": ([], _I),
+    "bsml_memcpy": ([_P, _P, _L, _P], _I),
+    "bsml_lora_moments": ([_P, ctypes.POINTER(_P), ctypes.POINTER(_P)], _I),
+    "bsml_gate_forward": ([_P, _P, _P, _I, _I, _I, _I, _P, _P, _P], _I),
+    "bsml_gate_backward": ([_P, _P, _P, _P, _I, _I, _I, _I, _P, _P, _P], _I),
     "bsml_harmonic_source": ([_CFG, _P, _I, _I, _P, _P, _P, _P], _I),
     "bsml_harmonic_source_mode": ([_CFG, _P, _I, _I, _P, _P, _P, _I, _P], _I),
     "bsml_decoder_set_phase_mode": ([_P, _I], _I),

@@ -69,6 +69,11 @@ void need(bool ok, const char* where, const char* why) {
     if (!ok) bsml::fail(where, why);
 }
 
+// an inner C-ABI call's failure re-raised with its own message
+void check_rc(int rc) {
+    if (rc != 0) throw std::runtime_error(g_err);
+}
+
 // output length of a conv; 0 (rejected by the callers) when the padded input is
 // shorter than the dilated kernel (a negative numerator must not truncate to 0)
 int conv_out(int L, int k, int s, int p, int d) {
@@ -233,6 +238,48 @@ int bsml_decoder_backward(bsml_decoder* d, const float* daudio, float* grads, fl
     });
 }
 
+int bsml_backbone_out_len(const bsml_decoder* d, int T, int* L_gen) {
+    return guarded([&] {
+        need(d != nullptr && L_gen != nullptr && T > 0, "bsml_backbone_out_len", "bad argument");
+        *L_gen = d->eng->backbone_out_len(T);
+    });
+}
+
+int bsml_backbone_forward(bsml_decoder* d, int B, int T, const float* params, const float* asr, const float* F0,
+                          const float* N, const float* style, int style_stride, const float* aff_in, float* gen_in,
+                          float* aff_out, void* stream) {
+    return guarded([&] {
+        need(d != nullptr, "bsml_backbone_forward", "null handle");
+        d->eng->forward_backbone(B, T, params, asr, F0, N, style, style_stride, aff_in, gen_in, aff_out, S(stream));
+    });
+}
+
+int bsml_backbone_backward(bsml_decoder* d, const float* dgen_in, float* grads, float* d_asr, float* d_style,
+                           float* d_aff, void* stream) {
+    return guarded([&] {
+        need(d != nullptr, "bsml_backbone_backward", "null handle");
+        d->eng->backward_backbone(dgen_in, grads, d_asr, d_style, d_aff, S(stream));
+    });
+}
+
+int bsml_generator_forward(bsml_decoder* d, int B, int L_in, const float* params, const float* gen_in,
+                           const float* har, int frames, const float* style, int style_stride, const float* aff_in,
+                           float* audio, float* aff_out, void* stream) {
+    return guarded([&] {
+        need(d != nullptr, "bsml_generator_forward", "null handle");
+        d->eng->forward_generator(B, L_in, params, gen_in, har, frames, style, style_stride, aff_in, audio, aff_out,
+                                  S(stream));
+    });
+}
+
+int bsml_generator_backward(bsml_decoder* d, const float* daudio, float* grads, float* dgen_in, float* d_style,
+                            float* d_aff, void* stream) {
+    return guarded([&] {
+        need(d != nullptr, "bsml_generator_backward", "null handle");
+        d->eng->backward_generator(daudio, grads, dgen_in, d_style, d_aff, S(stream));
+    });
+}
+
 int bsml_block_create(const bsml_block_spec* spec, int device, bsml_decoder** out) {
     return guarded([&] {
         need(spec && out, "bsml_block_create", "null argument");
@@ -373,6 +420,32 @@ int bsml_lora_buffers(bsml_lora* l, float** params, float** grads) {
         need(l != nullptr, "bsml_lora_buffers", "null handle");
         if (params) *params = l->lora->params();
         if (grads) *grads = l->lora->grads();
+    });
+}
+
+int bsml_lora_moments(bsml_lora* l, float** m, float** v) {
+    return guarded([&] {
+        need(l != nullptr, "bsml_lora_moments", "null handle");
+        if (m) *m = l->lora->moment1();
+        if (v) *v = l->lora->moment2();
+    });
+}
+
+int bsml_gate_forward(const float* W1, const float* W2, const float* v, int B, int in_dim, int hidden, int gate_dim,
+                      float* act, float* g, void* stream) {
+    return guarded([&] {
+        need(W1 && W2 && v && act && g && B > 0 && in_dim > 0 && hidden > 0 && gate_dim > 0, "bsml_gate_forward",
+             "bad argument");
+        bsml::gate_forward(W1, W2, v, B, in_dim, hidden, gate_dim, act, g, S(stream));
+    });
+}
+
+int bsml_gate_backward(const float* W2, const float* v, const float* act, const float* dG, int B, int in_dim,
+                       int hidden, int gate_dim, float* dW1, float* dW2, void* stream) {
+    return guarded([&] {
+        need(W2 && v && act && dG && dW1 && dW2 && B > 0 && in_dim > 0 && hidden > 0 && gate_dim > 0,
+             "bsml_gate_backward", "bad argument");
+        bsml::gate_backward(W2, v, act, dG, B, in_dim, hidden, gate_dim, dW1, dW2, S(stream));
     });
 }
 
@@ -987,6 +1060,100 @@ int bsml_istft_backward(const float* daudio, int B, int n_fft, int hop, int L, f
     return guarded([&] {
         need(daudio && dre && dim && B > 0 && L > 1 && hop > 0, "bsml_istft_backward", "bad argument");
         bsml::istft_bwd_ncl(daudio, B, L, n_fft, hop, dre, dim, S(stream));
+    });
+}
+
+int bsml_spectral_head_forward(const float* x, int B, int C, int L, const float* W, const float* bias, int n_fft,
+                               int hop, int post_kernel, float* post, float* audio, void* stream) {
+    return guarded([&] {
+        const char* where = "bsml_spectral_head_forward";
+        need(x && W && post && audio && B > 0 && C > 0 && L > 1 && hop > 0, where, "bad argument");
+        need(n_fft >= 2 && n_fft <= 64 && !(n_fft & 1), where, "n_fft must be even and at most 64");
+        need(post_kernel >= 1 && (post_kernel & 1), where, "post_kernel must be odd");
+        cudaStream_t st = S(stream);
+        Scratch sc(st);
+        const int Cp = n_fft + 2, nf = n_fft / 2 + 1;
+        bsml::Act xa = sc.act(B, L, C), xl = sc.act(B, L, C);
+        bsml::ncl_to_cl(x, xa, st);
+        bsml::leaky_fwd(xa, 0.01f, xl, st);
+        // conv_post (kokoro_decoder_backward.cpp:387-389) through the conv atom (NCL)
+        float* xl_ncl = sc.f((int64_t)B * C * L);
+        bsml::cl_to_ncl(xl, xl_ncl, st);
+        check_rc(bsml_conv1d_forward(xl_ncl, B, C, L, W, bias, Cp, post_kernel, 1, (post_kernel - 1) / 2, 1, post,
+                                     stream));
+        bsml::Act pa = sc.act(B, L, Cp);
+        bsml::ncl_to_cl(post, pa, st);
+        float* spec = sc.f((int64_t)B * L * 2 * nf);
+        bsml::polar_fwd(pa, nf, spec, st);
+        bsml::istft_fwd(spec, B, L, n_fft, hop, audio, st);
+    });
+}
+
+int bsml_spectral_head_backward(const float* x, const float* post, const float* daudio, int B, int C, int L,
+                                const float* W, int n_fft, int hop, int post_kernel, float* dx, void* stream) {
+    return guarded([&] {
+        const char* where = "bsml_spectral_head_backward";
+        need(x && post && daudio && W && dx && B > 0 && C > 0 && L > 1 && hop > 0, where, "bad argument");
+        need(n_fft >= 2 && n_fft <= 64 && !(n_fft & 1), where, "n_fft must be even and at most 64");
+        need(post_kernel >= 1 && (post_kernel & 1), where, "post_kernel must be odd");
+        cudaStream_t st = S(stream);
+        Scratch sc(st);
+        const int Cp = n_fft + 2;
+        bsml::Act pa = sc.act(B, L, Cp), dpa = sc.act(B, L, Cp);
+        bsml::ncl_to_cl(post, pa, st);
+        // iSTFT adjoint fused with the polar exp / sin adjoint (kokoro_decoder_backward.cpp:424-451)
+        bsml::istft_polar_bwd(daudio, pa, n_fft, hop, dpa, st);
+        float* dpost = sc.f((int64_t)B * Cp * L);
+        bsml::cl_to_ncl(dpa, dpost, st);
+        float* dxl = sc.f((int64_t)B * C * L);
+        check_rc(bsml_conv1d_backward_input(dpost, B, C, L, W, Cp, post_kernel, 1, (post_kernel - 1) / 2, 1, dxl,
+                                            stream));
+        bsml::Act xa = sc.act(B, L, C), dxla = sc.act(B, L, C), dxa = sc.act(B, L, C);
+        bsml::ncl_to_cl(x, xa, st);
+        bsml::ncl_to_cl(dxl, dxla, st);
+        bsml::leaky_bwd(xa, 0.01f, dxla, dxa, st);
+        bsml::cl_to_ncl(dxa, dx, st);
+    });
+}
+
+int bsml_transpose(const float* src, int64_t batch, int rows, int cols, float* dst, void* stream) {
+    return guarded([&] {
+        need(src && dst && batch > 0 && rows > 0 && cols > 0, "bsml_transpose", "bad argument");
+        // (batch, rows, cols) -> (batch, cols, rows): the channels-last conversion with C = rows
+        cudaStream_t st = S(stream);
+        bsml::Act a;
+        a.B = (int)batch; a.L = cols; a.C = rows; a.ld = rows; a.bstride = (int64_t)rows * cols;
+        a.p = dst;
+        bsml::ncl_to_cl(src, a, st);
+    });
+}
+
+int bsml_managed_alloc(int64_t bytes, void** out) {
+    return guarded([&] {
+        need(out != nullptr && bytes >= 0, "bsml_managed_alloc", "bad argument");
+        *out = nullptr;
+        void* p = nullptr;
+        bsml::check_cuda(cudaMallocManaged(&p, std::max<int64_t>(bytes, 16)), "cudaMallocManaged");
+        bsml::check_cuda(cudaMemset(p, 0, std::max<int64_t>(bytes, 16)), "cudaMemset");
+        bsml::check_cuda(cudaDeviceSynchronize(), "cudaDeviceSynchronize");
+        *out = p;
+    });
+}
+
+int bsml_managed_free(void* p) {
+    return guarded([&] {
+        if (p) bsml::check_cuda(cudaFree(p), "cudaFree");
+    });
+}
+
+int bsml_synchronize(void) {
+    return guarded([&] { bsml::check_cuda(cudaDeviceSynchronize(), "cudaDeviceSynchronize"); });
+}
+
+int bsml_memcpy(void* dst, const void* src, int64_t bytes, void* stream) {
+    return guarded([&] {
+        need(dst && src && bytes >= 0, "bsml_memcpy", "bad argument");
+        bsml::check_cuda(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDefault, S(stream)), "cudaMemcpyAsync");
     });
 }
 

@@ -263,42 +263,56 @@ void Engine::plan(Planner& P) {
         max_elems = std::max<int64_t>(max_elems, (int64_t)B * L * pitch(C));
         max_c = std::max(max_c, C);
     };
-    asr_ = P.act(B, T, cf.asr_dim);
-    F0_copy_ = P.f((int64_t)B * 2 * T);
-    N_copy_ = P.f((int64_t)B * 2 * T);
     style_copy_ = P.f((int64_t)B * cf.style_dim);
-    F0dn_ = P.act(B, T, 1);
-    Ndn_ = P.act(B, T, 1);
-    asrres_ = P.act(B, T, cf.asr_res_dim);
-    enc_in_ = P.act(B, T, cf.asr_dim + 2);
     aff_ = P.f((int64_t)B * lay_.aff_per_clip);
     daff_ = P.f((int64_t)B * lay_.aff_per_clip);
-    encc_ = plan_blk(P, lay_.enc, T, true);
-    encc_.x = enc_in_;
-    note(T, lay_.enc.cin);
-    note(T, lay_.enc.cout);
-    const int nd = (int)lay_.dec.size();
-    dec_in_.resize(nd);
-    decc_.resize(nd);
-    res_applied_.assign(nd, 0);
-    x_ch_.assign(nd, 0);
-    int L = T, Cx = cf.enc_dim;
-    bool res = true;
-    for (int i = 0; i < nd; ++i) {
-        const BlkP& w = lay_.dec[i];
-        x_ch_[i] = Cx;
-        res_applied_[i] = res ? 1 : 0;
-        dec_in_[i] = P.act(B, L, w.cin);
-        decc_[i] = plan_blk(P, w, L, true);
-        decc_[i].x = dec_in_[i];
-        note(L, w.cin);
-        note(decc_[i].Lout, w.cin);
-        note(decc_[i].Lout, w.cout);
-        L = decc_[i].Lout;
-        Cx = w.cout;
-        if (w.up) res = false;
+    int L = T;
+    if (plan_part_ != PART_GENERATOR) {
+        asr_ = P.act(B, T, cf.asr_dim);
+        F0_copy_ = P.f((int64_t)B * 2 * T);
+        N_copy_ = P.f((int64_t)B * 2 * T);
+        F0dn_ = P.act(B, T, 1);
+        Ndn_ = P.act(B, T, 1);
+        asrres_ = P.act(B, T, cf.asr_res_dim);
+        enc_in_ = P.act(B, T, cf.asr_dim + 2);
+        encc_ = plan_blk(P, lay_.enc, T, true);
+        encc_.x = enc_in_;
+        note(T, lay_.enc.cin);
+        note(T, lay_.enc.cout);
+        const int nd = (int)lay_.dec.size();
+        dec_in_.resize(nd);
+        decc_.resize(nd);
+        res_applied_.assign(nd, 0);
+        x_ch_.assign(nd, 0);
+        int Cx = cf.enc_dim;
+        bool res = true;
+        for (int i = 0; i < nd; ++i) {
+            const BlkP& w = lay_.dec[i];
+            x_ch_[i] = Cx;
+            res_applied_[i] = res ? 1 : 0;
+            dec_in_[i] = P.act(B, L, w.cin);
+            decc_[i] = plan_blk(P, w, L, true);
+            decc_[i].x = dec_in_[i];
+            note(L, w.cin);
+            note(decc_[i].Lout, w.cin);
+            note(decc_[i].Lout, w.cout);
+            L = decc_[i].Lout;
+            Cx = w.cout;
+            if (w.up) res = false;
+        }
+        // backward-only buffers
+        dasr_cl_ = P.act(B, T, cf.asr_dim);
+        dasrres_ = P.act(B, T, cf.asr_res_dim);
+        dF0dn_ = P.act(B, T, 1);
+        dNdn_ = P.act(B, T, 1);
     }
+    // the generator part on its own takes gen_in of length T_ (its L_in)
     genin_ = P.act(B, L, cf.init_ch);
+    note(L, cf.init_ch);
+    if (plan_part_ == PART_BACKBONE) {
+        plan_scratch(P, max_elems, max_c);
+        return;
+    }
     // harmonic source / har
     const int Fr = 2 * T;
     if (have_har_) {
@@ -344,11 +358,6 @@ void Engine::plan(Planner& P) {
     post_ = P.act(B, L, lay_.post.cout);
     spec_ = P.f((int64_t)B * L * (cf.n_fft + 2));
     note(L, lay_.post.cout);
-    // backward-only buffers
-    dasr_cl_ = P.act(B, T, cf.asr_dim);
-    dasrres_ = P.act(B, T, cf.asr_res_dim);
-    dF0dn_ = P.act(B, T, 1);
-    dNdn_ = P.act(B, T, 1);
     plan_scratch(P, max_elems, max_c);
 }
 
@@ -405,9 +414,10 @@ void Engine::plan_block(Planner& P) {
     plan_scratch(P, max_elems, max_c);
 }
 
-void Engine::ensure_plan(int B, int T, int frames, bool have_har) {
-    if (planned_ && B == B_ && T == T_ && have_har == have_har_ && (!have_har || frames == frames_)) return;
-    B_ = B; T_ = T; frames_ = frames; have_har_ = have_har;
+void Engine::ensure_plan(int B, int T, int frames, bool have_har, int part) {
+    if (planned_ && B == B_ && T == T_ && part == plan_part_ && have_har == have_har_ && (!have_har || frames == frames_))
+        return;
+    B_ = B; T_ = T; frames_ = frames; have_har_ = have_har; plan_part_ = part;
     Planner p0;
     if (lay_.block_kind) plan_block(p0);
     else plan(p0);
@@ -954,33 +964,30 @@ void Engine::rb1_bwd(const RB1P& w, RB1C& c, const Act& dOut, float scale, const
 }
 
 // ── forward
-void Engine::forward(int B, int T, const float* params, const float* asr, const float* F0, const float* N,
-                     const float* style, const float* har, int frames, const float* aff_in, float* audio,
-                     float* aff_out, cudaStream_t st, int style_stride) {
-    if (lay_.block_kind) fail("bsml_decoder_forward", "the handle holds a single block: use bsml_block_forward");
-    if (B < 1 || T < 1) fail("bsml_decoder_forward", "B and T must be positive");
-    if (style_stride != 0 && style_stride < lay_.cfg.style_dim)
-        fail("bsml_decoder_forward", "style row stride below the style width");
-    if (!params || !asr || !F0 || !N || !audio) fail("bsml_decoder_forward", "null input");
-    if (!aff_in && !style) fail("bsml_decoder_forward", "style is required unless aff_in is given");
-    if (!har && lay_.cfg.har_ch != lay_.cfg.n_fft + 2)
-        fail("bsml_decoder_forward", "the harmonic source makes n_fft + 2 channels but har_ch = " +
-                                         std::to_string(lay_.cfg.har_ch) + ": pass har");
+// Set-up shared by the forward entry points: the plan, copies of what the
+// backward reads (F0, N, style), the packed weights and the resolved affines.
+void Engine::begin_forward(int B, int T, int frames, bool have_har, int part, const float* params, const float* F0,
+                           const float* N, const float* style, int style_stride, const float* aff_in,
+                           float* aff_out, cudaStream_t st) {
     BSML_CUDA(cudaSetDevice(device_));
-    ensure_plan(B, T, frames, har != nullptr);
+    ensure_plan(B, T, frames, have_har, part);
     const auto& cf = lay_.cfg;
     params_ = params;
-    // the backward needs F0, N (conv weight grads) and style (fc grads): keep copies
-    BSML_CUDA(cudaMemcpyAsync(F0_copy_, F0, sizeof(float) * B * 2 * T, cudaMemcpyDeviceToDevice, st));
-    BSML_CUDA(cudaMemcpyAsync(N_copy_, N, sizeof(float) * B * 2 * T, cudaMemcpyDeviceToDevice, st));
+    if (part != PART_GENERATOR) {
+        BSML_CUDA(cudaMemcpyAsync(F0_copy_, F0, sizeof(float) * B * 2 * T, cudaMemcpyDeviceToDevice, st));
+        BSML_CUDA(cudaMemcpyAsync(N_copy_, N, sizeof(float) * B * 2 * T, cudaMemcpyDeviceToDevice, st));
+        F0_ = F0_copy_;
+        N_ = N_copy_;
+    }
     if (style)
         BSML_CUDA(cudaMemcpy2DAsync(style_copy_, sizeof(float) * cf.style_dim, style,
                                     sizeof(float) * (style_stride > 0 ? style_stride : cf.style_dim),
                                     sizeof(float) * cf.style_dim, B, cudaMemcpyDeviceToDevice, st));
-    F0_ = F0_copy_;
-    N_ = N_copy_;
     style_ = style ? style_copy_ : nullptr;
-    if (!have_har_) {
+    ref_mode_ = aff_in != nullptr;
+    fwd_done_ = false;
+    fwd_part_ = part;
+    if (part == PART_FULL && !have_har_) {
         // har is first read by the generator; the source runs on the side stream meanwhile
         BSML_CUDA(cudaEventRecord(ev_fork_, st));
         BSML_CUDA(cudaStreamWaitEvent(side_, ev_fork_, 0));
@@ -988,8 +995,6 @@ void Engine::forward(int B, int T, const float* params, const float* asr, const 
                         params_ + lay_.llin_w, params_ + lay_.llin_b, hs_phase_, hs_src_, har_, side_, phase_mode_);
         BSML_CUDA(cudaEventRecord(ev_join_, side_));
     }
-    ref_mode_ = aff_in != nullptr;
-    fwd_done_ = false;
     pack_weights(st);
     // affines: fc(style) (compute_style_affine, kokoro_modules.cpp:563-572) or caller-supplied
     if (ref_mode_)
@@ -999,10 +1004,15 @@ void Engine::forward(int B, int T, const float* params, const float* asr, const 
                       aff_, st);
     if (aff_out)
         BSML_CUDA(cudaMemcpyAsync(aff_out, aff_, sizeof(float) * B * lay_.aff_per_clip, cudaMemcpyDeviceToDevice, st));
-    // backbone (kokoro_decoder_backward.cpp:482-537)
+}
+
+// backbone (kokoro_decoder_backward.cpp:482-537): asr, F0_, N_ -> genin_
+void Engine::run_backbone(const float* asr, cudaStream_t st) {
+    const auto& cf = lay_.cfg;
+    const int B = B_, T = T_;
     ncl_to_cl(asr, asr_, st);
-    conv(lay_.F0c, flat_input(F0, B, 2 * T), F0dn_, nullptr, 0, 1.f, false, st);
-    conv(lay_.Nc, flat_input(N, B, 2 * T), Ndn_, nullptr, 0, 1.f, false, st);
+    conv(lay_.F0c, flat_input(F0_, B, 2 * T), F0dn_, nullptr, 0, 1.f, false, st);
+    conv(lay_.Nc, flat_input(N_, B, 2 * T), Ndn_, nullptr, 0, 1.f, false, st);
     conv(lay_.asr_res, asr_, asrres_, nullptr, 0, 1.f, false, st);
     copy_act(asr_, enc_in_.slice_c(0, cf.asr_dim), st);
     copy_act(F0dn_, enc_in_.slice_c(cf.asr_dim, 1), st);
@@ -1026,12 +1036,16 @@ void Engine::forward(int B, int T, const float* params, const float* asr, const 
             copy_act(Ndn_, din.slice_c(Cx + cf.asr_res_dim + 1, 1), st);
         }
     }
-    // har
+}
+
+// generator (kokoro_decoder_backward.cpp:592-667) and spectral head (:378-410): genin_, har -> audio
+void Engine::run_generator(const float* har, float* audio, cudaStream_t st) {
+    const auto& cf = lay_.cfg;
+    const int B = B_;
     if (have_har_)
         ncl_to_cl(har, har_, st);
     else
         BSML_CUDA(cudaStreamWaitEvent(st, ev_join_, 0));
-    // generator (kokoro_decoder_backward.cpp:592-667)
     const int U = cf.n_ups, K = cf.n_kernels;
     for (int i = 0; i < U; ++i) {
         StageC& s = stc_[i];
@@ -1050,28 +1064,85 @@ void Engine::forward(int B, int T, const float* params, const float* asr, const 
         for (int j = 0; j < K; ++j)
             rb1_fwd(lay_.rbs[i * K + j], s.res[j], s.m, j > 0, s.out, 1.f / (float)K, j > 0, st);
     }
-    // spectral head (kokoro_decoder_backward.cpp:378-410)
     const Act& xlast = stc_[U - 1].out;
     leaky_fwd(xlast, 0.01f, xl_, st);
     conv(lay_.post, xl_, post_, nullptr, 0, 1.f, false, st);
     const int nf = cf.n_fft / 2 + 1;
     polar_fwd(post_, nf, spec_, st);
     istft_fwd(spec_, B, post_.L, cf.n_fft, cf.hop, audio, st);
+}
+
+void Engine::forward(int B, int T, const float* params, const float* asr, const float* F0, const float* N,
+                     const float* style, const float* har, int frames, const float* aff_in, float* audio,
+                     float* aff_out, cudaStream_t st, int style_stride) {
+    const char* where = "bsml_decoder_forward";
+    if (lay_.block_kind) fail(where, "the handle holds a single block: use bsml_block_forward");
+    if (B < 1 || T < 1) fail(where, "B and T must be positive");
+    if (style_stride != 0 && style_stride < lay_.cfg.style_dim) fail(where, "style row stride below the style width");
+    if (!params || !asr || !F0 || !N || !audio) fail(where, "null input");
+    if (!aff_in && !style) fail(where, "style is required unless aff_in is given");
+    if (!har && lay_.cfg.har_ch != lay_.cfg.n_fft + 2)
+        fail(where, "the harmonic source makes n_fft + 2 channels but har_ch = " + std::to_string(lay_.cfg.har_ch) +
+                        ": pass har");
+    begin_forward(B, T, frames, har != nullptr, PART_FULL, params, F0, N, style, style_stride, aff_in, aff_out, st);
+    run_backbone(asr, st);
+    run_generator(har, audio, st);
     fwd_done_ = true;
 }
 
+void Engine::forward_backbone(int B, int T, const float* params, const float* asr, const float* F0, const float* N,
+                              const float* style, int style_stride, const float* aff_in, float* gen_in,
+                              float* aff_out, cudaStream_t st) {
+    const char* where = "bsml_backbone_forward";
+    if (lay_.block_kind) fail(where, "the handle holds a single block");
+    if (B < 1 || T < 1) fail(where, "B and T must be positive");
+    if (style_stride != 0 && style_stride < lay_.cfg.style_dim) fail(where, "style row stride below the style width");
+    if (!params || !asr || !F0 || !N || !gen_in) fail(where, "null input");
+    if (!aff_in && !style) fail(where, "style is required unless aff_in is given");
+    begin_forward(B, T, 0, false, PART_BACKBONE, params, F0, N, style, style_stride, aff_in, aff_out, st);
+    run_backbone(asr, st);
+    cl_to_ncl(genin_, gen_in, st);
+    fwd_done_ = true;
+}
+
+void Engine::forward_generator(int B, int L_in, const float* params, const float* gen_in, const float* har,
+                               int frames, const float* style, int style_stride, const float* aff_in, float* audio,
+                               float* aff_out, cudaStream_t st) {
+    const char* where = "bsml_generator_forward";
+    if (lay_.block_kind) fail(where, "the handle holds a single block");
+    if (B < 1 || L_in < 1 || frames < 2) fail(where, "B, L_in must be positive and frames at least 2");
+    if (style_stride != 0 && style_stride < lay_.cfg.style_dim) fail(where, "style row stride below the style width");
+    if (!params || !gen_in || !har || !audio) fail(where, "null input (the generator takes har as an input)");
+    if (!aff_in && !style) fail(where, "style is required unless aff_in is given");
+    begin_forward(B, L_in, frames, true, PART_GENERATOR, params, nullptr, nullptr, style, style_stride, aff_in,
+                  aff_out, st);
+    ncl_to_cl(gen_in, genin_, st);
+    run_generator(har, audio, st);
+    fwd_done_ = true;
+}
+
+int Engine::backbone_out_len(int T) const {
+    int L = T;
+    for (const BlkP& d : lay_.dec)
+        if (d.up) L *= 2;
+    return L;
+}
+
 // ── backward
-void Engine::backward(const float* daudio, float* grads, float* d_asr, float* d_style, float* d_aff,
-                      cudaStream_t st) {
-    if (lay_.block_kind) fail("bsml_decoder_backward", "the handle holds a single block: use bsml_block_backward");
-    if (!fwd_done_) fail("bsml_decoder_backward", "no matching forward");
-    if (!daudio) fail("bsml_decoder_backward", "null daudio");
+void Engine::begin_backward(const char* where, int part, float* grads, cudaStream_t st) {
+    if (lay_.block_kind) fail(where, "the handle holds a single block: use bsml_block_backward");
+    if (!fwd_done_ || fwd_part_ != part) fail(where, "no matching forward");
     BSML_CUDA(cudaSetDevice(device_));
-    const auto& cf = lay_.cfg;
-    const int B = B_, T = T_;
     grads_ = grads;
     if (grads_) fill(grads_, lay_.total, 0.f, st);
+    // a part leaves the other part's affine gradients unwritten
+    if (part != PART_FULL) fill(daff_, (int64_t)B_ * lay_.aff_per_clip, 0.f, st);
     pack_dgrad_weights(st);
+}
+
+// generator + spectral head backward; returns d(gen_in), channels-last, in S_[2] or S_[3]
+Act Engine::gen_backward(const float* daudio, cudaStream_t st) {
+    const auto& cf = lay_.cfg;
     const int U = cf.n_ups, K = cf.n_kernels;
     // spectral head
     const int L1 = post_.L;
@@ -1113,13 +1184,17 @@ void Engine::backward(const float* daudio, float* grads, float* d_asr, float* d_
         leaky_bwd(s.x_in, 0.1f, da, dprev, st);
         dX = dprev;
     }
-    // backbone (kokoro_decoder_backward.cpp:539-574) + the cat-channel grads
+    return dX;
+}
+
+// backbone backward (kokoro_decoder_backward.cpp:539-574) + the cat-channel grads; dY = d(gen_in) in S_[4]
+void Engine::bb_backward(Act dY, cudaStream_t st) {
+    const auto& cf = lay_.cfg;
+    const int B = B_, T = T_;
     fill(dasrres_.p, (int64_t)B * dasrres_.bstride, 0.f, st);
     fill(dF0dn_.p, (int64_t)B * dF0dn_.bstride, 0.f, st);
     fill(dNdn_.p, (int64_t)B * dNdn_.bstride, 0.f, st);
     // the block backward uses S_[0..3]; the running dX alternates between S_[4] and S_[5]
-    Act dY = view(S_[4], dX.L, dX.C);
-    copy_act(dX, dY, st);
     int ybuf = 4;
     const int nd = (int)lay_.dec.size();
     for (int i = nd - 1; i >= -1; --i) {
@@ -1147,7 +1222,12 @@ void Engine::backward(const float* daudio, float* grads, float* d_asr, float* d_
     conv_wgrad(lay_.Nc, dNdn_, flat_input(N_, B, 2 * T), st);
     conv_dgrad(lay_.asr_res, dasrres_, dasr_cl_, true, st);
     conv_wgrad(lay_.asr_res, dasrres_, asr_, st);
-    if (d_asr) cl_to_ncl(dasr_cl_, d_asr, st);
+}
+
+// the affine outputs and the fc weight / style gradients (all AdaINs)
+void Engine::finish_backward(float* d_style, float* d_aff, cudaStream_t st) {
+    const auto& cf = lay_.cfg;
+    const int B = B_;
     if (d_aff)
         BSML_CUDA(cudaMemcpyAsync(d_aff, daff_, sizeof(float) * B * lay_.aff_per_clip, cudaMemcpyDeviceToDevice, st));
     if (ref_mode_) {
@@ -1159,6 +1239,38 @@ void Engine::backward(const float* daudio, float* grads, float* d_asr, float* d_
     grads_ = nullptr;
 }
 
+void Engine::backward(const float* daudio, float* grads, float* d_asr, float* d_style, float* d_aff,
+                      cudaStream_t st) {
+    if (!daudio) fail("bsml_decoder_backward", "null daudio");
+    begin_backward("bsml_decoder_backward", PART_FULL, grads, st);
+    const Act dX = gen_backward(daudio, st);
+    Act dY = view(S_[4], dX.L, dX.C);
+    copy_act(dX, dY, st);
+    bb_backward(dY, st);
+    if (d_asr) cl_to_ncl(dasr_cl_, d_asr, st);
+    finish_backward(d_style, d_aff, st);
+}
+
+void Engine::backward_backbone(const float* dgen_in, float* grads, float* d_asr, float* d_style, float* d_aff,
+                               cudaStream_t st) {
+    if (!dgen_in) fail("bsml_backbone_backward", "null dgen_in");
+    begin_backward("bsml_backbone_backward", PART_BACKBONE, grads, st);
+    Act dY = view(S_[4], genin_.L, genin_.C);
+    ncl_to_cl(dgen_in, dY, st);
+    bb_backward(dY, st);
+    if (d_asr) cl_to_ncl(dasr_cl_, d_asr, st);
+    finish_backward(d_style, d_aff, st);
+}
+
+void Engine::backward_generator(const float* daudio, float* grads, float* dgen_in, float* d_style, float* d_aff,
+                                cudaStream_t st) {
+    if (!daudio) fail("bsml_generator_backward", "null daudio");
+    begin_backward("bsml_generator_backward", PART_GENERATOR, grads, st);
+    const Act dX = gen_backward(daudio, st);
+    if (dgen_in) cl_to_ncl(dX, dgen_in, st);
+    finish_backward(d_style, d_aff, st);
+}
+
 // ── one block (detail::adain_resblk_1d_* / adain_resblock1_*, kokoro_decoder_backward.cpp:152-376)
 void Engine::forward_block(int B, int L, const float* params, const float* x, const float* style,
                            const float* aff_in, float* y, float* aff_out, cudaStream_t st) {
@@ -1167,7 +1279,7 @@ void Engine::forward_block(int B, int L, const float* params, const float* x, co
     if (!params || !x || !y) fail("bsml_block_forward", "null input");
     if (!aff_in && !style) fail("bsml_block_forward", "style is required unless aff_in is given");
     BSML_CUDA(cudaSetDevice(device_));
-    ensure_plan(B, L, 0, false);
+    ensure_plan(B, L, 0, false, PART_FULL);
     const int S = lay_.cfg.style_dim;
     params_ = params;
     if (style) BSML_CUDA(cudaMemcpyAsync(style_copy_, style, sizeof(float) * B * S, cudaMemcpyDeviceToDevice, st));

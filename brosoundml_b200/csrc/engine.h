@@ -31,6 +31,23 @@ class Engine {
                  const float* style, const float* har, int frames, const float* aff_in, float* audio,
                  float* aff_out, cudaStream_t st, int style_stride = 0);
     void backward(const float* daudio, float* grads, float* d_asr, float* d_style, float* d_aff, cudaStream_t st);
+    // The two assemblies on their own (detail::decoder_backbone_* / generator_*,
+    // src/kokoro_decoder_backward.h:213-293): the backbone maps (asr, F0, N) to
+    // gen_in (B, init_ch, L_gen) NCL; the generator maps gen_in (B, init_ch, L_in)
+    // and har (B, har_ch, frames) to audio. Affines: the whole packing, of which
+    // each part reads (and writes the gradients of) its own AdaINs.
+    void forward_backbone(int B, int T, const float* params, const float* asr, const float* F0, const float* N,
+                          const float* style, int style_stride, const float* aff_in, float* gen_in, float* aff_out,
+                          cudaStream_t st);
+    void backward_backbone(const float* dgen_in, float* grads, float* d_asr, float* d_style, float* d_aff,
+                           cudaStream_t st);
+    void forward_generator(int B, int L_in, const float* params, const float* gen_in, const float* har, int frames,
+                           const float* style, int style_stride, const float* aff_in, float* audio, float* aff_out,
+                           cudaStream_t st);
+    void backward_generator(const float* daudio, float* grads, float* dgen_in, float* d_style, float* d_aff,
+                            cudaStream_t st);
+    // gen_in length of the backbone for T asr frames
+    int backbone_out_len(int T) const;
     // one block (a handle made from a bsml_block_spec): x, y, dy, dx NCL
     void forward_block(int B, int L, const float* params, const float* x, const float* style, const float* aff_in,
                        float* y, float* aff_out, cudaStream_t st);
@@ -85,7 +102,17 @@ class Engine {
     void plan(Planner& P);
     void plan_block(Planner& P);
     void plan_scratch(Planner& P, int64_t max_elems, int max_c);
-    void ensure_plan(int B, int T, int frames, bool have_har);
+    enum { PART_FULL = 0, PART_BACKBONE = 1, PART_GENERATOR = 2 };
+    void ensure_plan(int B, int T, int frames, bool have_har, int part);
+    void begin_forward(int B, int T, int frames, bool have_har, int part, const float* params, const float* F0,
+                       const float* N, const float* style, int style_stride, const float* aff_in, float* aff_out,
+                       cudaStream_t st);
+    void run_backbone(const float* asr, cudaStream_t st);
+    void run_generator(const float* har, float* audio, cudaStream_t st);
+    void begin_backward(const char* where, int part, float* grads, cudaStream_t st);
+    Act gen_backward(const float* daudio, cudaStream_t st);
+    void bb_backward(Act dY, cudaStream_t st);
+    void finish_backward(float* d_style, float* d_aff, cudaStream_t st);
     Stats stats(Planner& P, int B, int C);
     BlkC plan_blk(Planner& P, const BlkP& w, int Lin, bool input_owned);
     RB1C plan_rb1(Planner& P, int L, int C);
@@ -208,6 +235,8 @@ class Engine {
     int B_ = 0, T_ = 0, frames_ = 0;
     bool have_har_ = false;
     bool planned_ = false;
+    int plan_part_ = PART_FULL;       // what the plan covers
+    int fwd_part_ = PART_FULL;        // what the last forward ran
 
     // per-call pointers
     const float* params_ = nullptr;

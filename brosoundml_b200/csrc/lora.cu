@@ -178,6 +178,23 @@ T* dalloc(int64_t n) {
 
 }  // namespace
 
+void gate_forward(const float* W1, const float* W2, const float* v, int B, int in_dim, int hidden, int gate_dim,
+                  float* act, float* g, cudaStream_t st) {
+    if (hidden > 64 || gate_dim > 64) fail("bsml_gate_forward", "hidden and gate widths above 64 are not supported");
+    ::bsml::count_launch();
+    gate_fwd_kernel<<<B, 64, 0, st>>>(W1, W2, v, in_dim, hidden, gate_dim, act, g);
+    BSML_LAUNCH("gate_fwd");
+}
+
+void gate_backward(const float* W2, const float* v, const float* act, const float* dG, int B, int in_dim,
+                   int hidden, int gate_dim, float* dW1, float* dW2, cudaStream_t st) {
+    if (gate_dim * hidden > 512 || hidden * in_dim > 512)
+        fail("bsml_gate_backward", "gate weights above 512 elements are not supported");
+    ::bsml::count_launch();
+    gate_bwd_kernel<<<1, 512, 0, st>>>(W2, dW1, dW2, v, act, dG, B, in_dim, hidden, gate_dim);
+    BSML_LAUNCH("gate_bwd");
+}
+
 Lora::Lora(Engine& eng, int rank, float scale, uint64_t seed) : eng_(eng), rank_(rank), scale_(scale) {
     if (rank < 1 || rank > kMaxRank) fail("bsml_lora_create", "rank must be in 1..32");
     BSML_CUDA(cudaGetDevice(&device_));

@@ -16,6 +16,14 @@
 
 namespace bsml {
 
+// ConditioningGate on its own (decoder_lora.cpp:28-78), batched over B condition
+// vectors v (B, in_dim): act = tanh(W1 v), g = W2 act; the backward accumulates
+// dW1, dW2 (+=) from dG (B, gate_dim).
+void gate_forward(const float* W1, const float* W2, const float* v, int B, int in_dim, int hidden, int gate_dim,
+                  float* act, float* g, cudaStream_t st);
+void gate_backward(const float* W2, const float* v, const float* act, const float* dG, int B, int in_dim,
+                   int hidden, int gate_dim, float* dW1, float* dW2, cudaStream_t st);
+
 // Per adapter (one per AdaIN, DecoderLora::adapters() order), device side.
 struct LoraAd {
     int64_t fw, fb;        // base fc weight [2C][S] / bias [2C] in the decoder parameters
@@ -44,6 +52,8 @@ class Lora {
     int step() const { return step_; }
     float* params() { return P_; }
     float* grads() { return G_; }
+    float* moment1() { return M_; }
+    float* moment2() { return V_; }
     int64_t off_W1() const { return 0; }
     int64_t off_W2() const { return (int64_t)kHidden * kInDim; }
     const std::vector<LoraAd>& adapters() const { return ads_; }

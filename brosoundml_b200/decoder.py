@@ -155,6 +155,64 @@ class Decoder:
         return dict(grads=grads, d_asr=d_asr, d_style=d_style, d_aff=d_aff)
 
 
+    # ── the two assemblies on their own (detail::decoder_backbone_* / generator_*)
+    def backbone_out_len(self, T: int) -> int:
+        n = ctypes.c_int(0)
+        _lib.check(_lib.lib().bsml_backbone_out_len(self._h, T, ctypes.byref(n)))
+        return n.value
+
+    def forward_backbone(self, params, asr, F0, N, style=None, aff_in=None, gen_in=None, aff_out=None):
+        """asr (B, asr_dim, T), F0 / N (B, 2T) -> gen_in (B, init_ch, L_gen)."""
+        params, asr, F0, N, style, aff_in = map(_f32, (params, asr, F0, N, style, aff_in))
+        B, _, T = asr.shape
+        if gen_in is None:
+            gen_in = torch.empty((B, self.cfg["init_ch"], self.backbone_out_len(T)), device=self.device)
+        self._borrowed = params
+        self._last = (B, T)
+        st = 0 if style is None else style.shape[-1]
+        _lib.check(_lib.lib().bsml_backbone_forward(self._h, B, T, _ptr(params), _ptr(asr), _ptr(F0), _ptr(N),
+                                                    _ptr(style), st, _ptr(aff_in), _ptr(gen_in), _ptr(aff_out),
+                                                    _stream()))
+        return gen_in
+
+    def backward_backbone(self, dgen_in, want_aff=False):
+        B, T = self._last
+        dev = self.device
+        grads = torch.empty(self.n_params, device=dev)
+        d_asr = torch.empty((B, self.cfg["asr_dim"], T), device=dev)
+        d_style = torch.empty((B, self.cfg["style_dim"]), device=dev)
+        d_aff = torch.empty(B * self.aff_per_clip, device=dev) if want_aff else None
+        _lib.check(_lib.lib().bsml_backbone_backward(self._h, _ptr(_f32(dgen_in)), _ptr(grads), _ptr(d_asr),
+                                                     _ptr(d_style), _ptr(d_aff), _stream()))
+        return dict(grads=grads, d_asr=d_asr, d_style=d_style, d_aff=d_aff)
+
+    def forward_generator(self, params, gen_in, har, style=None, aff_in=None, audio=None, aff_out=None):
+        """gen_in (B, init_ch, L_in), har (B, har_ch, frames) -> audio (B, hop*(frames-1))."""
+        params, gen_in, har, style, aff_in = map(_f32, (params, gen_in, har, style, aff_in))
+        B, _, L_in = gen_in.shape
+        frames = har.shape[2]
+        if audio is None:
+            audio = torch.empty((B, self.cfg["hop"] * (frames - 1)), device=self.device)
+        self._borrowed = params
+        self._last_gen = (B, L_in)
+        st = 0 if style is None else style.shape[-1]
+        _lib.check(_lib.lib().bsml_generator_forward(self._h, B, L_in, _ptr(params), _ptr(gen_in), _ptr(har),
+                                                     frames, _ptr(style), st, _ptr(aff_in), _ptr(audio),
+                                                     _ptr(aff_out), _stream()))
+        return audio
+
+    def backward_generator(self, daudio, want_aff=False):
+        B, L_in = self._last_gen
+        dev = self.device
+        grads = torch.empty(self.n_params, device=dev)
+        dgen = torch.empty((B, self.cfg["init_ch"], L_in), device=dev)
+        d_style = torch.empty((B, self.cfg["style_dim"]), device=dev)
+        d_aff = torch.empty(B * self.aff_per_clip, device=dev) if want_aff else None
+        _lib.check(_lib.lib().bsml_generator_backward(self._h, _ptr(_f32(daudio)), _ptr(grads), _ptr(dgen),
+                                                      _ptr(d_style), _ptr(d_aff), _stream()))
+        return dict(grads=grads, dgen_in=dgen, d_style=d_style, d_aff=d_aff)
+
+
 class Block(Decoder):
     """One decoder block on its own over the same engine: ``spec`` =
     dict(kind=1, style_dim, cin, cout, upsample) for an AdainResBlk1d

@@ -128,6 +128,33 @@ int bsml_decoder_decode(bsml_decoder* d, int B, int T, const float* params, cons
 int bsml_decoder_backward(bsml_decoder* d, const float* daudio, float* grads, float* d_asr, float* d_style,
                           float* d_aff, void* stream);
 
+/* The two assemblies on their own, on a whole-decoder handle, batched over B
+ * clips. The reference runs them as separate calls with caller-owned caches:
+ * decoder_backbone_forward_train / _backward (src/kokoro_decoder_backward.h:213-231)
+ * and generator_forward_train / generator_backward (:273-293). Here the engine
+ * keeps the caches of its last forward.
+ *   backbone:  asr (B, asr_dim, T), F0, N (B, 2T) -> gen_in (B, init_ch, L_gen),
+ *              L_gen from bsml_backbone_out_len. The backward takes dgen_in and
+ *              gives grads (n_params, OVERWRITTEN), d_asr, d_style, d_aff (optional).
+ *   generator: gen_in (B, init_ch, L_in), har (B, har_ch, frames) -> audio
+ *              (B, hop*(frames-1)). The backward takes daudio and gives grads,
+ *              dgen_in (B, init_ch, L_in), d_style, d_aff (optional).
+ * style rows are style_stride floats apart (0 = style_dim). aff_in / d_aff use
+ * the whole decoder's packing; each part reads its own AdaINs and writes the
+ * gradients of its own (the others' are zero). A backward follows the forward of
+ * the same part. */
+int bsml_backbone_out_len(const bsml_decoder* d, int T, int* L_gen);
+int bsml_backbone_forward(bsml_decoder* d, int B, int T, const float* params, const float* asr, const float* F0,
+                          const float* N, const float* style, int style_stride, const float* aff_in, float* gen_in,
+                          float* aff_out, void* stream);
+int bsml_backbone_backward(bsml_decoder* d, const float* dgen_in, float* grads, float* d_asr, float* d_style,
+                           float* d_aff, void* stream);
+int bsml_generator_forward(bsml_decoder* d, int B, int L_in, const float* params, const float* gen_in,
+                           const float* har, int frames, const float* style, int style_stride, const float* aff_in,
+                           float* audio, float* aff_out, void* stream);
+int bsml_generator_backward(bsml_decoder* d, const float* daudio, float* grads, float* dgen_in, float* d_style,
+                            float* d_aff, void* stream);
+
 /* Bytes of device workspace the engine holds for the current (B, T). */
 int64_t bsml_decoder_workspace_bytes(const bsml_decoder* d);
 
@@ -285,6 +312,17 @@ int bsml_lora_layout(const bsml_lora* l, int64_t* n_params, int* n_adapters, int
                      int64_t* off_W1, int64_t* off_W2, int64_t* off_A, int64_t* off_B, int* adapter_C);
 /* Device pointers to the parameter and gradient vectors (owned by the object). */
 int bsml_lora_buffers(bsml_lora* l, float** params, float** grads);
+/* Adam's first and second moments (device; the parameter vector's layout). */
+int bsml_lora_moments(bsml_lora* l, float** m, float** v);
+/* ConditioningGate on its own (src/decoder_lora.cpp:28-78), batched over B
+ * condition vectors v (B, in_dim): act = tanh(W1 v) (B, hidden), g = W2 act
+ * (B, gate_dim); W1 (hidden, in_dim), W2 (gate_dim, hidden), no biases. The
+ * backward ACCUMULATES dW1, dW2 (+=) from dG (B, gate_dim), like the reference's
+ * gradient accumulators (zero them between steps). hidden, gate_dim <= 64. */
+int bsml_gate_forward(const float* W1, const float* W2, const float* v, int B, int in_dim, int hidden, int gate_dim,
+                      float* act, float* g, void* stream);
+int bsml_gate_backward(const float* W2, const float* v, const float* act, const float* dG, int B, int in_dim,
+                       int hidden, int gate_dim, float* dW1, float* dW2, void* stream);
 /* DecoderLora::forward (src/decoder_lora.cpp:211-246), batched: style of clip b
  * = ref_s[b*ref_s_stride .. + style_dim), cond (B, 3), har optional (NULL: the
  * harmonic source). params = the frozen decoder weights, borrowed until the
@@ -407,6 +445,30 @@ int bsml_istft_forward(const float* re, const float* im, int B, int n_fft, int h
                        void* stream);
 int bsml_istft_backward(const float* daudio, int B, int n_fft, int hop, int L, float* dre, float* dim,
                         void* stream);
+/* spectral_head_forward_train / _backward (src/kokoro_decoder_backward.h:145-161),
+ * batched: x (B, C, L) -> leaky 0.01 -> conv_post (W (n_fft+2, C, post_kernel),
+ * bias or NULL, padding (post_kernel-1)/2) -> post (B, n_fft+2, L), the cache the
+ * backward reads -> mag = exp(post[:nf]), phase = sin(post[nf:]) -> iSTFT (center,
+ * periodic Hann of n_fft, hop) -> audio (B, hop*(L-1)). The backward maps daudio
+ * to dx (B, C, L) given the forward's x and post (conv_post frozen, as in the
+ * reference). */
+int bsml_spectral_head_forward(const float* x, int B, int C, int L, const float* W, const float* bias, int n_fft,
+                               int hop, int post_kernel, float* post, float* audio, void* stream);
+int bsml_spectral_head_backward(const float* x, const float* post, const float* daudio, int B, int C, int L,
+                                const float* W, int n_fft, int hop, int post_kernel, float* dx, void* stream);
+/* (batch, rows, cols) -> (batch, cols, rows): NCL <-> the reference's (L, C)
+ * sequence layout (bt::nchw_to_sequence, kokoro_decoder_backward.cpp:112-116). */
+int bsml_transpose(const float* src, int64_t batch, int rows, int cols, float* dst, void* stream);
+
+/* Memory for callers that keep host-addressable tensors (the reference's
+ * brotensor::Tensor is read and written element by element on the host, e.g. by
+ * its finite-difference tests): CUDA managed memory, zero-filled. bsml_memcpy
+ * copies between any two addresses the device can reach. */
+int bsml_managed_alloc(int64_t bytes, void** out);
+int bsml_managed_free(void* p);
+int bsml_synchronize(void);
+int bsml_memcpy(void* dst, const void* src, int64_t bytes, void* stream);
+
 /* HarmonicSource::forward (kokoro_modules.cpp:1574-1665): F0 (B, F) -> har (B, n_fft+2, F*scale/hop+1).
  * Phase arithmetic: BSML_PHASE_FP32_RUNNING is the reference's own (one fp32
  * accumulator per harmonic, per-sample add and a single 2*pi subtraction,

@@ -1,11 +1,14 @@
-// bsml_decoder.hpp — C++ layer over the C ABI in bsml_decoder.h, with the
-// reference's class and function names (wlejon/brosoundml:
-// include/brosoundml/decoder_lora.h, src/kokoro_decoder_backward.h), for a
-// maintainer who swaps the decoder training path under existing C++ callers.
+// bsml_decoder.hpp — batched C++ layer over the C ABI in bsml_decoder.h
+// (namespace brosoundml::b200), with class and function names modelled on the
+// reference's (wlejon/brosoundml: include/brosoundml/decoder_lora.h,
+// src/kokoro_decoder_backward.h) for callers that train many clips per call.
+// Callers of the reference's own signatures use the reference-signature layer
+// instead (include/brosoundml/decoder_lora.h, include/kokoro_decoder_backward.h,
+// libbsml_ref.so), which takes brotensor::Tensor and runs one clip per call.
 //
 // Header-only; needs no CUDA header (streams are void*, tensors are device
-// float pointers). Differences from the reference interface, all forced by the
-// absent brotensor::Tensor type or by batching:
+// float pointers). Differences from the reference interface, all from batching
+// and device pointers:
 //  * tensors are device pointers with explicit sizes, NCL with a leading batch
 //    axis B (B = 1 is the reference's case);
 //  * (gamma, beta) travel packed per clip as (B, 2C) rows, and the affines of a
@@ -32,7 +35,12 @@ inline void check(int rc) {
     if (rc < 0) throw std::runtime_error(bsml_last_error());
 }
 
-enum class Math { FP32 = BSML_MATH_FP32_SIMT, TF32X3 = BSML_MATH_TF32X3, BF16 = BSML_MATH_BF16 };
+enum class Math {
+    FP32 = BSML_MATH_FP32_SIMT,
+    TF32X3 = BSML_MATH_TF32X3,
+    BF16 = BSML_MATH_BF16,
+    BF16X3 = BSML_MATH_BF16X3
+};
 
 // Parameter table of an engine handle (names, offsets into the flat buffer).
 struct ParamLayout {
@@ -216,7 +224,6 @@ class SafeTensors {
     bsml_st* f_ = nullptr;
 };
 
-}  // namespace b200
 
 // ─── DecoderLora (include/brosoundml/decoder_lora.h:36-164) ─────────────────
 
@@ -301,6 +308,7 @@ class DecoderLora {
             off_B_ = std::move(o.off_B_);
             C_ = std::move(o.C_);
             weights_ = o.weights_;
+            cond_ = o.cond_;
         }
         return *this;
     }
@@ -316,13 +324,16 @@ class DecoderLora {
         b200::check(bsml_lora_forward(h_, ctx.batch, ctx.total, weights, ctx.asr, ctx.F0_pred, ctx.N_pred, ctx.ref_s,
                                       stride, ctx.har, ctx.frames, cond, audio, stream));
         weights_ = weights;
+        cond_ = cond;
     }
     // Backward of the last forward: accumulates every LoRA + gate gradient. The
-    // weights must be the forward's; cond must match the forward's (the gate's
+    // weights and the condition buffer must be the forward's (the gate's
     // activations are cached by the forward, as in the reference).
-    void backward(const float* weights, const float* /*cond*/, const float* dAudio, void* stream = nullptr) {
+    void backward(const float* weights, const float* cond, const float* dAudio, void* stream = nullptr) {
         if (weights != weights_)
             throw std::runtime_error("brosoundml: DecoderLora::backward: weights differ from the forward's");
+        if (cond != cond_)
+            throw std::runtime_error("brosoundml: DecoderLora::backward: cond differs from the forward's");
         b200::check(bsml_lora_backward(h_, dAudio, stream));
     }
     void zero_grad(void* stream = nullptr) { b200::check(bsml_lora_zero_grad(h_, stream)); }
@@ -383,6 +394,7 @@ class DecoderLora {
     std::vector<int64_t> off_A_, off_B_;
     std::vector<int> C_;
     const float* weights_ = nullptr;
+    const float* cond_ = nullptr;
 };
 
 // ─── the reference's detail:: atoms (src/kokoro_decoder_backward.h) ─────────
@@ -435,4 +447,5 @@ inline void decoder_backward(b200::Decoder& dec, const float* dAudio, float* dAf
 }
 
 }  // namespace detail
+}  // namespace b200
 }  // namespace brosoundml

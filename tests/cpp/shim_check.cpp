@@ -102,15 +102,15 @@ static int gpu_mode(const bsml_decoder_config& cfg, const std::string& dir) {
     const size_t S = (size_t)dec.audio_len(T, frames);
     Dev audio(B * S), audio_base(B * S), daudio(B * S);
 
-    auto lora = brosoundml::DecoderLora::make(dec, 4, 2.0f, 0);
+    auto lora = bb::DecoderLora::make(dec, 4, 2.0f, 0);
     EXPECT(lora.rank() == 4 && std::fabs(lora.scale() - 2.0f) < 1e-6f);
     EXPECT(lora.adapters().size() == L.affine_channels.size());
-    const brosoundml::ConditioningGate gate = lora.gate();
+    const bb::ConditioningGate gate = lora.gate();
     std::vector<float> w2(gate.gate_dim * gate.hidden);
     cudaMemcpy(w2.data(), gate.W2, sizeof(float) * w2.size(), cudaMemcpyDeviceToHost);
     for (float v : w2) EXPECT(v == 0.f);   // W2 = 0 at make
 
-    brosoundml::DecoderLoraContext ctx;
+    bb::DecoderLoraContext ctx;
     ctx.asr = dA.p; ctx.F0_pred = dF.p; ctx.N_pred = dN.p; ctx.ref_s = dR.p; ctx.har = dH.p;
     ctx.total = T; ctx.frames = frames; ctx.batch = B;
     std::vector<float> c = rnd((size_t)B * 3, g, -1, 1);
@@ -163,7 +163,7 @@ static int gpu_mode(const bsml_decoder_config& cfg, const std::string& dir) {
     EXPECT(std::memcmp(saved.data(), back.data(), sizeof(float) * saved.size()) == 0);
     // full training state: a fresh object resumes at the same step
     lora.save_state(dir + "/state.elra");
-    auto resumed = brosoundml::DecoderLora::make(dec, 4, 2.0f, 99);
+    auto resumed = bb::DecoderLora::make(dec, 4, 2.0f, 99);
     resumed.load_state(dir + "/state.elra");
     EXPECT(resumed.step() == lora.step());
     lora.load(dir + "/state.elra");   // the plain reader stops before the optimiser state
@@ -195,7 +195,7 @@ static int gpu_mode(const bsml_decoder_config& cfg, const std::string& dir) {
     EXPECT(std::sqrt(dn / dd) < 1e-6);
     cudaStreamDestroy(s);
     // move-only ownership
-    brosoundml::DecoderLora moved = std::move(lora);
+    bb::DecoderLora moved = std::move(lora);
     EXPECT(moved.rank() == 4);
     std::printf("OK\n");
     return 0;
