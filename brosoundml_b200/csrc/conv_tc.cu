@@ -50,7 +50,10 @@ __device__ int g_tc_err = 0;
 
 constexpr int TILE_BYTES = 16384;   // 128 rows x 128 bytes
 // promoted accumulation: K steps summed in TMEM before the epilogue folds them into registers
-constexpr int PG = 2;
+#ifndef BSML_PG
+#define BSML_PG 2
+#endif
+constexpr int PG = BSML_PG;
 constexpr int SMEM_OPTIN = 232448;  // opt-in dynamic shared memory per block on sm_100
 
 __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {

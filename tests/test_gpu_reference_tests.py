@@ -37,3 +37,43 @@ def test_reference_cpp_test_passes(name, tmp_path):
     r = subprocess.run([exe], capture_output=True, text=True, timeout=900, cwd=str(tmp_path))
     print(r.stdout[-4000:])
     assert r.returncode == 0 and f"{name}: OK" in r.stdout, (r.stdout[-4000:], r.stderr[-2000:])
+
+
+def test_gpu_checkpoint_loads_in_the_reference(tmp_path):
+    """An ELRA1 file written by the GPU DecoderLora (bsml_lora_save) restores, through
+    the reference's own DecoderLora::load (oracle/_ref/libref_compose.so, the
+    reference's src/decoder_lora.cpp compiled here), to exactly the GPU's values."""
+    import ctypes
+
+    import numpy as np
+    import torch
+
+    from brosoundml_b200 import config
+    from brosoundml_b200.decoder import Decoder
+    from brosoundml_b200.lora import DecoderLora
+    from oracle.oracle import Oracle
+    from tests.test_ref_compose_cpu import LIB, _cfg, _lib, _p, _table
+
+    if not os.path.exists(LIB):
+        pytest.skip("libref_compose.so is built where the reference checkout is present")
+    cfg = config.miniature()
+    o = Oracle(cfg)
+    d = Decoder(cfg, 0)
+    lora = DecoderLora(d, rank=4, scale=1.75, seed=3)
+    with torch.no_grad():
+        lora.params().uniform_(-0.3, 0.3)
+    torch.cuda.synchronize()
+    path = str(tmp_path / "gpu.elra")
+    lora.save(path)
+    want = lora.params().cpu().numpy()
+    L = _lib()
+    names, offs, nums = _table(o)
+    c = _cfg(cfg)
+    params = np.zeros(o.n_params, np.float32)
+    oA, oB = np.array(lora.off_A, np.int64), np.array(lora.off_B, np.int64)
+    back = np.zeros(lora.n_params, np.float32)
+    sc = ctypes.c_float(0)
+    rc = L.refc_lora_load(ctypes.byref(c), len(o.table), names, _p(offs), _p(nums), _p(params), 4, path.encode(),
+                          lora.off_W1, lora.off_W2, _p(oA), _p(oB), _p(back), ctypes.byref(sc))
+    assert rc == 0, L.refc_last_error()
+    assert np.array_equal(back, want) and abs(sc.value - 1.75) < 1e-7
