@@ -10,7 +10,8 @@ import ctypes
 import os
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_HERE, "libbsml_b200.so")
+# BSML_LIB selects another build of the library (e.g. the DEBUG=1 bounds-checking one)
+LIB_PATH = os.environ.get("BSML_LIB") or os.path.join(_HERE, "libbsml_b200.so")
 
 
 class BsmlConfig(ctypes.Structure):
@@ -153,6 +154,7 @@ SIGNATURES = {
     "bsml_lora_moments": ([_P, ctypes.POINTER(_P), ctypes.POINTER(_P)], _I),
     "bsml_gate_forward": ([_P, _P, _P, _I, _I, _I, _I, _P, _P, _P], _I),
     "bsml_gate_backward": ([_P, _P, _P, _P, _I, _I, _I, _I, _P, _P, _P], _I),
+    "bsml_debug_bounds": ([_P], _I),
     "bsml_harmonic_source": ([_CFG, _P, _I, _I, _P, _P, _P, _P], _I),
     "bsml_harmonic_source_mode": ([_CFG, _P, _I, _I, _P, _P, _P, _I, _P], _I),
     "bsml_decoder_set_phase_mode": ([_P, _I], _I),

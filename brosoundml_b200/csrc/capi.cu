@@ -348,6 +348,27 @@ int bsml_set_atom_math(int math_mode) {
     });
 }
 
+#ifdef BSML_DEBUG_BOUNDS
+}  // extern "C"
+namespace bsml {
+__device__ int g_dbg_bounds[5];
+}
+extern "C" {
+#endif
+
+int bsml_debug_bounds(int* record) {
+    return guarded([&] {
+        need(record != nullptr, "bsml_debug_bounds", "null argument");
+        for (int i = 0; i < 5; ++i) record[i] = 0;
+#ifdef BSML_DEBUG_BOUNDS
+        BSML_CUDA(cudaDeviceSynchronize());
+        BSML_CUDA(cudaMemcpyFromSymbol(record, bsml::g_dbg_bounds, sizeof(int) * 5));
+        const int zero[5] = {0, 0, 0, 0, 0};
+        BSML_CUDA(cudaMemcpyToSymbol(bsml::g_dbg_bounds, zero, sizeof(zero)));
+#endif
+    });
+}
+
 int bsml_device_error(void) {
     int v = 0;
     const int rc = guarded([&] { v = bsml::tc_error_flag(); });

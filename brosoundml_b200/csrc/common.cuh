@@ -36,12 +36,33 @@ int64_t launch_count();
 inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 inline int64_t round_up(int64_t a, int64_t b) { return ceil_div(a, b) * b; }
 
+#if defined(BSML_DEBUG_BOUNDS) && defined(__CUDACC__)
+// Debug builds (make DEBUG=1: relocatable device code, one copy of this word for
+// the whole library): the first out-of-range row access of any kernel is recorded
+// here as (1, b, l, B, L) and the access is clamped into range, so the kernel
+// finishes and the host reads the record (bsml_debug_bounds).
+extern __device__ int g_dbg_bounds[5];
+#endif
+
 // Channels-last activation view: element (b, l, c) at p[b*bstride + l*ld + c].
 struct Act {
     float* p = nullptr;
     int B = 0, L = 0, C = 0, ld = 0;
     int64_t bstride = 0;
+#if defined(BSML_DEBUG_BOUNDS) && defined(__CUDA_ARCH__)
+    __device__ float* row(int b, int l) const {
+        if (b < 0 || b >= B || l < 0 || l >= L) {
+            if (atomicCAS(&g_dbg_bounds[0], 0, 1) == 0) {
+                g_dbg_bounds[1] = b; g_dbg_bounds[2] = l; g_dbg_bounds[3] = B; g_dbg_bounds[4] = L;
+            }
+            b = b < 0 ? 0 : (b >= B ? B - 1 : b);
+            l = l < 0 ? 0 : (l >= L ? L - 1 : l);
+        }
+        return p + (int64_t)b * bstride + (int64_t)l * ld;
+    }
+#else
     __host__ __device__ float* row(int b, int l) const { return p + (int64_t)b * bstride + (int64_t)l * ld; }
+#endif
     Act slice_c(int c0, int nc) const {
         Act a = *this;
         a.p = p + c0;

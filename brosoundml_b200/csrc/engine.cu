@@ -4,6 +4,8 @@
 // Snake-alpha, fc and input gradients the reference drops.
 #include "engine.h"
 
+#include <nvtx3/nvToolsExt.h>
+
 #include <algorithm>
 #include <cmath>
 #include <cstring>
@@ -43,6 +45,17 @@ int conv_out(int L, const ConvP& c) {
     return num < 0 ? 0 : (int)(num / c.s + 1);
 }
 
+}  // namespace
+
+namespace {
+// NVTX range for the lifetime of the object: the engine's phases and conv calls
+// show up by name in a profiler timeline (header-only NVTX; no cost without a tool)
+struct Range {
+    explicit Range(const char* n) { nvtxRangePushA(n); }
+    ~Range() { nvtxRangePop(); }
+    Range(const Range&) = delete;
+    Range& operator=(const Range&) = delete;
+};
 }  // namespace
 
 Engine::Engine(const bsml_decoder_config& cfg, int device) : lay_(cfg), device_(device) { init(); }
@@ -573,6 +586,7 @@ void Engine::tc_launch(const Act& x, const TcPlanes& xp, const float* whi, const
 // ── conv wrappers
 void Engine::conv(const ConvP& c, const Act& x, const Act& y, const Act* r, int r_shift, float alpha, bool accum,
                   cudaStream_t st, const TcPlanes* xp, double* stats) {
+    const Range nvtx_range("bsml.conv.fwd");
     ConvFwd a;
     a.x = x; a.y = y; a.wp = wp_fwd_[c.id]; a.bias = P(c.b); a.r = r; a.r_shift = r_shift;
     a.k = c.k; a.s = c.s; a.p = c.p; a.d = c.d;
@@ -599,6 +613,7 @@ void Engine::conv(const ConvP& c, const Act& x, const Act& y, const Act* r, int 
 // flipped, transposed weight and padding d*(k-1) - p (stride 1 only).
 void Engine::conv_dgrad(const ConvP& c, const Act& dy, const Act& dx, bool accum, cudaStream_t st,
                         const TcPlanes* dyp) {
+    const Range nvtx_range("bsml.conv.dgrad");
     if (c.s != 1) fail("conv_dgrad", "strided conv input gradients are not needed on this path");
     ConvFwd a;
     a.x = dy; a.y = dx; a.wp = wp_dgrad_[c.id];
@@ -621,6 +636,7 @@ void Engine::conv_dgrad(const ConvP& c, const Act& dy, const Act& dx, bool accum
 
 void Engine::conv_wgrad(const ConvP& c, const Act& dy, const Act& x, cudaStream_t st, const TcPlanes* dyp,
                         const TcPlanes* xp, const double* bias_sum) {
+    const Range nvtx_range("bsml.conv.wgrad");
     if (!grads_) return;
     if (tc_ok(c.cin, c.cout, c.s)) {
         const int mode = tc_mode();
@@ -660,6 +676,7 @@ void Engine::conv_wgrad(const ConvP& c, const Act& dy, const Act& x, cudaStream_
 // ConvTranspose1d forward as one forward conv per stride phase r:
 //   y[q*s + r - p] = sum_m sum_ci W[ci, co, r + m*s] x[q - m, ci]
 void Engine::convT(const UpP& u, const Act& x, const Act& y, int row_off, const Act* r, cudaStream_t st) {
+    const Range nvtx_range("bsml.convT.fwd");
     const int Lu = (x.L - 1) * u.s - 2 * u.p + u.k;
     const bool tc = tc_ok(u.cin, u.cout, 1);
     TcPlanes tp;
@@ -690,6 +707,7 @@ void Engine::convT(const UpP& u, const Act& x, const Act& y, int row_off, const 
 // conv over dy viewed row-packed (ConvTPack: K = s*Co, taps u_min..u_max); CUDA
 // cores: a strided forward conv over dy.
 void Engine::convT_dgrad(const UpP& u, const Act& dy, const Act& dx, cudaStream_t st, const TcPlanes* dyp) {
+    const Range nvtx_range("bsml.convT.dgrad");
     if (dyp) {
         const ConvTPack pk = convT_pack(u.k, u.s, u.p);
         TcConvFwd a;
@@ -717,6 +735,7 @@ void Engine::convT_dgrad(const UpP& u, const Act& dy, const Act& dx, cudaStream_
 // dW[ci, co, t] = sum x[l, ci] dy[l*s - p + t, co] (conv wgrad with roles swapped; on
 // the tensor cores over the row-packed dy), db = colsum(dy)
 void Engine::convT_wgrad(const UpP& u, const Act& dy, const Act& x, cudaStream_t st, const TcPlanes* dyp) {
+    const Range nvtx_range("bsml.convT.wgrad");
     if (!grads_) return;
     if (dyp) {
         const ConvTPack pk = convT_pack(u.k, u.s, u.p);
@@ -760,6 +779,7 @@ void Engine::stats_of(const Act& x, const Stats& s, cudaStream_t st) { in_stats(
 
 // ── AdainResBlk1d (kokoro_decoder_backward.cpp:152-285)
 void Engine::blk_fwd(const BlkP& w, BlkC& c, const Act& y, cudaStream_t st) {
+    const Range nvtx_range("bsml.AdainResBlk1d.fwd");
     // The leaky AdaIN outputs are cached in fp32 (the weight gradients read them)
     // and, where the next conv runs on the tensor cores, also written as its
     // operand planes in the same pass; conv1's epilogue returns norm2's statistics.
@@ -797,6 +817,7 @@ void Engine::blk_fwd(const BlkP& w, BlkC& c, const Act& y, cudaStream_t st) {
 }
 
 void Engine::blk_bwd(const BlkP& w, BlkC& c, const Act& dY, const Act& dX, cudaStream_t st) {
+    const Range nvtx_range("bsml.AdainResBlk1d.bwd");
     const int Lin = c.Lin, Lout = c.Lout;
     double* bs = grads_ ? bsum_ : nullptr;
     auto zero_bs = [&](int C) {
@@ -865,6 +886,7 @@ void Engine::blk_bwd(const BlkP& w, BlkC& c, const Act& dY, const Act& dX, cudaS
 // returns the statistics of its output for the next AdaIN.
 void Engine::rb1_fwd(const RB1P& w, RB1C& c, const Act& x0, bool x0_stats, const Act& out, float out_alpha,
                      bool out_accum, cudaStream_t st) {
+    const Range nvtx_range("bsml.AdaINResBlock1.fwd");
     c.x[0] = x0;
     const int L = c.L, C = w.C;
     const bool tc = tc_ok(C, C, 1);   // every conv of the block is C -> C, stride 1
@@ -902,6 +924,7 @@ void Engine::rb1_fwd(const RB1P& w, RB1C& c, const Act& x0, bool x0_stats, const
 // the operand of the next input- and weight-gradient convs and sums its
 // columns for the preceding conv's bias gradient.
 void Engine::rb1_bwd(const RB1P& w, RB1C& c, const Act& dOut, float scale, const Act& D, cudaStream_t st) {
+    const Range nvtx_range("bsml.AdaINResBlock1.bwd");
     const int L = c.L, C = w.C;
     const bool tc = tc_ok(C, C, 1);
     const double pb = !tc ? 4.0 : plane_bytes();
@@ -1008,6 +1031,7 @@ void Engine::begin_forward(int B, int T, int frames, bool have_har, int part, co
 
 // backbone (kokoro_decoder_backward.cpp:482-537): asr, F0_, N_ -> genin_
 void Engine::run_backbone(const float* asr, cudaStream_t st) {
+    const Range nvtx_range("bsml.backbone.fwd");
     const auto& cf = lay_.cfg;
     const int B = B_, T = T_;
     ncl_to_cl(asr, asr_, st);
@@ -1040,6 +1064,7 @@ void Engine::run_backbone(const float* asr, cudaStream_t st) {
 
 // generator (kokoro_decoder_backward.cpp:592-667) and spectral head (:378-410): genin_, har -> audio
 void Engine::run_generator(const float* har, float* audio, cudaStream_t st) {
+    const Range nvtx_range("bsml.generator.fwd");
     const auto& cf = lay_.cfg;
     const int B = B_;
     if (have_har_)
@@ -1142,6 +1167,7 @@ void Engine::begin_backward(const char* where, int part, float* grads, cudaStrea
 
 // generator + spectral head backward; returns d(gen_in), channels-last, in S_[2] or S_[3]
 Act Engine::gen_backward(const float* daudio, cudaStream_t st) {
+    const Range nvtx_range("bsml.generator.bwd");
     const auto& cf = lay_.cfg;
     const int U = cf.n_ups, K = cf.n_kernels;
     // spectral head
@@ -1189,6 +1215,7 @@ Act Engine::gen_backward(const float* daudio, cudaStream_t st) {
 
 // backbone backward (kokoro_decoder_backward.cpp:539-574) + the cat-channel grads; dY = d(gen_in) in S_[4]
 void Engine::bb_backward(Act dY, cudaStream_t st) {
+    const Range nvtx_range("bsml.backbone.bwd");
     const auto& cf = lay_.cfg;
     const int B = B_, T = T_;
     fill(dasrres_.p, (int64_t)B * dasrres_.bstride, 0.f, st);

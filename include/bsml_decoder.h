@@ -391,6 +391,13 @@ int bsml_set_atom_math(int math_mode);
 /* Reads and clears the error word a tensor-core kernel sets when one of its
  * bounded waits gives up (0 = none). Synchronises the device. */
 int bsml_device_error(void);
+/* Debug builds (make -C brosoundml_b200 DEBUG=1, a separate libbsml_b200_debug.so;
+ * no reference counterpart) check every channels-last row access of the
+ * elementwise, normalisation and spectral kernels: the first access outside its
+ * view is recorded and clamped into range. record[0..4] = (1, b, l, B, L) of that
+ * access, or zeros (always zeros in release builds); reading clears it and
+ * synchronises the device. */
+int bsml_debug_bounds(int* record);
 /* Self-test of that mechanism (no reference counterpart): launches one kernel
  * whose bounded wait, on a barrier nothing completes, gives up after about 2 s
  * and leaves code 1 (wait for data) in the error word; the context stays usable. */
