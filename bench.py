@@ -48,6 +48,19 @@ WORKLOADS = {
 C1_METRIC = "AdaINResBlock1 [8,128,24000] k7 fwd+bwd conv TFLOP/s (fwd+dgrad+wgrad); Snake/AdaIN GB/s"
 
 
+_JSON_FD = None   # the original stdout of a multi-rank run (file descriptor 1 then points at stderr)
+
+
+def emit_json(line):
+    """The bench line, alone on stdout."""
+    s = json.dumps(line) + "\n"
+    if _JSON_FD is None:
+        sys.stdout.write(s)
+        sys.stdout.flush()
+    else:
+        os.write(_JSON_FD, s.encode())
+
+
 def audio_seconds(B, T):
     return B * 600 * T / 24000.0
 
@@ -571,6 +584,9 @@ def main():
     ap.add_argument("--eager", action="store_true",
                     help="launch every kernel from the host instead of replaying forward + loss + backward as "
                          "one CUDA graph (decoder workloads)")
+    ap.add_argument("--batch", type=int, default=None,
+                    help="clips per GPU instead of the workload's (a smaller case for profiler captures; "
+                         "the bench line's config then names the batch)")
     ap.add_argument("--probe", default=None, choices=["conv", "block"],
                     help="time one kernel workload on its own instead (see probe()); sizes below")
     ap.add_argument("--B", type=int, default=16)
@@ -606,12 +622,23 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     if world > 1:
-        # rank 0's stdout carries only the JSON line: no NCCL version banner
+        # rank 0's stdout carries only the JSON line: file descriptor 1 is pointed at
+        # stderr, so NCCL's log (written to C stdout) lands there, and the JSON line
+        # goes to a duplicate of the original stdout. Without a caller's NCCL_DEBUG the
+        # log holds the communicator set-up lines (version, ranks, transports).
+        global _JSON_FD
+        sys.stdout.flush()
+        _JSON_FD = os.dup(1)
+        os.dup2(2, 1)
         if os.environ.get("NCCL_DEBUG", "VERSION").upper() == "VERSION":
-            os.environ["NCCL_DEBUG"] = "WARN"
+            os.environ["NCCL_DEBUG"] = "INFO"
+            os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
         dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=torch.device("cuda", local))
     math = args.math or Decoder.DEFAULT_MATH
     B, T, desc = WORKLOADS[args.workload]
+    if args.batch:
+        B = args.batch
+        desc = f"{desc} [batch overridden: B={B} per GPU]"
     dev = torch.device("cuda", local)
     args.graph = not args.eager and args.workload in ("c0", "c2", "c3")
     if args.graph:
@@ -697,7 +724,13 @@ def main():
             rl_all[k] = {"ms": pms, "launches": n, "tflops": work / (pms / 1e3) / 1e12, "share": pms / ms,
                          "flops_per_launch": work / max(n, 1)}
         else:
-            rl_all[k] = {"ms": pms, "launches": n, "gbs": work / (pms / 1e3) / 1e9, "share": pms / ms}
+            gbs = work / (pms / 1e3) / 1e9
+            rl_all[k] = {"ms": pms, "launches": n, "gbs": gbs, "share": pms / ms,
+                         "frac_of_hbm_peak": gbs / load_peaks()["hbm_gbs"],
+                         "bytes": ("algorithmic: AdaIN+Snake forward 8 B per element (read x, write y), backward "
+                                   "12 B (read x and dy, write dx); the operand planes written for the next "
+                                   "conv, the recomputed Snake operand and the backward's second read of x "
+                                   "and dy are not counted")}
     dom = max(rl_all, key=lambda k: rl_all[k]["ms"])
     # the measured dense bf16 figure is the tensor roofline (sustained: these kernels run
     # inside a long step); TF32 operands run at half that rate on the same pipe
@@ -779,7 +812,7 @@ def main():
             "clocks": clk, "e2e": e2e, "gpu_launches": int(launches), "roofline": roofline,
             "roofline_by_class": rl_all, "cpu_baseline": cpu, "other_modes": modes,
         }
-        print(json.dumps(line), flush=True)
+        emit_json(line)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

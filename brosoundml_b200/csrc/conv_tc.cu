@@ -735,6 +735,10 @@ __device__ __forceinline__ void pack_one(const float* W, int kind, int Co, int C
         } else if (kind == PACK_CONVT_PHASE) {  // convT phase: m = co, kk = ci
             const int tt = r + (taps - 1 - t) * s;
             v = W[((int64_t)kk * Co + m) * k + tt];
+        } else if (kind == PACK_CONV_STRIDED) { // row-packed strided conv: m = co, kk = j*ld + ci (ld = r)
+            const int j = kk / r, ci = kk - j * r;
+            const int tt = t * s + j;
+            if (ci < Ci && tt < k) v = W[((int64_t)m * Ci + ci) * k + tt];
         } else {                                // convT dgrad, row-packed: m = ci, kk = j*Co + co
             const int u_min = -((r + s - 1) / s);
             const int j = kk / Co, co = kk - j * Co;
@@ -784,6 +788,20 @@ __global__ void wgrad_reduce_kernel(const float* part, int splits, int taps, int
         const double s = sum_strided(part + i, n, splits);
         const int64_t o = ((int64_t)co * Ci + ci) * taps + t;
         dW[o] = (float)(accum ? dW[o] + s : s);
+    }
+}
+
+// dW[co][ci][u*s + j] = dW2[co][j*ld + ci][u]   (strided conv, row-packed form)
+__global__ void wgrad_unpack_strided_kernel(const float* dW2, int Co, int Ci, int k, int s, int ld, int U,
+                                            float* dW) {
+    const int64_t n = (int64_t)Co * Ci * k;
+    const int K2 = s * ld;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const int t = (int)(i % k);
+        const int64_t q = i / k;
+        const int ci = (int)(q % Ci), co = (int)(q / Ci);
+        const int u = t / s, j = t - u * s;
+        dW[i] = dW2[((int64_t)co * K2 + j * ld + ci) * U + u];
     }
 }
 
@@ -1054,6 +1072,13 @@ void make_act_planes(const Act& x, int mode, void* hi, void* lo, cudaStream_t st
     BSML_LAUNCH("make_act_planes");
 }
 
+void wgrad_unpack_strided(const float* dW2, int Co, int Ci, int k, int s, int ld, float* dW, cudaStream_t st) {
+    ::bsml::count_launch();
+    wgrad_unpack_strided_kernel<<<grid_for((int64_t)Co * Ci * k), 256, 0, st>>>(dW2, Co, Ci, k, s, ld,
+                                                                                 (k + s - 1) / s, dW);
+    BSML_LAUNCH("wgrad_unpack_strided");
+}
+
 PackJob make_pack_job(int64_t w_off, int kind, int Co, int Ci, int k, int s, int r, void* hi, void* lo) {
     PackJob J;
     J.w_off = w_off; J.kind = kind; J.Co = Co; J.Ci = Ci; J.k = k; J.s = s; J.r = r; J.hi = hi; J.lo = lo;
@@ -1063,6 +1088,10 @@ PackJob make_pack_job(int64_t w_off, int kind, int Co, int Ci, int k, int s, int
     if (kind == PACK_CONVT_DGRAD) {
         if (r < 0) fail("pack_w_tc", "negative ConvTranspose1d padding");
         J.M = Ci; J.K = s * Co; J.taps = convT_pack(k, s, r).taps;
+    }
+    if (kind == PACK_CONV_STRIDED) {
+        if (r < Ci || s < 1) fail("pack_w_tc", "bad row-packed strided conv");
+        J.K = s * r; J.taps = (k + s - 1) / s;
     }
     J.Kp = (int)round_up(J.K, 8);
     J.n = (int64_t)J.taps * J.M * J.Kp;

@@ -36,7 +36,10 @@ void make_act_planes(const Act& x, int mode, void* hi, void* lo, cudaStream_t st
 //   convT dgrad:    M = Ci, K = s*Co (row-packed, see ConvTPack), r = the convT padding p
 void pack_w_tc(const float* W, int kind, int Co, int Ci, int k, int s, int r, int mode, void* hi, void* lo,
                cudaStream_t st);
-enum { PACK_CONV_FWD = 0, PACK_CONV_DGRAD = 1, PACK_CONVT_PHASE = 2, PACK_CONVT_DGRAD = 3 };
+//   strided conv:   M = Co, K = s*ld (row-packed input, see the engine's strided noise conv),
+//                   r = ld (the unpacked input's row pitch), taps = ceil(k / s):
+//                   W2[u][co][j*ld + ci] = W[co][ci][u*s + j] (0 for ci >= Ci or u*s + j >= k)
+enum { PACK_CONV_FWD = 0, PACK_CONV_DGRAD = 1, PACK_CONVT_PHASE = 2, PACK_CONVT_DGRAD = 3, PACK_CONV_STRIDED = 4 };
 
 // One weight packing of a batch: the weight at params + w_off, packed as pack_w_tc
 // would, into elements [start, start + n) of the batch's flat index space.
@@ -50,6 +53,11 @@ PackJob make_pack_job(int64_t w_off, int kind, int Co, int Ci, int k, int s, int
 // Every job of `jobs` (device array, starts as prefix sums, `total` elements) in one launch.
 constexpr int PACK_MAX_JOBS = 256;
 void pack_w_tc_batch(const float* params, const PackJob* jobs, int n_jobs, int64_t total, int mode, cudaStream_t st);
+
+// Weight gradient of a strided conv from its row-packed form: dW2 [Co][s*ld][U] (the
+// tensor-core weight gradient's (co, channel, tap) order) -> dW [Co][Ci][k], element
+// (co, ci, u*s + j) = dW2 (co, j*ld + ci, u).
+void wgrad_unpack_strided(const float* dW2, int Co, int Ci, int k, int s, int ld, float* dW, cudaStream_t st);
 
 // ConvTranspose1d (weight W[Ci][Co][k], stride s, padding p, output length Lu)
 // input and weight gradients as stride-1 problems over dy viewed row-packed:

@@ -95,12 +95,25 @@ void Engine::init() {
         for (int r = 0; r < u.s; ++r) wp_up_[u.id].push_back(take((int64_t)((u.k - r + u.s - 1) / u.s) * u.cin * round_up(u.cout, 4)));
         wp_up_dgrad_[u.id] = take((int64_t)u.k * u.cout * round_up(u.cin, 4));
     }
+    // the first strided noise conv runs in row-packed form on the tensor cores
+    for (size_t i = 0; i < lay_.noise.size(); ++i)
+        if (lay_.noise[i].s > 1) {
+            spk_ = (int)i;
+            break;
+        }
+    // forward tensor-core planes of a conv: [k][Co][Ci] or, for the row-packed one, [ceil(k/s)][Co][s*ld]
+    auto fwd_floats = [&](const ConvP* c) {
+        int64_t n = (int64_t)c->k * c->cout * round_up(c->cin, 8);
+        if (spk_ >= 0 && c == &lay_.noise[spk_])
+            n = std::max<int64_t>(n, (int64_t)ceil_div(c->k, c->s) * c->cout * round_up((int64_t)c->s * pitch(c->cin), 8));
+        return n;
+    };
     // tensor-core weight planes: 2 fp32 planes per layout (bf16 uses the first half)
     {
         int64_t tb = 0;
         auto tsz = [&](int64_t floats) { tb = round_up(tb, 256) + floats * 4; };
         for (auto* c : lay_.convs) {
-            tsz((int64_t)c->k * c->cout * round_up(c->cin, 8)); tsz((int64_t)c->k * c->cout * round_up(c->cin, 8));
+            tsz(fwd_floats(c)); tsz(fwd_floats(c));
             tsz((int64_t)c->k * c->cin * round_up(c->cout, 8)); tsz((int64_t)c->k * c->cin * round_up(c->cout, 8));
         }
         for (auto& u : lay_.ups) {
@@ -121,8 +134,8 @@ void Engine::init() {
         const size_t nc = lay_.convs.size();
         tcw_fwd_hi_.resize(nc); tcw_fwd_lo_.resize(nc); tcw_dg_hi_.resize(nc); tcw_dg_lo_.resize(nc);
         for (auto* c : lay_.convs) {
-            tcw_fwd_hi_[c->id] = ttake((int64_t)c->k * c->cout * round_up(c->cin, 8));
-            tcw_fwd_lo_[c->id] = ttake((int64_t)c->k * c->cout * round_up(c->cin, 8));
+            tcw_fwd_hi_[c->id] = ttake(fwd_floats(c));
+            tcw_fwd_lo_[c->id] = ttake(fwd_floats(c));
             tcw_dg_hi_[c->id] = ttake((int64_t)c->k * c->cin * round_up(c->cout, 8));
             tcw_dg_lo_[c->id] = ttake((int64_t)c->k * c->cin * round_up(c->cout, 8));
         }
@@ -328,13 +341,25 @@ void Engine::plan(Planner& P) {
     }
     // harmonic source / har
     const int Fr = 2 * T;
-    if (have_har_) {
-        har_ = P.act(B, frames_, cf.har_ch);
-    } else {
+    if (!have_har_) {
         frames_ = (Fr * cf.upsample_scale) / cf.hop + 1;
-        har_ = P.act(B, frames_, cf.har_ch);
         hs_phase_ = P.d((int64_t)B * (cf.harmonic_num + 1) * Fr);
         hs_src_ = P.f((int64_t)B * Fr * cf.upsample_scale);
+    }
+    if (spk_ >= 0) {
+        // rows [0, p) and [p + frames, R) stay zero; the packed conv reads rows < s * (No + taps - 1)
+        const ConvP& c = lay_.noise[spk_];
+        const int No = conv_out(frames_, c);
+        const int64_t need = std::max<int64_t>((int64_t)c.s * (No + ceil_div(c.k, c.s) - 1), (int64_t)c.p + frames_);
+        spk_rows_ = (int)round_up(need, c.s);
+        har_full_ = P.act(B, spk_rows_, cf.har_ch);
+        har_ = har_full_;
+        har_.p = har_full_.p ? har_full_.p + (int64_t)c.p * har_full_.ld : nullptr;
+        har_.L = frames_;
+        note(spk_rows_, cf.har_ch);
+        spk_dw_ = P.f((int64_t)c.cout * c.s * pitch(c.cin) * ceil_div(c.k, c.s));
+    } else {
+        har_ = P.act(B, frames_, cf.har_ch);
     }
     // generator stages
     const int U = cf.n_ups, K = cf.n_kernels;
@@ -382,6 +407,7 @@ void Engine::plan_scratch(Planner& P, int64_t max_elems, int max_c) {
     dacc_ = P.d((int64_t)B * std::max(max_c, 1) * 3);
     ssum_ = P.d((int64_t)B * std::max(max_c, 1) * 2);
     bsum_ = P.d(std::max(max_c, 1));
+    bsum0_ = P.d(std::max(max_c, 1));
     part_floats_ = 48ll << 20;
     part_ = P.f(part_floats_);
     fc_part_ = P.f(ceil_div(fc_rows_, 256) * (int64_t)B * cf.style_dim + 64);
@@ -397,6 +423,8 @@ void Engine::plan_scratch(Planner& P, int64_t max_elems, int max_c) {
     tc_yl_ = P.f(max_elems);
     tc_dh_ = P.f(max_elems);
     tc_dl_ = P.f(max_elems);
+    tc_eh_ = P.f(max_elems);
+    tc_el_ = P.f(max_elems);
 }
 
 // One block (block_kind != 0): T_ is the block's input length L
@@ -477,6 +505,9 @@ void Engine::build_pack_jobs() {
             if (tc_ok(c->cin, c->cout, c->s))
                 add(fw, make_pack_job(c->w, PACK_CONV_FWD, c->cout, c->cin, c->k, 1, 0, tcw_fwd_hi_[c->id],
                                       tcw_fwd_lo_[c->id]));
+            else if (strided_tc(*c))
+                add(fw, make_pack_job(c->w, PACK_CONV_STRIDED, c->cout, c->cin, c->k, c->s, pitch(c->cin),
+                                      tcw_fwd_hi_[c->id], tcw_fwd_lo_[c->id]));
             if (c->s == 1 && tc_ok(c->cout, c->cin, 1))
                 add(dg, make_pack_job(c->w, PACK_CONV_DGRAD, c->cout, c->cin, c->k, 1, 0, tcw_dg_hi_[c->id],
                                       tcw_dg_lo_[c->id]));
@@ -509,7 +540,8 @@ void Engine::pack_weights(cudaStream_t st) {
     if (pack_jobs_math_ != math_) build_pack_jobs();
     pack_w_tc_batch(params_, pack_jobs_, n_pack_fw_, tot_pack_fw_, tc_mode(), st);
     for (auto* c : lay_.convs)
-        if (!tc_ok(c->cin, c->cout, c->s)) pack_conv_fwd(params_ + c->w, c->cout, c->cin, c->k, wp_fwd_[c->id], st);
+        if (!tc_ok(c->cin, c->cout, c->s) && !strided_tc(*c))
+            pack_conv_fwd(params_ + c->w, c->cout, c->cin, c->k, wp_fwd_[c->id], st);
     for (auto& u : lay_.ups)
         if (!tc_ok(u.cin, u.cout, 1))
             for (int r = 0; r < u.s; ++r) pack_convT_phase(params_ + u.w, u.cin, u.cout, u.k, u.s, r, wp_up_[u.id][r], st);
@@ -552,11 +584,11 @@ void Engine::adain_fwd_to(const Act& x, const double* sums, const Stats& s, cons
 
 void Engine::adain_bwd_to(const Act& x, const Stats& s, const float* gb, int act, float slope, const float* alpha,
                           const Act& dy, const Opnd& out, const Act* skip, double* colsum, float* dgb, float* dalpha,
-                          cudaStream_t st, bool acc_ready) {
+                          cudaStream_t st, bool acc_ready, float skip_scale, bool out_accum) {
     PlaneOut po;
     po.hi = const_cast<void*>(out.tp.hi); po.lo = const_cast<void*>(out.tp.lo); po.ld = out.tp.ld; po.mode = tc_mode();
     adain_act_bwd_v(x, s.mean, s.rstd, gb, act, slope, alpha, dy, out.f.p ? &out.f : nullptr, skip,
-                    out.tp.hi ? &po : nullptr, colsum, dgb, dalpha, dacc_, st, acc_ready);
+                    out.tp.hi ? &po : nullptr, colsum, dgb, dalpha, dacc_, st, acc_ready, skip_scale, out_accum);
 }
 
 void Engine::recompute_reduce_to(const Act& x, const Stats& s, const float* gb, int act, float slope,
@@ -594,6 +626,16 @@ void Engine::conv(const ConvP& c, const Act& x, const Act& y, const Act* r, int 
     a.alpha = alpha; a.accum = accum;
     if (a.No != y.L) fail("conv", "output length mismatch");
     if (stats) BSML_CUDA(cudaMemsetAsync(stats, 0, sizeof(double) * 2 * (size_t)y.B * c.cout, st));
+    if (strided_tc(c)) {
+        // x is har_, a view inside har_full_: the packed rows start at the buffer's first (zero) row
+        const Act X2 = packed_view(c);
+        const TcPlanes tp = tc_planes(X2, st);
+        const int id = prof_begin(PROF_CONV_TC, 2.0 * c.cin * c.cout * c.k * (double)a.No * x.B, st);
+        tc_launch(X2, tp, tcw_fwd_hi_[c.id], tcw_fwd_lo_[c.id], (int)ceil_div(c.k, c.s), c.cout, y, a.bias, r,
+                  r_shift, 0, 1, a.No, 0, 1, 0, alpha, accum, stats, st);
+        prof_end(id, st);
+        return;
+    }
     if (tc_ok(c.cin, c.cout, c.s)) {
         const TcPlanes tp = xp ? *xp : tc_planes(x, st);
         const int id = prof_begin(PROF_CONV_TC, 2.0 * c.cin * c.cout * c.k * (double)a.No * x.B, st);
@@ -638,6 +680,29 @@ void Engine::conv_wgrad(const ConvP& c, const Act& dy, const Act& x, cudaStream_
                         const TcPlanes* xp, const double* bias_sum) {
     const Range nvtx_range("bsml.conv.wgrad");
     if (!grads_) return;
+    if (strided_tc(c)) {
+        const int mode = tc_mode();
+        const Act X2 = packed_view(c);
+        TcConvWgrad w;
+        if (dyp) {
+            w.dy = *dyp;
+        } else {
+            make_act_planes(dy, mode, tc_yh_, tc_yl_, st);
+            w.dy.hi = tc_yh_; w.dy.lo = tc_yl_; w.dy.ld = tc_pitch(dy.C, mode);
+        }
+        w.x = tc_planes(X2, st);
+        w.B = dy.B; w.Lo = dy.L; w.Co = dy.C; w.L_in = X2.L; w.Ci = X2.C;
+        w.taps = (int)ceil_div(c.k, c.s); w.p = 0; w.d = 1; w.dW = spk_dw_;
+        const int id = prof_begin(PROF_WGRAD_TC, 2.0 * c.cin * c.cout * c.k * (double)dy.L * dy.B, st);
+        conv_wgrad_tc(w, mode, part_, part_floats_, st);
+        wgrad_unpack_strided(spk_dw_, c.cout, c.cin, c.k, c.s, har_full_.ld, grads_ + c.w, st);
+        if (c.b >= 0) {
+            if (bias_sum) d2f(bias_sum, c.cout, grads_ + c.b, false, st);
+            else colsum(dy, grads_ + c.b, false, part_, st);
+        }
+        prof_end(id, st);
+        return;
+    }
     if (tc_ok(c.cin, c.cout, c.s)) {
         const int mode = tc_mode();
         TcConvWgrad w;
@@ -890,9 +955,9 @@ void Engine::rb1_fwd(const RB1P& w, RB1C& c, const Act& x0, bool x0_stats, const
     c.x[0] = x0;
     const int L = c.L, C = w.C;
     const bool tc = tc_ok(C, C, 1);   // every conv of the block is C -> C, stride 1
-    // bytes of one AdaIN+Snake forward: read x, write the conv operand
-    const double out_b = !tc ? 4.0 : plane_bytes();
-    const double nb = (4.0 + out_b) * (double)x0.numel();
+    // algorithmic bytes of one AdaIN+Snake forward: read x, write y (fp32), 8 B per
+    // element; the operand planes written instead of y are implementation traffic
+    const double nb = 8.0 * (double)x0.numel();
     for (int i = 0; i < 3; ++i) {
         int id = prof_begin(PROF_NORM_FWD, nb, st);
         const double* sums = ssum_;   // from the previous conv's epilogue
@@ -923,48 +988,56 @@ void Engine::rb1_fwd(const RB1P& w, RB1C& c, const Act& x0, bool x0_stats, const
 // recomputed from the cached inputs; each AdaIN backward writes its result as
 // the operand of the next input- and weight-gradient convs and sums its
 // columns for the preceding conv's bias gradient.
-void Engine::rb1_bwd(const RB1P& w, RB1C& c, const Act& dOut, float scale, const Act& D, cudaStream_t st) {
+void Engine::rb1_bwd(const RB1P& w, RB1C& c, const Act& dOut, float scale, const Act& D, cudaStream_t st,
+                     const RB1Io* io) {
     const Range nvtx_range("bsml.AdaINResBlock1.bwd");
     const int L = c.L, C = w.C;
     const bool tc = tc_ok(C, C, 1);
-    const double pb = !tc ? 4.0 : plane_bytes();
     const double n = (double)D.numel();
     Act t = view(S_[4], L, C);
     double* bs = grads_ ? bsum_ : nullptr;
     auto zero_bs = [&]() {
         if (bs) BSML_CUDA(cudaMemsetAsync(bs, 0, sizeof(double) * C, st));
     };
-    // D = scale * dOut: fp32 (the running gradient), planes, bias sum of c2[2]
+    // D = scale * dOut: fp32 (the running gradient), planes, bias sum of c2[2]; or,
+    // with the entry made by the caller, planes and bias sum from there and D first
+    // written by the first pair's last pass (dOut, scaled, as its skip term)
     Opnd Dp;
     Dp.f = D;
     if (tc) { Dp.tp.hi = tc_dh_; Dp.tp.lo = tc_dl_; Dp.tp.ld = tc_pitch(C, tc_mode()); }
-    {
+    const bool pre = io && io->in_planes;
+    if (pre && !tc) fail("rb1_bwd", "internal: entry planes without the tensor-core path");
+    const TcPlanes* in_planes = pre ? io->in_planes : Dp.planes();
+    const double* in_bs = pre ? (grads_ ? io->in_bsum : nullptr) : bs;
+    if (!pre) {
         PlaneOut po;
         po.hi = tc_dh_; po.lo = tc_dl_; po.ld = Dp.tp.ld; po.mode = tc_mode();
         zero_bs();
         scale_out_v(dOut, scale, &D, tc ? &po : nullptr, bs, st);
     }
-    // Algorithmic bytes per element of one AdaIN+Snake backward with its recompute:
-    // x and dy read once, the recomputed operand and the gradient written (the
-    // second read of x and dy by the apply pass is implementation traffic).
+    // Algorithmic bytes per element of one AdaIN+Snake backward: x and dy read, dx
+    // written (fp32), 12 B, credited 8 B to the reduction pass and 4 B to the apply
+    // pass; the recomputed Snake operand, the operand planes and the apply pass's
+    // second read of x and dy are implementation traffic.
     for (int i = 2; i >= 0; --i) {
-        conv_dgrad(w.c2[i], D, t, false, st, Dp.planes());
+        const TcPlanes* dpl = i == 2 ? in_planes : Dp.planes();
+        conv_dgrad(w.c2[i], D, t, false, st, dpl);
         // s2[i] = Snake(AdaIN(c1[i])) again, as the weight-gradient operand, in the
         // same pass as the backward's reduction over (c1[i], t)
-        int id = prof_begin(PROF_NORM_BWD, (8.0 + pb) * n, st);
+        int id = prof_begin(PROF_NORM_BWD, 8.0 * n, st);
         const Opnd s2 = operand(tc, L, C, S_[0], tc_xh_, tc_xl_);
         recompute_reduce_to(c.c1[i], c.st2[i], aff(w.a2[i]), ACT_SNAKE, 0.f, P(w.al2[i]), t, s2, st);
         prof_end(id, st);
-        conv_wgrad(w.c2[i], D, s2.f, st, Dp.planes(), s2.planes(), bs);
+        conv_wgrad(w.c2[i], D, s2.f, st, dpl, s2.planes(), i == 2 ? in_bs : bs);
         // u = gradient at conv1's output (operand of c1's dgrad and wgrad)
-        id = prof_begin(PROF_NORM_BWD, pb * n, st);
+        id = prof_begin(PROF_NORM_BWD, 4.0 * n, st);
         const Opnd u = operand(tc, L, C, S_[5], tc_yh_, tc_yl_);
         zero_bs();
         adain_bwd_to(c.c1[i], c.st2[i], aff(w.a2[i]), ACT_SNAKE, 0.f, P(w.al2[i]), t, u, nullptr, bs, daff(w.a2[i]),
                      G(w.al2[i]), st, true);
         prof_end(id, st);
         conv_dgrad(w.c1[i], u.f, t, false, st, u.planes());
-        id = prof_begin(PROF_NORM_BWD, (8.0 + pb) * n, st);
+        id = prof_begin(PROF_NORM_BWD, 8.0 * n, st);
         const Opnd s1 = operand(tc, L, C, S_[0], tc_xh_, tc_xl_);
         recompute_reduce_to(c.x[i], c.st1[i], aff(w.a1[i]), ACT_SNAKE, 0.f, P(w.al1[i]), t, s1, st);
         prof_end(id, st);
@@ -979,9 +1052,23 @@ void Engine::rb1_bwd(const RB1P& w, RB1C& c, const Act& dOut, float scale, const
         } else {
             Dn.tp = TcPlanes{};
         }
-        id = prof_begin(PROF_NORM_BWD, (4.0 + 4.0 + (Dn.tp.hi ? pb : 0.0)) * n, st);   // skip read, fp32 out, planes
-        adain_bwd_to(c.x[i], c.st1[i], aff(w.a1[i]), ACT_SNAKE, 0.f, P(w.al1[i]), t, Dn, &D, bsn, daff(w.a1[i]),
-                     G(w.al1[i]), st, true);
+        const Act* skip = &D;
+        float skip_scale = 1.f;
+        if (pre && i == 2) {
+            skip = &dOut;
+            skip_scale = scale;
+        }
+        bool out_accum = false;
+        if (i == 0 && io && io->out) {
+            Dn.f = *io->out;
+            Dn.tp = io->out_planes;
+            out_accum = io->out_accum;
+            bsn = grads_ ? io->out_bsum : nullptr;
+            if (bsn) BSML_CUDA(cudaMemsetAsync(bsn, 0, sizeof(double) * C, st));
+        }
+        id = prof_begin(PROF_NORM_BWD, 4.0 * n, st);
+        adain_bwd_to(c.x[i], c.st1[i], aff(w.a1[i]), ACT_SNAKE, 0.f, P(w.al1[i]), t, Dn, skip, bsn, daff(w.a1[i]),
+                     G(w.al1[i]), st, true, skip_scale, out_accum);
         prof_end(id, st);
     }
 }
@@ -1071,6 +1158,16 @@ void Engine::run_generator(const float* har, float* audio, cudaStream_t st) {
         ncl_to_cl(har, har_, st);
     else
         BSML_CUDA(cudaStreamWaitEvent(st, ev_join_, 0));
+    if (spk_ >= 0) {
+        // the zero rows around the frames of the row-packed noise conv's input
+        const int lead = lay_.noise[spk_].p, tail = spk_rows_ - lead - frames_;
+        const size_t pitch_b = sizeof(float) * (size_t)har_full_.bstride;
+        if (lead > 0)
+            BSML_CUDA(cudaMemset2DAsync(har_full_.p, pitch_b, 0, sizeof(float) * (size_t)lead * har_full_.ld, B, st));
+        if (tail > 0)
+            BSML_CUDA(cudaMemset2DAsync(har_full_.p + (int64_t)(lead + frames_) * har_full_.ld, pitch_b, 0,
+                                        sizeof(float) * (size_t)tail * har_full_.ld, B, st));
+    }
     const int U = cf.n_ups, K = cf.n_kernels;
     for (int i = 0; i < U; ++i) {
         StageC& s = stc_[i];
@@ -1188,13 +1285,45 @@ Act Engine::gen_backward(const float* daudio, cudaStream_t st) {
         // dm = sum_j rb_j^T (dX / K)   (D in S_[xbuf^1], dm in S_[1])
         Act D = view(S_[xbuf ^ 1], s.Lx, u.cout);
         Act dm = view(S_[1], s.Lx, u.cout);
-        for (int j = 0; j < K; ++j) {
-            rb1_bwd(lay_.rbs[i * K + j], s.res[j], dX, 1.f / (float)K, D, st);
-            if (j == 0) copy_act(D, dm, st);
-            else add_act(D, dm, 1.f, st);
+        if (tc_ok(u.cout, u.cout, 1)) {
+            // the resblocks' common entry dX / K as planes and column sums, made once;
+            // each resblock adds its input gradient into dm, the last one also writing
+            // dm's planes (tc_dh_) and column sums (bsum_), the noise resblock's entry
+            const int mode = tc_mode();
+            PlaneOut p0;
+            p0.hi = tc_eh_; p0.lo = tc_el_; p0.ld = tc_pitch(u.cout, mode); p0.mode = mode;
+            TcPlanes t0;
+            t0.hi = tc_eh_; t0.lo = tc_el_; t0.ld = p0.ld;
+            double* bs0 = grads_ ? bsum0_ : nullptr;
+            if (bs0) BSML_CUDA(cudaMemsetAsync(bs0, 0, sizeof(double) * u.cout, st));
+            scale_out_v(dX, 1.f / (float)K, nullptr, &p0, bs0, st);
+            TcPlanes tdm;
+            tdm.hi = tc_dh_; tdm.lo = tc_dl_; tdm.ld = p0.ld;
+            for (int j = 0; j < K; ++j) {
+                RB1Io io;
+                io.in_planes = &t0;
+                io.in_bsum = bs0;
+                io.out = &dm;
+                io.out_accum = j > 0;
+                if (j == K - 1) {
+                    io.out_planes = tdm;
+                    io.out_bsum = bsum_;
+                }
+                rb1_bwd(lay_.rbs[i * K + j], s.res[j], dX, 1.f / (float)K, D, st, &io);
+            }
+            // noise branch: affine / alpha / conv grads; its input grad only feeds noise_convs' wgrad
+            RB1Io nio;
+            nio.in_planes = &tdm;
+            nio.in_bsum = bsum_;
+            rb1_bwd(lay_.nres[i], s.noise, dm, 1.f, D, st, &nio);
+        } else {
+            for (int j = 0; j < K; ++j) {
+                rb1_bwd(lay_.rbs[i * K + j], s.res[j], dX, 1.f / (float)K, D, st);
+                if (j == 0) copy_act(D, dm, st);
+                else add_act(D, dm, 1.f, st);
+            }
+            rb1_bwd(lay_.nres[i], s.noise, dm, 1.f, D, st);
         }
-        // noise branch: affine / alpha / conv grads; its input grad only feeds noise_convs' wgrad
-        rb1_bwd(lay_.nres[i], s.noise, dm, 1.f, D, st);
         conv_wgrad(lay_.noise[i], D, har_, st);
         Act du = dm;
         if (i == U - 1) {

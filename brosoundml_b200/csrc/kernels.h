@@ -70,13 +70,15 @@ void in_stats(const Act& x, float eps, double* acc, float* mean, float* rstd, cu
 // Writes y (fp32, nullable) and / or operand planes (nullable).
 void adain_act_fwd_v(const Act& x, const double* sums, float eps, float* mean, float* rstd, const float* gb, int act,
                      float slope, const float* alpha, const Act* y, const PlaneOut* planes, cudaStream_t st);
-// Backward of adain_act_fwd_v. out = dx (+ skip; dx may alias skip) goes to dx
-// (nullable) and / or planes (nullable); colsum[c] += sum over (b, l) of out
-// (double, nullable, not zeroed here). dgb, dalpha as in adain_act_bwd.
+// Backward of adain_act_fwd_v. out = dx (+ skip_scale * skip; dx may alias skip)
+// goes to dx (nullable) and / or planes (nullable); with dx_accum the prior dx is
+// added as well (out = dx_old + ..., then stored to dx and the planes);
+// colsum[c] += sum over (b, l) of out (double, nullable, not zeroed here). dgb,
+// dalpha as in adain_act_bwd.
 void adain_act_bwd_v(const Act& x, const float* mean, const float* rstd, const float* gb, int act, float slope,
                      const float* alpha, const Act& dy, const Act* dx, const Act* skip, const PlaneOut* planes,
                      double* colsum, float* dgb, float* dalpha, double* acc, cudaStream_t st,
-                     bool acc_ready = false);
+                     bool acc_ready = false, float skip_scale = 1.f, bool dx_accum = false);
 // The backward's reduction pass fused with recomputing the forward output act(AdaIN(x))
 // into y / planes (a weight gradient's operand): acc is zeroed and filled for a
 // following adain_act_bwd_v(..., acc_ready = true) with the same x, dy and affine.

@@ -33,6 +33,7 @@ struct Out4 {
     float* y = nullptr; int64_t y_bs = 0; int y_ld = 0;                 // fp32 output (nullable)
     void* hi = nullptr; void* lo = nullptr; int64_t p_bs = 0; int p_ld = 0; int mode = 1;   // planes (nullable)
     const float* skip = nullptr; int64_t s_bs = 0; int s_ld = 0;       // added before the store (nullable)
+    float s_scale = 1.f;                                                // factor on skip
 };
 
 __device__ __forceinline__ void put(const Out4& o, int b, int l, int c, const float4& v, int nv) {
@@ -338,8 +339,9 @@ __global__ void __launch_bounds__(NT, 2) adain_recompute_reduce_kernel(Act x, in
     }
 }
 
-// out = rstd * g1 * (dz - mean(dz) - xhat * mean(dz * xhat)) (+ skip); colsum[c] += sum out
-template <int ACT>
+// out = rstd * g1 * (dz - mean(dz) - xhat * mean(dz * xhat)) (+ s_scale * skip)
+// (+ the prior out when YACC); colsum[c] += sum out
+template <int ACT, bool YACC>
 __global__ void __launch_bounds__(NT, 2) adain_bwd_apply_kernel(Act x, int rows, const float* mean, const float* rstd,
                                                              const float* gb, float slope, const float* alpha, Act dy,
                                                              const double* acc, Out4 o, double* colsum) {
@@ -377,11 +379,20 @@ __global__ void __launch_bounds__(NT, 2) adain_bwd_apply_kernel(Act x, int rows,
                 }
                 put(o, b, l, c0, make_float4(r[0], r[1], r[2], r[3]), nv);
             };
+            // the terms added to the gradient: s_scale * skip and, accumulating, the prior output
             auto skip_at = [&](int l) {
-                return o.skip ? ld4(o.skip + (int64_t)b * o.s_bs + (int64_t)l * o.s_ld + c0)
-                              : make_float4(0.f, 0.f, 0.f, 0.f);
+                float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (o.skip) {
+                    const float4 v = ld4(o.skip + (int64_t)b * o.s_bs + (int64_t)l * o.s_ld + c0);
+                    s = make_float4(o.s_scale * v.x, o.s_scale * v.y, o.s_scale * v.z, o.s_scale * v.w);
+                }
+                if (YACC) {
+                    const float4 v = ld4(o.y + (int64_t)b * o.y_bs + (int64_t)l * o.y_ld + c0);
+                    s = make_float4(s.x + v.x, s.y + v.y, s.z + v.z, s.w + v.w);
+                }
+                return s;
             };
-            constexpr int U2 = APPLY_ROWS;   // up to three loads per row
+            constexpr int U2 = YACC ? 3 : APPLY_ROWS;   // up to four loads per row (fewer rows in flight with four)
             const int dl = blockDim.y;
             int l = l0 + threadIdx.y;
             for (; l + (U2 - 1) * dl < l1; l += U2 * dl) {
@@ -578,13 +589,16 @@ void adain_recompute_reduce(const Act& x, const float* mean, const float* rstd, 
 
 void adain_act_bwd_v(const Act& x, const float* mean, const float* rstd, const float* gb, int act, float slope,
                      const float* alpha, const Act& dy, const Act* dx, const Act* skip, const PlaneOut* planes,
-                     double* colsum, float* dgb, float* dalpha, double* acc, cudaStream_t st, bool acc_ready) {
+                     double* colsum, float* dgb, float* dalpha, double* acc, cudaStream_t st, bool acc_ready,
+                     float skip_scale, bool dx_accum) {
     const int64_t n = (int64_t)x.B * x.C;
+    if (dx_accum && !dx) fail("adain_act_bwd", "accumulating into a missing dx");
     if (!acc_ready) BSML_CUDA(cudaMemsetAsync(acc, 0, sizeof(double) * 3 * n, st));
     if (x.numel() > 0) {
         need_vec(x, "adain_act_bwd");
         need_vec(dy, "adain_act_bwd");
-        const Out4 o = make_out(dx, planes, skip, x, "adain_act_bwd");
+        Out4 o = make_out(dx, planes, skip, x, "adain_act_bwd");
+        o.s_scale = skip_scale;
         const Geo g = geo(x);
         if (!acc_ready) {
             ::bsml::count_launch();
@@ -600,12 +614,16 @@ void adain_act_bwd_v(const Act& x, const float* mean, const float* rstd, const f
             BSML_LAUNCH("adain_bwd_reduce");
         }
         ::bsml::count_launch();
-        if (act == ACT_SNAKE)
-            adain_bwd_apply_kernel<ACT_SNAKE><<<g.grid, g.block, 0, st>>>(x, g.rows, mean, rstd, gb, slope, alpha, dy, acc, o, colsum);
+        if (act == ACT_SNAKE && dx_accum)
+            adain_bwd_apply_kernel<ACT_SNAKE, true><<<g.grid, g.block, 0, st>>>(x, g.rows, mean, rstd, gb, slope, alpha, dy, acc, o, colsum);
+        else if (act == ACT_SNAKE)
+            adain_bwd_apply_kernel<ACT_SNAKE, false><<<g.grid, g.block, 0, st>>>(x, g.rows, mean, rstd, gb, slope, alpha, dy, acc, o, colsum);
+        else if (dx_accum)
+            fail("adain_act_bwd", "accumulating output is implemented for Snake only");
         else if (act == ACT_LEAKY)
-            adain_bwd_apply_kernel<ACT_LEAKY><<<g.grid, g.block, 0, st>>>(x, g.rows, mean, rstd, gb, slope, alpha, dy, acc, o, colsum);
+            adain_bwd_apply_kernel<ACT_LEAKY, false><<<g.grid, g.block, 0, st>>>(x, g.rows, mean, rstd, gb, slope, alpha, dy, acc, o, colsum);
         else
-            adain_bwd_apply_kernel<ACT_NONE><<<g.grid, g.block, 0, st>>>(x, g.rows, mean, rstd, gb, slope, alpha, dy, acc, o, colsum);
+            adain_bwd_apply_kernel<ACT_NONE, false><<<g.grid, g.block, 0, st>>>(x, g.rows, mean, rstd, gb, slope, alpha, dy, acc, o, colsum);
         BSML_LAUNCH("adain_bwd_apply");
     }
     ::bsml::count_launch();

@@ -4,7 +4,10 @@ Tolerances (rel-L2 per tensor, gradient tensors floored at 1e-3 of the global
 gradient norm because biases feeding an instance norm have a zero true gradient):
   fp32 CUDA-core path  ......... 1e-5 (atoms), 1e-4 (whole decoder)
   tf32x3 tensor-core path ...... 1e-4 (the bar the north star sets)
-  bf16 tensor-core path ........ 2e-2
+  bf16x3 tensor-core path ...... 2e-2 (BASELINE's BF16 bar)
+  bf16 (one product) ........... audio 2e-2, gradients 1.5e-1: an opt-in fast mode
+                                 that is not one of BASELINE's modes (its gradients
+                                 miss the 2e-2 BF16 bar)
 """
 
 import ctypes
@@ -29,7 +32,8 @@ from tests.helpers import per_tensor_rel, random_params, rel_l2
 TOL = {"fp32": 1e-4, "tf32x3": 1e-4, "bf16": 2e-2}
 # BF16 operands (8-bit mantissa) through this random-init decoder: the audio stays
 # within ~1e-2 but gradients drift by ~7e-2 (instance norms over short rows amplify
-# operand rounding), so BF16 is a fast mode with a looser, stated bar.
+# operand rounding), so one-product BF16 is an opt-in fast mode with a looser, stated
+# bar; BASELINE's BF16 mode is BF16x3, held to 2e-2.
 BF16_GRAD_BAR = 1.5e-1
 
 
