@@ -505,7 +505,7 @@ void Engine::build_pack_jobs() {
             if (tc_ok(c->cin, c->cout, c->s))
                 add(fw, make_pack_job(c->w, PACK_CONV_FWD, c->cout, c->cin, c->k, 1, 0, tcw_fwd_hi_[c->id],
                                       tcw_fwd_lo_[c->id]));
-            else if (strided_tc(*c))
+            else if (strided_tc_fwd(*c))
                 add(fw, make_pack_job(c->w, PACK_CONV_STRIDED, c->cout, c->cin, c->k, c->s, pitch(c->cin),
                                       tcw_fwd_hi_[c->id], tcw_fwd_lo_[c->id]));
             if (c->s == 1 && tc_ok(c->cout, c->cin, 1))
@@ -540,7 +540,7 @@ void Engine::pack_weights(cudaStream_t st) {
     if (pack_jobs_math_ != math_) build_pack_jobs();
     pack_w_tc_batch(params_, pack_jobs_, n_pack_fw_, tot_pack_fw_, tc_mode(), st);
     for (auto* c : lay_.convs)
-        if (!tc_ok(c->cin, c->cout, c->s) && !strided_tc(*c))
+        if (!tc_ok(c->cin, c->cout, c->s) && !strided_tc_fwd(*c))
             pack_conv_fwd(params_ + c->w, c->cout, c->cin, c->k, wp_fwd_[c->id], st);
     for (auto& u : lay_.ups)
         if (!tc_ok(u.cin, u.cout, 1))
@@ -626,7 +626,7 @@ void Engine::conv(const ConvP& c, const Act& x, const Act& y, const Act* r, int 
     a.alpha = alpha; a.accum = accum;
     if (a.No != y.L) fail("conv", "output length mismatch");
     if (stats) BSML_CUDA(cudaMemsetAsync(stats, 0, sizeof(double) * 2 * (size_t)y.B * c.cout, st));
-    if (strided_tc(c)) {
+    if (strided_tc_fwd(c)) {
         // x is har_, a view inside har_full_: the packed rows start at the buffer's first (zero) row
         const Act X2 = packed_view(c);
         const TcPlanes tp = tc_planes(X2, st);

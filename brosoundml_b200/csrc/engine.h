@@ -239,23 +239,24 @@ class Engine {
     // zero rows after the last, so s consecutive rows read as one row of s*ld channels
     // form a stride-1 conv with ceil(k/s) taps over K = s*ld (weights packed to match,
     // PACK_CONV_STRIDED); its weight gradient is unpacked from that form.
-    // BF16 modes only: the TF32x3 result is accurate per element (5.8e-7 rel-L2 against
-    // the CUDA-core conv at the bench shape) but shrinks the output's magnitude by about
-    // 4e-7 (its sum of squares is 8.8e-7 below the CUDA-core one; consistent with the
-    // in-TMEM accumulation rounding toward zero), and the decoder's gradients
-    // are ill-conditioned in that scale: scaling this conv's output by 1 - 3.5e-6 moves
-    // the float64 reference's whole gradient by 1.5e-3 (this conv's output enters the
-    // stage through the noise resblock's residual path, unnormalised). Under TF32x3 it
-    // took the config-2 gradient error from 1.7e-5 to 3.2e-4, past the 1e-4 bar, so the
-    // fp32-grade mode keeps this conv on the CUDA cores.
+    // The forward runs in this form in the BF16 modes only. Under TF32x3 its result is
+    // accurate per element (5.8e-7 rel-L2 against the CUDA-core conv at the bench shape)
+    // but its magnitude is about 4e-7 smaller (sum of squares 8.8e-7 below the CUDA-core
+    // one; consistent with the in-TMEM accumulation rounding toward zero), and the
+    // decoder's gradients are ill-conditioned in that scale: scaling this conv's output
+    // by 1 - 3.5e-6 moves the float64 reference's whole gradient by 1.5e-3 (the output
+    // enters the stage through the noise resblock's residual path, unnormalised). It
+    // took the config-2 gradient error from 1.7e-5 to 3.2e-4, past the 1e-4 bar, so
+    // under TF32x3 the forward stays on the CUDA cores. The weight gradient runs in this
+    // form in every tensor-core mode: a bias of that size in dW reaches nothing else.
     int spk_ = -1;                    // index into lay_.noise of that conv, or -1
     int spk_rows_ = 0;                // har rows per clip in the packed buffer (a multiple of s)
     Act har_full_;                    // har with its zero rows (har_ views the frames inside it)
     float* spk_dw_ = nullptr;         // weight gradient in packed form [Co][s*ld][taps]
-    bool strided_tc(const ConvP& c) const {
-        return spk_ >= 0 && &c == &lay_.noise[spk_] && tc_mode() != TC_TF32X3 &&
-               tc_ok(c.s * pitch(c.cin), c.cout, 1);
+    bool strided_tc(const ConvP& c) const {   // the weight gradient
+        return spk_ >= 0 && &c == &lay_.noise[spk_] && tc_ok(c.s * pitch(c.cin), c.cout, 1);
     }
+    bool strided_tc_fwd(const ConvP& c) const { return strided_tc(c) && tc_mode() != TC_TF32X3; }
     Act packed_view(const ConvP& c) const {
         Act a = har_full_;
         a.ld = c.s * har_full_.ld;
