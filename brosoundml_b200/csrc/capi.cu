@@ -92,6 +92,8 @@ int atom_tc_mode() {
     const int m = g_atom_math.load();
     return m == BSML_MATH_BF16 ? bsml::TC_BF16 : m == BSML_MATH_BF16X3 ? bsml::TC_BF16X3 : bsml::TC_TF32X3;
 }
+// weight gradients: BF16X3 under TF32X3W, else the mode above
+int atom_wg_mode() { return g_atom_math.load() == BSML_MATH_TF32X3W ? bsml::TC_BF16X3 : atom_tc_mode(); }
 
 // Tensor-core forward-like conv for the atoms: planes of x, packed weight planes, launch.
 void atom_tc_conv(Scratch& sc, const bsml::Act& xa, const float* W, int kind, int Co_w, int Ci_w, int k, int s_ph,
@@ -342,7 +344,7 @@ int64_t bsml_launch_count(void) { return bsml::launch_count(); }
 int bsml_set_atom_math(int math_mode) {
     return guarded([&] {
         need(math_mode == BSML_MATH_FP32_SIMT || math_mode == BSML_MATH_TF32X3 || math_mode == BSML_MATH_BF16 ||
-                 math_mode == BSML_MATH_BF16X3,
+                 math_mode == BSML_MATH_BF16X3 || math_mode == BSML_MATH_TF32X3W,
              "bsml_set_atom_math", "unknown math mode");
         g_atom_math.store(math_mode);
     });
@@ -869,7 +871,7 @@ int bsml_conv1d_backward_weight(const float* dy, const float* x, int B, int Ci, 
         bsml::ncl_to_cl(dy, ga, st);
         bsml::ncl_to_cl(x, xa, st);
         if (atom_tc(Ci, Co, stride)) {
-            const int mode = atom_tc_mode();
+            const int mode = atom_wg_mode();
             float* yh = sc.f((int64_t)B * Lo * bsml::tc_pitch(Co, mode));
             float* yl = sc.f((int64_t)B * Lo * bsml::tc_pitch(Co, mode));
             float* xh = sc.f((int64_t)B * L * bsml::tc_pitch(Ci, mode));
@@ -977,7 +979,7 @@ int bsml_conv_transpose1d_backward_weight(const float* dy, const float* x, int B
         bsml::ncl_to_cl(dy, ga, st);
         bsml::ncl_to_cl(x, xa, st);
         if (atom_convT_tc(Ci, Co, stride, Lu)) {
-            const int mode = atom_tc_mode();
+            const int mode = atom_wg_mode();
             const bsml::ConvTPack pk = bsml::convT_pack(k, stride, pad);
             const int K = stride * Co;
             float* gh = sc.f((int64_t)B * Lu * Co);

@@ -719,42 +719,47 @@ __global__ void act_planes_kernel(Act x, void* hi, void* lo, int ld) {
     }
 }
 
-// Element i of one packed weight: [tap][M][Kp] with zero padding of K to Kp.
-template <int MODE>
-__device__ __forceinline__ void pack_one(const float* W, int kind, int Co, int Ci, int k, int s, int r, int taps,
-                                         int M, int K, int Kp, void* hi, void* lo, int64_t i) {
-    const int kk = (int)(i % Kp);
-    const int64_t q = i / Kp;
-    const int m = (int)(q % M), t = (int)(q / M);
-    float v = 0.f;
-    if (kk < K) {
-        if (kind == PACK_CONV_FWD) {            // m = co, kk = ci
-            v = W[((int64_t)m * Ci + kk) * k + t];
-        } else if (kind == PACK_CONV_DGRAD) {   // m = ci, kk = co
-            v = W[((int64_t)kk * Ci + m) * k + (k - 1 - t)];
-        } else if (kind == PACK_CONVT_PHASE) {  // convT phase: m = co, kk = ci
-            const int tt = r + (taps - 1 - t) * s;
-            v = W[((int64_t)kk * Co + m) * k + tt];
-        } else if (kind == PACK_CONV_STRIDED) { // row-packed strided conv: m = co, kk = j*ld + ci (ld = r)
-            const int j = kk / r, ci = kk - j * r;
-            const int tt = t * s + j;
-            if (ci < Ci && tt < k) v = W[((int64_t)m * Ci + ci) * k + tt];
-        } else {                                // convT dgrad, row-packed: m = ci, kk = j*Co + co
-            const int u_min = -((r + s - 1) / s);
-            const int j = kk / Co, co = kk - j * Co;
-            const int tt = (t + u_min) * s + j + r;
-            if (tt >= 0 && tt < k) v = W[((int64_t)m * Co + co) * k + tt];
-        }
+// Element (t, m, kk) of one packed weight [tap][M][Kp] (zero padding of K to Kp).
+__device__ __forceinline__ float pack_value(const float* W, int kind, int Co, int Ci, int k, int s, int r, int taps,
+                                            int K, int t, int m, int kk) {
+    if (kk >= K) return 0.f;
+    if (kind == PACK_CONV_FWD) return W[((int64_t)m * Ci + kk) * k + t];                 // m = co, kk = ci
+    if (kind == PACK_CONV_DGRAD) return W[((int64_t)kk * Ci + m) * k + (k - 1 - t)];     // m = ci, kk = co
+    if (kind == PACK_CONVT_PHASE) {                                                       // m = co, kk = ci
+        const int tt = r + (taps - 1 - t) * s;
+        return W[((int64_t)kk * Co + m) * k + tt];
     }
-    put_planes<MODE>(hi, lo, i, v);
+    if (kind == PACK_CONV_STRIDED) {   // row-packed strided conv: m = co, kk = j*ld + ci (ld = r)
+        const int j = kk / r, ci = kk - j * r;
+        const int tt = t * s + j;
+        return (ci < Ci && tt < k) ? W[((int64_t)m * Ci + ci) * k + tt] : 0.f;
+    }
+    // convT dgrad, row-packed: m = ci, kk = j*Co + co
+    const int u_min = -((r + s - 1) / s);
+    const int j = kk / Co, co = kk - j * Co;
+    const int tt = (t + u_min) * s + j + r;
+    return (tt >= 0 && tt < k) ? W[((int64_t)m * Co + co) * k + tt] : 0.f;
+}
+
+// Item i = m*Kp + kk of one packed weight: every tap of (m, kk). A thread's taps come
+// from one source row of the weight (k consecutive floats for a conv), so a warp's
+// loads cover a contiguous span instead of striding by k per lane; each tap's stores
+// are consecutive kk across the warp.
+template <int MODE>
+__device__ __forceinline__ void pack_item(const float* W, int kind, int Co, int Ci, int k, int s, int r, int taps,
+                                          int M, int K, int Kp, void* hi, void* lo, int64_t i) {
+    const int kk = (int)(i % Kp);
+    const int m = (int)(i / Kp);
+    for (int t = 0; t < taps; ++t)
+        put_planes<MODE>(hi, lo, ((int64_t)t * M + m) * Kp + kk, pack_value(W, kind, Co, Ci, k, s, r, taps, K, t, m, kk));
 }
 
 template <int MODE>
 __global__ void pack_w_kernel(const float* W, int kind, int Co, int Ci, int k, int s, int r, int taps, int M, int K,
                               int Kp, void* hi, void* lo) {
-    const int64_t n = (int64_t)taps * M * Kp;
+    const int64_t n = (int64_t)M * Kp;
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
-        pack_one<MODE>(W, kind, Co, Ci, k, s, r, taps, M, K, Kp, hi, lo, i);
+        pack_item<MODE>(W, kind, Co, Ci, k, s, r, taps, M, K, Kp, hi, lo, i);
 }
 
 // All jobs of a batch over one flat index space; each thread finds its job by
@@ -772,8 +777,8 @@ __global__ void pack_w_batch_kernel(const float* params, const PackJob* jobs, in
             else hi = mid - 1;
         }
         const PackJob& J = jobs[lo];
-        pack_one<MODE>(params + J.w_off, J.kind, J.Co, J.Ci, J.k, J.s, J.r, J.taps, J.M, J.K, J.Kp, J.hi, J.lo,
-                       i - start[lo]);
+        pack_item<MODE>(params + J.w_off, J.kind, J.Co, J.Ci, J.k, J.s, J.r, J.taps, J.M, J.K, J.Kp, J.hi, J.lo,
+                        i - start[lo]);
     }
 }
 
@@ -1095,6 +1100,7 @@ PackJob make_pack_job(int64_t w_off, int kind, int Co, int Ci, int k, int s, int
     }
     J.Kp = (int)round_up(J.K, 8);
     J.n = (int64_t)J.taps * J.M * J.Kp;
+    J.items = (int64_t)J.M * J.Kp;
     return J;
 }
 
@@ -1121,7 +1127,7 @@ void pack_w_tc(const float* W, int kind, int Co, int Ci, int k, int s, int r, in
         M = Ci; K = s * Co; taps = convT_pack(k, s, r).taps;
     }
     const int Kp = (int)round_up(K, 8);
-    const int64_t n = (int64_t)taps * M * Kp;
+    const int64_t n = (int64_t)M * Kp;
     ::bsml::count_launch();
     if (mode == TC_TF32X3)
         pack_w_kernel<TC_TF32X3><<<grid_for(n), 256, 0, st>>>(W, kind, Co, Ci, k, s, r, taps, M, K, Kp, hi, lo);

@@ -44,13 +44,15 @@ enum { PACK_CONV_FWD = 0, PACK_CONV_DGRAD = 1, PACK_CONVT_PHASE = 2, PACK_CONVT_
 // One weight packing of a batch: the weight at params + w_off, packed as pack_w_tc
 // would, into elements [start, start + n) of the batch's flat index space.
 struct PackJob {
-    int64_t w_off = 0, n = 0, start = 0;
+    // n: packed elements (taps x M x Kp); items: threads' work items (M x Kp, every
+    // tap of one (m, kk) per item); start: prefix sum of items over the batch
+    int64_t w_off = 0, n = 0, items = 0, start = 0;
     void* hi = nullptr;
     void* lo = nullptr;
     int kind = 0, Co = 0, Ci = 0, k = 0, s = 1, r = 0, taps = 0, M = 0, K = 0, Kp = 0;
 };
 PackJob make_pack_job(int64_t w_off, int kind, int Co, int Ci, int k, int s, int r, void* hi, void* lo);
-// Every job of `jobs` (device array, starts as prefix sums, `total` elements) in one launch.
+// Every job of `jobs` (device array, starts as prefix sums of items, `total` items) in one launch.
 constexpr int PACK_MAX_JOBS = 256;
 void pack_w_tc_batch(const float* params, const PackJob* jobs, int n_jobs, int64_t total, int mode, cudaStream_t st);
 

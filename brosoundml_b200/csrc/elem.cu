@@ -1,6 +1,8 @@
 // Normalisation, activation, layout and small-op kernels (channels-last fp32).
 #include <cmath>
 
+#include <algorithm>
+
 #include "kernels.h"
 
 namespace bsml {
@@ -308,22 +310,44 @@ __global__ void fc_bwd_w_kernel(const FcRow* tab, int total_rows, const int* row
     }
 }
 
-// d_style[b, i] partials over row chunks: part[chunk][b][i]
+// d_style[b, i] partials over row chunks: part[chunk][b][i]. FC_RY rows of a chunk are
+// walked at once (threadIdx.y), each row's weights loaded once per FC_CLIPS clips and
+// applied to them from registers; the row lanes are summed in shared memory at the end.
 constexpr int FC_CHUNK = 256;
+constexpr int FC_CLIPS = 8;
+constexpr int FC_RY = 8;
 __global__ void fc_bwd_style_kernel(const FcRow* tab, int total_rows, const int* row_entry, const float* P,
                                     const float* daff, int B, int S, float* part) {
+    __shared__ float red[FC_RY][FC_CLIPS][128];
     const int chunk = blockIdx.x;
-    const int i = threadIdx.x;   // S <= blockDim.x
+    const int x = threadIdx.x, y = threadIdx.y;   // blockDim.x <= 128
     const int r0 = chunk * FC_CHUNK, r1 = min(total_rows, r0 + FC_CHUNK);
-    for (int b = 0; b < B; ++b) {
-        float s = 0.f;
+    for (int i0 = 0; i0 < S; i0 += blockDim.x)
+    for (int b0 = 0; b0 < B; b0 += FC_CLIPS) {
+        const int i = i0 + x;
+        const int nb = min(FC_CLIPS, B - b0);
+        float s[FC_CLIPS] = {};
         if (i < S)
-            for (int r = r0; r < r1; ++r) {
+            for (int r = r0 + y; r < r1; r += FC_RY) {
                 const FcRow f = tab[row_entry[r]];
                 const int o = r - f.row0;
-                s += P[f.w_off + (int64_t)o * S + i] * daff[f.out_off + (int64_t)b * f.n_out + o];
+                const float p = P[f.w_off + (int64_t)o * S + i];
+                const float* d = daff + f.out_off + (int64_t)b0 * f.n_out + o;
+#pragma unroll
+                for (int u = 0; u < FC_CLIPS; ++u)
+                    if (u < nb) s[u] = fmaf(p, d[(int64_t)u * f.n_out], s[u]);
             }
-        if (i < S) part[((int64_t)chunk * B + b) * S + i] = s;
+#pragma unroll
+        for (int u = 0; u < FC_CLIPS; ++u) red[y][u][x] = s[u];
+        __syncthreads();
+        if (y == 0 && i < S)
+            for (int u = 0; u < nb; ++u) {
+                float t = 0.f;
+#pragma unroll
+                for (int q = 0; q < FC_RY; ++q) t += red[q][u][x];
+                part[((int64_t)chunk * B + b0 + u) * S + i] = t;
+            }
+        __syncthreads();
     }
 }
 __global__ void fc_style_reduce_kernel(const float* part, int chunks, int n, float* d_style) {
@@ -459,8 +483,8 @@ void affine_fc_bwd(const FcRow* table, int n_entries, int total_rows, const int*
     if (d_style) {
         const int chunks = (int)ceil_div(total_rows, FC_CHUNK);
         ::bsml::count_launch();
-        fc_bwd_style_kernel<<<chunks, (int)round_up(S, 32), 0, st>>>(table, total_rows, row_entry, params, daff, B, S,
-                                                                   part);
+        fc_bwd_style_kernel<<<chunks, dim3((unsigned)std::min(round_up(S, 32), (int64_t)128), FC_RY), 0, st>>>(
+            table, total_rows, row_entry, params, daff, B, S, part);
         ::bsml::count_launch();
         fc_style_reduce_kernel<<<(unsigned)ceil_div(B * S, 128), 128, 0, st>>>(part, chunks, B * S, d_style);
     }

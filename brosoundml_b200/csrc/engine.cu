@@ -185,7 +185,8 @@ Engine::~Engine() {
 }
 
 void Engine::set_math(int m) {
-    if (m != BSML_MATH_FP32_SIMT && m != BSML_MATH_TF32X3 && m != BSML_MATH_BF16 && m != BSML_MATH_BF16X3)
+    if (m != BSML_MATH_FP32_SIMT && m != BSML_MATH_TF32X3 && m != BSML_MATH_BF16 && m != BSML_MATH_BF16X3 &&
+        m != BSML_MATH_TF32X3W)
         fail("bsml_decoder_set_math", "unknown math mode " + std::to_string(m));
     math_ = m;
 }
@@ -425,6 +426,15 @@ void Engine::plan_scratch(Planner& P, int64_t max_elems, int max_c) {
     tc_dl_ = P.f(max_elems);
     tc_eh_ = P.f(max_elems);
     tc_el_ = P.f(max_elems);
+    // the weight gradients' copies (bf16 hi + lo, 4 bytes per element: fits max_elems
+    // floats per plane even with the bf16 pitch's rounding to 8 channels)
+    const int64_t wn = plan_wg_ ? max_elems : 64;
+    tc_dwh_ = P.f(wn);
+    tc_dwl_ = P.f(wn);
+    tc_uwh_ = P.f(wn);
+    tc_uwl_ = P.f(wn);
+    tc_ewh_ = P.f(wn);
+    tc_ewl_ = P.f(wn);
 }
 
 // One block (block_kind != 0): T_ is the block's input length L
@@ -456,9 +466,10 @@ void Engine::plan_block(Planner& P) {
 }
 
 void Engine::ensure_plan(int B, int T, int frames, bool have_har, int part) {
-    if (planned_ && B == B_ && T == T_ && part == plan_part_ && have_har == have_har_ && (!have_har || frames == frames_))
+    if (planned_ && B == B_ && T == T_ && part == plan_part_ && have_har == have_har_ &&
+        (!have_har || frames == frames_) && plan_wg_ == wg_split())
         return;
-    B_ = B; T_ = T; frames_ = frames; have_har_ = have_har; plan_part_ = part;
+    B_ = B; T_ = T; frames_ = frames; have_har_ = have_har; plan_part_ = part; plan_wg_ = wg_split();
     Planner p0;
     if (lay_.block_kind) plan_block(p0);
     else plan(p0);
@@ -497,7 +508,7 @@ void Engine::build_pack_jobs() {
     std::vector<PackJob> fw, dg;
     auto add = [](std::vector<PackJob>& v, const PackJob& J) {
         PackJob j = J;
-        j.start = v.empty() ? 0 : v.back().start + v.back().n;
+        j.start = v.empty() ? 0 : v.back().start + v.back().items;
         v.push_back(j);
     };
     if (math_ != BSML_MATH_FP32_SIMT) {
@@ -531,8 +542,8 @@ void Engine::build_pack_jobs() {
                              cudaMemcpyHostToDevice));
     n_pack_fw_ = (int)fw.size();
     n_pack_dg_ = (int)dg.size();
-    tot_pack_fw_ = fw.empty() ? 0 : fw.back().start + fw.back().n;
-    tot_pack_dg_ = dg.empty() ? 0 : dg.back().start + dg.back().n;
+    tot_pack_fw_ = fw.empty() ? 0 : fw.back().start + fw.back().items;
+    tot_pack_dg_ = dg.empty() ? 0 : dg.back().start + dg.back().items;
     pack_jobs_math_ = math_;
 }
 
@@ -556,20 +567,21 @@ void Engine::pack_dgrad_weights(cudaStream_t st) {
     for (auto& u : lay_.ups) pack_convT_dgrad(params_ + u.w, u.cin, u.cout, u.k, wp_up_dgrad_[u.id], st);
 }
 
-TcPlanes Engine::tc_planes(const Act& x, cudaStream_t st) {
+TcPlanes Engine::tc_planes(const Act& x, cudaStream_t st, int mode) {
     if (!x.p) fail("conv", "internal: operand has neither fp32 data nor planes");
-    make_act_planes(x, tc_mode(), tc_xh_, tc_xl_, st);
+    if (mode < 0) mode = tc_mode();
+    make_act_planes(x, mode, tc_xh_, tc_xl_, st);
     TcPlanes t;
-    t.hi = tc_xh_; t.lo = tc_xl_; t.ld = tc_pitch(x.C, tc_mode());
+    t.hi = tc_xh_; t.lo = tc_xl_; t.ld = tc_pitch(x.C, mode);
     return t;
 }
 
-Engine::Opnd Engine::operand(bool tc, int L, int C, const Act& fbuf, void* hi, void* lo) const {
+Engine::Opnd Engine::operand(bool tc, int L, int C, const Act& fbuf, void* hi, void* lo, int mode) const {
     Opnd o;
     o.f = view(fbuf, L, C);
     if (tc) {
         o.f.p = nullptr;
-        o.tp.hi = hi; o.tp.lo = lo; o.tp.ld = tc_pitch(C, tc_mode());
+        o.tp.hi = hi; o.tp.lo = lo; o.tp.ld = tc_pitch(C, mode < 0 ? tc_mode() : mode);
     }
     return o;
 }
@@ -585,16 +597,19 @@ void Engine::adain_fwd_to(const Act& x, const double* sums, const Stats& s, cons
 void Engine::adain_bwd_to(const Act& x, const Stats& s, const float* gb, int act, float slope, const float* alpha,
                           const Act& dy, const Opnd& out, const Act* skip, double* colsum, float* dgb, float* dalpha,
                           cudaStream_t st, bool acc_ready, float skip_scale, bool out_accum) {
-    PlaneOut po;
+    PlaneOut po, po2;
     po.hi = const_cast<void*>(out.tp.hi); po.lo = const_cast<void*>(out.tp.lo); po.ld = out.tp.ld; po.mode = tc_mode();
+    po2.hi = const_cast<void*>(out.tpw.hi); po2.lo = const_cast<void*>(out.tpw.lo); po2.ld = out.tpw.ld;
+    po2.mode = wg_mode();
     adain_act_bwd_v(x, s.mean, s.rstd, gb, act, slope, alpha, dy, out.f.p ? &out.f : nullptr, skip,
-                    out.tp.hi ? &po : nullptr, colsum, dgb, dalpha, dacc_, st, acc_ready, skip_scale, out_accum);
+                    out.tp.hi ? &po : nullptr, colsum, dgb, dalpha, dacc_, st, acc_ready, skip_scale, out_accum,
+                    out.tpw.hi ? &po2 : nullptr);
 }
 
 void Engine::recompute_reduce_to(const Act& x, const Stats& s, const float* gb, int act, float slope,
                                  const float* alpha, const Act& dy, const Opnd& out, cudaStream_t st) {
     PlaneOut po;
-    po.hi = const_cast<void*>(out.tp.hi); po.lo = const_cast<void*>(out.tp.lo); po.ld = out.tp.ld; po.mode = tc_mode();
+    po.hi = const_cast<void*>(out.tp.hi); po.lo = const_cast<void*>(out.tp.lo); po.ld = out.tp.ld; po.mode = wg_mode();
     adain_recompute_reduce(x, s.mean, s.rstd, gb, act, slope, alpha, out.f.p ? &out.f : nullptr,
                            out.tp.hi ? &po : nullptr, dy, dacc_, st);
 }
@@ -680,8 +695,9 @@ void Engine::conv_wgrad(const ConvP& c, const Act& dy, const Act& x, cudaStream_
                         const TcPlanes* xp, const double* bias_sum) {
     const Range nvtx_range("bsml.conv.wgrad");
     if (!grads_) return;
+    // dyp / xp: planes in wg_mode(); otherwise they are made here from the fp32 data
     if (strided_tc(c)) {
-        const int mode = tc_mode();
+        const int mode = wg_mode();
         const Act X2 = packed_view(c);
         TcConvWgrad w;
         if (dyp) {
@@ -690,7 +706,7 @@ void Engine::conv_wgrad(const ConvP& c, const Act& dy, const Act& x, cudaStream_
             make_act_planes(dy, mode, tc_yh_, tc_yl_, st);
             w.dy.hi = tc_yh_; w.dy.lo = tc_yl_; w.dy.ld = tc_pitch(dy.C, mode);
         }
-        w.x = tc_planes(X2, st);
+        w.x = tc_planes(X2, st, mode);
         w.B = dy.B; w.Lo = dy.L; w.Co = dy.C; w.L_in = X2.L; w.Ci = X2.C;
         w.taps = (int)ceil_div(c.k, c.s); w.p = 0; w.d = 1; w.dW = spk_dw_;
         const int id = prof_begin(PROF_WGRAD_TC, 2.0 * c.cin * c.cout * c.k * (double)dy.L * dy.B, st);
@@ -704,7 +720,7 @@ void Engine::conv_wgrad(const ConvP& c, const Act& dy, const Act& x, cudaStream_
         return;
     }
     if (tc_ok(c.cin, c.cout, c.s)) {
-        const int mode = tc_mode();
+        const int mode = wg_mode();
         TcConvWgrad w;
         if (dyp) {
             w.dy = *dyp;
@@ -713,7 +729,7 @@ void Engine::conv_wgrad(const ConvP& c, const Act& dy, const Act& x, cudaStream_
             make_act_planes(dy, mode, tc_yh_, tc_yl_, st);
             w.dy.hi = tc_yh_; w.dy.lo = tc_yl_; w.dy.ld = tc_pitch(dy.C, mode);
         }
-        w.x = xp ? *xp : tc_planes(x, st);
+        w.x = xp ? *xp : tc_planes(x, st, mode);
         w.B = dy.B; w.Lo = dy.L; w.Co = dy.C; w.L_in = x.L; w.Ci = x.C;
         w.taps = c.k; w.p = c.p; w.d = c.d; w.dW = grads_ + c.w;
         const int id = prof_begin(PROF_WGRAD_TC, 2.0 * c.cin * c.cout * c.k * (double)dy.L * dy.B, st);
@@ -803,11 +819,20 @@ void Engine::convT_wgrad(const UpP& u, const Act& dy, const Act& x, cudaStream_t
     const Range nvtx_range("bsml.convT.wgrad");
     if (!grads_) return;
     if (dyp) {
+        // dyp: the input gradient's row-packed planes (tc_mode); under wg_split the
+        // weight gradient's are made again from dy in wg_mode (same buffers: the input
+        // gradient has already read them)
         const ConvTPack pk = convT_pack(u.k, u.s, u.p);
-        const int mode = tc_mode();
+        const int mode = wg_mode();
         TcConvWgrad w;
-        w.dy = tc_planes(x, st);   // the convT input plays dY's role (M = Ci of the convT)
-        w.x = *dyp;
+        w.dy = tc_planes(x, st, mode);   // the convT input plays dY's role (M = Ci of the convT)
+        if (wg_split()) {
+            make_act_planes(dy, mode, tc_yh_, tc_yl_, st);
+            w.x.hi = tc_yh_; w.x.lo = tc_yl_;
+            if (tc_pitch(dy.C, mode) != dy.C) fail("convT_wgrad", "internal: row-packed planes need compact rows");
+        } else {
+            w.x = *dyp;
+        }
         w.x.ld = u.s * u.cout;
         w.B = x.B; w.Lo = x.L; w.Co = u.cin; w.L_in = dy.L / u.s; w.Ci = u.s * u.cout;
         w.taps = pk.taps; w.p = -pk.u_min; w.d = 1;
@@ -903,7 +928,7 @@ void Engine::blk_bwd(const BlkP& w, BlkC& c, const Act& dY, const Act& dX, cudaS
     scale_out_v(dY, 1.f / std::sqrt(2.f), &db, tc2 ? &dbo : nullptr, bs, st);
     Act t1 = view(S_[1], Lout, w.cout);
     conv_dgrad(w.c2, db, t1, false, st, tc2 ? &dbp : nullptr);
-    conv_wgrad(w.c2, db, c.n2, st, tc2 ? &dbp : nullptr, nullptr, bs);
+    conv_wgrad(w.c2, db, c.n2, st, wgp(tc2 ? &dbp : nullptr), nullptr, bs);
     // dc1 (S_[2]) with its planes (tc_yh_) and column sums (conv1's bias gradient)
     const bool tc1 = tc_ok(w.cin, w.cout, 1) && tc_ok(w.cout, w.cin, 1);
     Act dc1 = view(S_[2], Lout, w.cout);
@@ -915,7 +940,7 @@ void Engine::blk_bwd(const BlkP& w, BlkC& c, const Act& dY, const Act& dX, cudaS
                     tc1 ? &dco : nullptr, bs, daff(w.n2), nullptr, dacc_, st);
     Act dpooled = view(S_[1], Lout, w.cin);
     conv_dgrad(w.c1, dc1, dpooled, false, st, tc1 ? &dcp : nullptr);
-    conv_wgrad(w.c1, dc1, w.up ? c.pooled : c.r, st, tc1 ? &dcp : nullptr, nullptr, bs);
+    conv_wgrad(w.c1, dc1, w.up ? c.pooled : c.r, st, wgp(tc1 ? &dcp : nullptr), nullptr, bs);
     Act dr = dpooled;
     if (w.up) {
         dr = view(S_[2], Lin, w.cin);
@@ -939,7 +964,7 @@ void Engine::blk_bwd(const BlkP& w, BlkC& c, const Act& dY, const Act& dX, cudaS
     const bool have_sp = tcs && (w.up || tc2);
     if (w.sc) {
         conv_dgrad(w.c1x1, dbs, dX, true, st, have_sp ? &sp : nullptr);
-        conv_wgrad(w.c1x1, dbs, c.x, st, have_sp ? &sp : nullptr);
+        conv_wgrad(w.c1x1, dbs, c.x, st, wgp(have_sp ? &sp : nullptr));
     } else {
         add_act(dbs, dX, 1.f, st);
     }
@@ -1002,18 +1027,26 @@ void Engine::rb1_bwd(const RB1P& w, RB1C& c, const Act& dOut, float scale, const
     // D = scale * dOut: fp32 (the running gradient), planes, bias sum of c2[2]; or,
     // with the entry made by the caller, planes and bias sum from there and D first
     // written by the first pair's last pass (dOut, scaled, as its skip term)
+    // Under wg_split every gradient operand shared by an input and a weight gradient
+    // is written twice: tc_mode() planes for the input gradient, wg_mode() ones (the
+    // `_w` buffers) for the weight gradient.
+    const bool split = tc && wg_split();
     Opnd Dp;
     Dp.f = D;
     if (tc) { Dp.tp.hi = tc_dh_; Dp.tp.lo = tc_dl_; Dp.tp.ld = tc_pitch(C, tc_mode()); }
+    if (split) { Dp.tpw.hi = tc_dwh_; Dp.tpw.lo = tc_dwl_; Dp.tpw.ld = tc_pitch(C, wg_mode()); }
     const bool pre = io && io->in_planes;
     if (pre && !tc) fail("rb1_bwd", "internal: entry planes without the tensor-core path");
+    if (pre && split && !io->in_planes_w) fail("rb1_bwd", "internal: entry planes for the weight gradient missing");
     const TcPlanes* in_planes = pre ? io->in_planes : Dp.planes();
+    const TcPlanes* in_planes_w = pre ? (split ? io->in_planes_w : io->in_planes) : Dp.planes_w();
     const double* in_bs = pre ? (grads_ ? io->in_bsum : nullptr) : bs;
     if (!pre) {
-        PlaneOut po;
+        PlaneOut po, po2;
         po.hi = tc_dh_; po.lo = tc_dl_; po.ld = Dp.tp.ld; po.mode = tc_mode();
+        po2.hi = tc_dwh_; po2.lo = tc_dwl_; po2.ld = Dp.tpw.ld; po2.mode = wg_mode();
         zero_bs();
-        scale_out_v(dOut, scale, &D, tc ? &po : nullptr, bs, st);
+        scale_out_v(dOut, scale, &D, tc ? &po : nullptr, bs, st, split ? &po2 : nullptr);
     }
     // Algorithmic bytes per element of one AdaIN+Snake backward: x and dy read, dx
     // written (fp32), 12 B, credited 8 B to the reduction pass and 4 B to the apply
@@ -1021,27 +1054,29 @@ void Engine::rb1_bwd(const RB1P& w, RB1C& c, const Act& dOut, float scale, const
     // second read of x and dy are implementation traffic.
     for (int i = 2; i >= 0; --i) {
         const TcPlanes* dpl = i == 2 ? in_planes : Dp.planes();
+        const TcPlanes* dplw = i == 2 ? in_planes_w : Dp.planes_w();
         conv_dgrad(w.c2[i], D, t, false, st, dpl);
         // s2[i] = Snake(AdaIN(c1[i])) again, as the weight-gradient operand, in the
         // same pass as the backward's reduction over (c1[i], t)
         int id = prof_begin(PROF_NORM_BWD, 8.0 * n, st);
-        const Opnd s2 = operand(tc, L, C, S_[0], tc_xh_, tc_xl_);
+        const Opnd s2 = operand(tc, L, C, S_[0], tc_xh_, tc_xl_, wg_mode());
         recompute_reduce_to(c.c1[i], c.st2[i], aff(w.a2[i]), ACT_SNAKE, 0.f, P(w.al2[i]), t, s2, st);
         prof_end(id, st);
-        conv_wgrad(w.c2[i], D, s2.f, st, dpl, s2.planes(), i == 2 ? in_bs : bs);
+        conv_wgrad(w.c2[i], D, s2.f, st, dplw, s2.planes(), i == 2 ? in_bs : bs);
         // u = gradient at conv1's output (operand of c1's dgrad and wgrad)
         id = prof_begin(PROF_NORM_BWD, 4.0 * n, st);
-        const Opnd u = operand(tc, L, C, S_[5], tc_yh_, tc_yl_);
+        Opnd u = operand(tc, L, C, S_[5], tc_yh_, tc_yl_);
+        if (split) { u.tpw.hi = tc_uwh_; u.tpw.lo = tc_uwl_; u.tpw.ld = tc_pitch(C, wg_mode()); }
         zero_bs();
         adain_bwd_to(c.c1[i], c.st2[i], aff(w.a2[i]), ACT_SNAKE, 0.f, P(w.al2[i]), t, u, nullptr, bs, daff(w.a2[i]),
                      G(w.al2[i]), st, true);
         prof_end(id, st);
         conv_dgrad(w.c1[i], u.f, t, false, st, u.planes());
         id = prof_begin(PROF_NORM_BWD, 8.0 * n, st);
-        const Opnd s1 = operand(tc, L, C, S_[0], tc_xh_, tc_xl_);
+        const Opnd s1 = operand(tc, L, C, S_[0], tc_xh_, tc_xl_, wg_mode());
         recompute_reduce_to(c.x[i], c.st1[i], aff(w.a1[i]), ACT_SNAKE, 0.f, P(w.al1[i]), t, s1, st);
         prof_end(id, st);
-        conv_wgrad(w.c1[i], u.f, s1.f, st, u.planes(), s1.planes(), bs);
+        conv_wgrad(w.c1[i], u.f, s1.f, st, u.planes_w(), s1.planes(), bs);
         // D += gradient at this pair's input: fp32, and (except for the last pair)
         // planes and the bias sum of c2[i-1]
         Opnd Dn = Dp;
@@ -1051,6 +1086,7 @@ void Engine::rb1_bwd(const RB1P& w, RB1C& c, const Act& dOut, float scale, const
             zero_bs();
         } else {
             Dn.tp = TcPlanes{};
+            Dn.tpw = TcPlanes{};
         }
         const Act* skip = &D;
         float skip_scale = 1.f;
@@ -1062,6 +1098,7 @@ void Engine::rb1_bwd(const RB1P& w, RB1C& c, const Act& dOut, float scale, const
         if (i == 0 && io && io->out) {
             Dn.f = *io->out;
             Dn.tp = io->out_planes;
+            Dn.tpw = split ? io->out_planes_w : TcPlanes{};
             out_accum = io->out_accum;
             bsn = grads_ ? io->out_bsum : nullptr;
             if (bsn) BSML_CUDA(cudaMemsetAsync(bsn, 0, sizeof(double) * C, st));
@@ -1254,6 +1291,7 @@ int Engine::backbone_out_len(int T) const {
 void Engine::begin_backward(const char* where, int part, float* grads, cudaStream_t st) {
     if (lay_.block_kind) fail(where, "the handle holds a single block: use bsml_block_backward");
     if (!fwd_done_ || fwd_part_ != part) fail(where, "no matching forward");
+    if (wg_split() && !plan_wg_) fail(where, "the math mode changed to TF32X3W after the forward");
     BSML_CUDA(cudaSetDevice(device_));
     grads_ = grads;
     if (grads_) fill(grads_, lay_.total, 0.f, st);
@@ -1296,17 +1334,26 @@ Act Engine::gen_backward(const float* daudio, cudaStream_t st) {
             t0.hi = tc_eh_; t0.lo = tc_el_; t0.ld = p0.ld;
             double* bs0 = grads_ ? bsum0_ : nullptr;
             if (bs0) BSML_CUDA(cudaMemsetAsync(bs0, 0, sizeof(double) * u.cout, st));
-            scale_out_v(dX, 1.f / (float)K, nullptr, &p0, bs0, st);
-            TcPlanes tdm;
+            const bool split = wg_split();
+            const int wmode = wg_mode();
+            PlaneOut p0w;
+            p0w.hi = tc_ewh_; p0w.lo = tc_ewl_; p0w.ld = tc_pitch(u.cout, wmode); p0w.mode = wmode;
+            TcPlanes t0w;
+            t0w.hi = tc_ewh_; t0w.lo = tc_ewl_; t0w.ld = p0w.ld;
+            scale_out_v(dX, 1.f / (float)K, nullptr, &p0, bs0, st, split ? &p0w : nullptr);
+            TcPlanes tdm, tdmw;
             tdm.hi = tc_dh_; tdm.lo = tc_dl_; tdm.ld = p0.ld;
+            tdmw.hi = tc_dwh_; tdmw.lo = tc_dwl_; tdmw.ld = p0w.ld;
             for (int j = 0; j < K; ++j) {
                 RB1Io io;
                 io.in_planes = &t0;
+                io.in_planes_w = split ? &t0w : nullptr;
                 io.in_bsum = bs0;
                 io.out = &dm;
                 io.out_accum = j > 0;
                 if (j == K - 1) {
                     io.out_planes = tdm;
+                    if (split) io.out_planes_w = tdmw;
                     io.out_bsum = bsum_;
                 }
                 rb1_bwd(lay_.rbs[i * K + j], s.res[j], dX, 1.f / (float)K, D, st, &io);
@@ -1314,6 +1361,7 @@ Act Engine::gen_backward(const float* daudio, cudaStream_t st) {
             // noise branch: affine / alpha / conv grads; its input grad only feeds noise_convs' wgrad
             RB1Io nio;
             nio.in_planes = &tdm;
+            nio.in_planes_w = split ? &tdmw : nullptr;
             nio.in_bsum = bsum_;
             rb1_bwd(lay_.nres[i], s.noise, dm, 1.f, D, st, &nio);
         } else {
@@ -1460,6 +1508,7 @@ void Engine::backward_block(const float* dy, float* grads, float* dx, float* d_s
                             cudaStream_t st) {
     if (!lay_.block_kind) fail("bsml_block_backward", "the handle holds a whole decoder: use bsml_decoder_backward");
     if (!fwd_done_) fail("bsml_block_backward", "no matching forward");
+    if (wg_split() && !plan_wg_) fail("bsml_block_backward", "the math mode changed to TF32X3W after the forward");
     if (!dy) fail("bsml_block_backward", "null dy");
     BSML_CUDA(cudaSetDevice(device_));
     const int B = B_, S = lay_.cfg.style_dim;

@@ -131,11 +131,13 @@ class Engine {
     struct Opnd {
         Act f;
         TcPlanes tp;
+        TcPlanes tpw;   // the weight gradients' planes when their mode differs (wg_split), else unset
         const TcPlanes* planes() const { return tp.hi ? &tp : nullptr; }
+        const TcPlanes* planes_w() const { return tpw.hi ? &tpw : planes(); }
     };
     // Output buffer for an elementwise producer feeding a conv: operand planes
     // (hi, lo) when that conv runs on the tensor cores, else fp32 in fbuf.
-    Opnd operand(bool tc, int L, int C, const Act& fbuf, void* hi, void* lo) const;
+    Opnd operand(bool tc, int L, int C, const Act& fbuf, void* hi, void* lo, int mode = -1) const;
     void adain_fwd_to(const Act& x, const double* sums, const Stats& s, const float* gb, int act, float slope,
                       const float* alpha, const Opnd& out, cudaStream_t st);
     // acc_ready: the reduction pass already ran (recompute_reduce_to with the same x, dy)
@@ -143,7 +145,8 @@ class Engine {
     void adain_bwd_to(const Act& x, const Stats& s, const float* gb, int act, float slope, const float* alpha,
                       const Act& dy, const Opnd& out, const Act* skip, double* colsum, float* dgb, float* dalpha,
                       cudaStream_t st, bool acc_ready = false, float skip_scale = 1.f, bool out_accum = false);
-    // out = act(AdaIN(x)) again, fused with the backward's reduction over (x, dy)
+    // out = act(AdaIN(x)) again, fused with the backward's reduction over (x, dy); the
+    // output is a weight gradient's operand, so its planes are in wg_mode()
     void recompute_reduce_to(const Act& x, const Stats& s, const float* gb, int act, float slope, const float* alpha,
                              const Act& dy, const Opnd& out, cudaStream_t st);
 
@@ -182,10 +185,12 @@ class Engine {
     // sum, the last one also writing that sum's planes and column sums.
     struct RB1Io {
         const TcPlanes* in_planes = nullptr;   // planes of scale * dOut (tensor-core path)
+        const TcPlanes* in_planes_w = nullptr; // the same in wg_mode (wg_split only)
         const double* in_bsum = nullptr;       // column sums of scale * dOut (nullable)
         const Act* out = nullptr;              // destination of the input gradient instead of D
         bool out_accum = false;                // out += instead of out =
         TcPlanes out_planes;                   // planes of the final out (hi null: none)
+        TcPlanes out_planes_w;                 // the same in wg_mode (wg_split only)
         double* out_bsum = nullptr;            // column sums of the final out (zeroed here; nullable)
     };
     // returns the gradient w.r.t. the block input in `D` (scratch, may alias nothing
@@ -228,9 +233,25 @@ class Engine {
     float* tc_dl_ = nullptr;
     float* tc_eh_ = nullptr;          // planes of a generator stage's resblock entry gradient
     float* tc_el_ = nullptr;
+    // wg_split: the weight gradients' copies of the running input gradient (tc_dh_),
+    // of conv1's output gradient in a resblock pair and of the stage entry (tc_eh_)
+    float* tc_dwh_ = nullptr;
+    float* tc_dwl_ = nullptr;
+    float* tc_uwh_ = nullptr;
+    float* tc_uwl_ = nullptr;
+    float* tc_ewh_ = nullptr;
+    float* tc_ewl_ = nullptr;
     int tc_mode() const {
         return math_ == BSML_MATH_BF16 ? TC_BF16 : math_ == BSML_MATH_BF16X3 ? TC_BF16X3 : TC_TF32X3;
     }
+    // the weight gradients' mode: BF16X3 under TF32X3W (their rounding ends in dW and
+    // propagates nowhere), else tc_mode(); wg_split: the two differ, so an operand
+    // shared by an input and a weight gradient is written in both forms
+    int wg_mode() const { return math_ == BSML_MATH_TF32X3W ? TC_BF16X3 : tc_mode(); }
+    bool wg_split() const { return wg_mode() != tc_mode(); }
+    // planes of an operand that also has fp32 data, handed to a weight gradient: under
+    // wg_split the weight gradient makes its own from the fp32 data
+    const TcPlanes* wgp(const TcPlanes* p) const { return wg_split() ? nullptr : p; }
     // stride-1 convs run on the tensor cores; narrow channel counts (conv_post's 22
     // outputs, the 22 harmonic channels) are zero-padded to the tile by TMA
     bool tc_ok(int K, int M, int s) const { return math_ != BSML_MATH_FP32_SIMT && s == 1 && K >= 8 && M >= 16; }
@@ -264,7 +285,7 @@ class Engine {
         a.L = spk_rows_ / c.s;
         return a;
     }
-    TcPlanes tc_planes(const Act& x, cudaStream_t st);   // x -> planes in tc_xh_ / tc_xl_
+    TcPlanes tc_planes(const Act& x, cudaStream_t st, int mode = -1);   // x -> planes in tc_xh_ / tc_xl_
     void tc_launch(const Act& x, const TcPlanes& xp, const float* whi, const float* wlo, int taps, int M,
                    const Act& y, const float* bias, const Act* r, int r_shift, int p, int d, int No, int o_base,
                    int orow_mul, int orow_off, float alpha, bool accum, double* stats, cudaStream_t st);
@@ -283,6 +304,7 @@ class Engine {
     bool have_har_ = false;
     bool planned_ = false;
     int plan_part_ = PART_FULL;       // what the plan covers
+    bool plan_wg_ = false;            // the plan holds the weight gradients' plane copies (wg_split)
     int fwd_part_ = PART_FULL;        // what the last forward ran
 
     // per-call pointers

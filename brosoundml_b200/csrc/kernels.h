@@ -78,16 +78,19 @@ void adain_act_fwd_v(const Act& x, const double* sums, float eps, float* mean, f
 void adain_act_bwd_v(const Act& x, const float* mean, const float* rstd, const float* gb, int act, float slope,
                      const float* alpha, const Act& dy, const Act* dx, const Act* skip, const PlaneOut* planes,
                      double* colsum, float* dgb, float* dalpha, double* acc, cudaStream_t st,
-                     bool acc_ready = false, float skip_scale = 1.f, bool dx_accum = false);
+                     bool acc_ready = false, float skip_scale = 1.f, bool dx_accum = false,
+                     const PlaneOut* planes2 = nullptr);
 // The backward's reduction pass fused with recomputing the forward output act(AdaIN(x))
 // into y / planes (a weight gradient's operand): acc is zeroed and filled for a
 // following adain_act_bwd_v(..., acc_ready = true) with the same x, dy and affine.
 void adain_recompute_reduce(const Act& x, const float* mean, const float* rstd, const float* gb, int act,
                             float slope, const float* alpha, const Act* y, const PlaneOut* planes, const Act& dy,
                             double* acc, cudaStream_t st);
-// out = alpha * src -> dst (nullable), planes (nullable), colsum (nullable, added to)
+// out = alpha * src -> dst (nullable), planes (nullable), colsum (nullable, added to).
+// planes2 (here and in adain_act_bwd_v): a second set of operand planes of the same
+// output in another mode (the weight gradients' operand when their mode differs)
 void scale_out_v(const Act& src, float alpha, const Act* dst, const PlaneOut* planes, double* colsum,
-                 cudaStream_t st);
+                 cudaStream_t st, const PlaneOut* planes2 = nullptr);
 // dst[i] (+)= (float) src[i]
 void d2f(const double* src, int n, float* dst, bool accum, cudaStream_t st);
 // y = act((1 + gamma) * (x - mean) * rstd + beta); gb = [B][2C] (gamma ; beta)

@@ -34,11 +34,13 @@ struct Out4 {
     void* hi = nullptr; void* lo = nullptr; int64_t p_bs = 0; int p_ld = 0; int mode = 1;   // planes (nullable)
     const float* skip = nullptr; int64_t s_bs = 0; int s_ld = 0;       // added before the store (nullable)
     float s_scale = 1.f;                                                // factor on skip
+    void* hi2 = nullptr; void* lo2 = nullptr; int64_t p_bs2 = 0; int p_ld2 = 0; int mode2 = 1;   // second planes
 };
 
 __device__ __forceinline__ void put(const Out4& o, int b, int l, int c, const float4& v, int nv) {
     if (o.y) st4(o.y + (int64_t)b * o.y_bs + (int64_t)l * o.y_ld + c, v, nv);
     if (o.hi) st_planes4(o.hi, o.lo, o.mode, (int64_t)b * o.p_bs + (int64_t)l * o.p_ld + c, v, nv);
+    if (o.hi2) st_planes4(o.hi2, o.lo2, o.mode2, (int64_t)b * o.p_bs2 + (int64_t)l * o.p_ld2 + c, v, nv);
 }
 
 // Adds the per-thread partials s[k][j] (k < NS sums, j < 4 channels of group v)
@@ -504,8 +506,14 @@ void need_vec(const Act& a, const char* where) {
         fail(where, "channels-last buffer must have 16-byte aligned rows");
 }
 
-Out4 make_out(const Act* y, const PlaneOut* pl, const Act* skip, const Act& geom, const char* where) {
+Out4 make_out(const Act* y, const PlaneOut* pl, const Act* skip, const Act& geom, const char* where,
+              const PlaneOut* pl2 = nullptr) {
     Out4 o;
+    if (pl2 && pl2->hi) {
+        if ((pl2->ld & 3) != 0 || (reinterpret_cast<uintptr_t>(pl2->hi) & 15) != 0)
+            fail(where, "operand planes must have 16-byte aligned rows");
+        o.hi2 = pl2->hi; o.lo2 = pl2->lo; o.p_ld2 = pl2->ld; o.p_bs2 = (int64_t)geom.L * pl2->ld; o.mode2 = pl2->mode;
+    }
     if (y) {
         need_vec(*y, where);
         o.y = y->p; o.y_bs = y->bstride; o.y_ld = y->ld;
@@ -590,14 +598,14 @@ void adain_recompute_reduce(const Act& x, const float* mean, const float* rstd, 
 void adain_act_bwd_v(const Act& x, const float* mean, const float* rstd, const float* gb, int act, float slope,
                      const float* alpha, const Act& dy, const Act* dx, const Act* skip, const PlaneOut* planes,
                      double* colsum, float* dgb, float* dalpha, double* acc, cudaStream_t st, bool acc_ready,
-                     float skip_scale, bool dx_accum) {
+                     float skip_scale, bool dx_accum, const PlaneOut* planes2) {
     const int64_t n = (int64_t)x.B * x.C;
     if (dx_accum && !dx) fail("adain_act_bwd", "accumulating into a missing dx");
     if (!acc_ready) BSML_CUDA(cudaMemsetAsync(acc, 0, sizeof(double) * 3 * n, st));
     if (x.numel() > 0) {
         need_vec(x, "adain_act_bwd");
         need_vec(dy, "adain_act_bwd");
-        Out4 o = make_out(dx, planes, skip, x, "adain_act_bwd");
+        Out4 o = make_out(dx, planes, skip, x, "adain_act_bwd", planes2);
         o.s_scale = skip_scale;
         const Geo g = geo(x);
         if (!acc_ready) {
@@ -640,10 +648,10 @@ void adain_act_bwd(const Act& x, const float* mean, const float* rstd, const flo
 }
 
 void scale_out_v(const Act& src, float alpha, const Act* dst, const PlaneOut* planes, double* colsum,
-                 cudaStream_t st) {
+                 cudaStream_t st, const PlaneOut* planes2) {
     if (src.numel() == 0) return;
     need_vec(src, "scale_out");
-    const Out4 o = make_out(dst, planes, nullptr, src, "scale_out");
+    const Out4 o = make_out(dst, planes, nullptr, src, "scale_out", planes2);
     const Geo g = geo(src);
     ::bsml::count_launch();
     scale_out_kernel<<<g.grid, g.block, 0, st>>>(src, g.rows, alpha, o, colsum);

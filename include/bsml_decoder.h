@@ -70,9 +70,12 @@ typedef struct bsml_decoder bsml_decoder;
  * kernels. TF32X3: tcgen05 tensor cores, each fp32 operand split hi+lo, three
  * products (fp32-equivalent accuracy). BF16: tcgen05 with bf16 operands, fp32
  * accumulation. BF16X3: each operand split into bf16 hi + bf16 lo, three products
- * at the bf16 rate (about 16 bits of operand precision). Elementwise,
- * normalisation and spectral work is fp32 in all modes. */
-enum { BSML_MATH_FP32_SIMT = 0, BSML_MATH_TF32X3 = 1, BSML_MATH_BF16 = 2, BSML_MATH_BF16X3 = 3 };
+ * at the bf16 rate (about 16 bits of operand precision). TF32X3W: TF32X3 for the
+ * forward and input-gradient contractions, BF16X3 for the weight gradients (their
+ * rounding ends in dW and propagates nowhere; the whole gradient stays within the
+ * TF32X3 bar at the benchmarked configuration). Elementwise, normalisation and
+ * spectral work is fp32 in all modes. */
+enum { BSML_MATH_FP32_SIMT = 0, BSML_MATH_TF32X3 = 1, BSML_MATH_BF16 = 2, BSML_MATH_BF16X3 = 3, BSML_MATH_TF32X3W = 4 };
 
 const char* bsml_last_error(void);
 int bsml_version(void);

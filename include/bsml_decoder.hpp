@@ -39,7 +39,8 @@ enum class Math {
     FP32 = BSML_MATH_FP32_SIMT,
     TF32X3 = BSML_MATH_TF32X3,
     BF16 = BSML_MATH_BF16,
-    BF16X3 = BSML_MATH_BF16X3
+    BF16X3 = BSML_MATH_BF16X3,
+    TF32X3W = BSML_MATH_TF32X3W
 };
 
 // Parameter table of an engine handle (names, offsets into the flat buffer).
