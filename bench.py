@@ -742,7 +742,9 @@ def main():
                          "bytes": ("algorithmic: AdaIN+Snake forward 8 B per element (read x, write y), backward "
                                    "12 B (read x and dy, write dx); the operand planes written for the next "
                                    "conv, the recomputed Snake operand and the backward's second read of x "
-                                   "and dy are not counted")}
+                                   "and dy are not counted. DRAM traffic per element in the ncu capture "
+                                   "(profiles/kernels_other_than_tcgen05_bench_c2_B6_T200_tf32x3.md): forward "
+                                   "12 B, backward 32-40 B over its two passes")}
     dom = max(rl_all, key=lambda k: rl_all[k]["ms"])
     # the measured dense bf16 figure is the tensor roofline (sustained: these kernels run
     # inside a long step); TF32 operands run at half that rate on the same pipe
