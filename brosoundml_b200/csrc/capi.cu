@@ -92,14 +92,19 @@ int atom_tc_mode() {
     const int m = g_atom_math.load();
     return m == BSML_MATH_BF16 ? bsml::TC_BF16 : m == BSML_MATH_BF16X3 ? bsml::TC_BF16X3 : bsml::TC_TF32X3;
 }
-// weight gradients: BF16X3 under TF32X3W, else the mode above
-int atom_wg_mode() { return g_atom_math.load() == BSML_MATH_TF32X3W ? bsml::TC_BF16X3 : atom_tc_mode(); }
+// input gradients: BF16X3 under TF32X3F; weight gradients: BF16X3 under TF32X3W and
+// TF32X3F; else the mode above
+int atom_dg_mode() { return g_atom_math.load() == BSML_MATH_TF32X3F ? bsml::TC_BF16X3 : atom_tc_mode(); }
+int atom_wg_mode() {
+    const int m = g_atom_math.load();
+    return (m == BSML_MATH_TF32X3W || m == BSML_MATH_TF32X3F) ? bsml::TC_BF16X3 : atom_tc_mode();
+}
 
 // Tensor-core forward-like conv for the atoms: planes of x, packed weight planes, launch.
 void atom_tc_conv(Scratch& sc, const bsml::Act& xa, const float* W, int kind, int Co_w, int Ci_w, int k, int s_ph,
                   int r_ph, int taps, int M, const bsml::Act& ya, const float* bias, int p, int d, int No, int o_base,
-                  int orow_mul, int orow_off, cudaStream_t st) {
-    const int mode = atom_tc_mode();
+                  int orow_mul, int orow_off, cudaStream_t st, int mode = -1) {
+    if (mode < 0) mode = atom_tc_mode();
     float* xh = sc.f((int64_t)xa.B * xa.L * bsml::tc_pitch(xa.C, mode));
     float* xl = sc.f((int64_t)xa.B * xa.L * bsml::tc_pitch(xa.C, mode));
     const int64_t wn = (int64_t)taps * M * bsml::round_up(xa.C, 8);
@@ -344,7 +349,7 @@ int64_t bsml_launch_count(void) { return bsml::launch_count(); }
 int bsml_set_atom_math(int math_mode) {
     return guarded([&] {
         need(math_mode == BSML_MATH_FP32_SIMT || math_mode == BSML_MATH_TF32X3 || math_mode == BSML_MATH_BF16 ||
-                 math_mode == BSML_MATH_BF16X3 || math_mode == BSML_MATH_TF32X3W,
+                 math_mode == BSML_MATH_BF16X3 || math_mode == BSML_MATH_TF32X3W || math_mode == BSML_MATH_TF32X3F,
              "bsml_set_atom_math", "unknown math mode");
         g_atom_math.store(math_mode);
     });
@@ -848,7 +853,7 @@ int bsml_conv1d_backward_input(const float* dy, int B, int Ci, int L, const floa
         bsml::ncl_to_cl(dy, ga, st);
         if (atom_tc(Co, Ci, 1)) {
             atom_tc_conv(sc, ga, W, bsml::PACK_CONV_DGRAD, Co, Ci, k, 1, 0, k, Ci, xa, nullptr, dil * (k - 1) - pad, dil,
-                         L, 0, 1, 0, st);
+                         L, 0, 1, 0, st, atom_dg_mode());
         } else {
             float* wp = sc.f((int64_t)k * Co * bsml::round_up(Ci, 4));
             bsml::pack_conv_dgrad(W, Co, Ci, k, wp, st);
@@ -937,7 +942,7 @@ int bsml_conv_transpose1d_backward_input(const float* dy, int B, int Ci, int L, 
         bsml::Act ga = sc.act(B, Lu, Co), xa = sc.act(B, L, Ci);
         bsml::ncl_to_cl(dy, ga, st);
         if (atom_convT_tc(Ci, Co, stride, Lu)) {
-            const int mode = atom_tc_mode();
+            const int mode = atom_dg_mode();
             const bsml::ConvTPack pk = bsml::convT_pack(k, stride, pad);
             const int K = stride * Co;
             float* gh = sc.f((int64_t)B * Lu * Co);

@@ -186,7 +186,7 @@ Engine::~Engine() {
 
 void Engine::set_math(int m) {
     if (m != BSML_MATH_FP32_SIMT && m != BSML_MATH_TF32X3 && m != BSML_MATH_BF16 && m != BSML_MATH_BF16X3 &&
-        m != BSML_MATH_TF32X3W)
+        m != BSML_MATH_TF32X3W && m != BSML_MATH_TF32X3F)
         fail("bsml_decoder_set_math", "unknown math mode " + std::to_string(m));
     math_ = m;
 }
@@ -559,7 +559,7 @@ void Engine::pack_weights(cudaStream_t st) {
 }
 void Engine::pack_dgrad_weights(cudaStream_t st) {
     if (pack_jobs_math_ != math_) build_pack_jobs();
-    pack_w_tc_batch(params_, pack_jobs_ + PACK_MAX_JOBS, n_pack_dg_, tot_pack_dg_, tc_mode(), st);
+    pack_w_tc_batch(params_, pack_jobs_ + PACK_MAX_JOBS, n_pack_dg_, tot_pack_dg_, bw_mode(), st);
     for (auto* c : lay_.convs)
         if (c->s == 1 && !tc_ok(c->cout, c->cin, 1))
             pack_conv_dgrad(params_ + c->w, c->cout, c->cin, c->k, wp_dgrad_[c->id], st);
@@ -598,7 +598,7 @@ void Engine::adain_bwd_to(const Act& x, const Stats& s, const float* gb, int act
                           const Act& dy, const Opnd& out, const Act* skip, double* colsum, float* dgb, float* dalpha,
                           cudaStream_t st, bool acc_ready, float skip_scale, bool out_accum) {
     PlaneOut po, po2;
-    po.hi = const_cast<void*>(out.tp.hi); po.lo = const_cast<void*>(out.tp.lo); po.ld = out.tp.ld; po.mode = tc_mode();
+    po.hi = const_cast<void*>(out.tp.hi); po.lo = const_cast<void*>(out.tp.lo); po.ld = out.tp.ld; po.mode = bw_mode();
     po2.hi = const_cast<void*>(out.tpw.hi); po2.lo = const_cast<void*>(out.tpw.lo); po2.ld = out.tpw.ld;
     po2.mode = wg_mode();
     adain_act_bwd_v(x, s.mean, s.rstd, gb, act, slope, alpha, dy, out.f.p ? &out.f : nullptr, skip,
@@ -616,7 +616,8 @@ void Engine::recompute_reduce_to(const Act& x, const Stats& s, const float* gb, 
 
 void Engine::tc_launch(const Act& x, const TcPlanes& xp, const float* whi, const float* wlo, int taps, int M,
                        const Act& y, const float* bias, const Act* r, int r_shift, int p, int d, int No, int o_base,
-                       int orow_mul, int orow_off, float alpha, bool accum, double* stats, cudaStream_t st) {
+                       int orow_mul, int orow_off, float alpha, bool accum, double* stats, cudaStream_t st,
+                       int mode) {
     TcConvFwd a;
     a.x = xp;
     a.B = x.B; a.L_in = x.L; a.Ci = x.C;
@@ -627,7 +628,7 @@ void Engine::tc_launch(const Act& x, const TcPlanes& xp, const float* whi, const
     a.alpha = alpha; a.accum = accum;
     a.stats = stats;
     a.part = part_; a.part_cap = part_floats_;   // split-K scratch, shared with the weight gradients
-    conv_fwd_tc(a, tc_mode(), st);
+    conv_fwd_tc(a, mode < 0 ? tc_mode() : mode, st);
 }
 
 // ── conv wrappers
@@ -678,10 +679,10 @@ void Engine::conv_dgrad(const ConvP& c, const Act& dy, const Act& dx, bool accum
     a.No = dx.L;
     a.accum = accum;
     if (tc_ok(c.cout, c.cin, 1)) {
-        const TcPlanes tp = dyp ? *dyp : tc_planes(dy, st);
+        const TcPlanes tp = dyp ? *dyp : tc_planes(dy, st, bw_mode());
         const int id = prof_begin(PROF_CONV_TC, 2.0 * c.cin * c.cout * c.k * (double)dy.L * dy.B, st);
         tc_launch(dy, tp, tcw_dg_hi_[c.id], tcw_dg_lo_[c.id], c.k, c.cin, dx, nullptr, nullptr, 0, a.p, c.d, a.No, 0,
-                  1, 0, 1.f, accum, nullptr, st);
+                  1, 0, 1.f, accum, nullptr, st, bw_mode());
         prof_end(id, st);
         return;
     }
@@ -800,7 +801,7 @@ void Engine::convT_dgrad(const UpP& u, const Act& dy, const Act& dx, cudaStream_
         a.y = dx;
         a.part = part_; a.part_cap = part_floats_;
         const int id = prof_begin(PROF_CONV_TC, 2.0 * u.cin * u.cout * u.k * (double)dx.L * dx.B, st);
-        conv_fwd_tc(a, tc_mode(), st);
+        conv_fwd_tc(a, bw_mode(), st);
         prof_end(id, st);
         return;
     }
@@ -859,8 +860,8 @@ void Engine::convT_wgrad(const UpP& u, const Act& dy, const Act& x, cudaStream_t
 // tc_yh_ / tc_yl_ (compact rows), or nullptr when the CUDA-core path applies.
 const TcPlanes* Engine::convT_dy_planes(const UpP& u, const Act& dy, TcPlanes& tp, cudaStream_t st) {
     if (!convT_tc(u) || dy.L % u.s != 0) return nullptr;
-    make_act_planes(dy, tc_mode(), tc_yh_, tc_yl_, st);
-    tp.hi = tc_yh_; tp.lo = tc_yl_; tp.ld = tc_pitch(dy.C, tc_mode());
+    make_act_planes(dy, bw_mode(), tc_yh_, tc_yl_, st);
+    tp.hi = tc_yh_; tp.lo = tc_yl_; tp.ld = tc_pitch(dy.C, bw_mode());
     if (tp.ld != dy.C) fail("convT_dgrad", "internal: row-packed planes need compact rows");
     return &tp;
 }
@@ -914,8 +915,8 @@ void Engine::blk_bwd(const BlkP& w, BlkC& c, const Act& dY, const Act& dX, cudaS
         if (bs) BSML_CUDA(cudaMemsetAsync(bs, 0, sizeof(double) * C, st));
     };
     auto planes_in = [&](void* hi, void* lo, int C, TcPlanes& tp, PlaneOut& po) {
-        tp.hi = hi; tp.lo = lo; tp.ld = tc_pitch(C, tc_mode());
-        po.hi = hi; po.lo = lo; po.ld = tp.ld; po.mode = tc_mode();
+        tp.hi = hi; tp.lo = lo; tp.ld = tc_pitch(C, bw_mode());
+        po.hi = hi; po.lo = lo; po.ld = tp.ld; po.mode = bw_mode();
     };
     // d_branch = dY / sqrt(2) (S_[0]), in the same pass its operand planes (tc_dh_)
     // for conv2's input and weight gradients and its column sums (conv2's bias gradient)
@@ -957,8 +958,8 @@ void Engine::blk_bwd(const BlkP& w, BlkC& c, const Act& dY, const Act& dX, cudaS
         dbs = view(S_[3], Lin, w.cout);
         pair_sum_rows(db, dbs, st);
         if (tcs) {
-            make_act_planes(dbs, tc_mode(), tc_dh_, tc_dl_, st);
-            sp.hi = tc_dh_; sp.lo = tc_dl_; sp.ld = tc_pitch(w.cout, tc_mode());
+            make_act_planes(dbs, bw_mode(), tc_dh_, tc_dl_, st);
+            sp.hi = tc_dh_; sp.lo = tc_dl_; sp.ld = tc_pitch(w.cout, bw_mode());
         }
     }
     const bool have_sp = tcs && (w.up || tc2);
@@ -1028,12 +1029,12 @@ void Engine::rb1_bwd(const RB1P& w, RB1C& c, const Act& dOut, float scale, const
     // with the entry made by the caller, planes and bias sum from there and D first
     // written by the first pair's last pass (dOut, scaled, as its skip term)
     // Under wg_split every gradient operand shared by an input and a weight gradient
-    // is written twice: tc_mode() planes for the input gradient, wg_mode() ones (the
+    // is written twice: bw_mode() planes for the input gradient, wg_mode() ones (the
     // `_w` buffers) for the weight gradient.
     const bool split = tc && wg_split();
     Opnd Dp;
     Dp.f = D;
-    if (tc) { Dp.tp.hi = tc_dh_; Dp.tp.lo = tc_dl_; Dp.tp.ld = tc_pitch(C, tc_mode()); }
+    if (tc) { Dp.tp.hi = tc_dh_; Dp.tp.lo = tc_dl_; Dp.tp.ld = tc_pitch(C, bw_mode()); }
     if (split) { Dp.tpw.hi = tc_dwh_; Dp.tpw.lo = tc_dwl_; Dp.tpw.ld = tc_pitch(C, wg_mode()); }
     const bool pre = io && io->in_planes;
     if (pre && !tc) fail("rb1_bwd", "internal: entry planes without the tensor-core path");
@@ -1043,7 +1044,7 @@ void Engine::rb1_bwd(const RB1P& w, RB1C& c, const Act& dOut, float scale, const
     const double* in_bs = pre ? (grads_ ? io->in_bsum : nullptr) : bs;
     if (!pre) {
         PlaneOut po, po2;
-        po.hi = tc_dh_; po.lo = tc_dl_; po.ld = Dp.tp.ld; po.mode = tc_mode();
+        po.hi = tc_dh_; po.lo = tc_dl_; po.ld = Dp.tp.ld; po.mode = bw_mode();
         po2.hi = tc_dwh_; po2.lo = tc_dwl_; po2.ld = Dp.tpw.ld; po2.mode = wg_mode();
         zero_bs();
         scale_out_v(dOut, scale, &D, tc ? &po : nullptr, bs, st, split ? &po2 : nullptr);
@@ -1065,7 +1066,7 @@ void Engine::rb1_bwd(const RB1P& w, RB1C& c, const Act& dOut, float scale, const
         conv_wgrad(w.c2[i], D, s2.f, st, dplw, s2.planes(), i == 2 ? in_bs : bs);
         // u = gradient at conv1's output (operand of c1's dgrad and wgrad)
         id = prof_begin(PROF_NORM_BWD, 4.0 * n, st);
-        Opnd u = operand(tc, L, C, S_[5], tc_yh_, tc_yl_);
+        Opnd u = operand(tc, L, C, S_[5], tc_yh_, tc_yl_, bw_mode());
         if (split) { u.tpw.hi = tc_uwh_; u.tpw.lo = tc_uwl_; u.tpw.ld = tc_pitch(C, wg_mode()); }
         zero_bs();
         adain_bwd_to(c.c1[i], c.st2[i], aff(w.a2[i]), ACT_SNAKE, 0.f, P(w.al2[i]), t, u, nullptr, bs, daff(w.a2[i]),
@@ -1327,7 +1328,7 @@ Act Engine::gen_backward(const float* daudio, cudaStream_t st) {
             // the resblocks' common entry dX / K as planes and column sums, made once;
             // each resblock adds its input gradient into dm, the last one also writing
             // dm's planes (tc_dh_) and column sums (bsum_), the noise resblock's entry
-            const int mode = tc_mode();
+            const int mode = bw_mode();
             PlaneOut p0;
             p0.hi = tc_eh_; p0.lo = tc_el_; p0.ld = tc_pitch(u.cout, mode); p0.mode = mode;
             TcPlanes t0;

@@ -244,11 +244,17 @@ class Engine {
     int tc_mode() const {
         return math_ == BSML_MATH_BF16 ? TC_BF16 : math_ == BSML_MATH_BF16X3 ? TC_BF16X3 : TC_TF32X3;
     }
-    // the weight gradients' mode: BF16X3 under TF32X3W (their rounding ends in dW and
-    // propagates nowhere), else tc_mode(); wg_split: the two differ, so an operand
-    // shared by an input and a weight gradient is written in both forms
-    int wg_mode() const { return math_ == BSML_MATH_TF32X3W ? TC_BF16X3 : tc_mode(); }
-    bool wg_split() const { return wg_mode() != tc_mode(); }
+    // tc_mode(): the forward's contractions and operand planes. bw_mode(): the
+    // backward's input gradients and the planes its producers write (BF16X3 under
+    // TF32X3F). wg_mode(): the weight gradients (BF16X3 under TF32X3W and TF32X3F:
+    // their rounding ends in dW and propagates nowhere). wg_split: the last two differ
+    // (TF32X3W), so an operand shared by an input and a weight gradient is written in
+    // both forms.
+    int bw_mode() const { return math_ == BSML_MATH_TF32X3F ? TC_BF16X3 : tc_mode(); }
+    int wg_mode() const {
+        return (math_ == BSML_MATH_TF32X3W || math_ == BSML_MATH_TF32X3F) ? TC_BF16X3 : tc_mode();
+    }
+    bool wg_split() const { return wg_mode() != bw_mode(); }
     // planes of an operand that also has fp32 data, handed to a weight gradient: under
     // wg_split the weight gradient makes its own from the fp32 data
     const TcPlanes* wgp(const TcPlanes* p) const { return wg_split() ? nullptr : p; }
@@ -288,7 +294,8 @@ class Engine {
     TcPlanes tc_planes(const Act& x, cudaStream_t st, int mode = -1);   // x -> planes in tc_xh_ / tc_xl_
     void tc_launch(const Act& x, const TcPlanes& xp, const float* whi, const float* wlo, int taps, int M,
                    const Act& y, const float* bias, const Act* r, int r_shift, int p, int d, int No, int o_base,
-                   int orow_mul, int orow_off, float alpha, bool accum, double* stats, cudaStream_t st);
+                   int orow_mul, int orow_off, float alpha, bool accum, double* stats, cudaStream_t st,
+                   int mode = -1);
     PackJob* pack_jobs_ = nullptr;                // device: forward jobs, then dgrad jobs at PACK_MAX_JOBS
     int n_pack_fw_ = 0, n_pack_dg_ = 0, pack_jobs_math_ = -1;
     int64_t tot_pack_fw_ = 0, tot_pack_dg_ = 0;

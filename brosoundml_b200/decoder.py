@@ -14,7 +14,7 @@ import torch
 
 from . import _lib
 
-MATH = {"fp32": 0, "tf32x3": 1, "bf16": 2, "bf16x3": 3, "tf32x3w": 4}
+MATH = {"fp32": 0, "tf32x3": 1, "bf16": 2, "bf16x3": 3, "tf32x3w": 4, "tf32x3f": 5}
 PHASE = {"fp32": 0, "exact": 1}
 
 
@@ -37,8 +37,8 @@ def _f32(t):
 class Decoder:
     # math modes smoke() exercises (the tensor-core modes join once built)
     SMOKE_MATH = ("fp32", "tf32x3", "bf16x3")
-    # the fp32-grade tensor-core mode (bench.py runs "tf32x3w": the same with BF16x3
-    # weight gradients, within the same bar at config 2)
+    # the fp32-grade tensor-core mode (bench.py runs "tf32x3f": TF32x3 forward, BF16x3
+    # backward, within the same bar at config 2)
     DEFAULT_MATH = "tf32x3"
 
     def __init__(self, cfg: dict, device: int = 0, math: str = "fp32"):

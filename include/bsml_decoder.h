@@ -73,9 +73,19 @@ typedef struct bsml_decoder bsml_decoder;
  * at the bf16 rate (about 16 bits of operand precision). TF32X3W: TF32X3 for the
  * forward and input-gradient contractions, BF16X3 for the weight gradients (their
  * rounding ends in dW and propagates nowhere; the whole gradient stays within the
- * TF32X3 bar at the benchmarked configuration). Elementwise, normalisation and
+ * TF32X3 bar at the benchmarked configuration). TF32X3F: TF32X3 for the forward
+ * contractions only, BF16X3 for every contraction of the backward (input and weight
+ * gradients): the decoder's gradients are sensitive to the forward's rounding, not
+ * to the backward's, and stay within the TF32X3 bar. Elementwise, normalisation and
  * spectral work is fp32 in all modes. */
-enum { BSML_MATH_FP32_SIMT = 0, BSML_MATH_TF32X3 = 1, BSML_MATH_BF16 = 2, BSML_MATH_BF16X3 = 3, BSML_MATH_TF32X3W = 4 };
+enum {
+    BSML_MATH_FP32_SIMT = 0,
+    BSML_MATH_TF32X3 = 1,
+    BSML_MATH_BF16 = 2,
+    BSML_MATH_BF16X3 = 3,
+    BSML_MATH_TF32X3W = 4,
+    BSML_MATH_TF32X3F = 5
+};
 
 const char* bsml_last_error(void);
 int bsml_version(void);

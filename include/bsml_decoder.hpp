@@ -40,7 +40,8 @@ enum class Math {
     TF32X3 = BSML_MATH_TF32X3,
     BF16 = BSML_MATH_BF16,
     BF16X3 = BSML_MATH_BF16X3,
-    TF32X3W = BSML_MATH_TF32X3W
+    TF32X3W = BSML_MATH_TF32X3W,
+    TF32X3F = BSML_MATH_TF32X3F
 };
 
 // Parameter table of an engine handle (names, offsets into the flat buffer).

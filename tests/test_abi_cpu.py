@@ -84,8 +84,8 @@ def test_math_mode_names_match_the_header():
     """The Python mode names map to the header's BSML_MATH_* values."""
     from brosoundml_b200.decoder import MATH
     text = open(HEADER).read()
-    enum = re.search(r"enum \{ (BSML_MATH_FP32_SIMT = 0[^}]*)\}", text).group(1)
+    enum = re.search(r"enum \{\s*(BSML_MATH_FP32_SIMT = 0[^}]*)\}", text).group(1)
     vals = {k.strip(): int(v) for k, v in (e.split("=") for e in enum.split(","))}
     names = {"fp32": "BSML_MATH_FP32_SIMT", "tf32x3": "BSML_MATH_TF32X3", "bf16": "BSML_MATH_BF16",
-             "bf16x3": "BSML_MATH_BF16X3", "tf32x3w": "BSML_MATH_TF32X3W"}
+             "bf16x3": "BSML_MATH_BF16X3", "tf32x3w": "BSML_MATH_TF32X3W", "tf32x3f": "BSML_MATH_TF32X3F"}
     assert {m: vals[names[m]] for m in names} == MATH
