@@ -828,9 +828,9 @@ void Engine::convT_wgrad(const UpP& u, const Act& dy, const Act& x, cudaStream_t
         TcConvWgrad w;
         w.dy = tc_planes(x, st, mode);   // the convT input plays dY's role (M = Ci of the convT)
         if (wg_split()) {
+            if (tc_pitch(dy.C, mode) != dy.C) fail("convT_wgrad", "internal: row-packed planes need compact rows");
             make_act_planes(dy, mode, tc_yh_, tc_yl_, st);
             w.x.hi = tc_yh_; w.x.lo = tc_yl_;
-            if (tc_pitch(dy.C, mode) != dy.C) fail("convT_wgrad", "internal: row-packed planes need compact rows");
         } else {
             w.x = *dyp;
         }
