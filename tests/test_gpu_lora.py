@@ -59,7 +59,7 @@ def _make(cfg, math, seed=5, rank=RANK):
 
 
 @pytest.mark.parametrize("which,math", [("miniature", "fp32"), ("miniature", "tf32x3"), ("kokoro", "tf32x3"),
-                                        ("kokoro", "bf16x3")])
+                                        ("kokoro", "bf16x3"), ("kokoro", "tf32x3f")])
 def test_lora_forward_backward_vs_oracle(which, math):
     torch = _torch()
     cfg, o, p, x, har, ref_s, cond = _case(which)
@@ -171,7 +171,7 @@ def _make_conv(cfg, math, seed=5, rank=RANK):
     return dec, ConvLora(dec, rank=rank, scale=SCALE, seed=seed)
 
 
-@pytest.mark.parametrize("which,math", [("miniature", "fp32"), ("kokoro", "tf32x3")])
+@pytest.mark.parametrize("which,math", [("miniature", "fp32"), ("kokoro", "tf32x3"), ("kokoro", "tf32x3f")])
 def test_conv_lora_forward_backward_vs_oracle(which, math):
     torch = _torch()
     cfg, o, p, x, har, ref_s, cond = _case(which)
@@ -191,7 +191,7 @@ def test_conv_lora_forward_backward_vs_oracle(which, math):
     torch.cuda.synchronize()
     r = lo.conv_lora_run(o, lay, p.astype(np.float64), lp.astype(np.float64), x["asr"], x["F0"], x["N"],
                          x["style"], SCALE, har=har, daudio=da.astype(np.float64))
-    tol = 1e-4   # fp32 / TF32x3 against the float64 oracle
+    tol = 1e-4   # fp32 / TF32x3 / TF32x3F against the float64 oracle
     assert rel_l2(audio.cpu().numpy(), r["audio"]) < tol
     g = cl.grads().cpu().numpy()
     assert rel_l2(g, r["grads"]) < tol
